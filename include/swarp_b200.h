@@ -1,0 +1,157 @@
+/*
+ * swarp_b200 — C ABI of the B200 (sm_100a) differentiable batched physics step.
+ *
+ * This is the boundary the Python layer (swarp_b200.interop / swarp_b200.core) calls
+ * through ctypes. Every entry point takes plain pointers and sizes, allocates nothing,
+ * launches on the caller's CUDA stream, never aborts, and returns SWARP_OK (0) or a
+ * negative error code (see swarp_error_string). All device pointers address
+ * contiguous row-major arrays in the dtype named by swarp_world_t.dtype.
+ *
+ * What each entry point replaces in the reference (ddebenedittis/swarp):
+ *   swarp_rollout_fwd  -> the forward half of swarp/interop/autograd.py:341-369
+ *                         (rollout: T x warp_step, each Stepper.launch_substeps at
+ *                         swarp/core/stepper.py:784-1011: neighbor build
+ *                         swarp/core/neighbors.py:76-97, collision_forces_kernel
+ *                         swarp/core/collisions.py:818-881, obstacle_dynamics_kernel
+ *                         swarp/core/bodies.py:367-569, integrate_kernel
+ *                         swarp/dynamics/kernels.py:812-971)
+ *   swarp_rollout_bwd  -> the backward half: _WarpStepFn.backward
+ *                         swarp/interop/autograd.py:277-296 (wp.Tape.backward replay of
+ *                         Warp's generated adjoints), T times in reverse
+ *   swarp_neighbors    -> NeighborGrid brute build + overflow view
+ *                         swarp/core/neighbors.py:76-97, 465-492, 709-714
+ */
+#ifndef SWARP_B200_H
+#define SWARP_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SWARP_OK 0
+#define SWARP_ERR_INVALID_ARG (-1)   /* null pointer, bad size or inconsistent config */
+#define SWARP_ERR_UNSUPPORTED (-2)   /* model / option this build does not run       */
+#define SWARP_ERR_TOO_MANY_AGENTS (-3) /* n_agents above SWARP_MAX_AGENTS            */
+#define SWARP_ERR_CUDA (-4)          /* a CUDA launch or attribute call failed       */
+#define SWARP_ERR_WORKSPACE (-5)     /* workspace pointer null or too small          */
+
+#define SWARP_MAX_AGENTS 1024
+#define SWARP_NUM_PARAMS 22
+
+typedef enum { SWARP_F32 = 0, SWARP_F64 = 1 } swarp_dtype_t;
+typedef enum { SWARP_BOUNDS_NONE = 0, SWARP_BOUNDS_SOFT = 1, SWARP_BOUNDS_CLAMP = 2 } swarp_bounds_t;
+
+/* The five live 2-D agent fields, structure of arrays. For a state at one time the
+ * shapes are pos/vel [E, A, 2] and theta/speed/ang_vel [E, A]; for a trajectory a
+ * leading [T] is added. A NULL field means "absent" where the entry point says so. */
+typedef struct {
+  void* pos;
+  void* theta;
+  void* vel;
+  void* speed;
+  void* ang_vel;
+} swarp_state_t;
+
+/* Obstacle set (E envs, N shapes). Poses and motion are per env, extents per shape.
+ * Movable compound bodies (kind == 1) are integrated inside the substep loop. */
+typedef struct {
+  int32_t n_obstacles;   /* N; 0 = no obstacles (all other fields ignored) */
+  const void* pos;       /* [E, N, 2] */
+  const void* angle;     /* [E, N]    */
+  const void* vel;       /* [E, N, 2] */
+  const void* ang_vel;   /* [E, N]    */
+  const void* radius;    /* [N]       */
+  const void* half;      /* [N, 2]    */
+  const int32_t* shape;  /* [N] 0 circle, 1 box, 2 segment */
+  const int32_t* kind;   /* [N] 0 immovable, 1 movable */
+  const void* mass;      /* [N] */
+  const void* inertia;   /* [N] */
+  const int32_t* body;   /* [N] body root index of each shape */
+  const void* body_off;  /* [N, 2] shape placement in its body frame */
+  int32_t any_movable;   /* 1 when any kind == 1 (host-known; selects the body pass) */
+  int32_t bodies_move;   /* 0 freezes movable bodies (the reference's taped-step rule) */
+} swarp_obstacles_t;
+
+/* Movable-body state per shape slot (only body-root slots are meaningful):
+ * pos/vel [E, N, 2], angle/ang_vel [E, N]; a trajectory adds a leading [T]. */
+typedef struct {
+  void* pos;
+  void* angle;
+  void* vel;
+  void* ang_vel;
+} swarp_bodies_t;
+
+typedef struct {
+  int32_t dtype;          /* swarp_dtype_t */
+  int32_t n_envs;         /* E */
+  int32_t n_agents;       /* A, 1..SWARP_MAX_AGENTS */
+  int32_t act_dim;        /* action slots per agent, >= 2 (slots past 2 are ignored) */
+  int32_t substeps;       /* >= 1 */
+  double dt;              /* env step; the substep is dt / substeps */
+  int32_t collisions;     /* agent-agent contacts on/off */
+  double k, c, margin, max_overlap;
+  double neighbor_radius; /* R of the within-radius lists */
+  int32_t max_neighbors;  /* K, list cap (first K by agent index) */
+  int32_t bounds_mode;    /* swarp_bounds_t */
+  double bounds[4];       /* x_min, x_max, y_min, y_max */
+  double lin_damping, ang_damping; /* movable-body drag */
+  const void* params;     /* [A, 22] shared, or [E, A, 22] per env */
+  int64_t params_env_stride; /* elements between consecutive envs' rows; 0 = shared */
+  const int32_t* model_tag;  /* [A] DynamicsModel (0..2 run here) */
+  const int32_t* ctrl_mode;  /* [A] ControlMode */
+  int32_t fleet_models;      /* host-known bitmask of the DynamicsModel values in model_tag */
+  int32_t fleet_modes;       /* host-known bitmask of the ControlMode values in ctrl_mode */
+  swarp_obstacles_t obstacles;
+} swarp_world_t;
+
+/* Bytes of device workspace swarp_rollout_fwd fills and swarp_rollout_bwd reads
+ * for this world and horizon (0 when none is needed). */
+size_t swarp_rollout_workspace_bytes(const swarp_world_t* w, int32_t horizon);
+
+/* Forward rollout of `horizon` steps from `init`.
+ *   actions   [T, E, A, act_dim]
+ *   traj      out: the state after every step, [T, E, A(,2)] (all five fields required)
+ *   final     out (fields may be NULL): the state after the last step
+ *   true_count_max  out [E, A] int32 or NULL: max over all substeps of the uncapped
+ *             within-radius neighbor count (overflow <=> > max_neighbors)
+ *   bodies_init / bodies_traj: movable-body state at t=0 and after every step
+ *             (required only when obstacles.any_movable)
+ *   workspace: device scratch of swarp_rollout_workspace_bytes() bytes, kept for the
+ *             matching swarp_rollout_bwd call. */
+int swarp_rollout_fwd(const swarp_world_t* w, int32_t horizon, swarp_state_t init,
+                      const void* actions, swarp_state_t traj, swarp_state_t final_out,
+                      int32_t* true_count_max, swarp_bodies_t bodies_init,
+                      swarp_bodies_t bodies_traj, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
+/* Adjoint of swarp_rollout_fwd (same world, horizon, init, actions, traj, bodies and
+ * workspace). Cotangents: adj_traj [T, ...] and adj_final (any field may be NULL =
+ * zero), adj_bodies_final (fields may be NULL; body pos/angle/vel/ang_vel after the
+ * last step). Outputs: adj_actions [T, E, A, act_dim] and adj_init (all five fields
+ * required). Deterministic: no atomics, fixed summation order. */
+int swarp_rollout_bwd(const swarp_world_t* w, int32_t horizon, swarp_state_t init,
+                      const void* actions, swarp_state_t traj, swarp_state_t adj_traj,
+                      swarp_state_t adj_final, swarp_bodies_t bodies_init,
+                      swarp_bodies_t bodies_traj, swarp_bodies_t adj_bodies_final,
+                      void* adj_actions, swarp_state_t adj_init, const void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* Padded within-radius neighbor lists of positions pos [E, A, 2] (brute force, ascending
+ * agent index, capped at max_neighbors): idx [E, A, K] int32 (unused slots untouched),
+ * count [E, A], true_count [E, A] (uncapped). */
+int swarp_neighbors(const swarp_world_t* w, const void* pos, int32_t* idx, int32_t* count,
+                    int32_t* true_count, void* stream);
+
+/* Static description of a return code. */
+const char* swarp_error_string(int code);
+
+/* ABI version of this library (bumped on any signature change). */
+int32_t swarp_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SWARP_B200_H */

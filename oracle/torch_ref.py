@@ -1,0 +1,679 @@
+"""CPU restatement of swarp's differentiable step, in torch (float64 by default).
+
+TEST INFRASTRUCTURE ONLY. This module is the parity checker for the CUDA path: only
+``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg may import
+it. The product (``swarp_b200``) never calls it and has no CPU fallback.
+
+What it restates (reference = ddebenedittis/swarp, paths relative to that project):
+
+* ``swarp/dynamics/kernels.py:68-71``  ``clamp_norm``
+* ``swarp/dynamics/kernels.py:166-190`` ``servo_command``
+* ``swarp/dynamics/kernels.py:194-275`` ``_step_2d`` (holonomic / diff-drive / bicycle)
+* ``swarp/dynamics/kernels.py:395-403`` the disc bounds clamp of ``_integrate_agent``
+* ``swarp/core/collisions.py:48``      ``_EPS2``
+* ``swarp/core/collisions.py:61-84``   ``shape_bound``, ``bounds_apart``
+* ``swarp/core/collisions.py:87-143``  ``_normal_coeff``, ``pair_force``
+* ``swarp/core/collisions.py:156-260`` ``closest_on_segment``, ``box_force``
+* ``swarp/core/collisions.py:690-815`` obstacle, wall and static forces
+* ``swarp/core/collisions.py:818-881`` ``collision_forces_kernel`` (list-order gather)
+* ``swarp/core/neighbors.py:76-97``    ``_brute_force`` (ascending index, cap, true count)
+* ``swarp/core/bodies.py:79-127,167-255,367-569`` movable compound-body pass
+* ``swarp/core/stepper.py:549-648``    substep order: neighbors, forces, bodies, integrate
+
+Gradients come from torch autograd over this restatement. Warp's adjoint conventions
+at kinks are reproduced with ``torch.where`` forms: ``max(a, b)`` sends the gradient
+to ``b`` on a tie, ``clamp`` passes it to ``x`` on the closed interval, ``length`` and
+``abs`` follow Warp's ``adj_length`` (zero at the zero vector) and ``adj_abs`` (+1 at
+0). Movable bodies are not differentiated by the reference (its body pass is
+untaped, ``swarp/core/bodies.py:40-43``); here they are, which makes this module the
+gradient oracle for bodies (pinned by finite differences in the tests).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+
+# Parameter-row columns (same layout as swarp/dynamics/base.py:114-169).
+P_RADIUS, P_MASS, P_MAX_SPEED, P_MAX_ACCEL, P_MAX_ANG_VEL, P_MAX_ANG_ACCEL = 0, 1, 2, 3, 4, 5
+P_LF, P_LR, P_MAX_STEER, P_MIN_SPEED = 6, 7, 8, 16
+P_CMD_GAIN_V, P_CMD_GAIN_W = 20, 21
+HOLONOMIC, DIFF_DRIVE, BICYCLE = 0, 1, 2
+VELOCITY, ACCELERATION, SERVO = 0, 1, 2
+CIRCLE, BOX, SEGMENT = 0, 1, 2
+EPS2 = 1.0e-10
+
+
+# --------------------------------------------------------------------------- kinks
+
+
+def wmax(a, b):
+    """Warp ``max``: value max(a, b); gradient to ``a`` iff ``a > b``."""
+    return torch.where(a > b, a, b)
+
+
+def wmin(a, b):
+    return torch.where(a < b, a, b)
+
+
+def wclamp(x, lo, hi):
+    """Warp ``clamp``: value ``min(max(lo, x), hi)``; gradient to ``x`` iff lo <= x <= hi."""
+    x_t = torch.as_tensor(x)
+    lo = torch.as_tensor(lo, dtype=x_t.dtype, device=x_t.device)
+    hi = torch.as_tensor(hi, dtype=x_t.dtype, device=x_t.device)
+    val = torch.minimum(torch.maximum(lo, x_t), hi).detach()
+    return torch.where((x_t >= lo) & (x_t <= hi), x_t, val)
+
+
+def wabs(x):
+    return torch.where(x < 0, -x, x)
+
+
+def wlength(x, y):
+    """Warp ``length``: sqrt(x*x + y*y), zero gradient at the zero vector."""
+    d2 = x * x + y * y
+    pos = d2 > 0
+    return torch.where(pos, torch.sqrt(torch.where(pos, d2, torch.ones_like(d2))), d2 * 0)
+
+
+def _zeros_like(x):
+    return torch.zeros_like(x)
+
+
+# ----------------------------------------------------------------------- world spec
+
+
+@dataclass
+class RefObstacles:
+    """Per-env obstacle state (``[E,N]``) and per-shape constants (``[N]``)."""
+
+    pos: torch.Tensor  # [E,N,2]
+    angle: torch.Tensor  # [E,N]
+    vel: torch.Tensor  # [E,N,2]
+    ang_vel: torch.Tensor  # [E,N]
+    radius: torch.Tensor  # [N]
+    half: torch.Tensor  # [N,2]
+    shape: list  # [N] ints
+    kind: list = field(default_factory=list)  # [N] ints (0 immovable, 1 movable)
+    mass: torch.Tensor | None = None  # [N]
+    inertia: torch.Tensor | None = None  # [N]
+    body: list = field(default_factory=list)  # [N] root index per shape
+    body_off: torch.Tensor | None = None  # [N,2]
+    # body state per root index [E,N,...] (only movable roots are meaningful)
+    body_pos: torch.Tensor | None = None
+    body_angle: torch.Tensor | None = None
+    body_vel: torch.Tensor | None = None
+    body_ang_vel: torch.Tensor | None = None
+
+    @property
+    def n(self) -> int:
+        return self.pos.shape[1]
+
+    def any_movable(self) -> bool:
+        return any(int(k) == 1 for k in self.kind)
+
+
+@dataclass
+class RefWorld:
+    params: torch.Tensor  # [A,22] or [E,A,22]
+    model_tag: list
+    ctrl_mode: list
+    dt: float
+    substeps: int = 1
+    collisions: bool = True
+    k: float = 100.0
+    c: float = 1.0
+    margin: float = 0.02
+    max_overlap: float = 0.0
+    neighbor_radius: float = 0.0
+    max_neighbors: int = 32
+    bounds: tuple | None = None
+    soft_walls: bool = False
+    clamp_bounds: bool = False
+    lin_damping: float = 10.0
+    ang_damping: float = 10.0
+    bodies_move: bool = True
+
+    def col(self, j):
+        """Parameter column ``j`` broadcastable to ``[E, A]``."""
+        p = self.params
+        return p[..., j] if p.dim() == 3 else p[:, j].unsqueeze(0)
+
+
+# ------------------------------------------------------------------- contact law
+
+
+def normal_coeff(ov, vn, k, c, denom, max_overlap):
+    """``swarp/core/collisions.py:87-106``: implicit damping, clamped repulsive."""
+    ovs = max_overlap * torch.tanh(ov / max_overlap) if max_overlap > 0.0 else ov
+    x = (k * ovs - c * vn) / denom
+    return wmax(x, torch.zeros_like(x))
+
+
+def pair_force(dx, dy, rvx, rvy, min_dist, k, c, denom, max_overlap):
+    """``swarp/core/collisions.py:109-143``: force on self from a disc at -d."""
+    d2 = dx * dx + dy * dy
+    dist = torch.sqrt(wmax(d2, torch.full_like(d2, EPS2)))
+    ov = min_dist - dist
+    active = ov > 0
+    nx = dx / dist
+    ny = dy / dist
+    vn = rvx * nx + rvy * ny
+    cf = normal_coeff(ov, vn, k, c, denom, max_overlap)
+    z = torch.zeros_like(d2)
+    return torch.where(active, cf * nx, z), torch.where(active, cf * ny, z)
+
+
+def closest_on_segment(px, py, cx, cy, angle, half_len):
+    """``swarp/core/collisions.py:156-171``."""
+    ux, uy = torch.cos(angle), torch.sin(angle)
+    t = wclamp((px - cx) * ux + (py - cy) * uy, -half_len, half_len)
+    return cx + t * ux, cy + t * uy
+
+
+def box_force(px, py, vx, vy, cx, cy, angle, hx, hy, reach, k, c, denom, max_overlap, vox, voy, om):
+    """``swarp/core/collisions.py:174-260``: oriented-box SDF contact."""
+    ca, sa = torch.cos(angle), torch.sin(angle)
+    dx, dy = px - cx, py - cy
+    lx = ca * dx + sa * dy
+    ly = -sa * dx + ca * dy
+    qx = wabs(lx) - hx
+    qy = wabs(ly) - hy
+    clx = wclamp(lx, -hx, hx)
+    cly = wclamp(ly, -hy, hy)
+    ox, oy = lx - clx, ly - cly
+    od2 = ox * ox + oy * oy
+    ext = od2 > EPS2
+    one = torch.ones_like(od2)
+    s_e = torch.sqrt(torch.where(ext, od2, one))
+    nlx_e, nly_e = ox / s_e, oy / s_e
+    use_x = qx > qy
+    sgx = torch.where(lx >= 0, one, -one)
+    sgy = torch.where(ly >= 0, one, -one)
+    zero = torch.zeros_like(od2)
+    s_i = torch.where(use_x, qx, qy)
+    nlx_i = torch.where(use_x, sgx, zero)
+    nly_i = torch.where(use_x, zero, sgy)
+    s = torch.where(ext, s_e, s_i)
+    nlx = torch.where(ext, nlx_e, nlx_i)
+    nly = torch.where(ext, nly_e, nly_i)
+    overlap = reach - s
+    active = overlap > 0
+    nx = ca * nlx - sa * nly
+    ny = sa * nlx + ca * nly
+    spx = lx - s * nlx
+    spy = ly - s * nly
+    rx = ca * spx - sa * spy
+    ry = sa * spx + ca * spy
+    vsx = vox + (-om * ry)
+    vsy = voy + om * rx
+    relx, rely = vx - vsx, vy - vsy
+    vn = relx * nx + rely * ny
+    cf = normal_coeff(overlap, vn, k, c, denom, max_overlap)
+    return torch.where(active, cf * nx, zero), torch.where(active, cf * ny, zero)
+
+
+def shape_bound(st: int, r, hx, hy):
+    if st == BOX:
+        return torch.sqrt(hx * hx + hy * hy)
+    if st == SEGMENT:
+        return hx + r
+    return r
+
+
+def bounds_apart(dx, dy, reach):
+    lim = reach * 1.0001 + 1.0e-6
+    return dx * dx + dy * dy > lim * lim
+
+
+def obstacle_forces(px, py, vx, vy, ra, obs: RefObstacles, w: RefWorld, denom):
+    """``swarp/core/collisions.py:690-742``: sum over obstacles in index order."""
+    fx = torch.zeros_like(px)
+    fy = torch.zeros_like(py)
+    if obs is None:
+        return fx, fy
+    k, c, margin, mo = w.k, w.c, w.margin, w.max_overlap
+    for o in range(obs.n):
+        st = int(obs.shape[o])
+        cx = obs.pos[:, o, 0].unsqueeze(1)
+        cy = obs.pos[:, o, 1].unsqueeze(1)
+        ang = obs.angle[:, o].unsqueeze(1)
+        r_o = obs.radius[o]
+        hx, hy = obs.half[o, 0], obs.half[o, 1]
+        apart = bounds_apart(px - cx, py - cy, ra + margin + shape_bound(st, r_o, hx, hy))
+        vox = obs.vel[:, o, 0].unsqueeze(1)
+        voy = obs.vel[:, o, 1].unsqueeze(1)
+        om = obs.ang_vel[:, o].unsqueeze(1)
+        if st == BOX:
+            gx, gy = box_force(px, py, vx, vy, cx, cy, ang, hx, hy, ra + margin, k, c, denom, mo,
+                               vox, voy, om)
+        elif st == SEGMENT:
+            qx, qy = closest_on_segment(px, py, cx, cy, ang, hx)
+            rx, ry = qx - cx, qy - cy
+            vsx = vox + (-om * ry)
+            vsy = voy + om * rx
+            gx, gy = pair_force(px - qx, py - qy, vx - vsx, vy - vsy, ra + r_o + margin, k, c,
+                                denom, mo)
+        else:
+            gx, gy = pair_force(px - cx, py - cy, vx - vox, vy - voy, ra + r_o + margin, k, c,
+                                denom, mo)
+        z = torch.zeros_like(gx)
+        fx = fx + torch.where(apart, z, gx)
+        fy = fy + torch.where(apart, z, gy)
+    return fx, fy
+
+
+def wall_forces(px, py, vx, vy, ra, w: RefWorld, denom):
+    """``swarp/core/collisions.py:745-780``: four soft walls, static closing velocity."""
+    x0, x1, y0, y1 = w.bounds
+    k, c, mo = w.k, w.c, w.max_overlap
+    reach = ra + w.margin
+    fx = torch.zeros_like(px)
+    fy = torch.zeros_like(py)
+    z = torch.zeros_like(px)
+    pen = reach - (px - x0)
+    fx = fx + torch.where(pen > 0, normal_coeff(pen, vx, k, c, denom, mo), z)
+    pen = reach - (x1 - px)
+    fx = fx + torch.where(pen > 0, -normal_coeff(pen, -vx, k, c, denom, mo), z)
+    pen = reach - (py - y0)
+    fy = fy + torch.where(pen > 0, normal_coeff(pen, vy, k, c, denom, mo), z)
+    pen = reach - (y1 - py)
+    fy = fy + torch.where(pen > 0, -normal_coeff(pen, -vy, k, c, denom, mo), z)
+    return fx, fy
+
+
+# ------------------------------------------------------------------ neighbor lists
+
+
+@torch.no_grad()
+def brute_neighbors(pos, radius: float, max_neighbors: int):
+    """``swarp/core/neighbors.py:76-97``: ascending-index within-radius lists.
+
+    Returns ``(in_list [E,A,A] bool, idx [E,A,K] int64 padded with -1, count [E,A],
+    true_count [E,A])``. ``in_list[e,a,b]`` is True iff b is among the first
+    ``max_neighbors`` agents (by index) within ``radius`` of a.
+    """
+    E, A, _ = pos.shape
+    dxy = pos.unsqueeze(1) - pos.unsqueeze(2)  # [E, a, b, 2] = p_b - p_a
+    dist = wlength(dxy[..., 0], dxy[..., 1])
+    eye = torch.eye(A, dtype=torch.bool, device=pos.device).unsqueeze(0)
+    inr = (dist <= radius) & ~eye
+    before = torch.cumsum(inr.to(torch.int64), dim=-1) - inr.to(torch.int64)
+    in_list = inr & (before < max_neighbors)
+    true_count = inr.sum(-1)
+    count = in_list.sum(-1)
+    K = max_neighbors
+    idx = torch.full((E, A, K), -1, dtype=torch.int64, device=pos.device)
+    order = torch.where(in_list, before, torch.full_like(before, K))
+    ar = torch.arange(A, device=pos.device).expand(E, A, A)
+    sel = order < K
+    idx[sel.nonzero(as_tuple=True)[0], sel.nonzero(as_tuple=True)[1], order[sel]] = ar[sel]
+    return in_list, idx, count, true_count
+
+
+def collision_forces(state, w: RefWorld, obs: RefObstacles | None):
+    """``swarp/core/collisions.py:818-881``: neighbor gather in list order + static."""
+    pos, _, vel, _, _ = state
+    px, py = pos[..., 0], pos[..., 1]
+    vx, vy = vel[..., 0], vel[..., 1]
+    E, A = px.shape
+    ra = w.col(P_RADIUS).expand(E, A)
+    denom = 1.0 + w.c * (w.dt / w.substeps) / w.col(P_MASS).expand(E, A)
+    fx = torch.zeros_like(px)
+    fy = torch.zeros_like(py)
+    true_count = torch.zeros(E, A, dtype=torch.int64, device=px.device)
+    if w.collisions:
+        in_list, _, _, true_count = brute_neighbors(pos.detach(), w.neighbor_radius,
+                                                    w.max_neighbors)
+        for b in range(A):
+            sel = in_list[:, :, b]
+            if not bool(sel.any()):
+                continue
+            gx, gy = pair_force(
+                px - px[:, b : b + 1], py - py[:, b : b + 1],
+                vx - vx[:, b : b + 1], vy - vy[:, b : b + 1],
+                ra + ra[:, b : b + 1] + w.margin, w.k, w.c, denom, w.max_overlap,
+            )
+            z = torch.zeros_like(gx)
+            fx = fx + torch.where(sel, gx, z)
+            fy = fy + torch.where(sel, gy, z)
+    sx, sy = obstacle_forces(px, py, vx, vy, ra, obs, w, denom)
+    if w.soft_walls:
+        wx, wy = wall_forces(px, py, vx, vy, ra, w, denom)
+        sx, sy = sx + wx, sy + wy
+    return fx + sx, fy + sy, true_count
+
+
+# ------------------------------------------------------------------------ dynamics
+
+
+def clamp_norm(x, y, limit):
+    """``swarp/dynamics/kernels.py:68-71``: ``v * (limit / max(|v|, limit))``."""
+    n = wlength(x, y)
+    s = limit / wmax(n, limit * torch.ones_like(n))
+    return x * s, y * s
+
+
+def integrate(state, act, fx, fy, w: RefWorld):
+    """``swarp/dynamics/kernels.py:166-275,395-403`` for one substep, per agent model."""
+    pos, th, vel, s, om = state
+    E, A = th.shape
+    dt = w.dt / w.substeps
+    a0, a1 = act[..., 0], act[..., 1]
+    col = lambda j: w.col(j).expand(E, A)  # noqa: E731
+    max_speed, min_speed = col(P_MAX_SPEED), col(P_MIN_SPEED)
+    max_accel, max_ang_vel, max_ang_acc = col(P_MAX_ACCEL), col(P_MAX_ANG_VEL), col(P_MAX_ANG_ACCEL)
+    l_f, l_r, max_steer, mass = col(P_LF), col(P_LR), col(P_MAX_STEER), col(P_MASS)
+    px, py = pos[..., 0], pos[..., 1]
+    vx, vy = vel[..., 0], vel[..., 1]
+    tag = torch.tensor(w.model_tag, device=th.device).unsqueeze(0).expand(E, A)
+    mode = torch.tensor(w.ctrl_mode, device=th.device).unsqueeze(0).expand(E, A)
+
+    # SERVO -> the VELOCITY command it amounts to (kernels.py:166-190, 856-871)
+    servo = mode == SERVO
+    if bool(servo.any()):
+        tv = wclamp(a0, -max_speed, max_speed) * col(P_CMD_GAIN_V)
+        tw = wclamp(a1, -max_ang_vel, max_ang_vel) * col(P_CMD_GAIN_W)
+        dv, dw = max_accel * dt, max_ang_acc * dt
+        a0 = torch.where(servo, s + wclamp(tv - s, -dv, dv), a0)
+        a1 = torch.where(servo, om + wclamp(tw - om, -dw, dw), a1)
+        mode = torch.where(servo, torch.zeros_like(mode), mode)
+
+    k_dt = dt / mass
+    dvx, dvy = fx * k_dt, fy * k_dt
+    zero = torch.zeros_like(th)
+
+    # holonomic
+    cvx, cvy = clamp_norm(a0, a1, max_speed)
+    ax_, ay_ = clamp_norm(a0, a1, max_accel)
+    ux, uy = clamp_norm(vx + ax_ * dt, vy + ay_ * dt, max_speed)
+    hvx = torch.where(mode == VELOCITY, cvx, ux) + dvx
+    hvy = torch.where(mode == VELOCITY, cvy, uy) + dvy
+    h = (px + hvx * dt, py + hvy * dt, th, hvx, hvy, wlength(hvx, hvy), zero)
+
+    # diff drive
+    s_vel = wclamp(a0, -max_speed, max_speed)
+    w_vel = wclamp(a1, -max_ang_vel, max_ang_vel)
+    s_acc = wclamp(s + wclamp(a0, -max_accel, max_accel) * dt, -max_speed, max_speed)
+    w_acc = wclamp(om + wclamp(a1, -max_ang_acc, max_ang_acc) * dt, -max_ang_vel, max_ang_vel)
+    s_dd = torch.where(mode == VELOCITY, s_vel, s_acc)
+    w_dd = torch.where(mode == VELOCITY, w_vel, w_acc)
+    dvtx = s_dd * torch.cos(th) + dvx
+    dvty = s_dd * torch.sin(th) + dvy
+    d = (px + dvtx * dt, py + dvty * dt, th + w_dd * dt, dvtx, dvty, s_dd, w_dd)
+
+    # kinematic bicycle (Polack et al. 2017, eq. 2)
+    acc = wclamp(a0, -max_accel, max_accel)
+    delta = wclamp(a1, -max_steer, max_steer)
+    s_b = wclamp(s + acc * dt, min_speed, max_speed)
+    wb = l_f + l_r
+    beta = torch.atan(torch.tan(delta) * l_r / wb)
+    bvx = s_b * torch.cos(th + beta) + dvx
+    bvy = s_b * torch.sin(th + beta) + dvy
+    w_b = s_b / wb * torch.cos(beta) * torch.tan(delta)
+    b = (px + bvx * dt, py + bvy * dt, th + w_b * dt, bvx, bvy, s_b, w_b)
+
+    hold = (px, py, th, vx, vy, s, om)
+    out = []
+    for i in range(7):
+        v = torch.where(tag == HOLONOMIC, h[i],
+                        torch.where(tag == DIFF_DRIVE, d[i],
+                                    torch.where(tag == BICYCLE, b[i], hold[i])))
+        out.append(v)
+    npx, npy, nth, nvx, nvy, ns, nw = out
+    if w.clamp_bounds:
+        x0, x1, y0, y1 = w.bounds
+        r = col(P_RADIUS)
+        npx = wclamp(npx, x0 + r, x1 - r)
+        npy = wclamp(npy, y0 + r, y1 - r)
+    return (torch.stack([npx, npy], -1), nth, torch.stack([nvx, nvy], -1), ns, nw)
+
+
+# -------------------------------------------------------------------------- bodies
+
+
+def _reaction(px, py, vx, vy, ra, am, cx, cy, ang, st, r_o, hx, hy, vox, voy, om, w: RefWorld):
+    """``swarp/core/bodies.py:79-127``: force on the body from one agent, and its lever."""
+    denom = 1.0 + w.c * (w.dt / w.substeps) / am
+    k, c, margin, mo = w.k, w.c, w.margin, w.max_overlap
+    z = torch.zeros_like(px)
+    if st == BOX:
+        fx, fy = box_force(px, py, vx, vy, cx, cy, ang, hx, hy, ra + margin, k, c, denom, mo,
+                           vox, voy, om)
+        rx, ry = px - cx, py - cy
+    elif st == SEGMENT:
+        qx, qy = closest_on_segment(px, py, cx, cy, ang, hx)
+        rrx, rry = qx - cx, qy - cy
+        vsx = vox + (-om * rry)
+        vsy = voy + om * rrx
+        fx, fy = pair_force(px - qx, py - qy, vx - vsx, vy - vsy, ra + r_o + margin, k, c, denom,
+                            mo)
+        rx, ry = rrx, rry
+    else:
+        fx, fy = pair_force(px - cx, py - cy, vx - vox, vy - voy, ra + r_o + margin, k, c, denom,
+                            mo)
+        rx, ry = z, z
+    return -fx, -fy, rx, ry
+
+
+def _closest_in_box(dx, dy, ang, hx, hy):
+    ca, sa = torch.cos(ang), torch.sin(ang)
+    lx = ca * dx + sa * dy
+    ly = -sa * dx + ca * dy
+    cx = wclamp(lx, -hx, hx)
+    cy = wclamp(ly, -hy, hy)
+    return ca * cx - sa * cy, sa * cx + ca * cy
+
+
+def _body_body(qx, qy, tvx, tvy, th, om_s, st, r_s, hxs, hys,
+               q2x, q2y, tv2x, tv2y, th2, om2, st2, r2, hx2, hy2, w: RefWorld, denom):
+    """``swarp/core/bodies.py:167-255``: contact on shape ``self`` from another shape."""
+    k, c, margin, mo = w.k, w.c, w.margin, w.max_overlap
+    z = torch.zeros_like(qx)
+    if st == BOX:
+        if st2 == BOX:
+            return z, z, z, z
+        c2x, c2y, v2x, v2y = q2x, q2y, tv2x, tv2y
+        if st2 == SEGMENT:
+            c2x, c2y = closest_on_segment(qx, qy, q2x, q2y, th2, hx2)
+            rrx, rry = c2x - q2x, c2y - q2y
+            v2x = tv2x + (-om2 * rry)
+            v2y = tv2y + om2 * rrx
+        fox, foy = box_force(c2x, c2y, v2x, v2y, qx, qy, th, hxs, hys, r2 + margin, k, c, denom, mo,
+                             tvx, tvy, om_s)
+        rx, ry = _closest_in_box(c2x - qx, c2y - qy, th, hxs, hys)
+        return -fox, -foy, rx, ry
+    if st2 == BOX:
+        fx, fy = box_force(qx, qy, tvx, tvy, q2x, q2y, th2, hx2, hy2, r_s + margin, k, c, denom, mo,
+                           tv2x, tv2y, om2)
+        return fx, fy, z, z
+    if st2 == SEGMENT:
+        cpx, cpy = closest_on_segment(qx, qy, q2x, q2y, th2, hx2)
+        rrx, rry = cpx - q2x, cpy - q2y
+        vs2x = tv2x + (-om2 * rry)
+        vs2y = tv2y + om2 * rrx
+        fx, fy = pair_force(qx - cpx, qy - cpy, tvx - vs2x, tvy - vs2y, r_s + r2 + margin, k, c,
+                            denom, mo)
+        return fx, fy, z, z
+    fx, fy = pair_force(qx - q2x, qy - q2y, tvx - tv2x, tvy - tv2y, r_s + r2 + margin, k, c, denom,
+                        mo)
+    return fx, fy, z, z
+
+
+def body_pass(state, obs: RefObstacles, w: RefWorld):
+    """``swarp/core/bodies.py:367-569``: one substep of every movable body root.
+
+    Every body reads the other shapes' pre-pass poses (the reference kernel reads
+    ``obs_pos`` of other bodies while their own threads rewrite it; with one movable
+    body, as in every configuration here, the two readings coincide).
+    Returns a new :class:`RefObstacles`.
+    """
+    pos, _, vel, _, _ = state
+    px, py = pos[..., 0], pos[..., 1]
+    vx, vy = vel[..., 0], vel[..., 1]
+    E, A = px.shape
+    dt = w.dt / w.substeps
+    ra_all = w.col(P_RADIUS).expand(E, A)
+    am_all = w.col(P_MASS).expand(E, A)
+    N = obs.n
+    new = {
+        "pos": [obs.pos[:, s] for s in range(N)],
+        "angle": [obs.angle[:, s] for s in range(N)],
+        "vel": [obs.vel[:, s] for s in range(N)],
+        "ang_vel": [obs.ang_vel[:, s] for s in range(N)],
+        "bpos": [obs.body_pos[:, s] for s in range(N)],
+        "bang": [obs.body_angle[:, s] for s in range(N)],
+        "bvel": [obs.body_vel[:, s] for s in range(N)],
+        "bom": [obs.body_ang_vel[:, s] for s in range(N)],
+    }
+    for o in range(N):
+        if int(obs.body[o]) != o or int(obs.kind[o]) != 1:
+            continue
+        qx, qy = obs.body_pos[:, o, 0], obs.body_pos[:, o, 1]
+        tvx, tvy = obs.body_vel[:, o, 0], obs.body_vel[:, o, 1]
+        th = obs.body_angle[:, o]
+        om = obs.body_ang_vel[:, o]
+        ca, sa = torch.cos(th), torch.sin(th)
+        fx = torch.zeros_like(qx)
+        fy = torch.zeros_like(qx)
+        tau = torch.zeros_like(qx)
+        denom_self = 1.0 + w.c * dt / obs.mass[o]
+        ext = torch.zeros_like(qx)
+        for s_ in range(N):
+            if int(obs.body[s_]) != o:
+                continue
+            offx, offy = obs.body_off[s_, 0], obs.body_off[s_, 1]
+            owx = ca * offx - sa * offy
+            owy = sa * offx + ca * offy
+            csx, csy = qx + owx, qy + owy
+            vsx, vsy = tvx - om * owy, tvy + om * owx
+            st = int(obs.shape[s_])
+            r_o = obs.radius[s_]
+            hx, hy = obs.half[s_, 0], obs.half[s_, 1]
+            ax, ay = wabs(offx), wabs(offy)
+            if st == BOX:
+                reach = torch.sqrt((ax + hx) * (ax + hx) + (ay + hy) * (ay + hy))
+            elif st == SEGMENT:
+                reach = torch.sqrt((ax + hx) * (ax + hx) + ay * ay) + r_o
+            else:
+                reach = torch.sqrt(ax * ax + ay * ay) + r_o
+            ext = wmax(ext, reach * torch.ones_like(ext))
+            bound = shape_bound(st, r_o, hx, hy)
+            for a in range(A):
+                pax, pay = px[:, a], py[:, a]
+                ra = ra_all[:, a]
+                apart = bounds_apart(pax - csx, pay - csy, ra + bound + w.margin)
+                rfx, rfy, rx, ry = _reaction(pax, pay, vx[:, a], vy[:, a], ra, am_all[:, a],
+                                             csx, csy, th, st, r_o, hx, hy, vsx, vsy, om, w)
+                lx, ly = owx + rx, owy + ry
+                z = torch.zeros_like(fx)
+                fx = fx + torch.where(apart, z, rfx)
+                fy = fy + torch.where(apart, z, rfy)
+                tau = tau + torch.where(apart, z, lx * rfy - ly * rfx)
+            for o2 in range(N):
+                if int(obs.body[o2]) == o:
+                    continue
+                st2 = int(obs.shape[o2])
+                q2x, q2y = obs.pos[:, o2, 0], obs.pos[:, o2, 1]
+                apart = bounds_apart(
+                    q2x - csx, q2y - csy,
+                    bound + shape_bound(st2, obs.radius[o2], obs.half[o2, 0], obs.half[o2, 1])
+                    + w.margin,
+                )
+                f2x, f2y, r2x, r2y = _body_body(
+                    csx, csy, vsx, vsy, th, om, st, r_o, hx, hy,
+                    q2x, q2y, obs.vel[:, o2, 0], obs.vel[:, o2, 1], obs.angle[:, o2],
+                    obs.ang_vel[:, o2], st2, obs.radius[o2], obs.half[o2, 0], obs.half[o2, 1],
+                    w, denom_self,
+                )
+                lx, ly = owx + r2x, owy + r2y
+                z = torch.zeros_like(fx)
+                fx = fx + torch.where(apart, z, f2x)
+                fy = fy + torch.where(apart, z, f2y)
+                tau = tau + torch.where(apart, z, lx * f2y - ly * f2x)
+        lin_decay = 1.0 - w.lin_damping * dt
+        ang_decay = 1.0 - w.ang_damping * dt
+        nvx = (tvx + fx / obs.mass[o] * dt) * lin_decay
+        nvy = (tvy + fy / obs.mass[o] * dt) * lin_decay
+        nom = (om + tau / obs.inertia[o] * dt) * ang_decay
+        nx = qx + nvx * dt
+        ny = qy + nvy * dt
+        if w.bounds is not None:
+            x0, x1, y0, y1 = w.bounds
+            lo_x = wmin(x0 + ext, torch.full_like(ext, (x0 + x1) * 0.5))
+            hi_x = wmax(x1 - ext, lo_x)
+            lo_y = wmin(y0 + ext, torch.full_like(ext, (y0 + y1) * 0.5))
+            hi_y = wmax(y1 - ext, lo_y)
+            cx_ = wclamp(nx, lo_x, hi_x)
+            cy_ = wclamp(ny, lo_y, hi_y)
+            nvx = torch.where(cx_ != nx, torch.zeros_like(nvx), nvx)
+            nvy = torch.where(cy_ != ny, torch.zeros_like(nvy), nvy)
+            nx, ny = cx_, cy_
+        nth = th + nom * dt
+        new["bvel"][o] = torch.stack([nvx, nvy], -1)
+        new["bom"][o] = nom
+        new["bpos"][o] = torch.stack([nx, ny], -1)
+        new["bang"][o] = nth
+        nca, nsa = torch.cos(nth), torch.sin(nth)
+        for s_ in range(N):
+            if int(obs.body[s_]) != o:
+                continue
+            offx, offy = obs.body_off[s_, 0], obs.body_off[s_, 1]
+            owx = nca * offx - nsa * offy
+            owy = nsa * offx + nca * offy
+            new["pos"][s_] = torch.stack([nx + owx, ny + owy], -1)
+            new["angle"][s_] = nth
+            new["vel"][s_] = torch.stack([nvx - nom * owy, nvy + nom * owx], -1)
+            new["ang_vel"][s_] = nom
+    st = lambda key: torch.stack(new[key], 1)  # noqa: E731
+    return RefObstacles(
+        pos=st("pos"), angle=st("angle"), vel=st("vel"), ang_vel=st("ang_vel"),
+        radius=obs.radius, half=obs.half, shape=obs.shape, kind=obs.kind, mass=obs.mass,
+        inertia=obs.inertia, body=obs.body, body_off=obs.body_off,
+        body_pos=st("bpos"), body_angle=st("bang"), body_vel=st("bvel"), body_ang_vel=st("bom"),
+    )
+
+
+def seed_bodies(obs: RefObstacles) -> RefObstacles:
+    """Body state derived from the root shapes' world poses (``stepper.py`` ``_body_seed``)."""
+    root = torch.tensor([int(b) for b in obs.body], device=obs.pos.device)
+    r_ang = obs.angle[:, root]
+    r_off = obs.body_off[root]
+    ca, sa = torch.cos(r_ang), torch.sin(r_ang)
+    wx = ca * r_off[:, 0] - sa * r_off[:, 1]
+    wy = sa * r_off[:, 0] + ca * r_off[:, 1]
+    obs.body_pos = obs.pos[:, root] - torch.stack([wx, wy], -1)
+    obs.body_angle = r_ang
+    obs.body_vel = obs.vel[:, root]
+    obs.body_ang_vel = obs.ang_vel[:, root]
+    return obs
+
+
+# ---------------------------------------------------------------------------- step
+
+
+def step(state, act, w: RefWorld, obs: RefObstacles | None = None):
+    """One env step (all substeps). Returns ``(state, obs, max_true_count)``."""
+    tmax = None
+    for _ in range(w.substeps):
+        fx, fy, tc = collision_forces(state, w, obs)
+        tmax = tc if tmax is None else torch.maximum(tmax, tc)
+        if obs is not None and w.bodies_move and obs.any_movable():
+            obs_next = body_pass(state, obs, w)
+        else:
+            obs_next = obs
+        state = integrate(state, act, fx, fy, w)
+        obs = obs_next
+    return state, obs, tmax
+
+
+def rollout(state, actions_seq, w: RefWorld, obs: RefObstacles | None = None):
+    """``swarp/interop/autograd.py:341-369`` restated: T steps, returns final + trajectory."""
+    traj = []
+    body_traj = []
+    for t in range(actions_seq.shape[0]):
+        state, obs, _ = step(state, actions_seq[t], w, obs)
+        traj.append(state)
+        body_traj.append(obs)
+    return state, traj, body_traj

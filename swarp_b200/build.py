@@ -1,0 +1,58 @@
+"""Build the sm_100a shared library ``swarp_b200/libswarp_b200.so`` in-tree with nvcc.
+
+``python -m swarp_b200.build`` (or ``__graft_entry__.build()``). Rebuilds only when a
+source is newer than the library. The library is a plain C ABI (include/swarp_b200.h)
+linked against the CUDA runtime; Python loads it with ctypes.
+"""
+
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+CSRC = os.path.join(HERE, "csrc")
+LIB = os.path.join(HERE, "libswarp_b200.so")
+SOURCES = ["capi.cu"]
+DEPS = ["capi.cu", "rollout.cuh", "physics.cuh"]
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+FLAGS = [
+    "-O3", "-lineinfo", "-std=c++17", "--extended-lambda", "-fmad=false",
+    "-Xcompiler", "-fPIC", "-Xcompiler", "-O2", "--shared", "-cudart", "shared",
+]
+
+
+def nvcc() -> str:
+    cand = os.environ.get("NVCC") or shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not os.path.exists(cand):
+        raise RuntimeError("nvcc not found: the CUDA toolkit is required to build swarp_b200")
+    return cand
+
+
+def _stale(lib: str, deps: list[str]) -> bool:
+    if not os.path.exists(lib):
+        return True
+    t = os.path.getmtime(lib)
+    hdr = os.path.join(ROOT, "include", "swarp_b200.h")
+    return any(os.path.getmtime(p) > t for p in [*deps, hdr])
+
+
+def build(force: bool = False, verbose: bool = False, extra: list[str] | None = None) -> str:
+    deps = [os.path.join(CSRC, d) for d in DEPS]
+    if not force and not _stale(LIB, deps):
+        return LIB
+    cmd = [nvcc(), *ARCH, *FLAGS, *(extra or []), "-o", LIB + ".tmp",
+           *[os.path.join(CSRC, s) for s in SOURCES]]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    os.replace(LIB + ".tmp", LIB)
+    return LIB
+
+
+if __name__ == "__main__":
+    print(build(force="--force" in sys.argv, verbose=True,
+                extra=["-Xptxas", "-v"] if "--ptxas-v" in sys.argv else None))

@@ -1,0 +1,313 @@
+"""Stepper: owns the agent parameters, the obstacle set and the substep pipeline.
+
+Drop-in for ``swarp.core.stepper.Stepper`` (reference ``swarp/core/stepper.py:66-240``,
+``set_obstacles`` ``:295-344``, ``set_agent_params_per_env`` ``:362-452``): same
+constructor arguments and validation. Instead of launching Warp kernels per substep it
+describes the world once (``swarp_world_t``) and runs whole rollouts through the C ABI
+of ``libswarp_b200.so``: one kernel for the forward horizon, one for its adjoint.
+
+``dtype`` accepts a torch dtype (``torch.float32``/``torch.float64``) or its name; the
+reference's Warp dtype argument has no meaning without Warp.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import torch
+
+from swarp_b200 import _lib
+from swarp_b200.core.config import Obstacles, WorldConfig
+from swarp_b200.dynamics.base import (
+    NUM_PARAMS,
+    P_RADIUS,
+    P_SHAPE,
+    AgentConfig,
+    AgentShape,
+    DynamicsModel,
+    Integrator,
+    param_rows,
+)
+
+_DTYPES = {
+    torch.float32: torch.float32, torch.float64: torch.float64,
+    "float32": torch.float32, "float64": torch.float64,
+    "f32": torch.float32, "f64": torch.float64,
+}
+
+
+def _as_torch_dtype(dtype) -> torch.dtype:
+    if dtype in _DTYPES:
+        return _DTYPES[dtype]
+    name = getattr(dtype, "__name__", str(dtype)).lower()
+    for key in ("float64", "float32"):
+        if key in name:
+            return _DTYPES[key]
+    raise TypeError(f"unsupported dtype {dtype!r}; use torch.float32 or torch.float64")
+
+
+class Stepper:
+    """Owns per-agent parameters, interaction config and the rollout launches."""
+
+    def __init__(
+        self,
+        configs: list[AgentConfig],
+        dt: float = 0.1,
+        substeps: int = 1,
+        device: str = "cuda:0",
+        dtype=torch.float32,
+        world: WorldConfig | None = None,
+    ) -> None:
+        # A bare Stepper is collision-free unless a config asks (reference stepper.py:97-101).
+        world = world if world is not None else WorldConfig(collisions=False)
+        if substeps < 1:
+            raise ValueError("substeps must be >= 1")
+        if not configs:
+            raise ValueError("a Stepper needs at least one agent")
+        self.configs = list(configs)
+        self.n_agents = len(configs)
+        self.dt = float(dt)
+        self.substeps = int(substeps)
+        self.sub_dt = self.dt / self.substeps
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise RuntimeError(
+                f"swarp_b200 steps only on CUDA devices (got {device!r}); there is no CPU path"
+            )
+        self.dtype = _as_torch_dtype(dtype)
+        self.torch_dtype = self.dtype
+        self.world = world
+        if self.n_agents > _lib.MAX_AGENTS:
+            raise ValueError(f"{self.n_agents} agents per env exceed the {_lib.MAX_AGENTS} this "
+                             "build runs in one CTA")
+        for c in self.configs:
+            if c.model == DynamicsModel.DRONE:
+                raise NotImplementedError("the 6-DOF drone model is not on the CUDA path yet")
+            if c.shape == AgentShape.BOX:
+                raise NotImplementedError("box agents (OBB contacts) are not on the CUDA path yet")
+        if world.integrator != Integrator.EULER:
+            raise NotImplementedError("only the semi-implicit Euler integrator runs on the CUDA path")
+        if world.wheel_contacts:
+            raise NotImplementedError("wheel contacts are not on the CUDA path")
+        self.params = torch.tensor(param_rows(self.configs), dtype=self.dtype, device=self.device)
+        self.params_per_env: torch.Tensor | None = None
+        self.model_tag = torch.tensor([int(c.model) for c in self.configs], dtype=torch.int32,
+                                      device=self.device)
+        self.ctrl_mode = torch.tensor([int(c.ctrl_mode) for c in self.configs],
+                                      dtype=torch.int32, device=self.device)
+        self.fleet_models = 0
+        self.fleet_modes = 0
+        for c in self.configs:
+            self.fleet_models |= 1 << int(c.model)
+            self.fleet_modes |= 1 << int(c.ctrl_mode)
+
+        self.collisions = bool(world.collisions)
+        self.max_agent_radius = max(c.radius for c in self.configs)
+        self.neighbor_radius = 0.0
+        if self.collisions:
+            reach = 2.0 * self.max_agent_radius + world.collision_margin
+            self.neighbor_radius = world.neighbor_radius or reach
+            if self.neighbor_radius < reach:
+                raise ValueError(
+                    f"neighbor_radius={self.neighbor_radius} is smaller than the collision "
+                    f"reach {reach} (= 2 * max radius + margin); collisions would be missed."
+                )
+        self._soft_walls = world.bounds is not None and world.bounds_mode == "soft"
+        self._clamp = world.bounds is not None and world.bounds_mode == "clamp"
+        self.n_obstacles = 0
+        self.obstacles: Obstacles | None = None
+        self.any_movable = False
+        #: Movable bodies advance on grad (taped) steps too, so gradients flow through
+        #: them. False reproduces the reference's taped-step rule (bodies frozen,
+        #: swarp/core/stepper.py:593-601).
+        self.bodies_in_grad = True
+        self.body_state: tuple[torch.Tensor, ...] | None = None
+
+    # ----------------------------------------------------------------- set-up
+    def set_obstacles(self, obstacles: Obstacles) -> None:
+        """Install (or refresh) an obstacle set; absent fields take their defaults."""
+        obs = obstacles.resolve(self.device, self.dtype)
+        self.obstacles = obs
+        self.n_obstacles = obs.n_obstacles
+        self.any_movable = bool((obs.kind != 0).any().item())
+        if self.any_movable:
+            self.body_state = self._body_seed(obs)
+        else:
+            self.body_state = None
+
+    def _body_seed(self, obs: Obstacles) -> tuple[torch.Tensor, ...]:
+        """Body state per shape slot derived from the root shapes' world poses."""
+        root = obs.body.long()
+        r_ang = obs.angle[:, root]
+        r_off = obs.body_offset[root]
+        ca, sa = torch.cos(r_ang), torch.sin(r_ang)
+        wx = ca * r_off[:, 0] - sa * r_off[:, 1]
+        wy = sa * r_off[:, 0] + ca * r_off[:, 1]
+        b_pos = (obs.pos[:, root] - torch.stack([wx, wy], dim=-1)).contiguous()
+        return (b_pos, r_ang.contiguous(), obs.vel[:, root].contiguous(),
+                obs.ang_vel[:, root].contiguous())
+
+    def set_agent_params_per_env(self, floats) -> None:
+        """Install a per-env ``[n_envs, n_agents, NUM_PARAMS]`` parameter override."""
+        t = torch.as_tensor(np.asarray(floats) if not torch.is_tensor(floats) else floats)
+        if t.dim() != 3 or tuple(t.shape[1:]) != (self.n_agents, NUM_PARAMS):
+            raise ValueError(
+                f"per-env params must have shape [n_envs, n_agents={self.n_agents}, "
+                f"NUM_PARAMS={NUM_PARAMS}]; got {tuple(t.shape)}"
+            )
+        shared = torch.tensor([float(c.shape) for c in self.configs], dtype=torch.float64)
+        if not torch.equal(t[..., P_SHAPE].detach().double().cpu(), shared.expand(t.shape[0], -1)):
+            raise ValueError("per-env params must not change the P_SHAPE column: an agent's "
+                             "AgentShape is structural and fixed by its AgentConfig.")
+        if self.collisions:
+            max_r = float(t[..., P_RADIUS].max())
+            reach = 2.0 * max_r + self.world.collision_margin
+            if self.neighbor_radius < reach:
+                raise ValueError(
+                    f"per-env radius up to {max_r} needs neighbor_radius >= {reach}, but "
+                    f"neighbor_radius={self.neighbor_radius}; set WorldConfig.neighbor_radius."
+                )
+        self.params_per_env = t.detach().to(device=self.device, dtype=self.dtype).contiguous()
+
+    # ------------------------------------------------------------- C world
+    def world_c(self, n_envs: int, act_dim: int) -> _lib.WorldC:
+        w = self.world
+        wc = _lib.WorldC()
+        wc.dtype = 0 if self.dtype == torch.float32 else 1
+        wc.n_envs = n_envs
+        wc.n_agents = self.n_agents
+        wc.act_dim = act_dim
+        wc.substeps = self.substeps
+        wc.dt = self.dt
+        wc.collisions = int(self.collisions)
+        wc.k = w.collision_k
+        wc.c = w.collision_c
+        wc.margin = w.collision_margin
+        wc.max_overlap = w.contact_max_overlap
+        wc.neighbor_radius = self.neighbor_radius
+        wc.max_neighbors = w.max_neighbors
+        wc.bounds_mode = 1 if self._soft_walls else (2 if self._clamp else 0)
+        b = w.bounds if w.bounds is not None else (0.0, 0.0, 0.0, 0.0)
+        wc.bounds = (C.c_double * 4)(*b)
+        wc.lin_damping = w.obstacle_linear_damping
+        wc.ang_damping = w.obstacle_angular_damping
+        if self.params_per_env is not None:
+            if self.params_per_env.shape[0] != n_envs:
+                raise ValueError(f"per-env params were installed for {self.params_per_env.shape[0]}"
+                                 f" envs, stepping {n_envs}")
+            wc.params = self.params_per_env.data_ptr()
+            wc.params_env_stride = self.n_agents * NUM_PARAMS
+        else:
+            wc.params = self.params.data_ptr()
+            wc.params_env_stride = 0
+        wc.model_tag = self.model_tag.data_ptr()
+        wc.ctrl_mode = self.ctrl_mode.data_ptr()
+        wc.fleet_models = self.fleet_models
+        wc.fleet_modes = self.fleet_modes
+        o = self.obstacles
+        if o is not None and self.n_obstacles > 0:
+            if o.n_envs != n_envs:
+                raise ValueError(f"obstacles were installed for {o.n_envs} envs, stepping {n_envs}")
+            oc = wc.obstacles
+            oc.n_obstacles = self.n_obstacles
+            oc.pos, oc.angle = o.pos.data_ptr(), o.angle.data_ptr()
+            oc.vel, oc.ang_vel = o.vel.data_ptr(), o.ang_vel.data_ptr()
+            oc.radius, oc.half = o.radius.data_ptr(), o.half_extents.data_ptr()
+            oc.shape, oc.kind = o.shape.data_ptr(), o.kind.data_ptr()
+            oc.mass, oc.inertia = o.mass.data_ptr(), o.inertia.data_ptr()
+            oc.body, oc.body_off = o.body.data_ptr(), o.body_offset.data_ptr()
+            oc.any_movable = int(self.any_movable)
+            oc.bodies_move = 1
+        return wc
+
+    # -------------------------------------------------------------- launches
+    def _check_inputs(self, state, actions: torch.Tensor, horizon_dim: bool):
+        exp = 4 if horizon_dim else 3
+        if actions.dim() != exp:
+            raise ValueError(f"actions must be {exp}-D, got shape {tuple(actions.shape)}")
+        if actions.dtype != self.dtype:
+            raise TypeError(f"actions dtype {actions.dtype} != stepper dtype {self.dtype}")
+        if actions.device != self.device:
+            raise ValueError(f"actions on {actions.device}, stepper on {self.device}")
+        E = actions.shape[-3]
+        if actions.shape[-2] != self.n_agents or actions.shape[-1] < 2:
+            raise ValueError(f"actions must be [..., n_envs, {self.n_agents}, act_dim>=2]; got "
+                             f"{tuple(actions.shape)}")
+        shapes = [(E, self.n_agents, 2), (E, self.n_agents), (E, self.n_agents, 2),
+                  (E, self.n_agents), (E, self.n_agents)]
+        for t, shp in zip(state, shapes, strict=True):
+            if tuple(t.shape) != shp:
+                raise ValueError(f"state field of shape {tuple(t.shape)}, expected {shp}")
+            if t.dtype != self.dtype or t.device != self.device:
+                raise TypeError(f"state field {t.dtype}/{t.device} != stepper "
+                                f"{self.dtype}/{self.device}")
+        return E
+
+    def workspace_bytes(self, n_envs: int, act_dim: int, horizon: int) -> int:
+        lib = _lib.load()
+        wc = self.world_c(n_envs, act_dim)
+        return int(lib.swarp_rollout_workspace_bytes(C.byref(wc), horizon))
+
+    def rollout_forward(self, state5, actions: torch.Tensor, *, final: bool = True,
+                        out=None, true_count: bool = False):
+        """Run the forward rollout kernel.
+
+        ``state5`` are the five contiguous initial-state tensors, ``actions`` is
+        ``[T, E, A, act_dim]``. Returns ``(traj5, final5 | None, true_max | None,
+        workspace)`` with ``traj5`` stacked ``[T, E, A(,2)]``.
+        """
+        lib = _lib.load()
+        H, E, _, D = actions.shape
+        wc = self.world_c(E, D)
+        opts = {"device": self.device, "dtype": self.dtype}
+        if out is None:
+            traj = (torch.empty(H, E, self.n_agents, 2, **opts), torch.empty(H, E, self.n_agents, **opts),
+                    torch.empty(H, E, self.n_agents, 2, **opts), torch.empty(H, E, self.n_agents, **opts),
+                    torch.empty(H, E, self.n_agents, **opts))
+        else:
+            traj = out
+        fin = tuple(torch.empty_like(t[0]) for t in traj) if final else None
+        tmax = (torch.empty(E, self.n_agents, dtype=torch.int32, device=self.device)
+                if true_count else None)
+        nbytes = int(lib.swarp_rollout_workspace_bytes(C.byref(wc), H))
+        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=self.device)
+        rc = lib.swarp_rollout_fwd(
+            C.byref(wc), H, _lib.state_c(state5), actions.data_ptr(), _lib.state_c(traj),
+            _lib.state_c(fin) if fin else _lib.State(), _lib.ptr(tmax), _lib.Bodies(),
+            _lib.Bodies(), ws.data_ptr(), nbytes, _lib.stream_ptr(self.device),
+        )
+        _lib.check(rc, "swarp_rollout_fwd")
+        return traj, fin, tmax, ws
+
+    def rollout_backward(self, state5, actions, traj5, gtraj5, gfin5, workspace):
+        lib = _lib.load()
+        H, E, _, D = actions.shape
+        wc = self.world_c(E, D)
+        g_act = torch.empty_like(actions)
+        g_init = tuple(torch.empty_like(t) for t in state5)
+        rc = lib.swarp_rollout_bwd(
+            C.byref(wc), H, _lib.state_c(state5), actions.data_ptr(), _lib.state_c(traj5),
+            _lib.state_c(gtraj5), _lib.state_c(gfin5), _lib.Bodies(), _lib.Bodies(), _lib.Bodies(),
+            g_act.data_ptr(), _lib.state_c(g_init), workspace.data_ptr(), workspace.numel(),
+            _lib.stream_ptr(self.device),
+        )
+        _lib.check(rc, "swarp_rollout_bwd")
+        return g_act, g_init
+
+    def neighbors(self, pos: torch.Tensor):
+        """Padded within-radius lists of ``pos [E, A, 2]``: ``(idx, count, true_count)``."""
+        if not self.collisions:
+            raise RuntimeError("neighbor lists require WorldConfig.collisions=True")
+        lib = _lib.load()
+        E = pos.shape[0]
+        wc = self.world_c(E, 2)
+        K = self.world.max_neighbors
+        idx = torch.zeros(E, self.n_agents, K, dtype=torch.int32, device=self.device)
+        cnt = torch.empty(E, self.n_agents, dtype=torch.int32, device=self.device)
+        tru = torch.empty_like(cnt)
+        pos = pos.detach().contiguous()
+        rc = lib.swarp_neighbors(C.byref(wc), pos.data_ptr(), idx.data_ptr(), cnt.data_ptr(),
+                                 tru.data_ptr(), _lib.stream_ptr(self.device))
+        _lib.check(rc, "swarp_neighbors")
+        return idx, cnt, tru

@@ -1,0 +1,334 @@
+// C ABI of the rollout kernels: argument validation, kernel-instance selection and
+// launch on the caller's stream. Declarations and contracts: include/swarp_b200.h.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <limits>
+
+#include "../../include/swarp_b200.h"
+#include "rollout.cuh"
+
+using namespace swarp;
+
+namespace {
+
+constexpr int kAbiVersion = 1;
+
+int threads_target() {
+  static int v = [] {
+    const char* s = std::getenv("SWARP_CTA_THREADS");
+    int t = s ? std::atoi(s) : 128;
+    return (t >= 32 && t <= 1024) ? t : 128;
+  }();
+  return v;
+}
+
+// Envs per CTA: whole envs, about threads_target() threads.
+int envs_per_cta(int A, int E) {
+  int G = A >= threads_target() ? 1 : threads_target() / A;
+  if (G > E) G = E;
+  return G < 1 ? 1 : G;
+}
+
+// Largest value x of type T with sqrt(x) <= R (both rounded in T): the exact set test
+// sqrt(d2) <= R of the reference, evaluated without a square root.
+template <typename T> T radius_sq_threshold(double Rd) {
+  const T R = static_cast<T>(Rd);
+  if (!(R > T(0))) return T(-1);
+  T x = R * R;
+  const T inf = std::numeric_limits<T>::infinity();
+  while (std::sqrt(std::nextafter(x, inf)) <= R) x = std::nextafter(x, inf);
+  while (std::sqrt(x) > R) x = std::nextafter(x, -inf);
+  return x;
+}
+
+int validate_world(const swarp_world_t* w, int horizon) {
+  if (!w || horizon < 1) return SWARP_ERR_INVALID_ARG;
+  if (w->dtype != SWARP_F32 && w->dtype != SWARP_F64) return SWARP_ERR_INVALID_ARG;
+  if (w->n_envs < 1 || w->n_agents < 1 || w->substeps < 1 || w->act_dim < 2) return SWARP_ERR_INVALID_ARG;
+  if (w->n_agents > SWARP_MAX_AGENTS) return SWARP_ERR_TOO_MANY_AGENTS;
+  if (!(w->dt > 0.0)) return SWARP_ERR_INVALID_ARG;
+  if (!w->params || !w->model_tag || !w->ctrl_mode) return SWARP_ERR_INVALID_ARG;
+  if (w->fleet_models & ~0x7) return SWARP_ERR_UNSUPPORTED;  // drone / unknown tags
+  if (w->fleet_models == 0 || w->fleet_modes == 0 || (w->fleet_modes & ~0x7)) return SWARP_ERR_INVALID_ARG;
+  if (w->bounds_mode < 0 || w->bounds_mode > 2) return SWARP_ERR_INVALID_ARG;
+  if (w->collisions) {
+    if (w->max_neighbors < 1 || !(w->neighbor_radius > 0.0)) return SWARP_ERR_INVALID_ARG;
+    if (w->n_agents > 32767) return SWARP_ERR_TOO_MANY_AGENTS;
+  }
+  const swarp_obstacles_t& o = w->obstacles;
+  if (o.n_obstacles < 0) return SWARP_ERR_INVALID_ARG;
+  if (o.n_obstacles > 0) {
+    if (!o.pos || !o.angle || !o.vel || !o.ang_vel || !o.radius || !o.half || !o.shape)
+      return SWARP_ERR_INVALID_ARG;
+    if (o.any_movable && o.bodies_move) return SWARP_ERR_UNSUPPORTED;
+  }
+  return SWARP_OK;
+}
+
+bool state_complete(const swarp_state_t& s) {
+  return s.pos && s.theta && s.vel && s.speed && s.ang_vel;
+}
+
+int flags_of(const swarp_world_t* w) {
+  int fl = 0;
+  if (w->collisions) {
+    fl |= F_COLL;
+    if (w->n_agents - 1 > w->max_neighbors) fl |= F_TRUNC;
+  }
+  if (w->obstacles.n_obstacles > 0) fl |= F_OBS;
+  if (w->fleet_models == 1 && w->fleet_modes == 1) fl |= F_HOLOVEL;
+  return fl;
+}
+
+template <typename T>
+void fill_common(const swarp_world_t* w, int horizon, RolloutArgs<T>& R) {
+  std::memset(&R, 0, sizeof(R));
+  R.E = w->n_envs;
+  R.A = w->n_agents;
+  R.G = envs_per_cta(R.A, R.E);
+  R.H = horizon;
+  R.S = w->substeps;
+  R.act_dim = w->act_dim;
+  R.N = w->obstacles.n_obstacles;
+  WorldC<T>& W = R.W;
+  W.dt = static_cast<T>(w->dt / w->substeps);
+  W.k = static_cast<T>(w->k);
+  W.c = static_cast<T>(w->c);
+  W.margin = static_cast<T>(w->margin);
+  W.max_overlap = static_cast<T>(w->max_overlap);
+  W.r2_thr = w->collisions ? radius_sq_threshold<T>(w->neighbor_radius) : T(-1);
+  W.bx0 = static_cast<T>(w->bounds[0]);
+  W.bx1 = static_cast<T>(w->bounds[1]);
+  W.by0 = static_cast<T>(w->bounds[2]);
+  W.by1 = static_cast<T>(w->bounds[3]);
+  W.lin_decay = static_cast<T>(1.0 - w->lin_damping * (w->dt / w->substeps));
+  W.ang_decay = static_cast<T>(1.0 - w->ang_damping * (w->dt / w->substeps));
+  W.K = w->max_neighbors;
+  W.bounds_mode = w->bounds_mode;
+  R.params = static_cast<const T*>(w->params);
+  R.params_env_stride = w->params_env_stride;
+  R.model_tag = w->model_tag;
+  R.ctrl_mode = w->ctrl_mode;
+  const swarp_obstacles_t& o = w->obstacles;
+  if (R.N > 0) {
+    R.o_pos = static_cast<const T*>(o.pos);
+    R.o_angle = static_cast<const T*>(o.angle);
+    R.o_vel = static_cast<const T*>(o.vel);
+    R.o_ang_vel = static_cast<const T*>(o.ang_vel);
+    R.o_radius = static_cast<const T*>(o.radius);
+    R.o_half = static_cast<const T*>(o.half);
+    R.o_shape = o.shape;
+  }
+}
+
+template <typename T>
+void set_state(const swarp_state_t& s, const T*& p, const T*& th, const T*& v, const T*& sp,
+               const T*& w) {
+  p = static_cast<const T*>(s.pos);
+  th = static_cast<const T*>(s.theta);
+  v = static_cast<const T*>(s.vel);
+  sp = static_cast<const T*>(s.speed);
+  w = static_cast<const T*>(s.ang_vel);
+}
+template <typename T>
+void set_state_out(const swarp_state_t& s, T*& p, T*& th, T*& v, T*& sp, T*& w) {
+  p = static_cast<T*>(s.pos);
+  th = static_cast<T*>(s.theta);
+  v = static_cast<T*>(s.vel);
+  sp = static_cast<T*>(s.speed);
+  w = static_cast<T*>(s.ang_vel);
+}
+
+template <typename Kernel>
+int launch(Kernel k, int grid, int block, size_t smem, cudaStream_t st, const void* args_ptr) {
+  (void)args_ptr;
+  if (smem > 48 * 1024) {
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return SWARP_ERR_CUDA;
+  }
+  return SWARP_OK;
+}
+
+#define SWARP_DISPATCH(FLV, KERNEL, T, ...)                       \
+  switch (FLV) {                                                  \
+    case 0: KERNEL<T, 0>__VA_ARGS__; break;                       \
+    case 1: KERNEL<T, 1>__VA_ARGS__; break;                       \
+    case 3: KERNEL<T, 3>__VA_ARGS__; break;                       \
+    case 4: KERNEL<T, 4>__VA_ARGS__; break;                       \
+    case 5: KERNEL<T, 5>__VA_ARGS__; break;                       \
+    case 7: KERNEL<T, 7>__VA_ARGS__; break;                       \
+    case 8: KERNEL<T, 8>__VA_ARGS__; break;                       \
+    case 9: KERNEL<T, 9>__VA_ARGS__; break;                       \
+    case 11: KERNEL<T, 11>__VA_ARGS__; break;                     \
+    case 12: KERNEL<T, 12>__VA_ARGS__; break;                     \
+    case 13: KERNEL<T, 13>__VA_ARGS__; break;                     \
+    case 15: KERNEL<T, 15>__VA_ARGS__; break;                     \
+    default: return SWARP_ERR_UNSUPPORTED;                        \
+  }
+
+template <typename T, int FL>
+int run_fwd(const RolloutArgs<T>& R, cudaStream_t st) {
+  const int grid = (R.E + R.G - 1) / R.G;
+  const int block = R.G * R.A;
+  const size_t smem = Smem<T>::fwd(block, R.G * R.N);
+  auto k = rollout_fwd_kernel<T, FL>;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return SWARP_ERR_CUDA;
+  k<<<grid, block, smem, st>>>(R);
+  return cudaGetLastError() == cudaSuccess ? SWARP_OK : SWARP_ERR_CUDA;
+}
+
+template <typename T, int FL>
+int run_bwd(const RolloutArgs<T>& R, cudaStream_t st) {
+  const int grid = (R.E + R.G - 1) / R.G;
+  const int block = R.G * R.A;
+  const size_t smem = Smem<T>::bwd(block, R.G * R.N, R.S);
+  auto k = rollout_bwd_kernel<T, FL>;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return SWARP_ERR_CUDA;
+  k<<<grid, block, smem, st>>>(R);
+  return cudaGetLastError() == cudaSuccess ? SWARP_OK : SWARP_ERR_CUDA;
+}
+
+template <typename T>
+int fwd_typed(const swarp_world_t* w, int horizon, swarp_state_t init, const void* actions,
+              swarp_state_t traj, swarp_state_t fin, int32_t* true_max, void* ws,
+              cudaStream_t st) {
+  RolloutArgs<T> R;
+  fill_common<T>(w, horizon, R);
+  set_state<T>(init, R.i_pos, R.i_th, R.i_vel, R.i_s, R.i_w);
+  R.act = static_cast<const T*>(actions);
+  set_state_out<T>(traj, R.t_pos, R.t_th, R.t_vel, R.t_s, R.t_w);
+  set_state_out<T>(fin, R.f_pos, R.f_th, R.f_vel, R.f_s, R.f_w);
+  R.true_max = true_max;
+  R.cutoff = static_cast<int16_t*>(ws);
+  const int fl = flags_of(w);
+  int rc = SWARP_OK;
+  SWARP_DISPATCH(fl, rc = run_fwd, T, (R, st))
+  return rc;
+}
+
+template <typename T>
+int bwd_typed(const swarp_world_t* w, int horizon, swarp_state_t init, const void* actions,
+              swarp_state_t traj, swarp_state_t gtraj, swarp_state_t gfin, void* gact,
+              swarp_state_t ginit, const void* ws, cudaStream_t st) {
+  RolloutArgs<T> R;
+  fill_common<T>(w, horizon, R);
+  set_state<T>(init, R.i_pos, R.i_th, R.i_vel, R.i_s, R.i_w);
+  R.act = static_cast<const T*>(actions);
+  set_state_out<T>(traj, R.t_pos, R.t_th, R.t_vel, R.t_s, R.t_w);
+  set_state<T>(gtraj, R.gt_pos, R.gt_th, R.gt_vel, R.gt_s, R.gt_w);
+  set_state<T>(gfin, R.gf_pos, R.gf_th, R.gf_vel, R.gf_s, R.gf_w);
+  R.g_act = static_cast<T*>(gact);
+  set_state_out<T>(ginit, R.gi_pos, R.gi_th, R.gi_vel, R.gi_s, R.gi_w);
+  R.cutoff = const_cast<int16_t*>(static_cast<const int16_t*>(ws));
+  const int fl = flags_of(w);
+  int rc = SWARP_OK;
+  SWARP_DISPATCH(fl, rc = run_bwd, T, (R, st))
+  return rc;
+}
+
+template <typename T>
+int nbr_typed(const swarp_world_t* w, const void* pos, int32_t* idx, int32_t* count,
+              int32_t* true_count, cudaStream_t st) {
+  const int E = w->n_envs, A = w->n_agents;
+  const int G = envs_per_cta(A, E);
+  const int grid = (E + G - 1) / G;
+  const size_t smem = (size_t)G * A * sizeof(typename V4<T>::t);
+  auto k = neighbors_kernel<T>;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return SWARP_ERR_CUDA;
+  k<<<grid, G * A, smem, st>>>(E, A, G, w->max_neighbors, radius_sq_threshold<T>(w->neighbor_radius),
+                               static_cast<const T*>(pos), idx, count, true_count);
+  return cudaGetLastError() == cudaSuccess ? SWARP_OK : SWARP_ERR_CUDA;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t swarp_rollout_workspace_bytes(const swarp_world_t* w, int32_t horizon) {
+  if (validate_world(w, horizon) != SWARP_OK) return 0;
+  size_t bytes = 0;
+  if (flags_of(w) & F_TRUNC)
+    bytes += (size_t)horizon * w->substeps * (size_t)w->n_envs * w->n_agents * sizeof(int16_t);
+  return bytes;
+}
+
+int swarp_rollout_fwd(const swarp_world_t* w, int32_t horizon, swarp_state_t init,
+                      const void* actions, swarp_state_t traj, swarp_state_t final_out,
+                      int32_t* true_count_max, swarp_bodies_t bodies_init,
+                      swarp_bodies_t bodies_traj, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  (void)bodies_init;
+  (void)bodies_traj;
+  int rc = validate_world(w, horizon);
+  if (rc != SWARP_OK) return rc;
+  if (!state_complete(init) || !state_complete(traj) || !actions) return SWARP_ERR_INVALID_ARG;
+  const bool any_fin = final_out.pos || final_out.theta || final_out.vel || final_out.speed || final_out.ang_vel;
+  if (any_fin && !state_complete(final_out)) return SWARP_ERR_INVALID_ARG;
+  const size_t need = swarp_rollout_workspace_bytes(w, horizon);
+  if (need > 0 && (!workspace || workspace_bytes < need)) return SWARP_ERR_WORKSPACE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (w->dtype == SWARP_F32)
+    return fwd_typed<float>(w, horizon, init, actions, traj, final_out, true_count_max, workspace, st);
+  return fwd_typed<double>(w, horizon, init, actions, traj, final_out, true_count_max, workspace, st);
+}
+
+int swarp_rollout_bwd(const swarp_world_t* w, int32_t horizon, swarp_state_t init,
+                      const void* actions, swarp_state_t traj, swarp_state_t adj_traj,
+                      swarp_state_t adj_final, swarp_bodies_t bodies_init,
+                      swarp_bodies_t bodies_traj, swarp_bodies_t adj_bodies_final,
+                      void* adj_actions, swarp_state_t adj_init, const void* workspace,
+                      size_t workspace_bytes, void* stream) {
+  (void)bodies_init;
+  (void)bodies_traj;
+  (void)adj_bodies_final;
+  int rc = validate_world(w, horizon);
+  if (rc != SWARP_OK) return rc;
+  if (!state_complete(init) || !state_complete(traj) || !state_complete(adj_init) || !actions ||
+      !adj_actions)
+    return SWARP_ERR_INVALID_ARG;
+  const size_t need = swarp_rollout_workspace_bytes(w, horizon);
+  if (need > 0 && (!workspace || workspace_bytes < need)) return SWARP_ERR_WORKSPACE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (w->dtype == SWARP_F32)
+    return bwd_typed<float>(w, horizon, init, actions, traj, adj_traj, adj_final, adj_actions,
+                            adj_init, workspace, st);
+  return bwd_typed<double>(w, horizon, init, actions, traj, adj_traj, adj_final, adj_actions,
+                           adj_init, workspace, st);
+}
+
+int swarp_neighbors(const swarp_world_t* w, const void* pos, int32_t* idx, int32_t* count,
+                    int32_t* true_count, void* stream) {
+  if (!w || !pos || !idx || !count || !true_count) return SWARP_ERR_INVALID_ARG;
+  if (w->n_envs < 1 || w->n_agents < 1 || w->max_neighbors < 1 || !(w->neighbor_radius > 0.0))
+    return SWARP_ERR_INVALID_ARG;
+  if (w->n_agents > SWARP_MAX_AGENTS) return SWARP_ERR_TOO_MANY_AGENTS;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (w->dtype == SWARP_F32) return nbr_typed<float>(w, pos, idx, count, true_count, st);
+  if (w->dtype == SWARP_F64) return nbr_typed<double>(w, pos, idx, count, true_count, st);
+  return SWARP_ERR_INVALID_ARG;
+}
+
+const char* swarp_error_string(int code) {
+  switch (code) {
+    case SWARP_OK: return "ok";
+    case SWARP_ERR_INVALID_ARG: return "invalid argument (null pointer, size or configuration)";
+    case SWARP_ERR_UNSUPPORTED: return "unsupported model or option in this build";
+    case SWARP_ERR_TOO_MANY_AGENTS: return "n_agents above SWARP_MAX_AGENTS";
+    case SWARP_ERR_CUDA: return "CUDA launch or attribute call failed";
+    case SWARP_ERR_WORKSPACE: return "workspace missing or too small";
+    default: return "unknown error code";
+  }
+}
+
+int32_t swarp_abi_version(void) { return kAbiVersion; }
+
+}  // extern "C"

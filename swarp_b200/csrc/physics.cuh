@@ -1,0 +1,663 @@
+// Device math of one agent substep: contact law, obstacles, walls and the three 2-D
+// motion models, each as a forward function and its hand-derived vector-Jacobian
+// product (VJP). Shared by the rollout forward and adjoint kernels.
+//
+// Reference semantics (ddebenedittis/swarp):
+//   contact law          swarp/core/collisions.py:87-143  (_normal_coeff, pair_force)
+//   segment / box        swarp/core/collisions.py:156-260 (closest_on_segment, box_force)
+//   broad phase          swarp/core/collisions.py:61-84   (shape_bound, bounds_apart)
+//   walls                swarp/core/collisions.py:745-780 (_wall_forces)
+//   motion models        swarp/dynamics/kernels.py:68-71, 166-275 (clamp_norm, servo, _step_2d)
+//   disc bounds clamp    swarp/dynamics/kernels.py:395-403
+// The reference differentiates these with Warp's generated adjoints; the VJPs here
+// follow the same branch conventions at kinks: max(a, b) sends the gradient to b on a
+// tie, clamp passes it on the closed interval, length() has zero gradient at the zero
+// vector, abs() has +1 at zero.
+//
+// The whole translation unit is compiled with -fmad=false: every multiply-add below
+// rounds exactly as written, so a quantity recomputed in the adjoint kernel (contact
+// activity, clamp activity, neighbor membership) is bitwise the value the forward
+// kernel saw. Fused multiply-adds are placed explicitly with fma().
+#pragma once
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+namespace swarp {
+
+// ------------------------------------------------------------------ scalar helpers
+template <typename T> struct Num;
+template <> struct Num<float> {
+  static __device__ __forceinline__ float sqrt_(float x) { return ::sqrtf(x); }
+  static __device__ __forceinline__ float fma_(float a, float b, float c) { return __fmaf_rn(a, b, c); }
+  static __device__ __forceinline__ float sin_(float x) { return ::sinf(x); }
+  static __device__ __forceinline__ float cos_(float x) { return ::cosf(x); }
+  static __device__ __forceinline__ float tan_(float x) { return ::tanf(x); }
+  static __device__ __forceinline__ float atan_(float x) { return ::atanf(x); }
+  static __device__ __forceinline__ float tanh_(float x) { return ::tanhf(x); }
+};
+template <> struct Num<double> {
+  static __device__ __forceinline__ double sqrt_(double x) { return ::sqrt(x); }
+  static __device__ __forceinline__ double fma_(double a, double b, double c) { return __fma_rn(a, b, c); }
+  static __device__ __forceinline__ double sin_(double x) { return ::sin(x); }
+  static __device__ __forceinline__ double cos_(double x) { return ::cos(x); }
+  static __device__ __forceinline__ double tan_(double x) { return ::tan(x); }
+  static __device__ __forceinline__ double atan_(double x) { return ::atan(x); }
+  static __device__ __forceinline__ double tanh_(double x) { return ::tanh(x); }
+};
+
+template <typename T> __device__ __forceinline__ T wmax(T a, T b) { return a > b ? a : b; }
+template <typename T> __device__ __forceinline__ T wmin(T a, T b) { return a < b ? a : b; }
+// Warp clamp: min(max(lo, x), hi)
+template <typename T> __device__ __forceinline__ T wclamp(T x, T lo, T hi) { return wmin(wmax(lo, x), hi); }
+// gradient gate of Warp's clamp adjoint (closed interval)
+template <typename T> __device__ __forceinline__ bool clamp_pass(T x, T lo, T hi) { return !(x < lo) && !(x > hi); }
+template <typename T> __device__ __forceinline__ T dot2(T ax, T ay, T bx, T by) { return Num<T>::fma_(ax, bx, ay * by); }
+template <typename T> __device__ __forceinline__ T len2(T x, T y) { return Num<T>::sqrt_(dot2(x, y, x, y)); }
+
+template <typename T> struct Eps2 { static constexpr T v = T(1.0e-10); };
+
+// Model / mode / shape tags (values of the reference enums).
+enum : int { TAG_HOLONOMIC = 0, TAG_DIFF_DRIVE = 1, TAG_BICYCLE = 2 };
+enum : int { MODE_VELOCITY = 0, MODE_ACCELERATION = 1, MODE_SERVO = 2 };
+enum : int { SHAPE_CIRCLE = 0, SHAPE_BOX = 1, SHAPE_SEGMENT = 2 };
+enum : int { BOUNDS_NONE = 0, BOUNDS_SOFT = 1, BOUNDS_CLAMP = 2 };
+
+// Per-agent state (the five live 2-D fields).
+template <typename T> struct Agent {
+  T px, py, th, vx, vy, s, w;
+};
+
+// Per-agent constants, loaded once per launch.
+template <typename T> struct AgentP {
+  T radius, mass, max_speed, min_speed, max_accel, max_ang_vel, max_ang_accel;
+  T l_f, l_r, max_steer, gain_v, gain_w;
+  T dt_over_m;  // sub_dt / mass  (the reference's force * (dt / mass))
+  T denom;      // 1 + c * sub_dt / mass  (implicit damping denominator)
+  int tag, mode;
+};
+
+// World constants of one launch.
+template <typename T> struct WorldC {
+  T dt;  // sub-step
+  T k, c, margin, max_overlap;
+  T r2_thr;  // largest d2 with sqrt(d2) <= neighbor_radius (exact membership test)
+  T bx0, bx1, by0, by1;
+  T lin_decay, ang_decay;  // movable bodies: 1 - damping * dt
+  int K;                   // max_neighbors
+  int bounds_mode;
+};
+
+// ------------------------------------------------------------------- contact law
+// f = max(0, (k*ov' - c*vn) / denom), ov' = mo*tanh(ov/mo) when mo > 0
+template <typename T>
+__device__ __forceinline__ T normal_coeff(T ov, T vn, T denom, const WorldC<T>& W) {
+  T ovs = ov;
+  if (W.max_overlap > T(0)) ovs = W.max_overlap * Num<T>::tanh_(ov / W.max_overlap);
+  T x = (W.k * ovs - W.c * vn) / denom;
+  return wmax(x, T(0));
+}
+// VJP of normal_coeff: cotangent g on its value -> (d ov, d vn)
+template <typename T>
+__device__ __forceinline__ void normal_coeff_vjp(T ov, T vn, T denom, T g, const WorldC<T>& W,
+                                                 T& gov, T& gvn) {
+  T ovs = ov, th = T(0);
+  if (W.max_overlap > T(0)) {
+    th = Num<T>::tanh_(ov / W.max_overlap);
+    ovs = W.max_overlap * th;
+  }
+  T x = (W.k * ovs - W.c * vn) / denom;
+  if (x > T(0)) {
+    T gnum = g / denom;
+    T govs = W.k * gnum;
+    gvn = -W.c * gnum;
+    gov = (W.max_overlap > T(0)) ? govs * (T(1) - th * th) : govs;
+  } else {
+    gov = T(0);
+    gvn = T(0);
+  }
+}
+
+// Disc-disc contact: force on self, d = p_self - p_other, rv = v_self - v_other.
+// d2 is dot(d, d) as computed by the caller (the membership test reuses it).
+template <typename T>
+__device__ __forceinline__ void pair_force_add(T dx, T dy, T d2, T rvx, T rvy, T min_dist, T denom,
+                                               const WorldC<T>& W, T& fx, T& fy) {
+  T dist = Num<T>::sqrt_(wmax(d2, Eps2<T>::v));
+  T ov = min_dist - dist;
+  if (ov > T(0)) {
+    T nx = dx / dist, ny = dy / dist;
+    T vn = dot2(rvx, rvy, nx, ny);
+    T cf = normal_coeff(ov, vn, denom, W);
+    fx = fx + cf * nx;
+    fy = fy + cf * ny;
+  }
+}
+// Force value (no accumulation), used where the result is negated/levered.
+template <typename T>
+__device__ __forceinline__ void pair_force(T dx, T dy, T rvx, T rvy, T min_dist, T denom,
+                                           const WorldC<T>& W, T& fx, T& fy) {
+  fx = T(0);
+  fy = T(0);
+  pair_force_add(dx, dy, dot2(dx, dy, dx, dy), rvx, rvy, min_dist, denom, W, fx, fy);
+}
+
+// VJP of pair_force: cotangent (gx, gy) on f -> adds to (gdx, gdy) and (grvx, grvy).
+template <typename T>
+__device__ __forceinline__ void pair_force_vjp(T dx, T dy, T rvx, T rvy, T min_dist, T denom,
+                                               T gx, T gy, const WorldC<T>& W, T& gdx, T& gdy,
+                                               T& grvx, T& grvy) {
+  T d2 = dot2(dx, dy, dx, dy);
+  T dist = Num<T>::sqrt_(wmax(d2, Eps2<T>::v));
+  T ov = min_dist - dist;
+  if (!(ov > T(0))) return;
+  T nx = dx / dist, ny = dy / dist;
+  T vn = dot2(rvx, rvy, nx, ny);
+  T cf = normal_coeff(ov, vn, denom, W);
+  T gcf = dot2(gx, gy, nx, ny);
+  T gnx = cf * gx, gny = cf * gy;
+  T gov, gvn;
+  normal_coeff_vjp(ov, vn, denom, gcf, W, gov, gvn);
+  grvx += gvn * nx;
+  grvy += gvn * ny;
+  gnx += gvn * rvx;
+  gny += gvn * rvy;
+  T gdist = -gov - dot2(gnx, gny, nx, ny) / dist;
+  T ddx = gnx / dist, ddy = gny / dist;
+  if (d2 > Eps2<T>::v) {
+    T gd2 = gdist * T(0.5) / dist;
+    ddx += T(2) * dx * gd2;
+    ddy += T(2) * dy * gd2;
+  }
+  gdx += ddx;
+  gdy += ddy;
+}
+
+// ------------------------------------------------------------- static obstacles
+// One obstacle as seen by the agent pass. Position/velocity are per env; the cos/sin
+// of the angle are precomputed (the reference evaluates cos(angle), sin(angle) in place;
+// same values).
+template <typename T> struct Obs {
+  T cx, cy, ca, sa, vx, vy, om;  // pose and motion
+  T r, hx, hy, bound;            // shape constants; bound = shape_bound()
+  int type;
+};
+
+template <typename T>
+__device__ __forceinline__ bool bounds_apart(T dx, T dy, T reach) {
+  T lim = reach * T(1.0001) + T(1.0e-6);
+  return dot2(dx, dy, dx, dy) > lim * lim;
+}
+
+// Box SDF contact (collisions.py:174-260): force on an agent at p with velocity v.
+template <typename T>
+__device__ __forceinline__ void box_force(T px, T py, T vx, T vy, const Obs<T>& o, T reach, T denom,
+                                          const WorldC<T>& W, T& fx, T& fy) {
+  fx = T(0);
+  fy = T(0);
+  const T ca = o.ca, sa = o.sa;
+  T dx = px - o.cx, dy = py - o.cy;
+  T lx = ca * dx + sa * dy;
+  T ly = -sa * dx + ca * dy;
+  T qx = fabs(lx) - o.hx;
+  T qy = fabs(ly) - o.hy;
+  T cx = wclamp(lx, -o.hx, o.hx), cy = wclamp(ly, -o.hy, o.hy);
+  T ox = lx - cx, oy = ly - cy;
+  T od2 = ox * ox + oy * oy;
+  T s, nlx, nly;
+  if (od2 > Eps2<T>::v) {
+    s = Num<T>::sqrt_(od2);
+    nlx = ox / s;
+    nly = oy / s;
+  } else if (qx > qy) {
+    s = qx;
+    nlx = lx >= T(0) ? T(1) : T(-1);
+    nly = T(0);
+  } else {
+    s = qy;
+    nlx = T(0);
+    nly = ly >= T(0) ? T(1) : T(-1);
+  }
+  T overlap = reach - s;
+  if (overlap > T(0)) {
+    T nx = ca * nlx - sa * nly, ny = sa * nlx + ca * nly;
+    T spx = lx - s * nlx, spy = ly - s * nly;
+    T rx = ca * spx - sa * spy, ry = sa * spx + ca * spy;
+    T vsx = o.vx + (-o.om * ry), vsy = o.vy + o.om * rx;
+    T vn = dot2(vx - vsx, vy - vsy, nx, ny);
+    T cf = normal_coeff(overlap, vn, denom, W);
+    fx = cf * nx;
+    fy = cf * ny;
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void box_force_vjp(T px, T py, T vx, T vy, const Obs<T>& o, T reach,
+                                              T denom, T gx, T gy, const WorldC<T>& W, T& gpx,
+                                              T& gpy, T& gvx, T& gvy) {
+  const T ca = o.ca, sa = o.sa;
+  T dx = px - o.cx, dy = py - o.cy;
+  T lx = ca * dx + sa * dy;
+  T ly = -sa * dx + ca * dy;
+  T qx = fabs(lx) - o.hx;
+  T qy = fabs(ly) - o.hy;
+  T cx = wclamp(lx, -o.hx, o.hx), cy = wclamp(ly, -o.hy, o.hy);
+  T ox = lx - cx, oy = ly - cy;
+  T od2 = ox * ox + oy * oy;
+  T s, nlx, nly;
+  const bool ext = od2 > Eps2<T>::v;
+  const bool use_x = qx > qy;
+  if (ext) {
+    s = Num<T>::sqrt_(od2);
+    nlx = ox / s;
+    nly = oy / s;
+  } else if (use_x) {
+    s = qx;
+    nlx = lx >= T(0) ? T(1) : T(-1);
+    nly = T(0);
+  } else {
+    s = qy;
+    nlx = T(0);
+    nly = ly >= T(0) ? T(1) : T(-1);
+  }
+  T overlap = reach - s;
+  if (!(overlap > T(0))) return;
+  T nx = ca * nlx - sa * nly, ny = sa * nlx + ca * nly;
+  T spx = lx - s * nlx, spy = ly - s * nly;
+  T rx = ca * spx - sa * spy, ry = sa * spx + ca * spy;
+  T vsx = o.vx + (-o.om * ry), vsy = o.vy + o.om * rx;
+  T relx = vx - vsx, rely = vy - vsy;
+  T vn = dot2(relx, rely, nx, ny);
+  T cf = normal_coeff(overlap, vn, denom, W);
+  // f = cf * n
+  T gcf = dot2(gx, gy, nx, ny);
+  T gnx = cf * gx, gny = cf * gy;
+  T gov, gvn;
+  normal_coeff_vjp(overlap, vn, denom, gcf, W, gov, gvn);
+  // vn = rel . n
+  T grelx = gvn * nx, grely = gvn * ny;
+  gnx += gvn * relx;
+  gny += gvn * rely;
+  gvx += grelx;
+  gvy += grely;
+  // vs = vo + om x r ; rel = v - vs
+  T grx = o.om * (-grely);   // vsy = vy_o + om*rx, gvs = -grel
+  T gry = -o.om * (-grelx);  // vsx = vx_o - om*ry
+  // r = R sp
+  T gspx = ca * grx + sa * gry;
+  T gspy = -sa * grx + ca * gry;
+  // sp = l - s*nl
+  T glx = gspx, gly = gspy;
+  T gs = -(nlx * gspx + nly * gspy) - gov;  // overlap = reach - s
+  T gnlx = -s * gspx + (ca * gnx + sa * gny);
+  T gnly = -s * gspy + (-sa * gnx + ca * gny);
+  if (ext) {
+    // nl = o / s, s = sqrt(od2), o = l - clamp(l)
+    T gox = gnlx / s, goy = gnly / s;
+    gs -= (gnlx * nlx + gnly * nly) / s;
+    T god2 = gs * T(0.5) / s;
+    gox += T(2) * ox * god2;
+    goy += T(2) * oy * god2;
+    glx += gox - (clamp_pass(lx, -o.hx, o.hx) ? gox : T(0));
+    gly += goy - (clamp_pass(ly, -o.hy, o.hy) ? goy : T(0));
+  } else if (use_x) {
+    glx += (lx < T(0) ? -gs : gs);  // s = |lx| - hx
+  } else {
+    gly += (ly < T(0) ? -gs : gs);
+  }
+  // l = R^T d
+  gpx += ca * glx - sa * gly;
+  gpy += sa * glx + ca * gly;
+}
+
+// Force on an agent (radius ra, implicit denominator denom) from one obstacle.
+template <typename T>
+__device__ __forceinline__ void obstacle_force(T px, T py, T vx, T vy, T ra, T denom, const Obs<T>& o,
+                                               const WorldC<T>& W, T& fx, T& fy) {
+  fx = T(0);
+  fy = T(0);
+  if (bounds_apart(px - o.cx, py - o.cy, ra + W.margin + o.bound)) return;
+  if (o.type == SHAPE_BOX) {
+    box_force(px, py, vx, vy, o, ra + W.margin, denom, W, fx, fy);
+  } else if (o.type == SHAPE_SEGMENT) {
+    T t = wclamp(dot2(px - o.cx, py - o.cy, o.ca, o.sa), -o.hx, o.hx);
+    T qx = o.cx + t * o.ca, qy = o.cy + t * o.sa;
+    T rx = qx - o.cx, ry = qy - o.cy;
+    T vsx = o.vx + (-o.om * ry), vsy = o.vy + o.om * rx;
+    pair_force(px - qx, py - qy, vx - vsx, vy - vsy, ra + o.r + W.margin, denom, W, fx, fy);
+  } else {
+    pair_force(px - o.cx, py - o.cy, vx - o.vx, vy - o.vy, ra + o.r + W.margin, denom, W, fx, fy);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void obstacle_force_vjp(T px, T py, T vx, T vy, T ra, T denom,
+                                                   const Obs<T>& o, T gx, T gy, const WorldC<T>& W,
+                                                   T& gpx, T& gpy, T& gvx, T& gvy) {
+  if (bounds_apart(px - o.cx, py - o.cy, ra + W.margin + o.bound)) return;
+  if (o.type == SHAPE_BOX) {
+    box_force_vjp(px, py, vx, vy, o, ra + W.margin, denom, gx, gy, W, gpx, gpy, gvx, gvy);
+  } else if (o.type == SHAPE_SEGMENT) {
+    T sproj = dot2(px - o.cx, py - o.cy, o.ca, o.sa);
+    T t = wclamp(sproj, -o.hx, o.hx);
+    T qx = o.cx + t * o.ca, qy = o.cy + t * o.sa;
+    T rx = qx - o.cx, ry = qy - o.cy;
+    T vsx = o.vx + (-o.om * ry), vsy = o.vy + o.om * rx;
+    T gdx = T(0), gdy = T(0), grvx = T(0), grvy = T(0);
+    pair_force_vjp(px - qx, py - qy, vx - vsx, vy - vsy, ra + o.r + W.margin, denom, gx, gy, W,
+                   gdx, gdy, grvx, grvy);
+    gpx += gdx;
+    gpy += gdy;
+    gvx += grvx;
+    gvy += grvy;
+    // q enters through d = p - q and vs (via r = q - c)
+    T gqx = -gdx, gqy = -gdy;
+    T gvsx = -grvx, gvsy = -grvy;
+    gqx += o.om * gvsy;    // vsy = vo_y + om*rx
+    gqy += -o.om * gvsx;   // vsx = vo_x - om*ry
+    T gt = dot2(gqx, gqy, o.ca, o.sa);
+    if (clamp_pass(sproj, -o.hx, o.hx)) {
+      gpx += gt * o.ca;
+      gpy += gt * o.sa;
+    }
+  } else {
+    T gdx = T(0), gdy = T(0), grvx = T(0), grvy = T(0);
+    pair_force_vjp(px - o.cx, py - o.cy, vx - o.vx, vy - o.vy, ra + o.r + W.margin, denom, gx, gy,
+                   W, gdx, gdy, grvx, grvy);
+    gpx += gdx;
+    gpy += gdy;
+    gvx += grvx;
+    gvy += grvy;
+  }
+}
+
+// ------------------------------------------------------------------------ walls
+template <typename T>
+__device__ __forceinline__ void wall_force(T px, T py, T vx, T vy, T ra, T denom, const WorldC<T>& W,
+                                           T& fx, T& fy) {
+  const T reach = ra + W.margin;
+  fx = T(0);
+  fy = T(0);
+  T pen = reach - (px - W.bx0);
+  if (pen > T(0)) fx = fx + normal_coeff(pen, vx, denom, W);
+  pen = reach - (W.bx1 - px);
+  if (pen > T(0)) fx = fx + (-normal_coeff(pen, -vx, denom, W));
+  pen = reach - (py - W.by0);
+  if (pen > T(0)) fy = fy + normal_coeff(pen, vy, denom, W);
+  pen = reach - (W.by1 - py);
+  if (pen > T(0)) fy = fy + (-normal_coeff(pen, -vy, denom, W));
+}
+
+template <typename T>
+__device__ __forceinline__ void wall_force_vjp(T px, T py, T vx, T vy, T ra, T denom, T gx, T gy,
+                                               const WorldC<T>& W, T& gpx, T& gpy, T& gvx, T& gvy) {
+  const T reach = ra + W.margin;
+  T gov, gvn;
+  T pen = reach - (px - W.bx0);
+  if (pen > T(0)) {
+    normal_coeff_vjp(pen, vx, denom, gx, W, gov, gvn);
+    gpx -= gov;
+    gvx += gvn;
+  }
+  pen = reach - (W.bx1 - px);
+  if (pen > T(0)) {
+    normal_coeff_vjp(pen, -vx, denom, -gx, W, gov, gvn);
+    gpx += gov;
+    gvx -= gvn;
+  }
+  pen = reach - (py - W.by0);
+  if (pen > T(0)) {
+    normal_coeff_vjp(pen, vy, denom, gy, W, gov, gvn);
+    gpy -= gov;
+    gvy += gvn;
+  }
+  pen = reach - (W.by1 - py);
+  if (pen > T(0)) {
+    normal_coeff_vjp(pen, -vy, denom, -gy, W, gov, gvn);
+    gpy += gov;
+    gvy -= gvn;
+  }
+}
+
+// ------------------------------------------------------------------- integrate
+// clamp_norm(v, L) = v * (L / max(|v|, L))
+template <typename T>
+__device__ __forceinline__ void clamp_norm(T x, T y, T L, T& ox, T& oy) {
+  T n = len2(x, y);
+  T sc = L / wmax(n, L);
+  ox = x * sc;
+  oy = y * sc;
+}
+template <typename T>
+__device__ __forceinline__ void clamp_norm_vjp(T x, T y, T L, T gx, T gy, T& rx, T& ry) {
+  T n = len2(x, y);
+  T mx = wmax(n, L);
+  T sc = L / mx;
+  rx = gx * sc;
+  ry = gy * sc;
+  if (n > L) {
+    T gsc = dot2(gx, gy, x, y);
+    T gn = -gsc * sc / mx;
+    rx += x / n * gn;
+    ry += y / n * gn;
+  }
+}
+
+// SERVO (diff-drive): the VELOCITY command the rate-limited servo delivers this substep.
+template <typename T>
+__device__ __forceinline__ void servo_cmd(T a0, T a1, T s, T w, const AgentP<T>& P, T dt, T& c0, T& c1) {
+  T tv = wclamp(a0, -P.max_speed, P.max_speed) * P.gain_v;
+  T tw = wclamp(a1, -P.max_ang_vel, P.max_ang_vel) * P.gain_w;
+  T dv = P.max_accel * dt, dw = P.max_ang_accel * dt;
+  c0 = s + wclamp(tv - s, -dv, dv);
+  c1 = w + wclamp(tw - w, -dw, dw);
+}
+template <typename T>
+__device__ __forceinline__ void servo_cmd_vjp(T a0, T a1, T s, T w, const AgentP<T>& P, T dt, T gc0,
+                                              T gc1, T& ga0, T& ga1, T& gs, T& gw) {
+  T tv = wclamp(a0, -P.max_speed, P.max_speed) * P.gain_v;
+  T tw = wclamp(a1, -P.max_ang_vel, P.max_ang_vel) * P.gain_w;
+  T dv = P.max_accel * dt, dw = P.max_ang_accel * dt;
+  gs += gc0;
+  gw += gc1;
+  T gd0 = clamp_pass(tv - s, -dv, dv) ? gc0 : T(0);
+  T gd1 = clamp_pass(tw - w, -dw, dw) ? gc1 : T(0);
+  gs -= gd0;
+  gw -= gd1;
+  ga0 += clamp_pass(a0, -P.max_speed, P.max_speed) ? gd0 * P.gain_v : T(0);
+  ga1 += clamp_pass(a1, -P.max_ang_vel, P.max_ang_vel) ? gd1 * P.gain_w : T(0);
+}
+
+// One semi-implicit Euler substep of a 2-D agent under force (fx, fy).
+// p_new = p + v_new * dt is an explicit fma in both directions, so the adjoint
+// reconstructs the pre-clamp position bit for bit from the stored output velocity.
+template <typename T>
+__device__ __forceinline__ void integrate_fwd(const Agent<T>& in, T a0, T a1, T fx, T fy,
+                                              const AgentP<T>& P, const WorldC<T>& W, Agent<T>& out) {
+  const T dt = W.dt;
+  int mode = P.mode;
+  if (mode == MODE_SERVO) {
+    servo_cmd(a0, a1, in.s, in.w, P, dt, a0, a1);
+    mode = MODE_VELOCITY;
+  }
+  const T dvx = fx * P.dt_over_m, dvy = fy * P.dt_over_m;
+  if (P.tag == TAG_HOLONOMIC) {
+    T vx, vy;
+    if (mode == MODE_VELOCITY) {
+      clamp_norm(a0, a1, P.max_speed, vx, vy);
+    } else {
+      T ax, ay;
+      clamp_norm(a0, a1, P.max_accel, ax, ay);
+      clamp_norm(Num<T>::fma_(ax, dt, in.vx), Num<T>::fma_(ay, dt, in.vy), P.max_speed, vx, vy);
+    }
+    vx = vx + dvx;
+    vy = vy + dvy;
+    out.px = Num<T>::fma_(vx, dt, in.px);
+    out.py = Num<T>::fma_(vy, dt, in.py);
+    out.th = in.th;
+    out.vx = vx;
+    out.vy = vy;
+    out.s = len2(vx, vy);
+    out.w = T(0);
+  } else if (P.tag == TAG_DIFF_DRIVE) {
+    T sn, wn;
+    if (mode == MODE_VELOCITY) {
+      sn = wclamp(a0, -P.max_speed, P.max_speed);
+      wn = wclamp(a1, -P.max_ang_vel, P.max_ang_vel);
+    } else {
+      T acc = wclamp(a0, -P.max_accel, P.max_accel);
+      T alp = wclamp(a1, -P.max_ang_accel, P.max_ang_accel);
+      sn = wclamp(Num<T>::fma_(acc, dt, in.s), -P.max_speed, P.max_speed);
+      wn = wclamp(Num<T>::fma_(alp, dt, in.w), -P.max_ang_vel, P.max_ang_vel);
+    }
+    T c = Num<T>::cos_(in.th), sn_ = Num<T>::sin_(in.th);
+    T vx = sn * c + dvx, vy = sn * sn_ + dvy;
+    out.px = Num<T>::fma_(vx, dt, in.px);
+    out.py = Num<T>::fma_(vy, dt, in.py);
+    out.th = Num<T>::fma_(wn, dt, in.th);
+    out.vx = vx;
+    out.vy = vy;
+    out.s = sn;
+    out.w = wn;
+  } else {  // TAG_BICYCLE (host rejects other tags)
+    T acc = wclamp(a0, -P.max_accel, P.max_accel);
+    T delta = wclamp(a1, -P.max_steer, P.max_steer);
+    T sn = wclamp(Num<T>::fma_(acc, dt, in.s), P.min_speed, P.max_speed);
+    T wb = P.l_f + P.l_r;
+    T td = Num<T>::tan_(delta);
+    T beta = Num<T>::atan_(td * P.l_r / wb);
+    T ang = in.th + beta;
+    T vx = sn * Num<T>::cos_(ang) + dvx, vy = sn * Num<T>::sin_(ang) + dvy;
+    T wn = sn / wb * Num<T>::cos_(beta) * td;
+    out.px = Num<T>::fma_(vx, dt, in.px);
+    out.py = Num<T>::fma_(vy, dt, in.py);
+    out.th = Num<T>::fma_(wn, dt, in.th);
+    out.vx = vx;
+    out.vy = vy;
+    out.s = sn;
+    out.w = wn;
+  }
+  if (W.bounds_mode == BOUNDS_CLAMP) {
+    out.px = wclamp(out.px, W.bx0 + P.radius, W.bx1 - P.radius);
+    out.py = wclamp(out.py, W.by0 + P.radius, W.by1 - P.radius);
+  }
+}
+
+// Adjoint of integrate_fwd. `out` is the substep's stored output (only its velocity
+// and speed are read). Writes the gradients that flow straight to the substep input
+// into gin (overwriting), the force cotangent into (gfx, gfy) and adds the action
+// cotangent into (ga0, ga1).
+template <typename T>
+__device__ __forceinline__ void integrate_vjp(const Agent<T>& in, T a0, T a1, const Agent<T>& out,
+                                              const Agent<T>& g, const AgentP<T>& P,
+                                              const WorldC<T>& W, Agent<T>& gin, T& gfx, T& gfy,
+                                              T& ga0, T& ga1) {
+  const T dt = W.dt;
+  gin.px = gin.py = gin.th = gin.vx = gin.vy = gin.s = gin.w = T(0);
+  // bounds clamp on the new position
+  T gpx = g.px, gpy = g.py;
+  if (W.bounds_mode == BOUNDS_CLAMP) {
+    T pxn = Num<T>::fma_(out.vx, dt, in.px), pyn = Num<T>::fma_(out.vy, dt, in.py);
+    if (!clamp_pass(pxn, W.bx0 + P.radius, W.bx1 - P.radius)) gpx = T(0);
+    if (!clamp_pass(pyn, W.by0 + P.radius, W.by1 - P.radius)) gpy = T(0);
+  }
+  int mode = P.mode;
+  T c0 = a0, c1 = a1;
+  if (mode == MODE_SERVO) {
+    servo_cmd(a0, a1, in.s, in.w, P, dt, c0, c1);
+    mode = MODE_VELOCITY;
+  }
+  T gc0 = T(0), gc1 = T(0);
+  // p_new = p + v_out*dt, v_out = vel-level + F*dt/m
+  gin.px = gpx;
+  gin.py = gpy;
+  T gvx = g.vx + gpx * dt, gvy = g.vy + gpy * dt;
+  if (P.tag == TAG_HOLONOMIC) {
+    // s_out = |v_new|
+    T n = len2(out.vx, out.vy);
+    if (n > T(0)) {
+      gvx += out.vx / n * g.s;
+      gvy += out.vy / n * g.s;
+    }
+    gin.th = g.th;
+    gfx = gvx * P.dt_over_m;
+    gfy = gvy * P.dt_over_m;
+    if (mode == MODE_VELOCITY) {
+      clamp_norm_vjp(c0, c1, P.max_speed, gvx, gvy, gc0, gc1);
+    } else {
+      T ax, ay;
+      clamp_norm(c0, c1, P.max_accel, ax, ay);
+      T ux = Num<T>::fma_(ax, dt, in.vx), uy = Num<T>::fma_(ay, dt, in.vy);
+      T gux, guy;
+      clamp_norm_vjp(ux, uy, P.max_speed, gvx, gvy, gux, guy);
+      gin.vx = gux;
+      gin.vy = guy;
+      clamp_norm_vjp(c0, c1, P.max_accel, gux * dt, guy * dt, gc0, gc1);
+    }
+  } else if (P.tag == TAG_DIFF_DRIVE) {
+    T c = Num<T>::cos_(in.th), sn_ = Num<T>::sin_(in.th);
+    T sn = out.s;
+    gfx = gvx * P.dt_over_m;
+    gfy = gvy * P.dt_over_m;
+    T gsn = g.s + dot2(gvx, gvy, c, sn_);
+    gin.th = g.th + sn * (c * gvy - sn_ * gvx);
+    T gwn = g.w + g.th * dt;
+    if (mode == MODE_VELOCITY) {
+      gc0 = clamp_pass(c0, -P.max_speed, P.max_speed) ? gsn : T(0);
+      gc1 = clamp_pass(c1, -P.max_ang_vel, P.max_ang_vel) ? gwn : T(0);
+    } else {
+      T acc = wclamp(c0, -P.max_accel, P.max_accel);
+      T alp = wclamp(c1, -P.max_ang_accel, P.max_ang_accel);
+      T us = Num<T>::fma_(acc, dt, in.s), uw = Num<T>::fma_(alp, dt, in.w);
+      T gus = clamp_pass(us, -P.max_speed, P.max_speed) ? gsn : T(0);
+      T guw = clamp_pass(uw, -P.max_ang_vel, P.max_ang_vel) ? gwn : T(0);
+      gin.s = gus;
+      gin.w = guw;
+      gc0 = clamp_pass(c0, -P.max_accel, P.max_accel) ? gus * dt : T(0);
+      gc1 = clamp_pass(c1, -P.max_ang_accel, P.max_ang_accel) ? guw * dt : T(0);
+    }
+  } else {  // bicycle
+    T acc = wclamp(c0, -P.max_accel, P.max_accel);
+    T delta = wclamp(c1, -P.max_steer, P.max_steer);
+    T us = Num<T>::fma_(acc, dt, in.s);
+    T sn = out.s;
+    T wb = P.l_f + P.l_r;
+    T td = Num<T>::tan_(delta);
+    T z = td * P.l_r / wb;
+    T beta = Num<T>::atan_(z);
+    T ang = in.th + beta;
+    T ca = Num<T>::cos_(ang), sa = Num<T>::sin_(ang);
+    T cb = Num<T>::cos_(beta), sb = Num<T>::sin_(beta);
+    gfx = gvx * P.dt_over_m;
+    gfy = gvy * P.dt_over_m;
+    T gwn = g.w + g.th * dt;
+    T gsn = g.s + dot2(gvx, gvy, ca, sa);
+    T gang = sn * (ca * gvy - sa * gvx);
+    gin.th = g.th + gang;
+    T gbeta = gang;
+    // wn = ((sn / wb) * cos(beta)) * tan(delta)
+    T q = sn / wb;
+    gsn += gwn * td * cb / wb;
+    gbeta += -gwn * td * q * sb;
+    T sec2 = T(1) + td * td;
+    T gdelta = gwn * q * cb * sec2;
+    // beta = atan(z), z = tan(delta) * l_r / wb
+    T gz = gbeta / (T(1) + z * z);
+    gdelta += gz * P.l_r / wb * sec2;
+    T gus = clamp_pass(us, P.min_speed, P.max_speed) ? gsn : T(0);
+    gin.s = gus;
+    gc0 = clamp_pass(c0, -P.max_accel, P.max_accel) ? gus * dt : T(0);
+    gc1 = clamp_pass(c1, -P.max_steer, P.max_steer) ? gdelta : T(0);
+  }
+  if (P.mode == MODE_SERVO) {
+    T gs = T(0), gw = T(0);
+    servo_cmd_vjp(a0, a1, in.s, in.w, P, dt, gc0, gc1, ga0, ga1, gs, gw);
+    gin.s += gs;
+    gin.w += gw;
+  } else {
+    ga0 += gc0;
+    ga1 += gc1;
+  }
+}
+
+}  // namespace swarp

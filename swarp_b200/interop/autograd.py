@@ -1,0 +1,162 @@
+"""PyTorch autograd bridge: ``warp_step`` and ``rollout`` as differentiable torch ops.
+
+Drop-in for the reference's ``swarp/interop/autograd.py`` (``TorchState`` ``:29-45``,
+``fill_state_defaults`` ``:48-68``, ``GradRing`` ``:184-226``, ``warp_step``
+``:299-338``, ``rollout`` ``:341-369``). Same signatures and return values; what
+differs is underneath: the reference records a Warp tape per step and replays Warp's
+generated adjoints step by step from a Python loop, while here ``rollout`` is ONE
+autograd node whose forward is one fused CUDA kernel over the whole horizon (the
+trajectory it returns doubles as the checkpoint) and whose backward is one fused
+adjoint kernel.
+
+The four 6-DOF drone fields are carried through unchanged (2-D fleets only on this
+path), exactly as the reference's full integrate kernel passes them through for 2-D
+agents; their gradient is therefore the identity.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import NamedTuple
+
+import torch
+
+from swarp_b200.core.stepper import Stepper
+
+
+class TorchState(NamedTuple):
+    """World state as torch tensors (``[n_envs, n_agents]`` leading dims)."""
+
+    pos: torch.Tensor
+    theta: torch.Tensor
+    vel: torch.Tensor
+    speed: torch.Tensor
+    ang_vel: torch.Tensor
+    z: torch.Tensor | None = None
+    vz: torch.Tensor | None = None
+    attitude: torch.Tensor | None = None
+    body_rates: torch.Tensor | None = None
+
+
+def fill_state_defaults(state: TorchState) -> TorchState:
+    """Materialise absent drone fields as zeros (identity attitude)."""
+    if all(t is not None for t in state):
+        return state
+    ref = state.pos
+    E, A = ref.shape[0], ref.shape[1]
+    opts = {"device": ref.device, "dtype": ref.dtype}
+    z = state.z if state.z is not None else torch.zeros(E, A, **opts)
+    vz = state.vz if state.vz is not None else torch.zeros(E, A, **opts)
+    if state.attitude is not None:
+        att = state.attitude
+    else:
+        att = torch.zeros(E, A, 4, **opts)
+        att[..., 3] = 1.0
+    br = state.body_rates if state.body_rates is not None else torch.zeros(E, A, 3, **opts)
+    return state._replace(z=z, vz=vz, attitude=att, body_rates=br)
+
+
+class _RolloutFn(torch.autograd.Function):
+    """``(actions [T,E,A,D], five state tensors) -> (final five, trajectory five [T,...])``."""
+
+    @staticmethod
+    def forward(ctx, stepper: Stepper, actions, pos, theta, vel, speed, ang_vel):
+        state5 = tuple(t.contiguous() for t in (pos, theta, vel, speed, ang_vel))
+        acts = actions.contiguous()
+        traj, fin, _, ws = stepper.rollout_forward(state5, acts, final=True)
+        ctx.stepper = stepper
+        ctx.ws = ws
+        ctx.set_materialize_grads(False)
+        ctx.save_for_backward(acts, *state5, *traj)
+        return (*fin, *traj)
+
+    @staticmethod
+    def backward(ctx, *grads):
+        acts, *rest = ctx.saved_tensors
+        state5, traj5 = tuple(rest[:5]), tuple(rest[5:10])
+        gfin = tuple(None if g is None else g.contiguous() for g in grads[:5])
+        gtraj = tuple(None if g is None else g.contiguous() for g in grads[5:10])
+        g_act, g_init = ctx.stepper.rollout_backward(state5, acts, traj5, gtraj, gfin, ctx.ws)
+        return (None, g_act, *g_init)
+
+
+def _run(stepper: Stepper, state: TorchState, actions_seq: torch.Tensor):
+    state = fill_state_defaults(state)
+    core = tuple(state[:5])
+    stepper._check_inputs(core, actions_seq, horizon_dim=True)
+    grad_mode = torch.is_grad_enabled() and (
+        actions_seq.requires_grad or any(t.requires_grad for t in core)
+    )
+    extra = tuple(state[5:])
+    if grad_mode:
+        out = _RolloutFn.apply(stepper, actions_seq, *core)
+        fin, traj = out[:5], out[5:]
+    else:
+        with torch.no_grad():
+            core_c = tuple(t.contiguous() for t in core)
+            traj, fin, _, _ = stepper.rollout_forward(core_c, actions_seq.contiguous(), final=True)
+    return TorchState(*fin, *extra), traj, extra
+
+
+def warp_step(stepper: Stepper, state: TorchState, actions: torch.Tensor, slot=None) -> TorchState:
+    """Differentiable env step: ``state, actions [E,A,act_dim] -> next state``."""
+    fin, _, _ = _run(stepper, state, actions.unsqueeze(0))
+    return fin
+
+
+def rollout(
+    stepper: Stepper,
+    state: TorchState,
+    actions_seq: torch.Tensor,
+    ring: GradRing | None = None,
+) -> tuple[TorchState, list[TorchState]]:
+    """Backprop-through-time rollout over ``actions_seq [T, n_envs, n_agents, act_dim]``.
+
+    Returns ``(final_state, trajectory)``; ``trajectory[t]`` is the state after step
+    ``t``. Gradients flow to ``state`` and ``actions_seq``.
+    """
+    T = actions_seq.shape[0]
+    if ring is not None:
+        ring.reset()
+        for _ in range(T):
+            ring.acquire()
+    fin, traj, extra = _run(stepper, state, actions_seq)
+    trajectory = [TorchState(*(f[t] for f in traj), *extra) for t in range(T)]
+    return fin, trajectory
+
+
+@dataclass
+class StepGradSlot:
+    """One reserved step of a :class:`GradRing` (API compatibility)."""
+
+    index: int
+
+
+class GradRing:
+    """Capacity bookkeeping of the reference's reusable BPTT scratch ring.
+
+    The fused rollout allocates its trajectory/checkpoint buffers once per call from
+    torch's caching allocator, so no per-step scratch exists to recycle; the ring
+    keeps the reference contract (``reset``, ``acquire``, ``RuntimeError`` when a
+    rollout is longer than ``capacity``).
+    """
+
+    def __init__(self, stepper: Stepper, n_envs: int, act_dim: int, capacity: int) -> None:
+        self.stepper = stepper
+        self.n_envs = n_envs
+        self.act_dim = act_dim
+        self.capacity = capacity
+        self._idx = 0
+        self.slots = [StepGradSlot(i) for i in range(capacity)]
+
+    def reset(self) -> None:
+        self._idx = 0
+
+    def acquire(self) -> StepGradSlot:
+        if self._idx >= self.capacity:
+            raise RuntimeError(
+                f"GradRing capacity {self.capacity} exhausted; size it to the rollout length T"
+            )
+        slot = self.slots[self._idx]
+        self._idx += 1
+        return slot

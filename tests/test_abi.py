@@ -1,0 +1,111 @@
+"""The C-ABI library loads and exports every entry point include/swarp_b200.h declares,
+and the ctypes mirrors of its structs have the C layout (checked with gcc). CPU only:
+no compute call is made here."""
+
+import ctypes as C
+import os
+import re
+import subprocess
+
+import pytest
+
+from swarp_b200 import _lib, build
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "swarp_b200.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(swarp_[a-z_0-9]+)\s*\(", src)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build.build()
+    return C.CDLL(_lib.LIB_PATH)
+
+
+def test_every_declared_symbol_is_exported(lib):
+    names = declared_functions()
+    assert "swarp_rollout_fwd" in names and "swarp_rollout_bwd" in names
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in the header but not exported"
+
+
+def test_bindings_cover_the_header():
+    assert sorted(_lib.SIGNATURES) == declared_functions()
+
+
+def test_error_strings_and_version(lib):
+    lib.swarp_error_string.restype = C.c_char_p
+    assert lib.swarp_error_string(0) == b"ok"
+    assert b"unsupported" in lib.swarp_error_string(-2)
+    assert lib.swarp_abi_version() == 1
+
+
+def test_invalid_world_is_rejected_without_a_gpu(lib):
+    """Argument validation happens before any CUDA call."""
+    fn = lib.swarp_rollout_workspace_bytes
+    fn.restype = C.c_size_t
+    fn.argtypes = [C.POINTER(_lib.WorldC), C.c_int32]
+    w = _lib.WorldC()
+    assert fn(C.byref(w), 4) == 0  # all-zero world is invalid -> 0
+    fwd = lib.swarp_rollout_fwd
+    fwd.restype = C.c_int
+    fwd.argtypes = _lib.SIGNATURES["swarp_rollout_fwd"][1]
+    rc = fwd(None, 4, _lib.State(), None, _lib.State(), _lib.State(), None, _lib.Bodies(),
+             _lib.Bodies(), None, 0, None)
+    assert rc == -1
+    w.dtype, w.n_envs, w.n_agents, w.act_dim, w.substeps, w.dt = 0, 2, 3, 2, 1, 0.1
+    w.params, w.model_tag, w.ctrl_mode = 8, 8, 8  # non-null placeholders, never dereferenced
+    w.fleet_models, w.fleet_modes = 1 << 3, 1  # a drone fleet
+    rc = fwd(C.byref(w), 4, _lib.State(), None, _lib.State(), _lib.State(), None, _lib.Bodies(),
+             _lib.Bodies(), None, 0, None)
+    assert rc == -2
+    w.fleet_models = 1
+    w.n_agents = 5000
+    rc = fwd(C.byref(w), 4, _lib.State(), None, _lib.State(), _lib.State(), None, _lib.Bodies(),
+             _lib.Bodies(), None, 0, None)
+    assert rc == -3
+
+
+LAYOUT_C = r"""
+#include <stdio.h>
+#include <stddef.h>
+#include "swarp_b200.h"
+#define F(T, f) printf(#T "." #f " %zu\n", offsetof(T, f))
+int main(void) {
+  printf("swarp_world_t %zu\n", sizeof(swarp_world_t));
+  printf("swarp_obstacles_t %zu\n", sizeof(swarp_obstacles_t));
+  printf("swarp_state_t %zu\n", sizeof(swarp_state_t));
+  printf("swarp_bodies_t %zu\n", sizeof(swarp_bodies_t));
+  F(swarp_world_t, dt); F(swarp_world_t, collisions); F(swarp_world_t, k);
+  F(swarp_world_t, max_neighbors); F(swarp_world_t, bounds); F(swarp_world_t, params);
+  F(swarp_world_t, params_env_stride); F(swarp_world_t, fleet_models);
+  F(swarp_world_t, obstacles); F(swarp_obstacles_t, pos); F(swarp_obstacles_t, any_movable);
+  F(swarp_obstacles_t, bodies_move);
+  return 0;
+}
+"""
+
+
+def test_ctypes_layout_matches_c(tmp_path):
+    src = tmp_path / "layout.c"
+    src.write_text(LAYOUT_C)
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)],
+                   check=True)
+    out = dict(line.rsplit(" ", 1) for line in subprocess.check_output([str(exe)]).decode().split("\n")
+               if line)
+    assert int(out["swarp_world_t"]) == C.sizeof(_lib.WorldC)
+    assert int(out["swarp_obstacles_t"]) == C.sizeof(_lib.ObstaclesC)
+    assert int(out["swarp_state_t"]) == C.sizeof(_lib.State)
+    assert int(out["swarp_bodies_t"]) == C.sizeof(_lib.Bodies)
+    for key, val in out.items():
+        if "." not in key:
+            continue
+        struct, field = key.split(".")
+        cls = _lib.WorldC if struct == "swarp_world_t" else _lib.ObstaclesC
+        assert getattr(cls, field).offset == int(val), key

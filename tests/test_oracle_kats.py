@@ -1,0 +1,316 @@
+"""Pin the CPU oracle against the reference's known-answer tests (CPU only).
+
+Each case restates a known answer from the reference test-suite (ddebenedittis/swarp):
+numpy recurrences (``tests/unit/test_dynamics.py:28-93,137-381``), hand-computed
+contacts (``tests/unit/test_collisions.py:24-138``), analytic BPTT gradients
+(``tests/unit/test_gradients.py:174-221``) and the neighbor overflow flag
+(``tests/unit/test_neighbors.py:229-264``). The reference has no stored golden
+arrays; these in-test answers are what pins its behaviour.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import torch_ref as R
+from swarp_b200.dynamics.base import AgentConfig, ControlMode, DynamicsModel, param_rows
+
+D = torch.float64
+BIG = 100.0
+
+
+def world(cfgs, dt, **kw):
+    return R.RefWorld(
+        params=torch.tensor(param_rows(cfgs), dtype=D),
+        model_tag=[int(c.model) for c in cfgs],
+        ctrl_mode=[int(c.ctrl_mode) for c in cfgs],
+        dt=dt,
+        **kw,
+    )
+
+
+def state_of(pos, theta=None, vel=None, speed=None, ang_vel=None):
+    pos = torch.as_tensor(np.asarray(pos, dtype=np.float64)).reshape(1, -1, 2)
+    n = pos.shape[1]
+
+    def s(x):
+        return torch.zeros(1, n, dtype=D) if x is None else torch.as_tensor(
+            np.asarray(x, dtype=np.float64)).reshape(1, n)
+
+    v = torch.zeros(1, n, 2, dtype=D) if vel is None else torch.as_tensor(
+        np.asarray(vel, dtype=np.float64)).reshape(1, n, 2)
+    return (pos, s(theta), v, s(speed), s(ang_vel))
+
+
+def run(w, st, actions):
+    traj = []
+    for a in actions:
+        st, _, _ = R.step(st, torch.as_tensor(a, dtype=D).reshape(1, -1, 2), w)
+        traj.append(st)
+    return traj
+
+
+def _clamp_norm(v, limit):
+    n = np.linalg.norm(v)
+    return v * (limit / max(n, limit))
+
+
+@pytest.mark.parametrize("mode", [ControlMode.VELOCITY, ControlMode.ACCELERATION])
+def test_holonomic_recurrence(mode):
+    cfg = AgentConfig(model=DynamicsModel.HOLONOMIC, ctrl_mode=mode, max_speed=1.3, max_accel=2.0)
+    rng = np.random.default_rng(0)
+    T, dt = 100, 0.05
+    acts = 2.0 * rng.standard_normal((T, 1, 2))
+    traj = run(world([cfg], dt, collisions=False), state_of([[0.3, -0.2]], vel=[[0.1, 0.2]]), acts)
+    p, v = np.array([0.3, -0.2]), np.array([0.1, 0.2])
+    for t in range(T):
+        if mode == ControlMode.VELOCITY:
+            v = _clamp_norm(acts[t, 0], cfg.max_speed)
+        else:
+            v = _clamp_norm(v + _clamp_norm(acts[t, 0], cfg.max_accel) * dt, cfg.max_speed)
+        p = p + v * dt
+        np.testing.assert_allclose(traj[t][0][0, 0].numpy(), p, atol=1e-12)
+        np.testing.assert_allclose(traj[t][2][0, 0].numpy(), v, atol=1e-12)
+    assert traj[-1][1][0, 0].item() == 0.0
+    np.testing.assert_allclose(traj[-1][3][0, 0].item(), np.linalg.norm(v), atol=1e-12)
+
+
+@pytest.mark.parametrize("mode", list(ControlMode))
+def test_diff_drive_recurrence(mode):
+    cfg = AgentConfig(model=DynamicsModel.DIFF_DRIVE, ctrl_mode=mode, max_speed=1.0,
+                      max_accel=1.5, max_ang_vel=2.0, max_ang_accel=4.0, cmd_gain_v=1.1,
+                      cmd_gain_w=0.8)
+    rng = np.random.default_rng(1)
+    T, dt = 100, 0.05
+    acts = 2.0 * rng.standard_normal((T, 1, 2))
+    st = state_of([[0.0, 0.0]], theta=[0.7], speed=[0.2], ang_vel=[-0.3])
+    traj = run(world([cfg], dt, collisions=False), st, acts)
+    p, th, s, w = np.zeros(2), 0.7, 0.2, -0.3
+    for t in range(T):
+        a = acts[t, 0]
+        if mode == ControlMode.VELOCITY:
+            s_n = np.clip(a[0], -cfg.max_speed, cfg.max_speed)
+            w_n = np.clip(a[1], -cfg.max_ang_vel, cfg.max_ang_vel)
+        elif mode == ControlMode.SERVO:
+            tv = np.clip(a[0], -cfg.max_speed, cfg.max_speed) * cfg.cmd_gain_v
+            tw = np.clip(a[1], -cfg.max_ang_vel, cfg.max_ang_vel) * cfg.cmd_gain_w
+            dv, dw = cfg.max_accel * dt, cfg.max_ang_accel * dt
+            s_n = np.clip(s + np.clip(tv - s, -dv, dv), -cfg.max_speed, cfg.max_speed)
+            w_n = np.clip(w + np.clip(tw - w, -dw, dw), -cfg.max_ang_vel, cfg.max_ang_vel)
+        else:
+            s_n = np.clip(s + np.clip(a[0], -cfg.max_accel, cfg.max_accel) * dt,
+                          -cfg.max_speed, cfg.max_speed)
+            w_n = np.clip(w + np.clip(a[1], -cfg.max_ang_accel, cfg.max_ang_accel) * dt,
+                          -cfg.max_ang_vel, cfg.max_ang_vel)
+        vt = s_n * np.array([np.cos(th), np.sin(th)])
+        p = p + vt * dt
+        th = th + w_n * dt
+        s, w = s_n, w_n
+        got = traj[t]
+        np.testing.assert_allclose(got[0][0, 0].numpy(), p, atol=1e-12)
+        np.testing.assert_allclose(got[1][0, 0].item(), th, atol=1e-12)
+        np.testing.assert_allclose(got[2][0, 0].numpy(), vt, atol=1e-12)
+        np.testing.assert_allclose(got[3][0, 0].item(), s, atol=1e-12)
+        np.testing.assert_allclose(got[4][0, 0].item(), w, atol=1e-12)
+
+
+def _bicycle_ref(p, th, s, acts, cfg, dt):
+    wb = cfg.l_f + cfg.l_r
+    out = []
+    lo = -cfg.max_speed if cfg.min_speed is None else cfg.min_speed
+    for a in acts:
+        acc = np.clip(a[0], -cfg.max_accel, cfg.max_accel)
+        delta = np.clip(a[1], -cfg.max_steer, cfg.max_steer)
+        s = np.clip(s + acc * dt, lo, cfg.max_speed)
+        beta = np.arctan2(np.tan(delta) * cfg.l_r / wb, 1.0)
+        vt = s * np.array([np.cos(th + beta), np.sin(th + beta)])
+        w = s / wb * np.cos(beta) * np.tan(delta)
+        p = p + vt * dt
+        th = th + w * dt
+        out.append((p.copy(), th, vt, s, w))
+    return out
+
+
+def test_bicycle_recurrence():
+    cfg = AgentConfig(model=DynamicsModel.KINEMATIC_BICYCLE, ctrl_mode=ControlMode.ACCELERATION,
+                      max_speed=2.0, max_accel=1.0, l_f=0.16, l_r=0.14, max_steer=0.6)
+    rng = np.random.default_rng(2)
+    T, dt = 100, 0.05
+    acts = 2.0 * rng.standard_normal((T, 1, 2))
+    traj = run(world([cfg], dt, collisions=False),
+               state_of([[1.0, -1.0]], theta=[-0.5], speed=[0.5]), acts)
+    ref = _bicycle_ref(np.array([1.0, -1.0]), -0.5, 0.5, acts[:, 0], cfg, dt)
+    for t in range(T):
+        np.testing.assert_allclose(traj[t][0][0, 0].numpy(), ref[t][0], atol=1e-12)
+        np.testing.assert_allclose(traj[t][1][0, 0].item(), ref[t][1], atol=1e-12)
+        np.testing.assert_allclose(traj[t][3][0, 0].item(), ref[t][3], atol=1e-12)
+        np.testing.assert_allclose(traj[t][4][0, 0].item(), ref[t][4], atol=1e-12)
+
+
+def test_bicycle_straight_line_analytic():
+    cfg = AgentConfig(model=DynamicsModel.KINEMATIC_BICYCLE, max_speed=10.0, max_accel=1.0,
+                      l_f=0.15, l_r=0.15, max_steer=0.6)
+    T, dt, acc = 20, 0.1, 0.8
+    traj = run(world([cfg], dt, collisions=False), state_of([[0.0, 0.0]]),
+               np.tile(np.array([acc, 0.0]), (T, 1, 1)))
+    np.testing.assert_allclose(traj[-1][0][0, 0].numpy(),
+                               [acc * dt * dt * T * (T + 1) / 2, 0.0], atol=1e-12)
+    np.testing.assert_allclose(traj[-1][3][0, 0].item(), acc * dt * T, atol=1e-12)
+
+
+def test_bicycle_min_speed_brakes_to_a_stop():
+    cfg = AgentConfig(model=DynamicsModel.KINEMATIC_BICYCLE, max_speed=5.0, max_accel=1.0,
+                      l_f=1.25, l_r=1.25, max_steer=0.6, min_speed=0.0)
+    traj = run(world([cfg], 0.1, collisions=False),
+               state_of([[0.0, 0.0]], vel=[[0.5, 0.0]], speed=[0.5]),
+               np.tile(np.array([-1.0, 0.3]), (30, 1, 1)))
+    speeds = np.array([s[3][0, 0].item() for s in traj])
+    assert speeds.min() == 0.0 and speeds[-1] == 0.0
+    stopped = int(np.argmax(speeds == 0.0))
+    assert torch.equal(traj[stopped][0], traj[-1][0])
+
+
+def test_clamping_saturates():
+    dt = 0.1
+    big = np.array([[[100.0, 100.0]]])
+    h = AgentConfig(model=DynamicsModel.HOLONOMIC, max_speed=1.0)
+    out = run(world([h], dt, collisions=False), state_of([[0.0, 0.0]]), big)
+    np.testing.assert_allclose(np.linalg.norm(out[0][2][0, 0].numpy()), 1.0, atol=1e-12)
+    b = AgentConfig(model=DynamicsModel.KINEMATIC_BICYCLE, max_speed=1.0, max_accel=0.5,
+                    max_steer=0.3, l_f=0.1, l_r=0.1)
+    out = run(world([b], dt, collisions=False), state_of([[0.0, 0.0]]), big)
+    np.testing.assert_allclose(out[0][3][0, 0].item(), 0.5 * dt, atol=1e-12)
+    ref = _bicycle_ref(np.zeros(2), 0.0, 0.0, np.array([[100.0, 100.0]]), b, dt)
+    np.testing.assert_allclose(out[0][1][0, 0].item(), ref[0][1], atol=1e-12)
+
+
+def holo(n, radius=0.1, mode=ControlMode.VELOCITY):
+    return [AgentConfig(model=DynamicsModel.HOLONOMIC, ctrl_mode=mode, radius=radius,
+                        max_speed=BIG, max_accel=BIG) for _ in range(n)]
+
+
+def test_two_agent_spring_analytic():
+    w = world(holo(2), 0.1, k=100.0, c=0.0, margin=0.02, neighbor_radius=0.22)
+    st, _, _ = R.step(state_of([[0.0, 0.0], [0.15, 0.0]]), torch.zeros(1, 2, 2, dtype=D), w)
+    np.testing.assert_allclose(st[0][0, 0].numpy(), [-0.07, 0.0], atol=1e-12)
+    np.testing.assert_allclose(st[0][0, 1].numpy(), [0.22, 0.0], atol=1e-12)
+    np.testing.assert_allclose(st[2][0, 0].numpy(), [-0.7, 0.0], atol=1e-12)
+
+
+def test_two_agent_spring_damper_analytic():
+    w = world(holo(2, mode=ControlMode.ACCELERATION), 0.1, k=100.0, c=2.0, margin=0.02,
+              neighbor_radius=0.22)
+    st, _, _ = R.step(state_of([[0.0, 0.0], [0.15, 0.0]], vel=[[0.5, 0.0], [-0.5, 0.0]]),
+                      torch.zeros(1, 2, 2, dtype=D), w)
+    # coeff = (100*0.07 + 2*1) / (1 + 2*0.1/1) = 7.5 -> v0 = 0.5 - 0.75
+    np.testing.assert_allclose(st[2][0, 0].numpy(), [-0.25, 0.0], atol=1e-12)
+    np.testing.assert_allclose(st[0][0, 0].numpy(), [-0.025, 0.0], atol=1e-12)
+    np.testing.assert_allclose(st[2][0, 1].numpy(), [0.25, 0.0], atol=1e-12)
+
+
+def test_momentum_symmetry():
+    w = world(holo(4, mode=ControlMode.ACCELERATION), 0.05, substeps=2, k=50.0, c=0.5,
+              margin=0.05, neighbor_radius=0.25)
+    rng = np.random.default_rng(0)
+    pos0 = rng.random((4, 2)) * 0.2
+    st = state_of(pos0)
+    com0 = st[0].mean(1)
+    for _ in range(20):
+        st, _, _ = R.step(st, torch.zeros(1, 4, 2, dtype=D), w)
+    torch.testing.assert_close(st[0].mean(1), com0, atol=1e-10, rtol=0)
+    assert (st[0][0, 0] - st[0][0, 1]).norm() > np.linalg.norm(pos0[0] - pos0[1])
+
+
+def _circle_obstacles(pos, radius):
+    pos = torch.tensor(pos, dtype=D)
+    E, N = pos.shape[0], pos.shape[1]
+    return R.RefObstacles(pos=pos, angle=torch.zeros(E, N, dtype=D),
+                          vel=torch.zeros(E, N, 2, dtype=D), ang_vel=torch.zeros(E, N, dtype=D),
+                          radius=torch.tensor(radius, dtype=D), half=torch.zeros(N, 2, dtype=D),
+                          shape=[0] * N, kind=[0] * N)
+
+
+def test_obstacle_repulsion_analytic():
+    w = world(holo(1), 0.1, k=100.0, c=0.0, margin=0.02, neighbor_radius=0.22)
+    st, _, _ = R.step(state_of([[0.1, 0.0]]), torch.zeros(1, 1, 2, dtype=D), w,
+                      _circle_obstacles([[[0.3, 0.0]]], [0.15]))
+    np.testing.assert_allclose(st[0][0, 0].numpy(), [0.1 - 0.07, 0.0], atol=1e-12)
+
+
+def test_soft_wall_analytic():
+    w = world(holo(1, radius=0.05), 0.1, k=100.0, c=0.0, margin=0.02, neighbor_radius=0.12,
+              bounds=(-1.0, 1.0, -1.0, 1.0), soft_walls=True)
+    st, _, _ = R.step(state_of([[0.95, 0.0]]), torch.zeros(1, 1, 2, dtype=D), w)
+    np.testing.assert_allclose(st[0][0, 0].numpy(), [0.95 - 0.02, 0.0], atol=1e-12)
+
+
+def test_clamp_bounds():
+    w = world(holo(1, radius=0.05), 0.1, collisions=False, bounds=(-1.0, 1.0, -1.0, 1.0),
+              clamp_bounds=True)
+    st, _, _ = R.step(state_of([[0.98, 0.0]]), torch.tensor([[[5.0, 0.0]]], dtype=D), w)
+    np.testing.assert_allclose(st[0][0, 0].numpy(), [0.95, 0.0], atol=1e-12)
+
+
+def _grad_state(seed, n=1):
+    g = torch.Generator().manual_seed(seed)
+    return tuple(torch.randn(*s, generator=g, dtype=D) * 0.5
+                 for s in ((1, n, 2), (1, n), (1, n, 2), (1, n), (1, n)))
+
+
+def test_bptt_analytic_holonomic():
+    T, dt = 6, 0.1
+    w = world([AgentConfig(model=DynamicsModel.HOLONOMIC, max_speed=BIG)], dt, collisions=False)
+    acts = (0.2 * torch.randn(T, 1, 1, 2, dtype=D)).requires_grad_(True)
+    final, _, _ = R.rollout(_grad_state(4), acts, w)
+    final[0][0, 0, 0].backward()
+    expected = torch.zeros_like(acts)
+    expected[:, 0, 0, 0] = dt
+    torch.testing.assert_close(acts.grad, expected)
+
+
+def test_bptt_analytic_holonomic_accel():
+    dt = 0.1
+    w = world([AgentConfig(model=DynamicsModel.HOLONOMIC, ctrl_mode=ControlMode.ACCELERATION,
+                           max_speed=BIG, max_accel=BIG)], dt, collisions=False)
+    acts = (0.2 * torch.randn(2, 1, 1, 2, dtype=D)).requires_grad_(True)
+    final, _, _ = R.rollout(_grad_state(5), acts, w)
+    final[0][0, 0, 0].backward()
+    torch.testing.assert_close(acts.grad[0, 0, 0, 0], torch.tensor(2 * dt * dt, dtype=D))
+
+
+def test_grads_zero_when_saturated():
+    w = world([AgentConfig(model=DynamicsModel.DIFF_DRIVE, max_speed=1.0, max_ang_vel=1.0)], 0.1,
+              collisions=False)
+    acts = torch.full((1, 1, 2), 50.0, dtype=D, requires_grad=True)
+    st, _, _ = R.step(_grad_state(6), acts, w)
+    st[0].sum().backward()
+    assert torch.isfinite(acts.grad).all() and acts.grad.abs().sum() == 0.0
+
+
+def test_neighbor_overflow_flag():
+    pos = torch.zeros(1, 5, 2, dtype=D)
+    pos[0, :, 0] = torch.linspace(0.0, 0.04, 5, dtype=D)
+    in_list, idx, cnt, true = R.brute_neighbors(pos, 0.5, 2)
+    assert torch.equal(true, torch.full((1, 5), 4))
+    assert torch.equal(cnt, torch.full((1, 5), 2))
+    for a in range(5):
+        picked = set(idx[0, a, :2].tolist())
+        assert len(picked) == 2 and a not in picked
+        # first two by index
+        assert sorted(picked) == [b for b in range(5) if b != a][:2]
+    _, _, cnt8, _ = R.brute_neighbors(pos, 0.5, 8)
+    assert torch.equal(cnt8, true)
+
+
+def test_gradcheck_oracle_with_collisions_and_walls():
+    w = world(holo(2, mode=ControlMode.ACCELERATION), 0.1, substeps=2, k=10.0, c=1.0,
+              margin=0.02, neighbor_radius=0.22, bounds=(-1.0, 1.0, -1.0, 1.0), soft_walls=True)
+    st = state_of([[0.0, 0.0], [0.18, 0.02]], vel=[[0.1, 0.0], [-0.1, 0.05]])
+    acts = 0.1 * torch.randn(1, 2, 2, dtype=D, generator=torch.Generator().manual_seed(0))
+
+    def fn(pos, th, vel, sp, om, act):
+        out, _, _ = R.step((pos, th, vel, sp, om), act, w)
+        return out
+
+    inputs = tuple(t.clone().requires_grad_(True) for t in (*st, acts))
+    assert torch.autograd.gradcheck(fn, inputs, eps=1e-6, atol=1e-5)
