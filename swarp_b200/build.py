@@ -16,13 +16,12 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libswarp_b200.so")
-SOURCES = ["capi.cu"]
-DEPS = ["capi.cu", "rollout.cuh", "physics.cuh"]
+SOURCES = ["capi.cu", "k_fwd_f32.cu", "k_fwd_f64.cu", "k_bwd_f32.cu", "k_bwd_f64.cu"]
+DEPS = [*SOURCES, "launch.cuh", "rollout.cuh", "physics.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-FLAGS = [
-    "-O3", "-lineinfo", "-std=c++17", "--extended-lambda", "-fmad=false",
-    "-Xcompiler", "-fPIC", "-Xcompiler", "-O2", "--shared", "-cudart", "shared",
-]
+FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--extended-lambda", "-fmad=false",
+         "-Xcompiler", "-fPIC", "-Xcompiler", "-O2"]
+LINK = ["--shared", "-cudart", "shared"]
 
 
 def nvcc() -> str:
@@ -44,8 +43,20 @@ def build(force: bool = False, verbose: bool = False, extra: list[str] | None = 
     deps = [os.path.join(CSRC, d) for d in DEPS]
     if not force and not _stale(LIB, deps):
         return LIB
-    cmd = [nvcc(), *ARCH, *FLAGS, *(extra or []), "-o", LIB + ".tmp",
-           *[os.path.join(CSRC, s) for s in SOURCES]]
+    objdir = os.path.join(HERE, "_build")
+    os.makedirs(objdir, exist_ok=True)
+    objs, procs = [], []
+    for src in SOURCES:
+        obj = os.path.join(objdir, src.replace(".cu", ".o"))
+        cmd = [nvcc(), *ARCH, *FLAGS, *(extra or []), "-c", "-o", obj, os.path.join(CSRC, src)]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        procs.append(subprocess.Popen(cmd))
+        objs.append(obj)
+    failed = [p.args[-1] for p in procs if p.wait() != 0]
+    if failed:
+        raise RuntimeError(f"nvcc failed on {failed}")
+    cmd = [nvcc(), *ARCH, *LINK, "-o", LIB + ".tmp", *objs]
     if verbose:
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)

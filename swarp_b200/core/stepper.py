@@ -123,11 +123,15 @@ class Stepper:
         #: swarp/core/stepper.py:593-601).
         self.bodies_in_grad = True
         self.body_state: tuple[torch.Tensor, ...] | None = None
+        # (n_envs, act_dim) -> filled swarp_world_t; cleared whenever an input it points to
+        # is replaced (obstacles, per-env parameters).
+        self._wc_cache: dict[tuple[int, int], _lib.WorldC] = {}
 
     # ----------------------------------------------------------------- set-up
     def set_obstacles(self, obstacles: Obstacles) -> None:
         """Install (or refresh) an obstacle set; absent fields take their defaults."""
         obs = obstacles.resolve(self.device, self.dtype)
+        self._wc_cache.clear()
         self.obstacles = obs
         self.n_obstacles = obs.n_obstacles
         self.any_movable = bool((obs.kind != 0).any().item())
@@ -168,10 +172,19 @@ class Stepper:
                     f"per-env radius up to {max_r} needs neighbor_radius >= {reach}, but "
                     f"neighbor_radius={self.neighbor_radius}; set WorldConfig.neighbor_radius."
                 )
+        self._wc_cache.clear()
         self.params_per_env = t.detach().to(device=self.device, dtype=self.dtype).contiguous()
 
     # ------------------------------------------------------------- C world
     def world_c(self, n_envs: int, act_dim: int) -> _lib.WorldC:
+        key = (n_envs, act_dim)
+        wc = self._wc_cache.get(key)
+        if wc is None:
+            wc = self._build_world_c(n_envs, act_dim)
+            self._wc_cache[key] = wc
+        return wc
+
+    def _build_world_c(self, n_envs: int, act_dim: int) -> _lib.WorldC:
         w = self.world
         wc = _lib.WorldC()
         wc.dtype = 0 if self.dtype == torch.float32 else 1

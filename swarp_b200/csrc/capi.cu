@@ -8,7 +8,7 @@
 #include <limits>
 
 #include "../../include/swarp_b200.h"
-#include "rollout.cuh"
+#include "launch.cuh"
 
 using namespace swarp;
 
@@ -76,7 +76,10 @@ int flags_of(const swarp_world_t* w) {
   int fl = 0;
   if (w->collisions) {
     fl |= F_COLL;
-    if (w->n_agents - 1 > w->max_neighbors) fl |= F_TRUNC;
+    if (w->n_agents - 1 > w->max_neighbors)
+      fl |= F_TRUNC;
+    else if (w->n_agents <= 32)
+      fl |= F_MASK;
   }
   if (w->obstacles.n_obstacles > 0) fl |= F_OBS;
   if (w->fleet_models == 1 && w->fleet_modes == 1) fl |= F_HOLOVEL;
@@ -142,59 +145,6 @@ void set_state_out(const swarp_state_t& s, T*& p, T*& th, T*& v, T*& sp, T*& w) 
   w = static_cast<T*>(s.ang_vel);
 }
 
-template <typename Kernel>
-int launch(Kernel k, int grid, int block, size_t smem, cudaStream_t st, const void* args_ptr) {
-  (void)args_ptr;
-  if (smem > 48 * 1024) {
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-      return SWARP_ERR_CUDA;
-  }
-  return SWARP_OK;
-}
-
-#define SWARP_DISPATCH(FLV, KERNEL, T, ...)                       \
-  switch (FLV) {                                                  \
-    case 0: KERNEL<T, 0>__VA_ARGS__; break;                       \
-    case 1: KERNEL<T, 1>__VA_ARGS__; break;                       \
-    case 3: KERNEL<T, 3>__VA_ARGS__; break;                       \
-    case 4: KERNEL<T, 4>__VA_ARGS__; break;                       \
-    case 5: KERNEL<T, 5>__VA_ARGS__; break;                       \
-    case 7: KERNEL<T, 7>__VA_ARGS__; break;                       \
-    case 8: KERNEL<T, 8>__VA_ARGS__; break;                       \
-    case 9: KERNEL<T, 9>__VA_ARGS__; break;                       \
-    case 11: KERNEL<T, 11>__VA_ARGS__; break;                     \
-    case 12: KERNEL<T, 12>__VA_ARGS__; break;                     \
-    case 13: KERNEL<T, 13>__VA_ARGS__; break;                     \
-    case 15: KERNEL<T, 15>__VA_ARGS__; break;                     \
-    default: return SWARP_ERR_UNSUPPORTED;                        \
-  }
-
-template <typename T, int FL>
-int run_fwd(const RolloutArgs<T>& R, cudaStream_t st) {
-  const int grid = (R.E + R.G - 1) / R.G;
-  const int block = R.G * R.A;
-  const size_t smem = Smem<T>::fwd(block, R.G * R.N);
-  auto k = rollout_fwd_kernel<T, FL>;
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-    return SWARP_ERR_CUDA;
-  k<<<grid, block, smem, st>>>(R);
-  return cudaGetLastError() == cudaSuccess ? SWARP_OK : SWARP_ERR_CUDA;
-}
-
-template <typename T, int FL>
-int run_bwd(const RolloutArgs<T>& R, cudaStream_t st) {
-  const int grid = (R.E + R.G - 1) / R.G;
-  const int block = R.G * R.A;
-  const size_t smem = Smem<T>::bwd(block, R.G * R.N, R.S);
-  auto k = rollout_bwd_kernel<T, FL>;
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-    return SWARP_ERR_CUDA;
-  k<<<grid, block, smem, st>>>(R);
-  return cudaGetLastError() == cudaSuccess ? SWARP_OK : SWARP_ERR_CUDA;
-}
-
 template <typename T>
 int fwd_typed(const swarp_world_t* w, int horizon, swarp_state_t init, const void* actions,
               swarp_state_t traj, swarp_state_t fin, int32_t* true_max, void* ws,
@@ -206,11 +156,10 @@ int fwd_typed(const swarp_world_t* w, int horizon, swarp_state_t init, const voi
   set_state_out<T>(traj, R.t_pos, R.t_th, R.t_vel, R.t_s, R.t_w);
   set_state_out<T>(fin, R.f_pos, R.f_th, R.f_vel, R.f_s, R.f_w);
   R.true_max = true_max;
-  R.cutoff = static_cast<int16_t*>(ws);
   const int fl = flags_of(w);
-  int rc = SWARP_OK;
-  SWARP_DISPATCH(fl, rc = run_fwd, T, (R, st))
-  return rc;
+  R.cutoff = (fl & F_TRUNC) ? static_cast<int16_t*>(ws) : nullptr;
+  R.cmask = (fl & F_MASK) ? static_cast<uint32_t*>(ws) : nullptr;
+  return launch_fwd<T>(R, fl, st);
 }
 
 template <typename T>
@@ -226,11 +175,10 @@ int bwd_typed(const swarp_world_t* w, int horizon, swarp_state_t init, const voi
   set_state<T>(gfin, R.gf_pos, R.gf_th, R.gf_vel, R.gf_s, R.gf_w);
   R.g_act = static_cast<T*>(gact);
   set_state_out<T>(ginit, R.gi_pos, R.gi_th, R.gi_vel, R.gi_s, R.gi_w);
-  R.cutoff = const_cast<int16_t*>(static_cast<const int16_t*>(ws));
   const int fl = flags_of(w);
-  int rc = SWARP_OK;
-  SWARP_DISPATCH(fl, rc = run_bwd, T, (R, st))
-  return rc;
+  R.cutoff = (fl & F_TRUNC) ? const_cast<int16_t*>(static_cast<const int16_t*>(ws)) : nullptr;
+  R.cmask = (fl & F_MASK) ? const_cast<uint32_t*>(static_cast<const uint32_t*>(ws)) : nullptr;
+  return launch_bwd<T>(R, fl, st);
 }
 
 template <typename T>
@@ -238,15 +186,8 @@ int nbr_typed(const swarp_world_t* w, const void* pos, int32_t* idx, int32_t* co
               int32_t* true_count, cudaStream_t st) {
   const int E = w->n_envs, A = w->n_agents;
   const int G = envs_per_cta(A, E);
-  const int grid = (E + G - 1) / G;
-  const size_t smem = (size_t)G * A * sizeof(typename V4<T>::t);
-  auto k = neighbors_kernel<T>;
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-    return SWARP_ERR_CUDA;
-  k<<<grid, G * A, smem, st>>>(E, A, G, w->max_neighbors, radius_sq_threshold<T>(w->neighbor_radius),
-                               static_cast<const T*>(pos), idx, count, true_count);
-  return cudaGetLastError() == cudaSuccess ? SWARP_OK : SWARP_ERR_CUDA;
+  return launch_neighbors<T>(E, A, G, w->max_neighbors, radius_sq_threshold<T>(w->neighbor_radius),
+                             static_cast<const T*>(pos), idx, count, true_count, st);
 }
 
 }  // namespace
@@ -255,10 +196,11 @@ extern "C" {
 
 size_t swarp_rollout_workspace_bytes(const swarp_world_t* w, int32_t horizon) {
   if (validate_world(w, horizon) != SWARP_OK) return 0;
-  size_t bytes = 0;
-  if (flags_of(w) & F_TRUNC)
-    bytes += (size_t)horizon * w->substeps * (size_t)w->n_envs * w->n_agents * sizeof(int16_t);
-  return bytes;
+  const size_t cells = (size_t)horizon * w->substeps * (size_t)w->n_envs * w->n_agents;
+  const int fl = flags_of(w);
+  if (fl & F_TRUNC) return cells * sizeof(int16_t);  // list cutoffs
+  if (fl & F_MASK) return cells * sizeof(uint32_t);  // contact masks
+  return 0;
 }
 
 int swarp_rollout_fwd(const swarp_world_t* w, int32_t horizon, swarp_state_t init,

@@ -1,0 +1,99 @@
+// Kernel-instance selection. The launchers are defined in one translation unit per
+// (direction, dtype) (k_*.cu) so the instances compile in parallel; capi.cu only
+// declares them.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <type_traits>
+
+#include "rollout.cuh"
+
+namespace swarp {
+
+constexpr int kErrUnsupported = -2;
+constexpr int kErrCuda = -4;
+
+template <typename T> int launch_fwd(const RolloutArgs<T>& R, int fl, cudaStream_t st);
+template <typename T> int launch_bwd(const RolloutArgs<T>& R, int fl, cudaStream_t st);
+template <typename T>
+int launch_neighbors(int E, int A, int G, int K, T r2, const T* pos, int* idx, int* cnt, int* tru,
+                     cudaStream_t st);
+
+#ifdef SWARP_DEFINE_LAUNCHERS
+
+template <typename K>
+inline int launch_kernel(K kernel, int grid, int block, size_t smem, cudaStream_t st,
+                         const void* arg) {
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+          cudaSuccess)
+    return kErrCuda;
+  void* args[] = {const_cast<void*>(arg)};
+  return cudaLaunchKernel(reinterpret_cast<const void*>(kernel), dim3(grid), dim3(block), args, smem,
+                          st) == cudaSuccess
+             ? 0
+             : kErrCuda;
+}
+
+template <typename T, int FL, int AS>
+int run_fwd(const RolloutArgs<T>& R, cudaStream_t st) {
+  const Layout<T> L(R.G, R.A, R.N, R.S, false);
+  return launch_kernel(rollout_fwd_kernel<T, FL, AS>, (R.E + R.G - 1) / R.G, R.G * R.A, L.total,
+                       st, &R);
+}
+template <typename T, int FL, int AS>
+int run_bwd(const RolloutArgs<T>& R, cudaStream_t st) {
+  const Layout<T> L(R.G, R.A, R.N, R.S, true);
+  return launch_kernel(rollout_bwd_kernel<T, FL, AS>, (R.E + R.G - 1) / R.G, R.G * R.A, L.total,
+                       st, &R);
+}
+
+// Every valid flag combination: no contacts, contacts, truncating contacts, checkpointed
+// contacts; each with/without obstacles and with/without the holonomic-velocity fleet.
+#define SWARP_FLAG_CASES(X) \
+  X(0) X(4) X(8) X(12) X(1) X(5) X(9) X(13) X(3) X(7) X(11) X(15) X(17) X(21) X(25) X(29)
+
+template <typename T> int launch_fwd(const RolloutArgs<T>& R, int fl, cudaStream_t st) {
+  const bool a16 = std::is_same<T, float>::value && R.A == 16;
+  switch (fl) {
+#define SWARP_X(F)                                                          \
+  case F:                                                                   \
+    if constexpr (std::is_same<T, float>::value && ((F) & F_COLL))          \
+      if (a16) return run_fwd<T, F, 16>(R, st);                             \
+    return run_fwd<T, F, 0>(R, st);
+    SWARP_FLAG_CASES(SWARP_X)
+#undef SWARP_X
+  }
+  return kErrUnsupported;
+}
+
+template <typename T> int launch_bwd(const RolloutArgs<T>& R, int fl, cudaStream_t st) {
+  const bool a16 = std::is_same<T, float>::value && R.A == 16;
+  switch (fl) {
+#define SWARP_X(F)                                                          \
+  case F:                                                                   \
+    if constexpr (std::is_same<T, float>::value && ((F) & F_COLL))          \
+      if (a16) return run_bwd<T, F, 16>(R, st);                             \
+    return run_bwd<T, F, 0>(R, st);
+    SWARP_FLAG_CASES(SWARP_X)
+#undef SWARP_X
+  }
+  return kErrUnsupported;
+}
+
+template <typename T>
+int launch_neighbors(int E, int A, int G, int K, T r2, const T* pos, int* idx, int* cnt, int* tru,
+                     cudaStream_t st) {
+  const size_t smem = ((size_t(G) * ((A + 1) / 2) * 4 * sizeof(T) + 15) & ~size_t(15)) +
+                      size_t(G) * A * 4 * sizeof(T);
+  auto k = neighbors_kernel<T>;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return kErrCuda;
+  k<<<(E + G - 1) / G, G * A, smem, st>>>(E, A, G, K, r2, pos, idx, cnt, tru);
+  return cudaGetLastError() == cudaSuccess ? 0 : kErrCuda;
+}
+
+#endif  // SWARP_DEFINE_LAUNCHERS
+
+}  // namespace swarp

@@ -35,6 +35,7 @@ template <> struct Num<float> {
   static __device__ __forceinline__ float tan_(float x) { return ::tanf(x); }
   static __device__ __forceinline__ float atan_(float x) { return ::atanf(x); }
   static __device__ __forceinline__ float tanh_(float x) { return ::tanhf(x); }
+  static __device__ __forceinline__ float rsqrt_(float x) { return ::rsqrtf(x); }
 };
 template <> struct Num<double> {
   static __device__ __forceinline__ double sqrt_(double x) { return ::sqrt(x); }
@@ -44,6 +45,7 @@ template <> struct Num<double> {
   static __device__ __forceinline__ double tan_(double x) { return ::tan(x); }
   static __device__ __forceinline__ double atan_(double x) { return ::atan(x); }
   static __device__ __forceinline__ double tanh_(double x) { return ::tanh(x); }
+  static __device__ __forceinline__ double rsqrt_(double x) { return ::rsqrt(x); }
 };
 
 template <typename T> __device__ __forceinline__ T wmax(T a, T b) { return a > b ? a : b; }
@@ -73,7 +75,7 @@ template <typename T> struct AgentP {
   T radius, mass, max_speed, min_speed, max_accel, max_ang_vel, max_ang_accel;
   T l_f, l_r, max_steer, gain_v, gain_w;
   T dt_over_m;  // sub_dt / mass  (the reference's force * (dt / mass))
-  T denom;      // 1 + c * sub_dt / mass  (implicit damping denominator)
+  T inv_denom;  // 1 / (1 + c * sub_dt / mass): implicit damping denominator, inverted once
   int tag, mode;
 };
 
@@ -89,26 +91,35 @@ template <typename T> struct WorldC {
 };
 
 // ------------------------------------------------------------------- contact law
+// Division and square root are formulated with one reciprocal square root and
+// multiplications by reciprocals precomputed per agent (the reference divides); the
+// forward and adjoint kernels use the same formulation, so every recomputed branch
+// decision is bitwise the forward's.
+//
+// Depth saturation mo * tanh(ov / mo) (contact_max_overlap > 0 only): a cold call, so the
+// common unsaturated contact stays a handful of instructions.
+template <typename T> __device__ __noinline__ T tanh_ratio(T ov, T mo) { return Num<T>::tanh_(ov / mo); }
+
 // f = max(0, (k*ov' - c*vn) / denom), ov' = mo*tanh(ov/mo) when mo > 0
 template <typename T>
-__device__ __forceinline__ T normal_coeff(T ov, T vn, T denom, const WorldC<T>& W) {
+__device__ __forceinline__ T normal_coeff(T ov, T vn, T inv_denom, const WorldC<T>& W) {
   T ovs = ov;
-  if (W.max_overlap > T(0)) ovs = W.max_overlap * Num<T>::tanh_(ov / W.max_overlap);
-  T x = (W.k * ovs - W.c * vn) / denom;
+  if (W.max_overlap > T(0)) ovs = W.max_overlap * tanh_ratio(ov, W.max_overlap);
+  T x = (W.k * ovs - W.c * vn) * inv_denom;
   return wmax(x, T(0));
 }
 // VJP of normal_coeff: cotangent g on its value -> (d ov, d vn)
 template <typename T>
-__device__ __forceinline__ void normal_coeff_vjp(T ov, T vn, T denom, T g, const WorldC<T>& W,
+__device__ __forceinline__ void normal_coeff_vjp(T ov, T vn, T inv_denom, T g, const WorldC<T>& W,
                                                  T& gov, T& gvn) {
   T ovs = ov, th = T(0);
   if (W.max_overlap > T(0)) {
-    th = Num<T>::tanh_(ov / W.max_overlap);
+    th = tanh_ratio(ov, W.max_overlap);
     ovs = W.max_overlap * th;
   }
-  T x = (W.k * ovs - W.c * vn) / denom;
+  T x = (W.k * ovs - W.c * vn) * inv_denom;
   if (x > T(0)) {
-    T gnum = g / denom;
+    T gnum = g * inv_denom;
     T govs = W.k * gnum;
     gvn = -W.c * gnum;
     gov = (W.max_overlap > T(0)) ? govs * (T(1) - th * th) : govs;
@@ -120,52 +131,103 @@ __device__ __forceinline__ void normal_coeff_vjp(T ov, T vn, T denom, T g, const
 
 // Disc-disc contact: force on self, d = p_self - p_other, rv = v_self - v_other.
 // d2 is dot(d, d) as computed by the caller (the membership test reuses it).
+// Returns whether the pair is in contact (overlap > 0).
 template <typename T>
-__device__ __forceinline__ void pair_force_add(T dx, T dy, T d2, T rvx, T rvy, T min_dist, T denom,
-                                               const WorldC<T>& W, T& fx, T& fy) {
-  T dist = Num<T>::sqrt_(wmax(d2, Eps2<T>::v));
-  T ov = min_dist - dist;
+__device__ __forceinline__ bool pair_force_add(T dx, T dy, T d2, T rvx, T rvy, T min_dist,
+                                               T inv_denom, const WorldC<T>& W, T& fx, T& fy) {
+  const T m = wmax(d2, Eps2<T>::v);
+  const T inv = Num<T>::rsqrt_(m);
+  const T ov = min_dist - m * inv;
   if (ov > T(0)) {
-    T nx = dx / dist, ny = dy / dist;
+    T nx = dx * inv, ny = dy * inv;
     T vn = dot2(rvx, rvy, nx, ny);
-    T cf = normal_coeff(ov, vn, denom, W);
+    T cf = normal_coeff(ov, vn, inv_denom, W);
     fx = fx + cf * nx;
     fy = fy + cf * ny;
+    return true;
   }
+  return false;
 }
 // Force value (no accumulation), used where the result is negated/levered.
 template <typename T>
-__device__ __forceinline__ void pair_force(T dx, T dy, T rvx, T rvy, T min_dist, T denom,
+__device__ __forceinline__ void pair_force(T dx, T dy, T rvx, T rvy, T min_dist, T inv_denom,
                                            const WorldC<T>& W, T& fx, T& fy) {
   fx = T(0);
   fy = T(0);
-  pair_force_add(dx, dy, dot2(dx, dy, dx, dy), rvx, rvy, min_dist, denom, W, fx, fy);
+  pair_force_add(dx, dy, dot2(dx, dy, dx, dy), rvx, rvy, min_dist, inv_denom, W, fx, fy);
 }
 
 // VJP of pair_force: cotangent (gx, gy) on f -> adds to (gdx, gdy) and (grvx, grvy).
 template <typename T>
-__device__ __forceinline__ void pair_force_vjp(T dx, T dy, T rvx, T rvy, T min_dist, T denom,
+__device__ __forceinline__ void pair_force_vjp(T dx, T dy, T rvx, T rvy, T min_dist, T inv_denom,
                                                T gx, T gy, const WorldC<T>& W, T& gdx, T& gdy,
                                                T& grvx, T& grvy) {
-  T d2 = dot2(dx, dy, dx, dy);
-  T dist = Num<T>::sqrt_(wmax(d2, Eps2<T>::v));
-  T ov = min_dist - dist;
+  const T d2 = dot2(dx, dy, dx, dy);
+  const T m = wmax(d2, Eps2<T>::v);
+  const T inv = Num<T>::rsqrt_(m);
+  const T ov = min_dist - m * inv;
   if (!(ov > T(0))) return;
-  T nx = dx / dist, ny = dy / dist;
+  T nx = dx * inv, ny = dy * inv;
   T vn = dot2(rvx, rvy, nx, ny);
-  T cf = normal_coeff(ov, vn, denom, W);
+  T cf = normal_coeff(ov, vn, inv_denom, W);
   T gcf = dot2(gx, gy, nx, ny);
   T gnx = cf * gx, gny = cf * gy;
   T gov, gvn;
-  normal_coeff_vjp(ov, vn, denom, gcf, W, gov, gvn);
+  normal_coeff_vjp(ov, vn, inv_denom, gcf, W, gov, gvn);
   grvx += gvn * nx;
   grvy += gvn * ny;
   gnx += gvn * rvx;
   gny += gvn * rvy;
-  T gdist = -gov - dot2(gnx, gny, nx, ny) / dist;
-  T ddx = gnx / dist, ddy = gny / dist;
+  // n = d / dist, dist = sqrt(max(d2, eps)), ov = min_dist - dist
+  T gdist = -gov - dot2(gnx, gny, nx, ny) * inv;
+  T ddx = gnx * inv, ddy = gny * inv;
   if (d2 > Eps2<T>::v) {
-    T gd2 = gdist * T(0.5) / dist;
+    T gd2 = gdist * T(0.5) * inv;
+    ddx += T(2) * dx * gd2;
+    ddy += T(2) * dy * gd2;
+  }
+  gdx += ddx;
+  gdy += ddy;
+}
+
+// Both directions of one disc-disc contact in a single VJP. With d = p_a - p_b and
+// rv = v_a - v_b, the force on a is cf_a n and on b is -cf_b n (cf_x uses x's implicit
+// denominator); ga and gb are their cotangents (zero to exclude a side, e.g. a truncated
+// list). L = cf_a (ga.n) - cf_b (gb.n); adds dL/dd and dL/drv (= dL/dp_a, dL/dv_a;
+// agent b receives the negatives from its own call with the roles swapped).
+template <typename T>
+__device__ __forceinline__ void pair_vjp_sym(T dx, T dy, T rvx, T rvy, T min_dist, T ida, T gax,
+                                             T gay, T idb, T gbx, T gby, const WorldC<T>& W,
+                                             T& gdx, T& gdy, T& grvx, T& grvy) {
+  const T d2 = dot2(dx, dy, dx, dy);
+  const T m = wmax(d2, Eps2<T>::v);
+  const T inv = Num<T>::rsqrt_(m);
+  const T ov = min_dist - m * inv;
+  if (!(ov > T(0))) return;
+  const T nx = dx * inv, ny = dy * inv;
+  const T vn = dot2(rvx, rvy, nx, ny);
+  T ovs = ov, th = T(0);
+  if (W.max_overlap > T(0)) {
+    th = tanh_ratio(ov, W.max_overlap);
+    ovs = W.max_overlap * th;
+  }
+  const T num = W.k * ovs - W.c * vn;
+  const T xa = num * ida, xb = num * idb;
+  const T cfa = wmax(xa, T(0)), cfb = wmax(xb, T(0));
+  const T q = (xa > T(0) ? ida * dot2(gax, gay, nx, ny) : T(0)) -
+              (xb > T(0) ? idb * dot2(gbx, gby, nx, ny) : T(0));  // dL/dnum
+  T gnx = cfa * gax - cfb * gbx, gny = cfa * gay - cfb * gby;    // dL/dn at fixed num
+  const T gvn = -W.c * q;
+  const T govs = W.k * q;
+  const T gov = (W.max_overlap > T(0)) ? govs * (T(1) - th * th) : govs;
+  grvx += gvn * nx;
+  grvy += gvn * ny;
+  gnx += gvn * rvx;
+  gny += gvn * rvy;
+  const T gdist = -gov - dot2(gnx, gny, nx, ny) * inv;
+  T ddx = gnx * inv, ddy = gny * inv;
+  if (d2 > Eps2<T>::v) {
+    const T gd2 = gdist * T(0.5) * inv;
     ddx += T(2) * dx * gd2;
     ddy += T(2) * dy * gd2;
   }
@@ -191,7 +253,7 @@ __device__ __forceinline__ bool bounds_apart(T dx, T dy, T reach) {
 
 // Box SDF contact (collisions.py:174-260): force on an agent at p with velocity v.
 template <typename T>
-__device__ __forceinline__ void box_force(T px, T py, T vx, T vy, const Obs<T>& o, T reach, T denom,
+__device__ __forceinline__ void box_force(T px, T py, T vx, T vy, const Obs<T>& o, T reach, T inv_denom,
                                           const WorldC<T>& W, T& fx, T& fy) {
   fx = T(0);
   fy = T(0);
@@ -206,9 +268,10 @@ __device__ __forceinline__ void box_force(T px, T py, T vx, T vy, const Obs<T>& 
   T od2 = ox * ox + oy * oy;
   T s, nlx, nly;
   if (od2 > Eps2<T>::v) {
-    s = Num<T>::sqrt_(od2);
-    nlx = ox / s;
-    nly = oy / s;
+    const T is = Num<T>::rsqrt_(od2);
+    s = od2 * is;
+    nlx = ox * is;
+    nly = oy * is;
   } else if (qx > qy) {
     s = qx;
     nlx = lx >= T(0) ? T(1) : T(-1);
@@ -225,7 +288,7 @@ __device__ __forceinline__ void box_force(T px, T py, T vx, T vy, const Obs<T>& 
     T rx = ca * spx - sa * spy, ry = sa * spx + ca * spy;
     T vsx = o.vx + (-o.om * ry), vsy = o.vy + o.om * rx;
     T vn = dot2(vx - vsx, vy - vsy, nx, ny);
-    T cf = normal_coeff(overlap, vn, denom, W);
+    T cf = normal_coeff(overlap, vn, inv_denom, W);
     fx = cf * nx;
     fy = cf * ny;
   }
@@ -233,7 +296,7 @@ __device__ __forceinline__ void box_force(T px, T py, T vx, T vy, const Obs<T>& 
 
 template <typename T>
 __device__ __forceinline__ void box_force_vjp(T px, T py, T vx, T vy, const Obs<T>& o, T reach,
-                                              T denom, T gx, T gy, const WorldC<T>& W, T& gpx,
+                                              T inv_denom, T gx, T gy, const WorldC<T>& W, T& gpx,
                                               T& gpy, T& gvx, T& gvy) {
   const T ca = o.ca, sa = o.sa;
   T dx = px - o.cx, dy = py - o.cy;
@@ -247,10 +310,12 @@ __device__ __forceinline__ void box_force_vjp(T px, T py, T vx, T vy, const Obs<
   T s, nlx, nly;
   const bool ext = od2 > Eps2<T>::v;
   const bool use_x = qx > qy;
+  T is = T(0);
   if (ext) {
-    s = Num<T>::sqrt_(od2);
-    nlx = ox / s;
-    nly = oy / s;
+    is = Num<T>::rsqrt_(od2);
+    s = od2 * is;
+    nlx = ox * is;
+    nly = oy * is;
   } else if (use_x) {
     s = qx;
     nlx = lx >= T(0) ? T(1) : T(-1);
@@ -268,12 +333,12 @@ __device__ __forceinline__ void box_force_vjp(T px, T py, T vx, T vy, const Obs<
   T vsx = o.vx + (-o.om * ry), vsy = o.vy + o.om * rx;
   T relx = vx - vsx, rely = vy - vsy;
   T vn = dot2(relx, rely, nx, ny);
-  T cf = normal_coeff(overlap, vn, denom, W);
+  T cf = normal_coeff(overlap, vn, inv_denom, W);
   // f = cf * n
   T gcf = dot2(gx, gy, nx, ny);
   T gnx = cf * gx, gny = cf * gy;
   T gov, gvn;
-  normal_coeff_vjp(overlap, vn, denom, gcf, W, gov, gvn);
+  normal_coeff_vjp(overlap, vn, inv_denom, gcf, W, gov, gvn);
   // vn = rel . n
   T grelx = gvn * nx, grely = gvn * ny;
   gnx += gvn * relx;
@@ -293,9 +358,9 @@ __device__ __forceinline__ void box_force_vjp(T px, T py, T vx, T vy, const Obs<
   T gnly = -s * gspy + (-sa * gnx + ca * gny);
   if (ext) {
     // nl = o / s, s = sqrt(od2), o = l - clamp(l)
-    T gox = gnlx / s, goy = gnly / s;
-    gs -= (gnlx * nlx + gnly * nly) / s;
-    T god2 = gs * T(0.5) / s;
+    T gox = gnlx * is, goy = gnly * is;
+    gs -= (gnlx * nlx + gnly * nly) * is;
+    T god2 = gs * T(0.5) * is;
     gox += T(2) * ox * god2;
     goy += T(2) * oy * god2;
     glx += gox - (clamp_pass(lx, -o.hx, o.hx) ? gox : T(0));
@@ -310,33 +375,33 @@ __device__ __forceinline__ void box_force_vjp(T px, T py, T vx, T vy, const Obs<
   gpy += sa * glx + ca * gly;
 }
 
-// Force on an agent (radius ra, implicit denominator denom) from one obstacle.
+// Force on an agent (radius ra, inverse implicit denominator) from one obstacle.
 template <typename T>
-__device__ __forceinline__ void obstacle_force(T px, T py, T vx, T vy, T ra, T denom, const Obs<T>& o,
+__device__ __forceinline__ void obstacle_force(T px, T py, T vx, T vy, T ra, T inv_denom, const Obs<T>& o,
                                                const WorldC<T>& W, T& fx, T& fy) {
   fx = T(0);
   fy = T(0);
   if (bounds_apart(px - o.cx, py - o.cy, ra + W.margin + o.bound)) return;
   if (o.type == SHAPE_BOX) {
-    box_force(px, py, vx, vy, o, ra + W.margin, denom, W, fx, fy);
+    box_force(px, py, vx, vy, o, ra + W.margin, inv_denom, W, fx, fy);
   } else if (o.type == SHAPE_SEGMENT) {
     T t = wclamp(dot2(px - o.cx, py - o.cy, o.ca, o.sa), -o.hx, o.hx);
     T qx = o.cx + t * o.ca, qy = o.cy + t * o.sa;
     T rx = qx - o.cx, ry = qy - o.cy;
     T vsx = o.vx + (-o.om * ry), vsy = o.vy + o.om * rx;
-    pair_force(px - qx, py - qy, vx - vsx, vy - vsy, ra + o.r + W.margin, denom, W, fx, fy);
+    pair_force(px - qx, py - qy, vx - vsx, vy - vsy, ra + o.r + W.margin, inv_denom, W, fx, fy);
   } else {
-    pair_force(px - o.cx, py - o.cy, vx - o.vx, vy - o.vy, ra + o.r + W.margin, denom, W, fx, fy);
+    pair_force(px - o.cx, py - o.cy, vx - o.vx, vy - o.vy, ra + o.r + W.margin, inv_denom, W, fx, fy);
   }
 }
 
 template <typename T>
-__device__ __forceinline__ void obstacle_force_vjp(T px, T py, T vx, T vy, T ra, T denom,
+__device__ __forceinline__ void obstacle_force_vjp(T px, T py, T vx, T vy, T ra, T inv_denom,
                                                    const Obs<T>& o, T gx, T gy, const WorldC<T>& W,
                                                    T& gpx, T& gpy, T& gvx, T& gvy) {
   if (bounds_apart(px - o.cx, py - o.cy, ra + W.margin + o.bound)) return;
   if (o.type == SHAPE_BOX) {
-    box_force_vjp(px, py, vx, vy, o, ra + W.margin, denom, gx, gy, W, gpx, gpy, gvx, gvy);
+    box_force_vjp(px, py, vx, vy, o, ra + W.margin, inv_denom, gx, gy, W, gpx, gpy, gvx, gvy);
   } else if (o.type == SHAPE_SEGMENT) {
     T sproj = dot2(px - o.cx, py - o.cy, o.ca, o.sa);
     T t = wclamp(sproj, -o.hx, o.hx);
@@ -344,7 +409,7 @@ __device__ __forceinline__ void obstacle_force_vjp(T px, T py, T vx, T vy, T ra,
     T rx = qx - o.cx, ry = qy - o.cy;
     T vsx = o.vx + (-o.om * ry), vsy = o.vy + o.om * rx;
     T gdx = T(0), gdy = T(0), grvx = T(0), grvy = T(0);
-    pair_force_vjp(px - qx, py - qy, vx - vsx, vy - vsy, ra + o.r + W.margin, denom, gx, gy, W,
+    pair_force_vjp(px - qx, py - qy, vx - vsx, vy - vsy, ra + o.r + W.margin, inv_denom, gx, gy, W,
                    gdx, gdy, grvx, grvy);
     gpx += gdx;
     gpy += gdy;
@@ -362,7 +427,7 @@ __device__ __forceinline__ void obstacle_force_vjp(T px, T py, T vx, T vy, T ra,
     }
   } else {
     T gdx = T(0), gdy = T(0), grvx = T(0), grvy = T(0);
-    pair_force_vjp(px - o.cx, py - o.cy, vx - o.vx, vy - o.vy, ra + o.r + W.margin, denom, gx, gy,
+    pair_force_vjp(px - o.cx, py - o.cy, vx - o.vx, vy - o.vy, ra + o.r + W.margin, inv_denom, gx, gy,
                    W, gdx, gdy, grvx, grvy);
     gpx += gdx;
     gpy += gdy;
@@ -372,75 +437,116 @@ __device__ __forceinline__ void obstacle_force_vjp(T px, T py, T vx, T vy, T ra,
 }
 
 // ------------------------------------------------------------------------ walls
+// Penetrations of the four walls (left, right, bottom, top); inward normals +x, -x, +y, -y.
 template <typename T>
-__device__ __forceinline__ void wall_force(T px, T py, T vx, T vy, T ra, T denom, const WorldC<T>& W,
-                                           T& fx, T& fy) {
-  const T reach = ra + W.margin;
-  fx = T(0);
-  fy = T(0);
-  T pen = reach - (px - W.bx0);
-  if (pen > T(0)) fx = fx + normal_coeff(pen, vx, denom, W);
-  pen = reach - (W.bx1 - px);
-  if (pen > T(0)) fx = fx + (-normal_coeff(pen, -vx, denom, W));
-  pen = reach - (py - W.by0);
-  if (pen > T(0)) fy = fy + normal_coeff(pen, vy, denom, W);
-  pen = reach - (W.by1 - py);
-  if (pen > T(0)) fy = fy + (-normal_coeff(pen, -vy, denom, W));
+__device__ __forceinline__ void wall_pens(T px, T py, T reach, const WorldC<T>& W, T& pl, T& pr,
+                                          T& pb, T& pt) {
+  pl = reach - (px - W.bx0);
+  pr = reach - (W.bx1 - px);
+  pb = reach - (py - W.by0);
+  pt = reach - (W.by1 - py);
+}
+
+// Four soft walls. Most warps have some lane at a wall on most steps, so a branch per
+// wall would be taken anyway: without depth saturation every wall's coefficient is
+// computed and masked by its penetration sign (no divergence). The accumulation order
+// matches the reference (left, right into fx; bottom, top into fy).
+template <typename T>
+__device__ __forceinline__ void wall_force(T px, T py, T vx, T vy, T ra, T inv_denom,
+                                           const WorldC<T>& W, T& fx, T& fy) {
+  T pl, pr, pb, pt;
+  wall_pens(px, py, ra + W.margin, W, pl, pr, pb, pt);
+  if (W.max_overlap > T(0)) {
+    fx = T(0);
+    fy = T(0);
+    if (pl > T(0)) fx = fx + normal_coeff(pl, vx, inv_denom, W);
+    if (pr > T(0)) fx = fx + (-normal_coeff(pr, -vx, inv_denom, W));
+    if (pb > T(0)) fy = fy + normal_coeff(pb, vy, inv_denom, W);
+    if (pt > T(0)) fy = fy + (-normal_coeff(pt, -vy, inv_denom, W));
+    return;
+  }
+  const T cl = wmax((W.k * pl - W.c * vx) * inv_denom, T(0));
+  const T cr = wmax((W.k * pr - W.c * (-vx)) * inv_denom, T(0));
+  const T cb = wmax((W.k * pb - W.c * vy) * inv_denom, T(0));
+  const T ct = wmax((W.k * pt - W.c * (-vy)) * inv_denom, T(0));
+  fx = (pl > T(0) ? cl : T(0)) + (pr > T(0) ? -cr : T(0));
+  fy = (pb > T(0) ? cb : T(0)) + (pt > T(0) ? -ct : T(0));
 }
 
 template <typename T>
-__device__ __forceinline__ void wall_force_vjp(T px, T py, T vx, T vy, T ra, T denom, T gx, T gy,
+__device__ __forceinline__ void wall_force_vjp(T px, T py, T vx, T vy, T ra, T inv_denom, T gx, T gy,
                                                const WorldC<T>& W, T& gpx, T& gpy, T& gvx, T& gvy) {
-  const T reach = ra + W.margin;
-  T gov, gvn;
-  T pen = reach - (px - W.bx0);
-  if (pen > T(0)) {
-    normal_coeff_vjp(pen, vx, denom, gx, W, gov, gvn);
-    gpx -= gov;
-    gvx += gvn;
+  T pl, pr, pb, pt;
+  wall_pens(px, py, ra + W.margin, W, pl, pr, pb, pt);
+  if (W.max_overlap > T(0)) {
+    T gov, gvn;
+    if (pl > T(0)) {
+      normal_coeff_vjp(pl, vx, inv_denom, gx, W, gov, gvn);
+      gpx -= gov;
+      gvx += gvn;
+    }
+    if (pr > T(0)) {
+      normal_coeff_vjp(pr, -vx, inv_denom, -gx, W, gov, gvn);
+      gpx += gov;
+      gvx -= gvn;
+    }
+    if (pb > T(0)) {
+      normal_coeff_vjp(pb, vy, inv_denom, gy, W, gov, gvn);
+      gpy -= gov;
+      gvy += gvn;
+    }
+    if (pt > T(0)) {
+      normal_coeff_vjp(pt, -vy, inv_denom, -gy, W, gov, gvn);
+      gpy += gov;
+      gvy -= gvn;
+    }
+    return;
   }
-  pen = reach - (W.bx1 - px);
-  if (pen > T(0)) {
-    normal_coeff_vjp(pen, -vx, denom, -gx, W, gov, gvn);
-    gpx += gov;
-    gvx -= gvn;
-  }
-  pen = reach - (py - W.by0);
-  if (pen > T(0)) {
-    normal_coeff_vjp(pen, vy, denom, gy, W, gov, gvn);
-    gpy -= gov;
-    gvy += gvn;
-  }
-  pen = reach - (W.by1 - py);
-  if (pen > T(0)) {
-    normal_coeff_vjp(pen, -vy, denom, -gy, W, gov, gvn);
-    gpy += gov;
-    gvy -= gvn;
-  }
+  // d(coefficient)/d(numerator) = inv_denom on the active side of max(x, 0)
+  const bool al = pl > T(0) && (W.k * pl - W.c * vx) * inv_denom > T(0);
+  const bool ar = pr > T(0) && (W.k * pr - W.c * (-vx)) * inv_denom > T(0);
+  const bool ab = pb > T(0) && (W.k * pb - W.c * vy) * inv_denom > T(0);
+  const bool at = pt > T(0) && (W.k * pt - W.c * (-vy)) * inv_denom > T(0);
+  const T nl = al ? gx * inv_denom : T(0);   // left:   f_x += c_l
+  const T nr = ar ? -gx * inv_denom : T(0);  // right:  f_x -= c_r
+  const T nb = ab ? gy * inv_denom : T(0);
+  const T nt = at ? -gy * inv_denom : T(0);
+  // numerator k*pen - c*vn; pen_l = reach - px + x0 (d/dpx = -1), pen_r (+1); vn = +-v
+  gpx += W.k * (nr - nl);
+  gvx += W.c * (nr - nl);
+  gpy += W.k * (nt - nb);
+  gvy += W.c * (nt - nb);
 }
 
 // ------------------------------------------------------------------- integrate
-// clamp_norm(v, L) = v * (L / max(|v|, L))
+// clamp_norm(v, L) = v * (L / max(|v|, L)): the scale is exactly 1 while |v|^2 <= L^2,
+// else L * rsqrt(|v|^2).
 template <typename T>
 __device__ __forceinline__ void clamp_norm(T x, T y, T L, T& ox, T& oy) {
-  T n = len2(x, y);
-  T sc = L / wmax(n, L);
+  const T n2 = dot2(x, y, x, y);
+  const T sc = (n2 > L * L) ? L * Num<T>::rsqrt_(n2) : T(1);
   ox = x * sc;
   oy = y * sc;
 }
 template <typename T>
 __device__ __forceinline__ void clamp_norm_vjp(T x, T y, T L, T gx, T gy, T& rx, T& ry) {
-  T n = len2(x, y);
-  T mx = wmax(n, L);
-  T sc = L / mx;
-  rx = gx * sc;
-  ry = gy * sc;
-  if (n > L) {
-    T gsc = dot2(gx, gy, x, y);
-    T gn = -gsc * sc / mx;
-    rx += x / n * gn;
-    ry += y / n * gn;
+  const T n2 = dot2(x, y, x, y);
+  if (n2 > L * L) {
+    const T inv = Num<T>::rsqrt_(n2);
+    const T sc = L * inv;
+    const T gn = -dot2(gx, gy, x, y) * sc * inv * inv;  // d/dn of L/n times (g . v) / n
+    rx = gx * sc + x * gn;
+    ry = gy * sc + y * gn;
+  } else {
+    rx = gx;
+    ry = gy;
   }
+}
+
+// |v| with Warp's adjoint convention (zero gradient at the zero vector).
+template <typename T> __device__ __forceinline__ T norm2(T x, T y) {
+  const T n2 = dot2(x, y, x, y);
+  return n2 > T(0) ? n2 * Num<T>::rsqrt_(n2) : T(0);
 }
 
 // SERVO (diff-drive): the VELOCITY command the rate-limited servo delivers this substep.
@@ -497,7 +603,7 @@ __device__ __forceinline__ void integrate_fwd(const Agent<T>& in, T a0, T a1, T 
     out.th = in.th;
     out.vx = vx;
     out.vy = vy;
-    out.s = len2(vx, vy);
+    out.s = norm2(vx, vy);
     out.w = T(0);
   } else if (P.tag == TAG_DIFF_DRIVE) {
     T sn, wn;
@@ -574,10 +680,11 @@ __device__ __forceinline__ void integrate_vjp(const Agent<T>& in, T a0, T a1, co
   T gvx = g.vx + gpx * dt, gvy = g.vy + gpy * dt;
   if (P.tag == TAG_HOLONOMIC) {
     // s_out = |v_new|
-    T n = len2(out.vx, out.vy);
-    if (n > T(0)) {
-      gvx += out.vx / n * g.s;
-      gvy += out.vy / n * g.s;
+    const T n2 = dot2(out.vx, out.vy, out.vx, out.vy);
+    if (n2 > T(0)) {
+      const T q = g.s * Num<T>::rsqrt_(n2);
+      gvx += out.vx * q;
+      gvy += out.vy * q;
     }
     gin.th = g.th;
     gfx = gvx * P.dt_over_m;

@@ -6,8 +6,19 @@
 // the state in registers and streams actions in / trajectory out (structure of arrays,
 // consecutive threads -> consecutive (env, agent) -> coalesced); the adjoint kernel
 // walks the horizon backwards, re-reading each step's input state from the trajectory
-// (the checkpoint) and recomputing contacts instead of storing them. Accumulation is
-// a gather in fixed (ascending agent index) order: no atomics, bitwise deterministic.
+// (the checkpoint). Accumulation is a gather in fixed (ascending agent index) order:
+// no atomics, bitwise deterministic.
+//
+// Neighbor pass: positions sit in shared memory packed by agent pairs
+// (x_2p, x_2p+1, y_2p, y_2p+1), so one 16-byte load feeds one packed fp32x2
+// (FFMA2/FMUL2, sm_100) distance test of two neighbors. The test builds a 32-bit
+// membership mask per chunk of 32 agents; only set bits run the contact law.
+//
+// Contact checkpoint (F_MASK, A <= 32 and no list truncation): the forward stores per
+// agent and substep the 32-bit mask of neighbors it was in contact with. Contact is
+// symmetric, so the adjoint runs the pair VJPs over exactly those bits and never
+// repeats the neighbor scan. Otherwise (A > 32 or a truncating cap) the adjoint
+// rescans, and with truncation the forward stores each list's cutoff index instead.
 #pragma once
 #include "physics.cuh"
 
@@ -22,11 +33,11 @@ template <> struct V4<double> { using t = double4; };
 
 // Compile-time feature switches of one kernel instance.
 enum : int {
-  F_COLL = 1,      // agent-agent contacts
-  F_TRUNC = 2,     // list cap can truncate (A - 1 > K): store/read per-substep cutoffs
-  F_OBS = 4,       // obstacles present
-  F_HOLOVEL = 8,   // every agent is holonomic / VELOCITY
-  F_BODIES = 16,   // movable bodies integrated in the substep loop
+  F_COLL = 1,     // agent-agent contacts
+  F_TRUNC = 2,    // list cap can truncate (A - 1 > K): cutoffs checkpointed
+  F_OBS = 4,      // obstacles present
+  F_HOLOVEL = 8,  // every agent is holonomic / VELOCITY
+  F_MASK = 16,    // contact masks checkpointed (A <= 32, no truncation)
 };
 
 template <typename T> struct RolloutArgs {
@@ -45,12 +56,35 @@ template <typename T> struct RolloutArgs {
   T *t_pos, *t_th, *t_vel, *t_s, *t_w;
   T *f_pos, *f_th, *f_vel, *f_s, *f_w;
   int* true_max;
-  int16_t* cutoff;  // workspace [H*S, E, A] (F_TRUNC)
+  int16_t* cutoff;   // workspace [H*S, E, A] (F_TRUNC)
+  uint32_t* cmask;   // workspace [H*S, E, A] (F_MASK)
   // adjoint
   const T *gt_pos, *gt_th, *gt_vel, *gt_s, *gt_w;  // cotangent of trajectory (nullable)
   const T *gf_pos, *gf_th, *gf_vel, *gf_s, *gf_w;  // cotangent of final (nullable)
   T* g_act;
   T *gi_pos, *gi_th, *gi_vel, *gi_s, *gi_w;
+};
+
+// Shared-memory carve-up, identical on host (sizes) and device (pointers).
+template <typename T> struct Layout {
+  int G, A, NP, nbuf, S;
+  size_t xy, rec, own, fb, cut, rad, iden, obs, total;
+  __host__ __device__ Layout(int G_, int A_, int N, int S_, bool bwd) : G(G_), A(A_), S(S_) {
+    NP = (A + 1) / 2;
+    nbuf = bwd ? (S > 2 ? S : 2) : 2;
+    const int GA = G * A;
+    size_t off = 0;
+    auto take = [&](size_t bytes) { size_t o = off; off = (off + bytes + 15) & ~size_t(15); return o; };
+    xy = take(size_t(nbuf) * G * NP * 4 * sizeof(T));   // scan table (pair-packed x, y)
+    rec = take(size_t(nbuf) * GA * 4 * sizeof(T));      // per-agent (x, y, vx, vy) records
+    own = bwd ? take(size_t(S) * GA * 4 * sizeof(T)) : 0;
+    fb = bwd ? take(size_t(2) * GA * 2 * sizeof(T)) : 0;
+    cut = bwd ? take(size_t(2) * GA * sizeof(int)) : 0;
+    rad = take(size_t(GA) * sizeof(T));
+    iden = take(size_t(GA) * sizeof(T));
+    obs = take(size_t(G) * (N > 0 ? N : 0) * sizeof(Obs<T>));
+    total = off;
+  }
 };
 
 // ------------------------------------------------------------------ loaders
@@ -72,7 +106,7 @@ __device__ __forceinline__ void load_params(const RolloutArgs<T>& R, int e, int 
   P.tag = R.model_tag[a];
   P.mode = R.ctrl_mode[a];
   P.dt_over_m = R.W.dt / P.mass;
-  P.denom = T(1) + R.W.c * R.W.dt / P.mass;
+  P.inv_denom = T(1) / (T(1) + R.W.c * R.W.dt / P.mass);
 }
 
 template <typename T>
@@ -134,8 +168,7 @@ __device__ __forceinline__ void load_action(const RolloutArgs<T>& R, long long i
   }
 }
 
-// Obstacles of this CTA's envs into shared memory (the agent pass re-reads them every
-// substep). Angle -> (cos, sin) once.
+// Obstacles of this CTA's envs into shared memory. Angle -> (cos, sin) once.
 template <typename T>
 __device__ __forceinline__ void load_obstacles(const RolloutArgs<T>& R, Obs<T>* sobs, int e0) {
   const int total = R.G * R.N;
@@ -167,58 +200,126 @@ __device__ __forceinline__ void load_obstacles(const RolloutArgs<T>& R, Obs<T>* 
   }
 }
 
-// ------------------------------------------------------------- neighbor scan
-// Calls fn(b, dx, dy, d2) for every agent b != a of this env with sqrt(d2) <= R, in
-// ascending b. Positions come from spv (x, y in the first two lanes).
-template <typename T, typename Fn>
-__device__ __forceinline__ int scan_radius(const typename V4<T>::t* spv, int base, int A, int a,
-                                           T px, T py, T r2_thr, Fn&& fn) {
+// ------------------------------------------------------- packed position table
+// Agent j of an env sits at xy[(j/2)*4 + j%2] (x) and xy[(j/2)*4 + 2 + j%2] (y).
+template <typename T> __device__ __forceinline__ int xslot(int j) { return (j >> 1) * 4 + (j & 1); }
+
+template <typename T>
+__device__ __forceinline__ void put_xy(T* xy_env, int j, T x, T y) {
+  xy_env[xslot<T>(j)] = x;
+  xy_env[xslot<T>(j) + 2] = y;
+}
+template <typename T>
+__device__ __forceinline__ void get_xy(const T* xy_env, int j, T& x, T& y) {
+  x = xy_env[xslot<T>(j)];
+  y = xy_env[xslot<T>(j) + 2];
+}
+
+// Membership mask of agents [32c, 32c + 32) of one env within the neighbor radius of
+// (px, py) (self not removed). Bit j is the sign of dx^2 + (dy^2 - R^2), shifted in with
+// one funnel shift per neighbor, neighbors visited in descending index. AS > 0: the env
+// has exactly AS agents (compile-time).
+template <int AS>
+__device__ __forceinline__ unsigned scan_chunk(const float* xy_env, int c, int npairs, float px,
+                                               float py, float thr) {
+  const float4* P = reinterpret_cast<const float4*>(xy_env) + c * 16;
+  const float2 PX = make_float2(px, px), PY = make_float2(py, py), M1 = make_float2(-1.f, -1.f);
+  const float2 NT = make_float2(-thr, -thr);
+  unsigned m = 0u;
+  constexpr int NPC = AS > 0 ? ((AS + 1) / 2 < 16 ? (AS + 1) / 2 : 16) : 16;
+#pragma unroll
+  for (int p = NPC - 1; p >= 0; --p) {
+    if (AS == 0 && p >= npairs) continue;
+    const float4 q = P[p];
+    const float2 dx = __ffma2_rn(make_float2(q.x, q.y), M1, PX);
+    const float2 dy = __ffma2_rn(make_float2(q.z, q.w), M1, PY);
+    const float2 d = __ffma2_rn(dx, dx, __ffma2_rn(dy, dy, NT));
+    m = __funnelshift_l(__float_as_uint(d.y), m, 1);
+    m = __funnelshift_l(__float_as_uint(d.x), m, 1);
+  }
+  return m;
+}
+template <int AS>
+__device__ __forceinline__ unsigned scan_chunk(const double* xy_env, int c, int npairs, double px,
+                                               double py, double thr) {
+  unsigned m = 0u;
+  constexpr int NPC = AS > 0 ? ((AS + 1) / 2 < 16 ? (AS + 1) / 2 : 16) : 16;
+#pragma unroll 4
+  for (int p = NPC - 1; p >= 0; --p) {
+    if (AS == 0 && p >= npairs) continue;
+    const double* q = xy_env + (c * 16 + p) * 4;
+    const double dx1 = px - q[1], dy1 = py - q[3];
+    const double dx0 = px - q[0], dy0 = py - q[2];
+    m = (m << 1) | (__fma_rn(dx1, dx1, __fma_rn(dy1, dy1, -thr)) < 0.0 ? 1u : 0u);
+    m = (m << 1) | (__fma_rn(dx0, dx0, __fma_rn(dy0, dy0, -thr)) < 0.0 ? 1u : 0u);
+  }
+  return m;
+}
+
+// Calls fn(b, q) for every agent b != a of the env within the neighbor radius, ascending
+// b, with q = b's (x, y, vx, vy) record. Returns the count of such agents.
+template <typename T, int AS, typename Fn>
+__device__ __forceinline__ int for_each_in_radius(const T* xy_env, const typename V4<T>::t* rec_env,
+                                                  int A, int a, T px, T py, T thr, Fn&& fn) {
+  const int NP = (A + 1) / 2;
   int total = 0;
-  for (int c0 = 0; c0 < A; c0 += 32) {
-    const int n = min(32, A - c0);
-    unsigned m = 0u;
-#pragma unroll 8
-    for (int jj = 0; jj < n; ++jj) {
-      const auto q = spv[base + c0 + jj];
-      const T dx = px - q.x, dy = py - q.y;
-      const T d2 = dot2(dx, dy, dx, dy);
-      m |= (d2 <= r2_thr) ? (1u << jj) : 0u;
-    }
-    const int rel = a - c0;
+  const int nchunk = AS > 0 ? (AS + 31) / 32 : (A + 31) / 32;
+  for (int c = 0; c < nchunk; ++c) {
+    const int npairs = min(16, NP - c * 16);
+    unsigned m = scan_chunk<AS>(xy_env, c, npairs, px, py, thr);
+    const int rel = a - 32 * c;
     if (rel >= 0 && rel < 32) m &= ~(1u << rel);
     total += __popc(m);
     while (m) {
       const int jj = __ffs(m) - 1;
       m &= m - 1u;
-      const int b = c0 + jj;
-      const auto q = spv[base + b];
-      const T dx = px - q.x, dy = py - q.y;
-      fn(b, dx, dy, dot2(dx, dy, dx, dy), q);
+      const int b = 32 * c + jj;
+      fn(b, rec_env[b]);
     }
   }
   return total;
 }
 
 // Contact force on agent a from its capped neighbor list (the first K within R by index).
-// Returns the uncapped count; cutoff = index of the K-th listed neighbor if truncated, else A.
-template <typename T, int FL>
-__device__ __forceinline__ int neighbor_force(const typename V4<T>::t* spv, const T* srad, int base,
-                                              int A, int a, const Agent<T>& x, const AgentP<T>& P,
-                                              const WorldC<T>& W, T& fx, T& fy, int& cutoff) {
+// Returns the uncapped count; cutoff = index of the K-th listed neighbor if truncated,
+// else A; cmask = contacts among agents 0..31.
+template <typename T, int FL, int AS>
+__device__ __forceinline__ int neighbor_force(const T* xy_env, const typename V4<T>::t* rec_env,
+                                              const T* rad_env, int A, int a, const Agent<T>& x,
+                                              const AgentP<T>& P, const WorldC<T>& W, T& fx, T& fy,
+                                              int& cutoff, unsigned& cmask) {
   int listed = 0;
   cutoff = A;
-  const int total = scan_radius<T>(spv, base, A, a, x.px, x.py, W.r2_thr,
-                                   [&](int b, T dx, T dy, T d2, const typename V4<T>::t& q) {
+  cmask = 0u;
+  const int total = for_each_in_radius<T, AS>(xy_env, rec_env, A, a, x.px, x.py, W.r2_thr,
+                                              [&](int b, const typename V4<T>::t& q) {
     if (FL & F_TRUNC) {
       if (listed >= W.K) return;
       ++listed;
       if (listed == W.K) cutoff = b;
     }
-    pair_force_add(dx, dy, d2, x.vx - q.z, x.vy - q.w, P.radius + srad[base + b] + W.margin,
-                   P.denom, W, fx, fy);
+    const T dx = x.px - q.x, dy = x.py - q.y;
+    if (pair_force_add(dx, dy, dot2(dx, dy, dx, dy), x.vx - q.z, x.vy - q.w,
+                       P.radius + rad_env[b] + W.margin, P.inv_denom, W, fx, fy))
+      cmask |= 1u << (b & 31);
   });
   if ((FL & F_TRUNC) && total <= W.K) cutoff = A;
   return total;
+}
+
+// Contact force from a checkpointed contact mask (ascending b, the forward's order).
+template <typename T>
+__device__ __forceinline__ void mask_force(const typename V4<T>::t* rec_env, const T* rad_env,
+                                           unsigned m, const Agent<T>& x, const AgentP<T>& P,
+                                           const WorldC<T>& W, T& fx, T& fy) {
+  while (m) {
+    const int b = __ffs(m) - 1;
+    m &= m - 1u;
+    const auto q = rec_env[b];
+    const T dx = x.px - q.x, dy = x.py - q.y;
+    pair_force_add(dx, dy, dot2(dx, dy, dx, dy), x.vx - q.z, x.vy - q.w,
+                   P.radius + rad_env[b] + W.margin, P.inv_denom, W, fx, fy);
+  }
 }
 
 template <typename T, int FL>
@@ -228,14 +329,14 @@ __device__ __forceinline__ void static_force(const Obs<T>* sobs, int N, const Ag
   if (FL & F_OBS) {
     for (int o = 0; o < N; ++o) {
       T gx, gy;
-      obstacle_force(x.px, x.py, x.vx, x.vy, P.radius, P.denom, sobs[o], W, gx, gy);
+      obstacle_force(x.px, x.py, x.vx, x.vy, P.radius, P.inv_denom, sobs[o], W, gx, gy);
       sx = sx + gx;
       sy = sy + gy;
     }
   }
   if (W.bounds_mode == BOUNDS_SOFT) {
     T wx, wy;
-    wall_force(x.px, x.py, x.vx, x.vy, P.radius, P.denom, W, wx, wy);
+    wall_force(x.px, x.py, x.vx, x.vy, P.radius, P.inv_denom, W, wx, wy);
     sx = sx + wx;
     sy = sy + wy;
   }
@@ -256,133 +357,6 @@ __device__ __forceinline__ void integrate_sel(const Agent<T>& in, T a0, T a1, T 
   }
 }
 
-// Shared-memory footprint.
-template <typename T> struct Smem {
-  static size_t fwd(int GA, int GN) {
-    return 2 * GA * sizeof(typename V4<T>::t) + GA * sizeof(T) + GN * sizeof(Obs<T>) + 64;
-  }
-  static size_t bwd(int GA, int GN, int S) {
-    const int nb = S > 2 ? S : 2;
-    return nb * GA * sizeof(typename V4<T>::t)      // pos/vel per substep
-           + S * GA * sizeof(typename V4<T>::t)     // own th/s/w per substep
-           + 2 * GA * sizeof(typename V2<T>::t)     // force cotangent, double buffered
-           + 2 * GA * sizeof(int)                   // cutoffs, double buffered
-           + 2 * GA * sizeof(T)                     // radius, denominator
-           + GN * sizeof(Obs<T>) + 128;
-  }
-};
-
-// ================================================================== forward
-template <typename T, int FL>
-__global__ void __launch_bounds__(1024) rollout_fwd_kernel(const RolloutArgs<T> R) {
-  using T4 = typename V4<T>::t;
-  extern __shared__ __align__(16) unsigned char smem[];
-  const int A = R.A, G = R.G, GA = G * A;
-  const int tid = threadIdx.x;
-  const int le = tid / A, a = tid - le * A;
-  const int e0 = blockIdx.x * G;
-  const int e = e0 + le;
-  const bool valid = e < R.E;
-  const int ec = valid ? e : R.E - 1;
-  const int base = le * A;
-
-  T4* spv = reinterpret_cast<T4*>(smem);            // [2][GA]
-  T* srad = reinterpret_cast<T*>(spv + 2 * GA);     // [GA]
-  Obs<T>* sobs = reinterpret_cast<Obs<T>*>(
-      (reinterpret_cast<uintptr_t>(srad + GA) + 15) & ~uintptr_t(15));  // [G][N]
-
-  AgentP<T> P;
-  load_params(R, ec, a, P);
-  const WorldC<T> W = R.W;
-  srad[tid] = P.radius;
-  if (FL & F_OBS) load_obstacles(R, sobs, e0);
-
-  const long long ia = (long long)ec * A + a;  // (env, agent) linear index
-  const long long EA = (long long)R.E * A;
-  Agent<T> x;
-  load_state(R.i_pos, R.i_th, R.i_vel, R.i_s, R.i_w, ia, x);
-  int tmax = 0;
-  int buf = 0;
-  T a0, a1, n0, n1;
-  load_action(R, ia, a0, a1);
-  for (int t = 0; t < R.H; ++t) {
-    if (t + 1 < R.H) load_action(R, (long long)(t + 1) * EA + ia, n0, n1);
-    for (int k = 0; k < R.S; ++k) {
-      T fx = T(0), fy = T(0);
-      if (FL & F_COLL) {
-        spv[buf * GA + tid] = T4{x.px, x.py, x.vx, x.vy};
-        __syncthreads();
-        int cutoff;
-        const int tc = neighbor_force<T, FL>(spv + buf * GA, srad, base, A, a, x, P, W, fx, fy, cutoff);
-        tmax = max(tmax, tc);
-        if ((FL & F_TRUNC) && valid) R.cutoff[((long long)t * R.S + k) * EA + ia] = (int16_t)cutoff;
-        buf ^= 1;
-      } else if (t == 0 && k == 0) {
-        __syncthreads();  // obstacles / radii visible
-      }
-      static_force<T, FL>(sobs + le * R.N, R.N, x, P, W, fx, fy);
-      Agent<T> y;
-      integrate_sel<T, FL>(x, a0, a1, fx, fy, P, W, y);
-      x = y;
-    }
-    if (valid)
-      store_state(R.t_pos, R.t_th, R.t_vel, R.t_s, R.t_w, (long long)t * EA + ia, x);
-    a0 = n0;
-    a1 = n1;
-  }
-  if (valid) {
-    if (R.f_pos) store_state(R.f_pos, R.f_th, R.f_vel, R.f_s, R.f_w, ia, x);
-    if (R.true_max) R.true_max[ia] = tmax;
-  }
-}
-
-// ================================================================== adjoint
-// Adjoint of the neighbor + static force pass of agent a at one substep: given the
-// force cotangents of every agent of the env (sfb), adds d(loss)/d(pos, vel) of agent a.
-template <typename T, int FL>
-__device__ __forceinline__ void force_vjp(const typename V4<T>::t* spv,
-                                          const typename V2<T>::t* sfb, const int* scut,
-                                          const T* srad, const T* sden, const Obs<T>* sobs,
-                                          int N, int base, int A, int a, const Agent<T>& x,
-                                          const AgentP<T>& P, const WorldC<T>& W, T gfx, T gfy,
-                                          Agent<T>& gin) {
-  if (FL & F_COLL) {
-    const int cut_a = (FL & F_TRUNC) ? scut[base + a] : A;
-    scan_radius<T>(spv, base, A, a, x.px, x.py, W.r2_thr,
-                   [&](int b, T dx, T dy, T d2, const typename V4<T>::t& q) {
-      const T rb = srad[base + b];
-      const T min_dist = P.radius + rb + W.margin;
-      const T dist = Num<T>::sqrt_(wmax(d2, Eps2<T>::v));
-      if (!(min_dist - dist > T(0))) return;  // not in contact: zero force both ways
-      const T rvx = x.vx - q.z, rvy = x.vy - q.w;
-      const bool own = !(FL & F_TRUNC) || b <= cut_a;
-      const bool cross = !(FL & F_TRUNC) || a <= scut[base + b];
-      if (own) {
-        pair_force_vjp(dx, dy, rvx, rvy, min_dist, P.denom, gfx, gfy, W, gin.px, gin.py, gin.vx,
-                       gin.vy);
-      }
-      if (cross) {
-        const auto gb = sfb[base + b];
-        T gdx = T(0), gdy = T(0), grx = T(0), gry = T(0);
-        pair_force_vjp(-dx, -dy, -rvx, -rvy, rb + P.radius + W.margin, sden[base + b], gb.x, gb.y,
-                       W, gdx, gdy, grx, gry);
-        gin.px -= gdx;
-        gin.py -= gdy;
-        gin.vx -= grx;
-        gin.vy -= gry;
-      }
-    });
-  }
-  if (FL & F_OBS) {
-    for (int o = 0; o < N; ++o)
-      obstacle_force_vjp(x.px, x.py, x.vx, x.vy, P.radius, P.denom, sobs[o], gfx, gfy, W, gin.px,
-                         gin.py, gin.vx, gin.vy);
-  }
-  if (W.bounds_mode == BOUNDS_SOFT)
-    wall_force_vjp(x.px, x.py, x.vx, x.vy, P.radius, P.denom, gfx, gfy, W, gin.px, gin.py, gin.vx,
-                   gin.vy);
-}
-
 template <typename T, int FL>
 __device__ __forceinline__ void integrate_vjp_sel(const Agent<T>& in, T a0, T a1, const Agent<T>& out,
                                                   const Agent<T>& g, const AgentP<T>& P,
@@ -398,70 +372,224 @@ __device__ __forceinline__ void integrate_vjp_sel(const Agent<T>& in, T a0, T a1
   }
 }
 
-template <typename T, int FL>
-__global__ void __launch_bounds__(1024) rollout_bwd_kernel(const RolloutArgs<T> R) {
-  using T2 = typename V2<T>::t;
+// Pad slot of an odd-sized env: never within any radius.
+template <typename T>
+__device__ __forceinline__ void init_pads(T* xy, int nbuf, int G, int A) {
+  if ((A & 1) == 0) return;
+  const int NP = (A + 1) / 2;
+  for (int i = threadIdx.x; i < nbuf * G; i += blockDim.x) {
+    T* env = xy + size_t(i) * NP * 4;
+    put_xy(env, A, T(1e30), T(1e30));
+  }
+}
+
+// ================================================================== forward
+template <typename T, int FL, int AS>
+__global__ void __launch_bounds__(1024) rollout_fwd_kernel(const RolloutArgs<T> R) {
   using T4 = typename V4<T>::t;
   extern __shared__ __align__(16) unsigned char smem[];
-  const int A = R.A, G = R.G, GA = G * A, S = R.S;
+  const int A = AS > 0 ? AS : R.A;
+  const int G = R.G, GA = G * A;
   const int tid = threadIdx.x;
   const int le = tid / A, a = tid - le * A;
   const int e0 = blockIdx.x * G;
   const int e = e0 + le;
   const bool valid = e < R.E;
   const int ec = valid ? e : R.E - 1;
-  const int base = le * A;
-  const int nb = S > 2 ? S : 2;
-
-  T4* spv = reinterpret_cast<T4*>(smem);           // [nb][GA] pos/vel of substep inputs
-  T4* sown = spv + nb * GA;                         // [S][GA]  th/s/w of substep inputs
-  T2* sfb = reinterpret_cast<T2*>(sown + S * GA);   // [2][GA]  force cotangents
-  int* scut = reinterpret_cast<int*>(sfb + 2 * GA); // [2][GA]  cutoffs
-  T* srad = reinterpret_cast<T*>(
-      (reinterpret_cast<uintptr_t>(scut + 2 * GA) + 15) & ~uintptr_t(15));  // [GA]
-  T* sden = srad + GA;                                                     // [GA]
-  Obs<T>* sobs = reinterpret_cast<Obs<T>*>(
-      (reinterpret_cast<uintptr_t>(sden + GA) + 15) & ~uintptr_t(15));
+  const Layout<T> L(G, A, R.N, R.S, false);
+  const int NP4 = L.NP * 4;
+  T* sxy = reinterpret_cast<T*>(smem + L.xy);
+  T4* srec = reinterpret_cast<T4*>(smem + L.rec);
+  T* srad = reinterpret_cast<T*>(smem + L.rad);
+  Obs<T>* sobs = reinterpret_cast<Obs<T>*>(smem + L.obs);
 
   AgentP<T> P;
   load_params(R, ec, a, P);
   const WorldC<T> W = R.W;
   srad[tid] = P.radius;
-  sden[tid] = P.denom;
   if (FL & F_OBS) load_obstacles(R, sobs, e0);
+  if (FL & F_COLL) init_pads(sxy, 2, G, A);
+  __syncthreads();
+
+  const long long ia = (long long)ec * A + a;
+  const long long EA = (long long)R.E * A;
+  Agent<T> x;
+  load_state(R.i_pos, R.i_th, R.i_vel, R.i_s, R.i_w, ia, x);
+  int tmax = 0;
+  int buf = 0;
+  T a0, a1, n0 = T(0), n1 = T(0);
+  load_action(R, ia, a0, a1);
+  const T* rad_env = srad + le * A;
+  for (int t = 0; t < R.H; ++t) {
+    if (t + 1 < R.H) load_action(R, (long long)(t + 1) * EA + ia, n0, n1);
+    for (int k = 0; k < R.S; ++k) {
+      T fx = T(0), fy = T(0);
+      if (FL & F_COLL) {
+        T* xy_env = sxy + (buf * G + le) * NP4;
+        T4* rec_env = srec + buf * GA + le * A;
+        put_xy(xy_env, a, x.px, x.py);
+        rec_env[a] = T4{x.px, x.py, x.vx, x.vy};
+        __syncthreads();
+        int cutoff;
+        unsigned cm;
+        const int tc = neighbor_force<T, FL, AS>(xy_env, rec_env, rad_env, A, a, x, P, W, fx, fy,
+                                                 cutoff, cm);
+        tmax = max(tmax, tc);
+        const long long ws = ((long long)t * R.S + k) * EA + ia;
+        if ((FL & F_TRUNC) && valid) R.cutoff[ws] = (int16_t)cutoff;
+        if ((FL & F_MASK) && valid) R.cmask[ws] = cm;
+        buf ^= 1;
+      }
+      static_force<T, FL>(sobs + le * R.N, R.N, x, P, W, fx, fy);
+      Agent<T> y;
+      integrate_sel<T, FL>(x, a0, a1, fx, fy, P, W, y);
+      x = y;
+    }
+    if (valid) store_state(R.t_pos, R.t_th, R.t_vel, R.t_s, R.t_w, (long long)t * EA + ia, x);
+    a0 = n0;
+    a1 = n1;
+  }
+  if (valid) {
+    if (R.f_pos) store_state(R.f_pos, R.f_th, R.f_vel, R.f_s, R.f_w, ia, x);
+    if (R.true_max) R.true_max[ia] = tmax;
+  }
+}
+
+// ================================================================== adjoint
+// Force VJP of agent a at one substep: given every env agent's (x, y, vx, vy) record and
+// force cotangent, adds d(loss)/d(pos, vel) of agent a through its own force and
+// through the forces its contacts feel from it.
+template <typename T, int FL, int AS>
+__device__ __forceinline__ void force_vjp(const T* xy_env, const typename V4<T>::t* rec_env,
+                                          const typename V2<T>::t* fb_env, const int* cut_env,
+                                          const T* rad_env, const T* iden_env, const Obs<T>* sobs,
+                                          int N, int A, int a, unsigned cmask, const Agent<T>& x,
+                                          const AgentP<T>& P, const WorldC<T>& W, T gfx, T gfy,
+                                          Agent<T>& gin) {
+  if (FL & F_MASK) {
+    unsigned m = cmask;
+    while (m) {
+      const int b = __ffs(m) - 1;
+      m &= m - 1u;
+      const auto q = rec_env[b];
+      const auto gb = fb_env[b];
+      pair_vjp_sym(x.px - q.x, x.py - q.y, x.vx - q.z, x.vy - q.w, P.radius + rad_env[b] + W.margin,
+                   P.inv_denom, gfx, gfy, iden_env[b], gb.x, gb.y, W, gin.px, gin.py, gin.vx,
+                   gin.vy);
+    }
+  } else if (FL & F_COLL) {
+    const int cut_a = (FL & F_TRUNC) ? cut_env[a] : A;
+    for_each_in_radius<T, AS>(xy_env, rec_env, A, a, x.px, x.py, W.r2_thr,
+                              [&](int b, const typename V4<T>::t& q) {
+      const bool own = !(FL & F_TRUNC) || b <= cut_a;
+      const bool cross = !(FL & F_TRUNC) || a <= cut_env[b];
+      const auto gb = fb_env[b];
+      pair_vjp_sym(x.px - q.x, x.py - q.y, x.vx - q.z, x.vy - q.w,
+                   P.radius + rad_env[b] + W.margin, P.inv_denom, own ? gfx : T(0),
+                   own ? gfy : T(0), iden_env[b], cross ? gb.x : T(0), cross ? gb.y : T(0), W,
+                   gin.px, gin.py, gin.vx, gin.vy);
+    });
+  }
+  if (FL & F_OBS) {
+    for (int o = 0; o < N; ++o)
+      obstacle_force_vjp(x.px, x.py, x.vx, x.vy, P.radius, P.inv_denom, sobs[o], gfx, gfy, W,
+                         gin.px, gin.py, gin.vx, gin.vy);
+  }
+  if (W.bounds_mode == BOUNDS_SOFT)
+    wall_force_vjp(x.px, x.py, x.vx, x.vy, P.radius, P.inv_denom, gfx, gfy, W, gin.px, gin.py,
+                   gin.vx, gin.vy);
+}
+
+template <typename T, int FL, int AS>
+__global__ void __launch_bounds__(1024) rollout_bwd_kernel(const RolloutArgs<T> R) {
+  using T2 = typename V2<T>::t;
+  using T4 = typename V4<T>::t;
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int A = AS > 0 ? AS : R.A;
+  const int G = R.G, GA = G * A, S = R.S;
+  const int tid = threadIdx.x;
+  const int le = tid / A, a = tid - le * A;
+  const int e0 = blockIdx.x * G;
+  const int e = e0 + le;
+  const bool valid = e < R.E;
+  const int ec = valid ? e : R.E - 1;
+  const Layout<T> L(G, A, R.N, S, true);
+  const int NP4 = L.NP * 4;
+  T* sxy = reinterpret_cast<T*>(smem + L.xy);       // [nbuf][G][NP*4] scan tables
+  T4* srec = reinterpret_cast<T4*>(smem + L.rec);   // [nbuf][GA] (x, y, vx, vy)
+  T* sown = reinterpret_cast<T*>(smem + L.own);     // [S][GA][4] th, s, w
+  T2* sfb = reinterpret_cast<T2*>(smem + L.fb);     // [2][GA] force cotangents
+  int* scut = reinterpret_cast<int*>(smem + L.cut); // [2][GA] list cutoffs
+  T* srad = reinterpret_cast<T*>(smem + L.rad);
+  T* siden = reinterpret_cast<T*>(smem + L.iden);
+  Obs<T>* sobs = reinterpret_cast<Obs<T>*>(smem + L.obs);
+  // A rescan is needed unless contacts come from checkpointed masks.
+  constexpr bool kScan = (FL & F_COLL) && !(FL & F_MASK);
+
+  AgentP<T> P;
+  load_params(R, ec, a, P);
+  const WorldC<T> W = R.W;
+  srad[tid] = P.radius;
+  siden[tid] = P.inv_denom;
+  if (FL & F_OBS) load_obstacles(R, sobs, e0);
+  if (kScan) init_pads(sxy, L.nbuf, G, A);
   __syncthreads();
 
   const long long ia = (long long)ec * A + a;
   const long long EA = (long long)R.E * A;
   const int H = R.H;
+  const T* rad_env = srad + le * A;
+  const T* iden_env = siden + le * A;
+  const Obs<T>* obs_env = sobs + le * R.N;
+  const bool has_gt = R.gt_pos || R.gt_th || R.gt_vel || R.gt_s || R.gt_w;
 
   Agent<T> g{};
   add_cotangent(R.gf_pos, R.gf_th, R.gf_vel, R.gf_s, R.gf_w, ia, g);
   Agent<T> nxt;  // output state of step t
   load_state(R.t_pos, R.t_th, R.t_vel, R.t_s, R.t_w, (long long)(H - 1) * EA + ia, nxt);
+  // software pipeline: the inputs of step t are loaded during step t+1
+  Agent<T> cur;
+  T a0, a1;
+  unsigned cm0 = 0u;
+  if (H > 1)
+    load_state(R.t_pos, R.t_th, R.t_vel, R.t_s, R.t_w, (long long)(H - 2) * EA + ia, cur);
+  else
+    load_state(R.i_pos, R.i_th, R.i_vel, R.i_s, R.i_w, ia, cur);
+  load_action(R, (long long)(H - 1) * EA + ia, a0, a1);
+  if ((FL & F_MASK) && S == 1) cm0 = R.cmask[(long long)(H - 1) * EA + ia];
   int fbuf = 0;
   for (int t = H - 1; t >= 0; --t) {
-    if (R.gt_pos || R.gt_th || R.gt_vel || R.gt_s || R.gt_w)
-      add_cotangent(R.gt_pos, R.gt_th, R.gt_vel, R.gt_s, R.gt_w, (long long)t * EA + ia, g);
-    Agent<T> cur;
-    if (t > 0)
-      load_state(R.t_pos, R.t_th, R.t_vel, R.t_s, R.t_w, (long long)(t - 1) * EA + ia, cur);
-    else
-      load_state(R.i_pos, R.i_th, R.i_vel, R.i_s, R.i_w, ia, cur);
-    T a0, a1;
-    load_action(R, (long long)t * EA + ia, a0, a1);
+    if (has_gt) add_cotangent(R.gt_pos, R.gt_th, R.gt_vel, R.gt_s, R.gt_w, (long long)t * EA + ia, g);
+    Agent<T> pcur{};
+    T pa0 = T(0), pa1 = T(0);
+    unsigned pcm = 0u;
+    if (t > 0) {
+      if (t > 1)
+        load_state(R.t_pos, R.t_th, R.t_vel, R.t_s, R.t_w, (long long)(t - 2) * EA + ia, pcur);
+      else
+        load_state(R.i_pos, R.i_th, R.i_vel, R.i_s, R.i_w, ia, pcur);
+      load_action(R, (long long)(t - 1) * EA + ia, pa0, pa1);
+      if ((FL & F_MASK) && S == 1) pcm = R.cmask[(long long)(t - 1) * EA + ia];
+    }
     T ga0 = T(0), ga1 = T(0);
 
     if (S == 1) {
       Agent<T> gin;
       T gfx, gfy;
       integrate_vjp_sel<T, FL>(cur, a0, a1, nxt, g, P, W, gin, gfx, gfy, ga0, ga1);
-      spv[fbuf * GA + tid] = T4{cur.px, cur.py, cur.vx, cur.vy};
-      sfb[fbuf * GA + tid] = T2{gfx, gfy};
-      if (FL & F_TRUNC) scut[fbuf * GA + tid] = R.cutoff[(long long)t * EA + ia];
-      __syncthreads();
-      force_vjp<T, FL>(spv + fbuf * GA, sfb + fbuf * GA, scut + fbuf * GA, srad, sden,
-                       sobs + le * R.N, R.N, base, A, a, cur, P, W, gfx, gfy, gin);
+      T* xy_env = sxy + (fbuf * G + le) * NP4;
+      T4* rec_env = srec + fbuf * GA + le * A;
+      T2* fb_env = sfb + fbuf * GA + le * A;
+      int* cut_env = scut + fbuf * GA + le * A;
+      if (FL & F_COLL) {
+        if (kScan) put_xy(xy_env, a, cur.px, cur.py);
+        rec_env[a] = T4{cur.px, cur.py, cur.vx, cur.vy};
+        fb_env[a] = T2{gfx, gfy};
+        if (FL & F_TRUNC) cut_env[a] = R.cutoff[(long long)t * EA + ia];
+        __syncthreads();
+      }
+      force_vjp<T, FL, AS>(xy_env, rec_env, fb_env, cut_env, rad_env, iden_env, obs_env, R.N, A, a,
+                           cm0, cur, P, W, gfx, gfy, gin);
       g = gin;
       fbuf ^= 1;
     } else {
@@ -469,33 +597,50 @@ __global__ void __launch_bounds__(1024) rollout_bwd_kernel(const RolloutArgs<T> 
       __syncthreads();  // every thread is done reading last step's stash
       Agent<T> x = cur;
       for (int k = 0; k < S; ++k) {
-        spv[k * GA + tid] = T4{x.px, x.py, x.vx, x.vy};
-        sown[k * GA + tid] = T4{x.th, x.s, x.w, T(0)};
+        T* xy_env = sxy + (k * G + le) * NP4;
+        T4* rec_env = srec + k * GA + le * A;
+        if (kScan) put_xy(xy_env, a, x.px, x.py);
+        rec_env[a] = T4{x.px, x.py, x.vx, x.vy};
+        T* ow = sown + (size_t(k) * GA + tid) * 4;
+        ow[0] = x.th;
+        ow[1] = x.s;
+        ow[2] = x.w;
         if (k == S - 1) break;
         T fx = T(0), fy = T(0);
         if (FL & F_COLL) {
           __syncthreads();
-          int cutoff;
-          neighbor_force<T, FL>(spv + k * GA, srad, base, A, a, x, P, W, fx, fy, cutoff);
+          if (FL & F_MASK) {
+            mask_force(rec_env, rad_env, R.cmask[((long long)t * S + k) * EA + ia], x, P, W, fx, fy);
+          } else {
+            int cutoff;
+            unsigned cm;
+            neighbor_force<T, FL, AS>(xy_env, rec_env, rad_env, A, a, x, P, W, fx, fy, cutoff, cm);
+          }
         }
-        static_force<T, FL>(sobs + le * R.N, R.N, x, P, W, fx, fy);
+        static_force<T, FL>(obs_env, R.N, x, P, W, fx, fy);
         Agent<T> y;
         integrate_sel<T, FL>(x, a0, a1, fx, fy, P, W, y);
         x = y;
       }
       Agent<T> out = nxt;
       for (int k = S - 1; k >= 0; --k) {
-        const T4 pv = spv[k * GA + tid];
-        const T4 ow = sown[k * GA + tid];
-        Agent<T> in{pv.x, pv.y, ow.x, pv.z, pv.w, ow.y, ow.z};
+        T* xy_env = sxy + (k * G + le) * NP4;
+        T4* rec_env = srec + k * GA + le * A;
+        const T* ow = sown + (size_t(k) * GA + tid) * 4;
+        const T4 rr = rec_env[a];
+        Agent<T> in{rr.x, rr.y, ow[0], rr.z, rr.w, ow[1], ow[2]};
         Agent<T> gin;
         T gfx, gfy;
         integrate_vjp_sel<T, FL>(in, a0, a1, out, g, P, W, gin, gfx, gfy, ga0, ga1);
-        sfb[fbuf * GA + tid] = T2{gfx, gfy};
-        if (FL & F_TRUNC) scut[fbuf * GA + tid] = R.cutoff[((long long)t * S + k) * EA + ia];
+        T2* fb_env = sfb + fbuf * GA + le * A;
+        int* cut_env = scut + fbuf * GA + le * A;
+        fb_env[a] = T2{gfx, gfy};
+        const long long ws = ((long long)t * S + k) * EA + ia;
+        if (FL & F_TRUNC) cut_env[a] = R.cutoff[ws];
+        const unsigned cm = (FL & F_MASK) ? R.cmask[ws] : 0u;
         __syncthreads();
-        force_vjp<T, FL>(spv + k * GA, sfb + fbuf * GA, scut + fbuf * GA, srad, sden,
-                         sobs + le * R.N, R.N, base, A, a, in, P, W, gfx, gfy, gin);
+        force_vjp<T, FL, AS>(xy_env, rec_env, fb_env, cut_env, rad_env, iden_env, obs_env, R.N, A,
+                             a, cm, in, P, W, gfx, gfy, gin);
         g = gin;
         out = in;
         fbuf ^= 1;
@@ -512,6 +657,10 @@ __global__ void __launch_bounds__(1024) rollout_bwd_kernel(const RolloutArgs<T> 
       }
     }
     nxt = cur;
+    cur = pcur;
+    a0 = pa0;
+    a1 = pa1;
+    cm0 = pcm;
   }
   if (valid) store_state(R.gi_pos, R.gi_th, R.gi_vel, R.gi_s, R.gi_w, ia, g);
 }
@@ -524,19 +673,24 @@ __global__ void __launch_bounds__(1024) neighbors_kernel(int E, int A, int G, in
   using T2 = typename V2<T>::t;
   using T4 = typename V4<T>::t;
   extern __shared__ __align__(16) unsigned char smem[];
-  T4* spv = reinterpret_cast<T4*>(smem);
+  const int NP4 = ((A + 1) / 2) * 4;
+  T* sxy = reinterpret_cast<T*>(smem);
+  T4* srec = reinterpret_cast<T4*>(smem + ((size_t(G) * NP4 * sizeof(T) + 15) & ~size_t(15)));
   const int tid = threadIdx.x;
   const int le = tid / A, a = tid - le * A;
   const int e = blockIdx.x * G + le;
   const bool valid = e < E;
   const int ec = valid ? e : E - 1;
   const long long ia = (long long)ec * A + a;
+  init_pads(sxy, 1, G, A);
   const T2 p = reinterpret_cast<const T2*>(pos)[ia];
-  spv[tid] = T4{p.x, p.y, T(0), T(0)};
+  T* xy_env = sxy + le * NP4;
+  put_xy(xy_env, a, p.x, p.y);
+  srec[tid] = T4{p.x, p.y, T(0), T(0)};
   __syncthreads();
   int listed = 0;
-  const int total = scan_radius<T>(spv, le * A, A, a, p.x, p.y, r2_thr,
-                                   [&](int b, T, T, T, const T4&) {
+  const int total = for_each_in_radius<T, 0>(xy_env, srec + le * A, A, a, p.x, p.y, r2_thr,
+                                             [&](int b, const T4&) {
     if (listed < K) {
       if (valid) idx[ia * K + listed] = b;
       ++listed;
