@@ -16,6 +16,7 @@ agents; their gradient is therefore the identity.
 
 from __future__ import annotations
 
+from collections.abc import Sequence
 from dataclasses import dataclass
 from typing import NamedTuple
 
@@ -38,22 +39,51 @@ class TorchState(NamedTuple):
     body_rates: torch.Tensor | None = None
 
 
+_DRONE_DEFAULTS: dict[tuple, tuple[torch.Tensor, ...]] = {}
+
+
 def fill_state_defaults(state: TorchState) -> TorchState:
-    """Materialise absent drone fields as zeros (identity attitude)."""
+    """Materialise absent drone fields as zeros (identity attitude).
+
+    The 2-D path never writes these fields, so the defaults of one batch shape are
+    allocated once and shared (read-only) by every state that omits them.
+    """
     if all(t is not None for t in state):
         return state
     ref = state.pos
     E, A = ref.shape[0], ref.shape[1]
-    opts = {"device": ref.device, "dtype": ref.dtype}
-    z = state.z if state.z is not None else torch.zeros(E, A, **opts)
-    vz = state.vz if state.vz is not None else torch.zeros(E, A, **opts)
-    if state.attitude is not None:
-        att = state.attitude
-    else:
+    key = (E, A, ref.dtype, ref.device)
+    dflt = _DRONE_DEFAULTS.get(key)
+    if dflt is None:
+        opts = {"device": ref.device, "dtype": ref.dtype}
         att = torch.zeros(E, A, 4, **opts)
         att[..., 3] = 1.0
-    br = state.body_rates if state.body_rates is not None else torch.zeros(E, A, 3, **opts)
+        dflt = (torch.zeros(E, A, **opts), torch.zeros(E, A, **opts), att,
+                torch.zeros(E, A, 3, **opts))
+        _DRONE_DEFAULTS[key] = dflt
+    z = state.z if state.z is not None else dflt[0]
+    vz = state.vz if state.vz is not None else dflt[1]
+    att = state.attitude if state.attitude is not None else dflt[2]
+    br = state.body_rates if state.body_rates is not None else dflt[3]
     return state._replace(z=z, vz=vz, attitude=att, body_rates=br)
+
+
+class Trajectory(Sequence):
+    """``trajectory[t]`` is the :class:`TorchState` after step ``t``: views of the stacked
+    ``[T, ...]`` rollout outputs, built on access (a T-step list of views costs more host
+    time than the fused rollout itself at large horizons). Behaves as a read-only list."""
+
+    def __init__(self, stacked: tuple[torch.Tensor, ...], extra: tuple) -> None:
+        self.stacked = stacked
+        self.extra = extra
+
+    def __len__(self) -> int:
+        return self.stacked[0].shape[0]
+
+    def __getitem__(self, t):
+        if isinstance(t, slice):
+            return [self[i] for i in range(*t.indices(len(self)))]
+        return TorchState(*(f[t] for f in self.stacked), *self.extra)
 
 
 class _RolloutFn(torch.autograd.Function):
@@ -113,7 +143,8 @@ def rollout(
     """Backprop-through-time rollout over ``actions_seq [T, n_envs, n_agents, act_dim]``.
 
     Returns ``(final_state, trajectory)``; ``trajectory[t]`` is the state after step
-    ``t``. Gradients flow to ``state`` and ``actions_seq``.
+    ``t`` (a read-only sequence of :class:`TorchState`; ``trajectory.stacked`` holds the
+    five ``[T, ...]`` tensors). Gradients flow to ``state`` and ``actions_seq``.
     """
     T = actions_seq.shape[0]
     if ring is not None:
@@ -121,8 +152,7 @@ def rollout(
         for _ in range(T):
             ring.acquire()
     fin, traj, extra = _run(stepper, state, actions_seq)
-    trajectory = [TorchState(*(f[t] for f in traj), *extra) for t in range(T)]
-    return fin, trajectory
+    return fin, Trajectory(tuple(traj), extra)
 
 
 @dataclass
