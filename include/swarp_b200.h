@@ -37,6 +37,8 @@ extern "C" {
 #define SWARP_ERR_TOO_MANY_AGENTS (-3) /* n_agents above SWARP_MAX_AGENTS            */
 #define SWARP_ERR_CUDA (-4)          /* a CUDA launch or attribute call failed       */
 #define SWARP_ERR_WORKSPACE (-5)     /* workspace pointer null or too small          */
+#define SWARP_ERR_SCRATCH_LIMIT (-6) /* swarp_rollout_noalloc: rollout needs more workspace
+                                        than SWARP_NOALLOC_SCRATCH_BYTES                 */
 
 #define SWARP_MAX_AGENTS 1024
 #define SWARP_NUM_PARAMS 22
@@ -144,6 +146,26 @@ int swarp_rollout_bwd(const swarp_world_t* w, int32_t horizon, swarp_state_t ini
  * count [E, A], true_count [E, A] (uncapped). */
 int swarp_neighbors(const swarp_world_t* w, const void* pos, int32_t* idx, int32_t* count,
                     int32_t* true_count, void* stream);
+
+/* Allocation-free BPTT rollout: swarp_rollout_fwd followed by swarp_rollout_bwd in one
+ * call, for callers that cannot allocate device memory (a plugin under another
+ * runtime's memory manager, such as an XLA/JAX custom call; a real-time loop or a
+ * stream being captured into a CUDA graph, where cudaMalloc may synchronize the device).
+ * This entry point has no counterpart in the reference. The two kernels' shared
+ * workspace lives in a static device array of SWARP_NOALLOC_SCRATCH_BYTES that the
+ * library owns (one per GPU that loads it, held until the process exits); nothing else
+ * is allocated. Arguments mean what they mean for swarp_rollout_fwd / _bwd (final_out,
+ * adj_traj, adj_final fields may be NULL); movable bodies are not accepted here.
+ * Returns SWARP_ERR_SCRATCH_LIMIT when swarp_rollout_workspace_bytes() exceeds
+ * SWARP_NOALLOC_SCRATCH_BYTES. The first call on each device resolves the array's
+ * device address (cudaGetSymbolAddress) with that device current: make it before any
+ * stream capture. All calls share the array, so calls that overlap on one GPU race on
+ * it; serialize them. */
+#define SWARP_NOALLOC_SCRATCH_BYTES (16u << 20)
+int swarp_rollout_noalloc(const swarp_world_t* w, int32_t horizon, swarp_state_t init,
+                          const void* actions, swarp_state_t traj, swarp_state_t final_out,
+                          swarp_state_t adj_traj, swarp_state_t adj_final, void* adj_actions,
+                          swarp_state_t adj_init, void* stream);
 
 /* Static description of a return code. */
 const char* swarp_error_string(int code);

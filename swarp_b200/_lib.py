@@ -21,6 +21,7 @@ ERRORS = {
     -3: "too many agents",
     -4: "CUDA launch failed",
     -5: "workspace missing or too small",
+    -6: "rollout needs more workspace than the allocation-free entry point's static scratch",
 }
 MAX_AGENTS = 1024
 
@@ -76,6 +77,8 @@ SIGNATURES = {
                                     C.c_size_t, C.c_void_p]),
     "swarp_neighbors": (C.c_int, [C.POINTER(WorldC), C.c_void_p, C.c_void_p, C.c_void_p,
                                   C.c_void_p, C.c_void_p]),
+    "swarp_rollout_noalloc": (C.c_int, [C.POINTER(WorldC), C.c_int32, State, C.c_void_p, State,
+                                        State, State, State, C.c_void_p, State, C.c_void_p]),
     "swarp_error_string": (C.c_char_p, [C.c_int]),
     "swarp_abi_version": (C.c_int32, []),
 }

@@ -267,6 +267,9 @@ const char* swarp_error_string(int code) {
     case SWARP_ERR_TOO_MANY_AGENTS: return "n_agents above SWARP_MAX_AGENTS";
     case SWARP_ERR_CUDA: return "CUDA launch or attribute call failed";
     case SWARP_ERR_WORKSPACE: return "workspace missing or too small";
+    case SWARP_ERR_SCRATCH_LIMIT:
+      return "rollout needs more workspace than the allocation-free entry point's static "
+             "scratch (SWARP_NOALLOC_SCRATCH_BYTES)";
     default: return "unknown error code";
   }
 }
