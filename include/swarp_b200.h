@@ -75,6 +75,11 @@ typedef struct {
   const void* body_off;  /* [N, 2] shape placement in its body frame */
   int32_t any_movable;   /* 1 when any kind == 1 (host-known; selects the body pass) */
   int32_t bodies_move;   /* 0 freezes movable bodies (the reference's taped-step rule) */
+  int32_t movable_shapes; /* host-known bitmask (1 << shape) over the shapes of movable
+                             bodies; the adjoint differentiates circle bodies only */
+  int32_t poses_from_bodies; /* 1: moving shapes start at the poses placed from the bodies'
+                                initial state (a continuing rollout); 0: at the installed
+                                pos/angle/vel/ang_vel (the first substep after an install) */
 } swarp_obstacles_t;
 
 /* Movable-body state per shape slot (only body-root slots are meaningful):
@@ -133,7 +138,8 @@ int swarp_rollout_fwd(const swarp_world_t* w, int32_t horizon, swarp_state_t ini
  * workspace). Cotangents: adj_traj [T, ...] and adj_final (any field may be NULL =
  * zero), adj_bodies_final (fields may be NULL; body pos/angle/vel/ang_vel after the
  * last step). Outputs: adj_actions [T, E, A, act_dim] and adj_init (all five fields
- * required). Deterministic: no atomics, fixed summation order. */
+ * required). Deterministic: no atomics, fixed summation order. Moving bodies are
+ * differentiated when all their shapes are circles (SWARP_ERR_UNSUPPORTED otherwise). */
 int swarp_rollout_bwd(const swarp_world_t* w, int32_t horizon, swarp_state_t init,
                       const void* actions, swarp_state_t traj, swarp_state_t adj_traj,
                       swarp_state_t adj_final, swarp_bodies_t bodies_init,

@@ -39,7 +39,8 @@ class ObstaclesC(C.Structure):
         ("shape", C.c_void_p), ("kind", C.c_void_p),
         ("mass", C.c_void_p), ("inertia", C.c_void_p),
         ("body", C.c_void_p), ("body_off", C.c_void_p),
-        ("any_movable", C.c_int32), ("bodies_move", C.c_int32),
+        ("any_movable", C.c_int32), ("bodies_move", C.c_int32), ("movable_shapes", C.c_int32),
+        ("poses_from_bodies", C.c_int32),
     ]
 
 

@@ -13,6 +13,7 @@ reference's Warp dtype argument has no meaning without Warp.
 from __future__ import annotations
 
 import ctypes as C
+from dataclasses import dataclass, replace
 
 import numpy as np
 import torch
@@ -45,6 +46,19 @@ def _as_torch_dtype(dtype) -> torch.dtype:
         if key in name:
             return _DTYPES[key]
     raise TypeError(f"unsupported dtype {dtype!r}; use torch.float32 or torch.float64")
+
+
+@dataclass
+class RolloutRecord:
+    """What a forward rollout hands to its adjoint: the exact C world it ran with, and
+    the buffers that world points to (kept alive until the adjoint has run)."""
+
+    wc: _lib.WorldC
+    workspace: torch.Tensor
+    obstacles: object
+    body_init: tuple | None
+    body_traj: tuple | None
+    moving: bool
 
 
 class Stepper:
@@ -118,11 +132,17 @@ class Stepper:
         self.n_obstacles = 0
         self.obstacles: Obstacles | None = None
         self.any_movable = False
-        #: Movable bodies advance on grad (taped) steps too, so gradients flow through
-        #: them. False reproduces the reference's taped-step rule (bodies frozen,
-        #: swarp/core/stepper.py:593-601).
-        self.bodies_in_grad = True
+        #: Bitmask (1 << ObstacleShape) of the shapes belonging to movable bodies.
+        self.movable_shapes = 0
+        #: Whether movable bodies advance on grad (taped) rollouts. False (default) is the
+        #: reference's rule: a taped step freezes them (swarp/core/stepper.py:593-601)
+        #: and only no-grad steps integrate them. True integrates them on grad rollouts
+        #: as well and differentiates through them (bodies of circle shapes).
+        self.bodies_in_grad = False
+        #: Body state per obstacle slot (pos [E,N,2], angle [E,N], vel [E,N,2],
+        #: ang_vel [E,N]); only body-root slots are meaningful.
         self.body_state: tuple[torch.Tensor, ...] | None = None
+        self._poses_from_bodies = False
         # (n_envs, act_dim) -> filled swarp_world_t; cleared whenever an input it points to
         # is replaced (obstacles, per-env parameters).
         self._wc_cache: dict[tuple[int, int], _lib.WorldC] = {}
@@ -134,8 +154,13 @@ class Stepper:
         self._wc_cache.clear()
         self.obstacles = obs
         self.n_obstacles = obs.n_obstacles
-        self.any_movable = bool((obs.kind != 0).any().item())
+        moving = obs.kind[obs.body.long()] != 0  # shapes whose body root is movable
+        self.any_movable = bool(moving.any().item())
+        self.movable_shapes = 0
+        self._poses_from_bodies = False
         if self.any_movable:
+            for st in obs.shape[moving].unique().tolist():
+                self.movable_shapes |= 1 << int(st)
             self.body_state = self._body_seed(obs)
         else:
             self.body_state = None
@@ -231,8 +256,37 @@ class Stepper:
             oc.mass, oc.inertia = o.mass.data_ptr(), o.inertia.data_ptr()
             oc.body, oc.body_off = o.body.data_ptr(), o.body_offset.data_ptr()
             oc.any_movable = int(self.any_movable)
-            oc.bodies_move = 1
+            oc.bodies_move = int(self.any_movable)
+            oc.movable_shapes = self.movable_shapes
+            oc.poses_from_bodies = int(self._poses_from_bodies)
         return wc
+
+    def _advance_bodies(self, body_traj) -> None:
+        """After a rollout that moved the bodies: the final body state becomes the stepper's,
+        and the moving shapes are re-placed on it (as the reference's body pass leaves its
+        obstacle arrays). The next rollout places them from the body state itself."""
+        bpos, bang, bvel, bom = (x[-1].clone() for x in body_traj)
+        self.body_state = (bpos, bang, bvel, bom)
+        o = self.obstacles
+        root = o.body.long()
+        moving = (o.kind[root] != 0).view(1, -1)
+        ang = bang[:, root]
+        ca, sa = torch.cos(ang), torch.sin(ang)
+        offx, offy = o.body_offset[:, 0], o.body_offset[:, 1]
+        owx = ca * offx - sa * offy
+        owy = sa * offx + ca * offy
+        om = bom[:, root]
+        pos = torch.stack([bpos[:, root, 0] + owx, bpos[:, root, 1] + owy], -1)
+        vel = torch.stack([bvel[:, root, 0] - om * owy, bvel[:, root, 1] + om * owx], -1)
+        m2 = moving.unsqueeze(-1)
+        new = replace(o, pos=torch.where(m2, pos, o.pos).contiguous(),
+                      angle=torch.where(moving, ang, o.angle).contiguous(),
+                      vel=torch.where(m2, vel, o.vel).contiguous(),
+                      ang_vel=torch.where(moving, om, o.ang_vel).contiguous())
+        new._resolved_for = o._resolved_for
+        self.obstacles = new
+        self._poses_from_bodies = True
+        self._wc_cache.clear()
 
     # -------------------------------------------------------------- launches
     def _check_inputs(self, state, actions: torch.Tensor, horizon_dim: bool):
@@ -263,16 +317,21 @@ class Stepper:
         return int(lib.swarp_rollout_workspace_bytes(C.byref(wc), horizon))
 
     def rollout_forward(self, state5, actions: torch.Tensor, *, final: bool = True,
-                        out=None, true_count: bool = False):
+                        out=None, true_count: bool = False, moving_bodies: bool = True):
         """Run the forward rollout kernel.
 
         ``state5`` are the five contiguous initial-state tensors, ``actions`` is
-        ``[T, E, A, act_dim]``. Returns ``(traj5, final5 | None, true_max | None,
-        workspace)`` with ``traj5`` stacked ``[T, E, A(,2)]``.
+        ``[T, E, A, act_dim]``. Movable bodies (if any) advance when ``moving_bodies``; the
+        stepper then carries their final state. Returns ``(traj5, final5 | None,
+        true_max | None, record)`` with ``traj5`` stacked ``[T, E, A(,2)]`` and ``record``
+        the :class:`RolloutRecord` the adjoint needs.
         """
         lib = _lib.load()
         H, E, _, D = actions.shape
+        moving = bool(self.any_movable and moving_bodies)
         wc = self.world_c(E, D)
+        if self.n_obstacles > 0:
+            wc.obstacles.bodies_move = int(moving)
         opts = {"device": self.device, "dtype": self.dtype}
         if out is None:
             traj = (torch.empty(H, E, self.n_agents, 2, **opts), torch.empty(H, E, self.n_agents, **opts),
@@ -285,27 +344,52 @@ class Stepper:
                 if true_count else None)
         nbytes = int(lib.swarp_rollout_workspace_bytes(C.byref(wc), H))
         ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=self.device)
+        bi = bt = None
+        if moving:
+            N = self.n_obstacles
+            bi = self.body_state
+            bt = (torch.empty(H, E, N, 2, **opts), torch.empty(H, E, N, **opts),
+                  torch.empty(H, E, N, 2, **opts), torch.empty(H, E, N, **opts))
+        rec = RolloutRecord(type(wc).from_buffer_copy(wc), ws, self.obstacles, bi, bt, moving)
         rc = lib.swarp_rollout_fwd(
-            C.byref(wc), H, _lib.state_c(state5), actions.data_ptr(), _lib.state_c(traj),
-            _lib.state_c(fin) if fin else _lib.State(), _lib.ptr(tmax), _lib.Bodies(),
-            _lib.Bodies(), ws.data_ptr(), nbytes, _lib.stream_ptr(self.device),
+            C.byref(rec.wc), H, _lib.state_c(state5), actions.data_ptr(), _lib.state_c(traj),
+            _lib.state_c(fin) if fin else _lib.State(), _lib.ptr(tmax),
+            _lib.Bodies(*(_lib.ptr(x) for x in bi)) if bi else _lib.Bodies(),
+            _lib.Bodies(*(_lib.ptr(x) for x in bt)) if bt else _lib.Bodies(),
+            ws.data_ptr(), nbytes, _lib.stream_ptr(self.device),
         )
         _lib.check(rc, "swarp_rollout_fwd")
-        return traj, fin, tmax, ws
+        if moving:
+            self._advance_bodies(bt)
+        return traj, fin, tmax, rec
 
-    def rollout_backward(self, state5, actions, traj5, gtraj5, gfin5, workspace):
+    def rollout_backward(self, state5, actions, traj5, gtraj5, gfin5, record: RolloutRecord,
+                         gbody_final=None):
+        """Adjoint of :meth:`rollout_forward` for the same inputs and its ``record``.
+
+        ``gbody_final``: cotangents of the final body state (pos, angle, vel, ang_vel;
+        entries may be None). Returns ``(grad_actions, grad_init5)``.
+        """
         lib = _lib.load()
-        H, E, _, D = actions.shape
-        wc = self.world_c(E, D)
         g_act = torch.empty_like(actions)
         g_init = tuple(torch.empty_like(t) for t in state5)
+        rec = record
+        ws = rec.workspace
+        gb = _lib.Bodies()
+        keep = ()
+        if gbody_final is not None:
+            keep = tuple(None if x is None else x.contiguous() for x in gbody_final)
+            gb = _lib.Bodies(*(_lib.ptr(x) for x in keep))
         rc = lib.swarp_rollout_bwd(
-            C.byref(wc), H, _lib.state_c(state5), actions.data_ptr(), _lib.state_c(traj5),
-            _lib.state_c(gtraj5), _lib.state_c(gfin5), _lib.Bodies(), _lib.Bodies(), _lib.Bodies(),
-            g_act.data_ptr(), _lib.state_c(g_init), workspace.data_ptr(), workspace.numel(),
+            C.byref(rec.wc), actions.shape[0], _lib.state_c(state5), actions.data_ptr(),
+            _lib.state_c(traj5), _lib.state_c(gtraj5), _lib.state_c(gfin5),
+            _lib.Bodies(*(_lib.ptr(x) for x in rec.body_init)) if rec.body_init else _lib.Bodies(),
+            _lib.Bodies(*(_lib.ptr(x) for x in rec.body_traj)) if rec.body_traj else _lib.Bodies(),
+            gb, g_act.data_ptr(), _lib.state_c(g_init), ws.data_ptr(), ws.numel(),
             _lib.stream_ptr(self.device),
         )
         _lib.check(rc, "swarp_rollout_bwd")
+        del keep
         return g_act, g_init
 
     def neighbors(self, pos: torch.Tensor):

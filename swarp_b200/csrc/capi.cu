@@ -14,7 +14,7 @@ using namespace swarp;
 
 namespace {
 
-constexpr int kAbiVersion = 1;
+constexpr int kAbiVersion = 2;
 
 int threads_target() {
   static int v = [] {
@@ -63,7 +63,8 @@ int validate_world(const swarp_world_t* w, int horizon) {
   if (o.n_obstacles > 0) {
     if (!o.pos || !o.angle || !o.vel || !o.ang_vel || !o.radius || !o.half || !o.shape)
       return SWARP_ERR_INVALID_ARG;
-    if (o.any_movable && o.bodies_move) return SWARP_ERR_UNSUPPORTED;
+    if (o.any_movable && o.bodies_move && (!o.kind || !o.mass || !o.inertia || !o.body || !o.body_off))
+      return SWARP_ERR_INVALID_ARG;
   }
   return SWARP_OK;
 }
@@ -81,7 +82,10 @@ int flags_of(const swarp_world_t* w) {
     else if (w->n_agents <= 32)
       fl |= F_MASK;
   }
-  if (w->obstacles.n_obstacles > 0) fl |= F_OBS;
+  if (w->obstacles.n_obstacles > 0) {
+    fl |= F_OBS;
+    if (w->obstacles.any_movable && w->obstacles.bodies_move) fl |= F_BODIES;
+  }
   if (w->fleet_models == 1 && w->fleet_modes == 1) fl |= F_HOLOVEL;
   return fl;
 }
@@ -124,7 +128,24 @@ void fill_common(const swarp_world_t* w, int horizon, RolloutArgs<T>& R) {
     R.o_radius = static_cast<const T*>(o.radius);
     R.o_half = static_cast<const T*>(o.half);
     R.o_shape = o.shape;
+    R.o_kind = o.kind;
+    R.o_body = o.body;
+    R.o_mass = static_cast<const T*>(o.mass);
+    R.o_inertia = static_cast<const T*>(o.inertia);
+    R.o_body_off = static_cast<const T*>(o.body_off);
   }
+  R.body_clamp = w->bounds_mode != SWARP_BOUNDS_NONE;
+  R.poses_from_bodies = o.poses_from_bodies;
+}
+
+bool bodies_complete(const swarp_bodies_t& b) { return b.pos && b.angle && b.vel && b.ang_vel; }
+
+template <typename T>
+void set_bodies(const swarp_bodies_t& b, const T*& p, const T*& a, const T*& v, const T*& w) {
+  p = static_cast<const T*>(b.pos);
+  a = static_cast<const T*>(b.angle);
+  v = static_cast<const T*>(b.vel);
+  w = static_cast<const T*>(b.ang_vel);
 }
 
 template <typename T>
@@ -147,10 +168,15 @@ void set_state_out(const swarp_state_t& s, T*& p, T*& th, T*& v, T*& sp, T*& w) 
 
 template <typename T>
 int fwd_typed(const swarp_world_t* w, int horizon, swarp_state_t init, const void* actions,
-              swarp_state_t traj, swarp_state_t fin, int32_t* true_max, void* ws,
-              cudaStream_t st) {
+              swarp_state_t traj, swarp_state_t fin, int32_t* true_max, swarp_bodies_t bi,
+              swarp_bodies_t bt, void* ws, cudaStream_t st) {
   RolloutArgs<T> R;
   fill_common<T>(w, horizon, R);
+  set_bodies<T>(bi, R.bi_pos, R.bi_ang, R.bi_vel, R.bi_om);
+  R.bt_pos = static_cast<T*>(bt.pos);
+  R.bt_ang = static_cast<T*>(bt.angle);
+  R.bt_vel = static_cast<T*>(bt.vel);
+  R.bt_om = static_cast<T*>(bt.ang_vel);
   set_state<T>(init, R.i_pos, R.i_th, R.i_vel, R.i_s, R.i_w);
   R.act = static_cast<const T*>(actions);
   set_state_out<T>(traj, R.t_pos, R.t_th, R.t_vel, R.t_s, R.t_w);
@@ -164,10 +190,17 @@ int fwd_typed(const swarp_world_t* w, int horizon, swarp_state_t init, const voi
 
 template <typename T>
 int bwd_typed(const swarp_world_t* w, int horizon, swarp_state_t init, const void* actions,
-              swarp_state_t traj, swarp_state_t gtraj, swarp_state_t gfin, void* gact,
-              swarp_state_t ginit, const void* ws, cudaStream_t st) {
+              swarp_state_t traj, swarp_state_t gtraj, swarp_state_t gfin, swarp_bodies_t bi,
+              swarp_bodies_t bt, swarp_bodies_t gbf, void* gact, swarp_state_t ginit,
+              const void* ws, cudaStream_t st) {
   RolloutArgs<T> R;
   fill_common<T>(w, horizon, R);
+  set_bodies<T>(bi, R.bi_pos, R.bi_ang, R.bi_vel, R.bi_om);
+  R.bt_pos = static_cast<T*>(bt.pos);
+  R.bt_ang = static_cast<T*>(bt.angle);
+  R.bt_vel = static_cast<T*>(bt.vel);
+  R.bt_om = static_cast<T*>(bt.ang_vel);
+  set_bodies<T>(gbf, R.gb_pos, R.gb_ang, R.gb_vel, R.gb_om);
   set_state<T>(init, R.i_pos, R.i_th, R.i_vel, R.i_s, R.i_w);
   R.act = static_cast<const T*>(actions);
   set_state_out<T>(traj, R.t_pos, R.t_th, R.t_vel, R.t_s, R.t_w);
@@ -208,19 +241,21 @@ int swarp_rollout_fwd(const swarp_world_t* w, int32_t horizon, swarp_state_t ini
                       int32_t* true_count_max, swarp_bodies_t bodies_init,
                       swarp_bodies_t bodies_traj, void* workspace, size_t workspace_bytes,
                       void* stream) {
-  (void)bodies_init;
-  (void)bodies_traj;
   int rc = validate_world(w, horizon);
   if (rc != SWARP_OK) return rc;
   if (!state_complete(init) || !state_complete(traj) || !actions) return SWARP_ERR_INVALID_ARG;
+  if ((flags_of(w) & F_BODIES) && (!bodies_complete(bodies_init) || !bodies_complete(bodies_traj)))
+    return SWARP_ERR_INVALID_ARG;
   const bool any_fin = final_out.pos || final_out.theta || final_out.vel || final_out.speed || final_out.ang_vel;
   if (any_fin && !state_complete(final_out)) return SWARP_ERR_INVALID_ARG;
   const size_t need = swarp_rollout_workspace_bytes(w, horizon);
   if (need > 0 && (!workspace || workspace_bytes < need)) return SWARP_ERR_WORKSPACE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (w->dtype == SWARP_F32)
-    return fwd_typed<float>(w, horizon, init, actions, traj, final_out, true_count_max, workspace, st);
-  return fwd_typed<double>(w, horizon, init, actions, traj, final_out, true_count_max, workspace, st);
+    return fwd_typed<float>(w, horizon, init, actions, traj, final_out, true_count_max, bodies_init,
+                            bodies_traj, workspace, st);
+  return fwd_typed<double>(w, horizon, init, actions, traj, final_out, true_count_max, bodies_init,
+                           bodies_traj, workspace, st);
 }
 
 int swarp_rollout_bwd(const swarp_world_t* w, int32_t horizon, swarp_state_t init,
@@ -229,11 +264,12 @@ int swarp_rollout_bwd(const swarp_world_t* w, int32_t horizon, swarp_state_t ini
                       swarp_bodies_t bodies_traj, swarp_bodies_t adj_bodies_final,
                       void* adj_actions, swarp_state_t adj_init, const void* workspace,
                       size_t workspace_bytes, void* stream) {
-  (void)bodies_init;
-  (void)bodies_traj;
-  (void)adj_bodies_final;
   int rc = validate_world(w, horizon);
   if (rc != SWARP_OK) return rc;
+  if (flags_of(w) & F_BODIES) {
+    if (!bodies_complete(bodies_init) || !bodies_complete(bodies_traj)) return SWARP_ERR_INVALID_ARG;
+    if (w->obstacles.movable_shapes & ~(1 << SHAPE_CIRCLE)) return SWARP_ERR_UNSUPPORTED;
+  }
   if (!state_complete(init) || !state_complete(traj) || !state_complete(adj_init) || !actions ||
       !adj_actions)
     return SWARP_ERR_INVALID_ARG;
@@ -241,10 +277,10 @@ int swarp_rollout_bwd(const swarp_world_t* w, int32_t horizon, swarp_state_t ini
   if (need > 0 && (!workspace || workspace_bytes < need)) return SWARP_ERR_WORKSPACE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (w->dtype == SWARP_F32)
-    return bwd_typed<float>(w, horizon, init, actions, traj, adj_traj, adj_final, adj_actions,
-                            adj_init, workspace, st);
-  return bwd_typed<double>(w, horizon, init, actions, traj, adj_traj, adj_final, adj_actions,
-                           adj_init, workspace, st);
+    return bwd_typed<float>(w, horizon, init, actions, traj, adj_traj, adj_final, bodies_init,
+                            bodies_traj, adj_bodies_final, adj_actions, adj_init, workspace, st);
+  return bwd_typed<double>(w, horizon, init, actions, traj, adj_traj, adj_final, bodies_init,
+                           bodies_traj, adj_bodies_final, adj_actions, adj_init, workspace, st);
 }
 
 int swarp_neighbors(const swarp_world_t* w, const void* pos, int32_t* idx, int32_t* count,

@@ -37,21 +37,23 @@ inline int launch_kernel(K kernel, int grid, int block, size_t smem, cudaStream_
 
 template <typename T, int FL, int AS>
 int run_fwd(const RolloutArgs<T>& R, cudaStream_t st) {
-  const Layout<T> L(R.G, R.A, R.N, R.S, false);
+  const Layout<T> L(R.G, R.A, R.N, R.S, false, (FL & F_BODIES) != 0);
   return launch_kernel(rollout_fwd_kernel<T, FL, AS>, (R.E + R.G - 1) / R.G, R.G * R.A, L.total,
                        st, &R);
 }
 template <typename T, int FL, int AS>
 int run_bwd(const RolloutArgs<T>& R, cudaStream_t st) {
-  const Layout<T> L(R.G, R.A, R.N, R.S, true);
+  const Layout<T> L(R.G, R.A, R.N, R.S, true, (FL & F_BODIES) != 0);
   return launch_kernel(rollout_bwd_kernel<T, FL, AS>, (R.E + R.G - 1) / R.G, R.G * R.A, L.total,
                        st, &R);
 }
 
 // Every valid flag combination: no contacts, contacts, truncating contacts, checkpointed
-// contacts; each with/without obstacles and with/without the holonomic-velocity fleet.
-#define SWARP_FLAG_CASES(X) \
-  X(0) X(4) X(8) X(12) X(1) X(5) X(9) X(13) X(3) X(7) X(11) X(15) X(17) X(21) X(25) X(29)
+// contacts; each with/without obstacles and with/without the holonomic-velocity fleet;
+// moving bodies (always with obstacles) with each contact mode and fleet kind.
+#define SWARP_FLAG_CASES(X)                                                                \
+  X(0) X(4) X(8) X(12) X(1) X(5) X(9) X(13) X(3) X(7) X(11) X(15) X(17) X(21) X(25) X(29) \
+  X(36) X(37) X(39) X(53) X(44) X(45) X(47) X(61)
 
 template <typename T> int launch_fwd(const RolloutArgs<T>& R, int fl, cudaStream_t st) {
   const bool a16 = std::is_same<T, float>::value && R.A == 16;

@@ -20,6 +20,7 @@
 // repeats the neighbor scan. Otherwise (A > 32 or a truncating cap) the adjoint
 // rescans, and with truncation the forward stores each list's cutoff index instead.
 #pragma once
+#include "bodies.cuh"
 #include "physics.cuh"
 
 namespace swarp {
@@ -38,6 +39,7 @@ enum : int {
   F_OBS = 4,      // obstacles present
   F_HOLOVEL = 8,  // every agent is holonomic / VELOCITY
   F_MASK = 16,    // contact masks checkpointed (A <= 32, no truncation)
+  F_BODIES = 32,  // movable bodies integrated in the substep loop (with F_OBS)
 };
 
 template <typename T> struct RolloutArgs {
@@ -63,13 +65,23 @@ template <typename T> struct RolloutArgs {
   const T *gf_pos, *gf_th, *gf_vel, *gf_s, *gf_w;  // cotangent of final (nullable)
   T* g_act;
   T *gi_pos, *gi_th, *gi_vel, *gi_s, *gi_w;
+  // movable bodies (F_BODIES): per-shape constants, state per shape slot [E, N] at t = 0
+  // and after every step [H, E, N], cotangent of the final body state (nullable)
+  const int *o_kind, *o_body;
+  const T *o_mass, *o_inertia, *o_body_off;
+  const T *bi_pos, *bi_ang, *bi_vel, *bi_om;
+  T *bt_pos, *bt_ang, *bt_vel, *bt_om;
+  const T *gb_pos, *gb_ang, *gb_vel, *gb_om;
+  int body_clamp;
+  int poses_from_bodies;
 };
 
 // Shared-memory carve-up, identical on host (sizes) and device (pointers).
 template <typename T> struct Layout {
   int G, A, NP, nbuf, S;
-  size_t xy, rec, own, fb, cut, rad, iden, obs, total;
-  __host__ __device__ Layout(int G_, int A_, int N, int S_, bool bwd) : G(G_), A(A_), S(S_) {
+  size_t xy, rec, own, fb, cut, rad, iden, obs, bc, bst, gpose, gag, gbody, gbnew, gshape, total;
+  __host__ __device__ Layout(int G_, int A_, int N, int S_, bool bwd, bool bodies = false)
+      : G(G_), A(A_), S(S_) {
     NP = (A + 1) / 2;
     nbuf = bwd ? (S > 2 ? S : 2) : 2;
     const int GA = G * A;
@@ -83,6 +95,14 @@ template <typename T> struct Layout {
     rad = take(size_t(GA) * sizeof(T));
     iden = take(size_t(GA) * sizeof(T));
     obs = take(size_t(G) * (N > 0 ? N : 0) * sizeof(Obs<T>));
+    const int NB = bodies ? N : 0;
+    bc = take(size_t(NB) * sizeof(BodyC<T>));
+    bst = take(size_t(bwd ? S : 1) * G * NB * sizeof(BodyS<T>));  // body states (per substep)
+    gpose = bwd ? take(size_t(GA) * NB * 4 * sizeof(T)) : 0;       // agent -> shape pose cot.
+    gag = bwd ? take(size_t(bodies ? GA : 0) * 4 * sizeof(T)) : 0;   // body -> agent cot.
+    gbody = bwd ? take(size_t(G) * NB * sizeof(BodyG<T>)) : 0;
+    gbnew = bwd ? take(size_t(G) * NB * sizeof(BodyG<T>)) : 0;
+    gshape = bwd ? take(size_t(G) * NB * 4 * sizeof(T)) : 0;
     total = off;
   }
 };
@@ -168,35 +188,124 @@ __device__ __forceinline__ void load_action(const RolloutArgs<T>& R, long long i
   }
 }
 
-// Obstacles of this CTA's envs into shared memory. Angle -> (cos, sin) once.
+// One obstacle's installed pose and constants (angle -> cos, sin once).
+template <typename T>
+__device__ __forceinline__ Obs<T> make_obs(const RolloutArgs<T>& R, int e, int o) {
+  const long long eo = (long long)e * R.N + o;
+  Obs<T> ob;
+  ob.cx = R.o_pos[2 * eo];
+  ob.cy = R.o_pos[2 * eo + 1];
+  const T ang = R.o_angle[eo];
+  ob.ca = Num<T>::cos_(ang);
+  ob.sa = Num<T>::sin_(ang);
+  ob.vx = R.o_vel[2 * eo];
+  ob.vy = R.o_vel[2 * eo + 1];
+  ob.om = R.o_ang_vel[eo];
+  ob.r = R.o_radius[o];
+  ob.hx = R.o_half[2 * o];
+  ob.hy = R.o_half[2 * o + 1];
+  ob.type = R.o_shape[o];
+  if (ob.type == SHAPE_BOX)
+    ob.bound = len2(ob.hx, ob.hy);
+  else if (ob.type == SHAPE_SEGMENT)
+    ob.bound = ob.hx + ob.r;
+  else
+    ob.bound = ob.r;
+  return ob;
+}
+
+// Obstacles of this CTA's envs into shared memory (the agent pass re-reads them every
+// substep).
 template <typename T>
 __device__ __forceinline__ void load_obstacles(const RolloutArgs<T>& R, Obs<T>* sobs, int e0) {
   const int total = R.G * R.N;
   for (int i = threadIdx.x; i < total; i += blockDim.x) {
     const int le = i / R.N, o = i - le * R.N;
-    int e = e0 + le;
-    if (e >= R.E) e = R.E - 1;
-    const long long eo = (long long)e * R.N + o;
-    Obs<T> ob;
-    ob.cx = R.o_pos[2 * eo];
-    ob.cy = R.o_pos[2 * eo + 1];
-    T ang = R.o_angle[eo];
-    ob.ca = Num<T>::cos_(ang);
-    ob.sa = Num<T>::sin_(ang);
-    ob.vx = R.o_vel[2 * eo];
-    ob.vy = R.o_vel[2 * eo + 1];
-    ob.om = R.o_ang_vel[eo];
-    ob.r = R.o_radius[o];
-    ob.hx = R.o_half[2 * o];
-    ob.hy = R.o_half[2 * o + 1];
-    ob.type = R.o_shape[o];
-    if (ob.type == SHAPE_BOX)
-      ob.bound = len2(ob.hx, ob.hy);
-    else if (ob.type == SHAPE_SEGMENT)
-      ob.bound = ob.hx + ob.r;
+    sobs[i] = make_obs(R, min(e0 + le, R.E - 1), o);
+  }
+}
+
+// ------------------------------------------------------------- movable bodies
+template <typename T>
+__device__ __forceinline__ void load_body_consts(const RolloutArgs<T>& R, BodyC<T>* sbc) {
+  for (int i = threadIdx.x; i < R.N; i += blockDim.x) {
+    BodyC<T> c;
+    c.offx = R.o_body_off[2 * i];
+    c.offy = R.o_body_off[2 * i + 1];
+    c.mass = R.o_mass[i];
+    c.inertia = R.o_inertia[i];
+    c.kind = R.o_kind[i];
+    c.body = R.o_body[i];
+    c.reach = shape_reach(R.o_shape[i], c.offx, c.offy, R.o_radius[i], R.o_half[2 * i],
+                          R.o_half[2 * i + 1]);
+    sbc[i] = c;
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ bool moving_shape(const BodyC<T>* bc, int s) {
+  return bc[bc[s].body].kind == 1;
+}
+template <typename T>
+__device__ __forceinline__ bool moving_root(const BodyC<T>* bc, int o) {
+  return bc[o].body == o && bc[o].kind == 1;
+}
+
+// Body state of one env's N shape slots from [.., E, N] arrays at element base (e*N).
+template <typename T>
+__device__ __forceinline__ void load_bodies(const T* pos, const T* ang, const T* vel, const T* om,
+                                            long long base, int N, BodyS<T>* dst) {
+  for (int o = 0; o < N; ++o) {
+    const long long i = base + o;
+    dst[o] = BodyS<T>{pos[2 * i], pos[2 * i + 1], ang[i], vel[2 * i], vel[2 * i + 1], om[i]};
+  }
+}
+template <typename T>
+__device__ __forceinline__ void store_bodies(T* pos, T* ang, T* vel, T* om, long long base, int N,
+                                             const BodyS<T>* src) {
+  for (int o = 0; o < N; ++o) {
+    const long long i = base + o;
+    const BodyS<T> b = src[o];
+    pos[2 * i] = b.qx;
+    pos[2 * i + 1] = b.qy;
+    ang[i] = b.th;
+    vel[2 * i] = b.vx;
+    vel[2 * i + 1] = b.vy;
+    om[i] = b.om;
+  }
+}
+
+// One substep of every moving body of an env (one thread): reads states `in`, the
+// shapes' current poses and the agents' records; writes states `out` (may alias `in`)
+// and re-places the moving shapes in `obs`.
+template <typename T, typename T4>
+__device__ __forceinline__ void bodies_step(const BodyS<T>* in, BodyS<T>* out, const BodyC<T>* bc,
+                                            Obs<T>* obs, int N, const T4* rec, const T* rad,
+                                            const T* iden, int A, const WorldC<T>& W, bool clamp) {
+  for (int o = 0; o < N; ++o) {
+    if (!moving_root(bc, o)) {
+      if (out != in) out[o] = in[o];
+      continue;
+    }
+    BodyPassOut<T> P;
+    body_pass_root(o, in[o], bc, obs, N, rec, rad, iden, A, W, clamp, P);
+    out[o] = P.next;
+  }
+  for (int s = 0; s < N; ++s)
+    if (moving_shape(bc, s)) place_shape(out[bc[s].body], bc[s], obs[s]);
+}
+
+// Shape poses of substep input states `st`: the installed poses at the very first
+// substep of the rollout, else placed from the body states.
+template <typename T>
+__device__ __forceinline__ void set_body_poses(const RolloutArgs<T>& R, int e, bool installed,
+                                               const BodyS<T>* st, const BodyC<T>* bc, Obs<T>* obs) {
+  for (int s = 0; s < R.N; ++s) {
+    if (!moving_shape(bc, s)) continue;
+    if (installed)
+      obs[s] = make_obs(R, e, s);
     else
-      ob.bound = ob.r;
-    sobs[i] = ob;
+      place_shape(st[bc[s].body], bc[s], obs[s]);
   }
 }
 
@@ -387,28 +496,41 @@ __device__ __forceinline__ void init_pads(T* xy, int nbuf, int G, int A) {
 template <typename T, int FL, int AS>
 __global__ void __launch_bounds__(1024) rollout_fwd_kernel(const RolloutArgs<T> R) {
   using T4 = typename V4<T>::t;
+  constexpr bool kBodies = (FL & F_BODIES) != 0;
+  constexpr bool kShare = (FL & (F_COLL | F_BODIES)) != 0;  // agent records in smem each substep
   extern __shared__ __align__(16) unsigned char smem[];
   const int A = AS > 0 ? AS : R.A;
-  const int G = R.G, GA = G * A;
+  const int G = R.G, GA = G * A, N = R.N;
   const int tid = threadIdx.x;
   const int le = tid / A, a = tid - le * A;
   const int e0 = blockIdx.x * G;
   const int e = e0 + le;
   const bool valid = e < R.E;
   const int ec = valid ? e : R.E - 1;
-  const Layout<T> L(G, A, R.N, R.S, false);
+  const Layout<T> L(G, A, N, R.S, false, kBodies);
   const int NP4 = L.NP * 4;
   T* sxy = reinterpret_cast<T*>(smem + L.xy);
   T4* srec = reinterpret_cast<T4*>(smem + L.rec);
   T* srad = reinterpret_cast<T*>(smem + L.rad);
+  T* siden = reinterpret_cast<T*>(smem + L.iden);
   Obs<T>* sobs = reinterpret_cast<Obs<T>*>(smem + L.obs);
+  BodyC<T>* sbc = reinterpret_cast<BodyC<T>*>(smem + L.bc);
+  BodyS<T>* sbst = reinterpret_cast<BodyS<T>*>(smem + L.bst);  // [G][N]
 
   AgentP<T> P;
   load_params(R, ec, a, P);
   const WorldC<T> W = R.W;
   srad[tid] = P.radius;
+  siden[tid] = P.inv_denom;
   if (FL & F_OBS) load_obstacles(R, sobs, e0);
   if (FL & F_COLL) init_pads(sxy, 2, G, A);
+  if (kBodies) {
+    load_body_consts(R, sbc);
+    if (a == 0) load_bodies(R.bi_pos, R.bi_ang, R.bi_vel, R.bi_om, (long long)ec * N, N, sbst + le * N);
+  }
+  __syncthreads();
+  if (kBodies && R.poses_from_bodies && a == 0)
+    set_body_poses(R, ec, false, sbst + le * N, sbc, sobs + le * N);
   __syncthreads();
 
   const long long ia = (long long)ec * A + a;
@@ -420,16 +542,20 @@ __global__ void __launch_bounds__(1024) rollout_fwd_kernel(const RolloutArgs<T> 
   T a0, a1, n0 = T(0), n1 = T(0);
   load_action(R, ia, a0, a1);
   const T* rad_env = srad + le * A;
+  const T* iden_env = siden + le * A;
+  Obs<T>* obs_env = sobs + le * N;
   for (int t = 0; t < R.H; ++t) {
     if (t + 1 < R.H) load_action(R, (long long)(t + 1) * EA + ia, n0, n1);
     for (int k = 0; k < R.S; ++k) {
       T fx = T(0), fy = T(0);
-      if (FL & F_COLL) {
-        T* xy_env = sxy + (buf * G + le) * NP4;
-        T4* rec_env = srec + buf * GA + le * A;
-        put_xy(xy_env, a, x.px, x.py);
+      T* xy_env = sxy + (buf * G + le) * NP4;
+      T4* rec_env = srec + buf * GA + le * A;
+      if (kShare) {
+        if (FL & F_COLL) put_xy(xy_env, a, x.px, x.py);
         rec_env[a] = T4{x.px, x.py, x.vx, x.vy};
         __syncthreads();
+      }
+      if (FL & F_COLL) {
         int cutoff;
         unsigned cm;
         const int tc = neighbor_force<T, FL, AS>(xy_env, rec_env, rad_env, A, a, x, P, W, fx, fy,
@@ -438,14 +564,23 @@ __global__ void __launch_bounds__(1024) rollout_fwd_kernel(const RolloutArgs<T> 
         const long long ws = ((long long)t * R.S + k) * EA + ia;
         if ((FL & F_TRUNC) && valid) R.cutoff[ws] = (int16_t)cutoff;
         if ((FL & F_MASK) && valid) R.cmask[ws] = cm;
-        buf ^= 1;
       }
-      static_force<T, FL>(sobs + le * R.N, R.N, x, P, W, fx, fy);
+      static_force<T, FL>(obs_env, N, x, P, W, fx, fy);
+      if (kBodies) {
+        __syncthreads();  // every agent has read this substep's shape poses
+        if (a == 0)
+          bodies_step(sbst + le * N, sbst + le * N, sbc, obs_env, N, rec_env, rad_env, iden_env, A,
+                      W, R.body_clamp != 0);
+      }
+      if (kShare) buf ^= 1;
       Agent<T> y;
       integrate_sel<T, FL>(x, a0, a1, fx, fy, P, W, y);
       x = y;
     }
     if (valid) store_state(R.t_pos, R.t_th, R.t_vel, R.t_s, R.t_w, (long long)t * EA + ia, x);
+    if (kBodies && a == 0 && valid)
+      store_bodies(R.bt_pos, R.bt_ang, R.bt_vel, R.bt_om, ((long long)t * R.E + e) * N, N,
+                   sbst + le * N);
     a0 = n0;
     a1 = n1;
   }
@@ -458,14 +593,18 @@ __global__ void __launch_bounds__(1024) rollout_fwd_kernel(const RolloutArgs<T> 
 // ================================================================== adjoint
 // Force VJP of agent a at one substep: given every env agent's (x, y, vx, vy) record and
 // force cotangent, adds d(loss)/d(pos, vel) of agent a through its own force and
-// through the forces its contacts feel from it.
+// through the forces its contacts feel from it. With moving bodies, also writes the
+// cotangent of each moving (circle) shape's centre and velocity through this agent's
+// force into gpose[s] (x, y, vx, vy).
 template <typename T, int FL, int AS>
 __device__ __forceinline__ void force_vjp(const T* xy_env, const typename V4<T>::t* rec_env,
                                           const typename V2<T>::t* fb_env, const int* cut_env,
                                           const T* rad_env, const T* iden_env, const Obs<T>* sobs,
-                                          int N, int A, int a, unsigned cmask, const Agent<T>& x,
+                                          const BodyC<T>* sbc, typename V4<T>::t* gpose, int N,
+                                          int A, int a, unsigned cmask, const Agent<T>& x,
                                           const AgentP<T>& P, const WorldC<T>& W, T gfx, T gfy,
                                           Agent<T>& gin) {
+  using T4 = typename V4<T>::t;
   if (FL & F_MASK) {
     unsigned m = cmask;
     while (m) {
@@ -480,7 +619,7 @@ __device__ __forceinline__ void force_vjp(const T* xy_env, const typename V4<T>:
   } else if (FL & F_COLL) {
     const int cut_a = (FL & F_TRUNC) ? cut_env[a] : A;
     for_each_in_radius<T, AS>(xy_env, rec_env, A, a, x.px, x.py, W.r2_thr,
-                              [&](int b, const typename V4<T>::t& q) {
+                              [&](int b, const T4& q) {
       const bool own = !(FL & F_TRUNC) || b <= cut_a;
       const bool cross = !(FL & F_TRUNC) || a <= cut_env[b];
       const auto gb = fb_env[b];
@@ -491,29 +630,78 @@ __device__ __forceinline__ void force_vjp(const T* xy_env, const typename V4<T>:
     });
   }
   if (FL & F_OBS) {
-    for (int o = 0; o < N; ++o)
+    for (int o = 0; o < N; ++o) {
       obstacle_force_vjp(x.px, x.py, x.vx, x.vy, P.radius, P.inv_denom, sobs[o], gfx, gfy, W,
                          gin.px, gin.py, gin.vx, gin.vy);
+      if ((FL & F_BODIES) && moving_shape(sbc, o)) {
+        T gcx = T(0), gcy = T(0), gvx = T(0), gvy = T(0);
+        circle_obstacle_vjp_pose(x.px, x.py, x.vx, x.vy, P.radius, P.inv_denom, sobs[o], gfx, gfy,
+                                 W, gcx, gcy, gvx, gvy);
+        gpose[o] = T4{gcx, gcy, gvx, gvy};
+      }
+    }
   }
   if (W.bounds_mode == BOUNDS_SOFT)
     wall_force_vjp(x.px, x.py, x.vx, x.vy, P.radius, P.inv_denom, gfx, gfy, W, gin.px, gin.py,
                    gin.vx, gin.vy);
 }
 
+// Adjoint of one env's body substep (one thread): consumes the cotangent of the bodies'
+// output states (gbody) and the agents' shape-pose cotangents (gpose [A][N]); writes the
+// cotangent of the input states back to gbody and the agents' (pos, vel) cotangents
+// through the reactions to gag [A].
+template <typename T, typename T4>
+__device__ __forceinline__ void bodies_step_vjp(const BodyS<T>* st, const BodyC<T>* bc,
+                                                const Obs<T>* obs, int N, const T4* rec,
+                                                const T* rad, const T* iden, int A,
+                                                const WorldC<T>& W, bool clamp, bool placed,
+                                                const T4* gpose, T4* gag, T4* gshape,
+                                                BodyG<T>* gbody, BodyG<T>* gbnew) {
+  for (int s = 0; s < N; ++s) {
+    T4 acc = T4{T(0), T(0), T(0), T(0)};
+    if (moving_shape(bc, s)) {
+      for (int a = 0; a < A; ++a) {
+        const T4 g = gpose[a * N + s];
+        acc.x += g.x;
+        acc.y += g.y;
+        acc.z += g.z;
+        acc.w += g.w;
+      }
+    }
+    gshape[s] = acc;
+  }
+  for (int a = 0; a < A; ++a) gag[a] = T4{T(0), T(0), T(0), T(0)};
+  for (int o = 0; o < N; ++o) {
+    gbnew[o] = BodyG<T>{T(0), T(0), T(0), T(0), T(0), T(0)};
+    if (!moving_root(bc, o)) continue;
+    body_pass_root_vjp(o, st[o], bc, obs, N, rec, rad, iden, A, W, clamp, gbody[o], gag, gshape,
+                       gbnew[o]);
+  }
+  if (placed) {
+    for (int s = 0; s < N; ++s) {
+      if (!moving_shape(bc, s)) continue;
+      const T4 g = gshape[s];
+      place_vjp(st[bc[s].body], bc[s], g.x, g.y, g.z, g.w, gbnew[bc[s].body]);
+    }
+  }
+  for (int o = 0; o < N; ++o) gbody[o] = gbnew[o];
+}
+
 template <typename T, int FL, int AS>
 __global__ void __launch_bounds__(1024) rollout_bwd_kernel(const RolloutArgs<T> R) {
   using T2 = typename V2<T>::t;
   using T4 = typename V4<T>::t;
+  constexpr bool kBodies = (FL & F_BODIES) != 0;
   extern __shared__ __align__(16) unsigned char smem[];
   const int A = AS > 0 ? AS : R.A;
-  const int G = R.G, GA = G * A, S = R.S;
+  const int G = R.G, GA = G * A, S = R.S, N = R.N;
   const int tid = threadIdx.x;
   const int le = tid / A, a = tid - le * A;
   const int e0 = blockIdx.x * G;
   const int e = e0 + le;
   const bool valid = e < R.E;
   const int ec = valid ? e : R.E - 1;
-  const Layout<T> L(G, A, R.N, S, true);
+  const Layout<T> L(G, A, N, S, true, kBodies);
   const int NP4 = L.NP * 4;
   T* sxy = reinterpret_cast<T*>(smem + L.xy);       // [nbuf][G][NP*4] scan tables
   T4* srec = reinterpret_cast<T4*>(smem + L.rec);   // [nbuf][GA] (x, y, vx, vy)
@@ -523,8 +711,16 @@ __global__ void __launch_bounds__(1024) rollout_bwd_kernel(const RolloutArgs<T> 
   T* srad = reinterpret_cast<T*>(smem + L.rad);
   T* siden = reinterpret_cast<T*>(smem + L.iden);
   Obs<T>* sobs = reinterpret_cast<Obs<T>*>(smem + L.obs);
+  BodyC<T>* sbc = reinterpret_cast<BodyC<T>*>(smem + L.bc);
+  BodyS<T>* sbst = reinterpret_cast<BodyS<T>*>(smem + L.bst);  // [S][G][N]
+  T4* sgpose = reinterpret_cast<T4*>(smem + L.gpose);          // [GA][N]
+  T4* sgag = reinterpret_cast<T4*>(smem + L.gag);              // [GA]
+  BodyG<T>* sgbody = reinterpret_cast<BodyG<T>*>(smem + L.gbody);  // [G][N]
+  BodyG<T>* sgbnew = reinterpret_cast<BodyG<T>*>(smem + L.gbnew);  // [G][N]
+  T4* sgshape = reinterpret_cast<T4*>(smem + L.gshape);        // [G][N]
   // A rescan is needed unless contacts come from checkpointed masks.
   constexpr bool kScan = (FL & F_COLL) && !(FL & F_MASK);
+  constexpr bool kShare = (FL & (F_COLL | F_BODIES)) != 0;
 
   AgentP<T> P;
   load_params(R, ec, a, P);
@@ -533,6 +729,20 @@ __global__ void __launch_bounds__(1024) rollout_bwd_kernel(const RolloutArgs<T> 
   siden[tid] = P.inv_denom;
   if (FL & F_OBS) load_obstacles(R, sobs, e0);
   if (kScan) init_pads(sxy, L.nbuf, G, A);
+  if (kBodies) {
+    load_body_consts(R, sbc);
+    if (a == 0) {
+      for (int o = 0; o < N; ++o) {
+        const long long i = (long long)ec * N + o;
+        BodyG<T> gb{T(0), T(0), T(0), T(0), T(0), T(0)};
+        if (R.gb_pos) { gb.qx = R.gb_pos[2 * i]; gb.qy = R.gb_pos[2 * i + 1]; }
+        if (R.gb_ang) gb.th = R.gb_ang[i];
+        if (R.gb_vel) { gb.vx = R.gb_vel[2 * i]; gb.vy = R.gb_vel[2 * i + 1]; }
+        if (R.gb_om) gb.om = R.gb_om[i];
+        sgbody[le * N + o] = gb;
+      }
+    }
+  }
   __syncthreads();
 
   const long long ia = (long long)ec * A + a;
@@ -540,7 +750,7 @@ __global__ void __launch_bounds__(1024) rollout_bwd_kernel(const RolloutArgs<T> 
   const int H = R.H;
   const T* rad_env = srad + le * A;
   const T* iden_env = siden + le * A;
-  const Obs<T>* obs_env = sobs + le * R.N;
+  Obs<T>* obs_env = sobs + le * N;
   const bool has_gt = R.gt_pos || R.gt_th || R.gt_vel || R.gt_s || R.gt_w;
 
   Agent<T> g{};
@@ -573,7 +783,7 @@ __global__ void __launch_bounds__(1024) rollout_bwd_kernel(const RolloutArgs<T> 
     }
     T ga0 = T(0), ga1 = T(0);
 
-    if (S == 1) {
+    if (S == 1 && !kBodies) {
       Agent<T> gin;
       T gfx, gfy;
       integrate_vjp_sel<T, FL>(cur, a0, a1, nxt, g, P, W, gin, gfx, gfy, ga0, ga1);
@@ -588,13 +798,21 @@ __global__ void __launch_bounds__(1024) rollout_bwd_kernel(const RolloutArgs<T> 
         if (FL & F_TRUNC) cut_env[a] = R.cutoff[(long long)t * EA + ia];
         __syncthreads();
       }
-      force_vjp<T, FL, AS>(xy_env, rec_env, fb_env, cut_env, rad_env, iden_env, obs_env, R.N, A, a,
-                           cm0, cur, P, W, gfx, gfy, gin);
+      force_vjp<T, FL, AS>(xy_env, rec_env, fb_env, cut_env, rad_env, iden_env, obs_env, sbc,
+                           nullptr, N, A, a, cm0, cur, P, W, gfx, gfy, gin);
       g = gin;
       fbuf ^= 1;
     } else {
-      // recompute the substep chain from the checkpointed step input
-      __syncthreads();  // every thread is done reading last step's stash
+      // recompute the substep chain (agents and bodies) from the checkpointed step input
+      __syncthreads();  // every thread is done with last step's stash and shape poses
+      if (kBodies && a == 0) {
+        BodyS<T>* b0 = sbst + le * N;
+        if (t > 0)
+          load_bodies(R.bt_pos, R.bt_ang, R.bt_vel, R.bt_om, ((long long)(t - 1) * R.E + ec) * N, N, b0);
+        else
+          load_bodies(R.bi_pos, R.bi_ang, R.bi_vel, R.bi_om, (long long)ec * N, N, b0);
+        set_body_poses(R, ec, t == 0 && !R.poses_from_bodies, b0, sbc, obs_env);
+      }
       Agent<T> x = cur;
       for (int k = 0; k < S; ++k) {
         T* xy_env = sxy + (k * G + le) * NP4;
@@ -607,8 +825,8 @@ __global__ void __launch_bounds__(1024) rollout_bwd_kernel(const RolloutArgs<T> 
         ow[2] = x.w;
         if (k == S - 1) break;
         T fx = T(0), fy = T(0);
+        if (kShare) __syncthreads();
         if (FL & F_COLL) {
-          __syncthreads();
           if (FL & F_MASK) {
             mask_force(rec_env, rad_env, R.cmask[((long long)t * S + k) * EA + ia], x, P, W, fx, fy);
           } else {
@@ -617,7 +835,13 @@ __global__ void __launch_bounds__(1024) rollout_bwd_kernel(const RolloutArgs<T> 
             neighbor_force<T, FL, AS>(xy_env, rec_env, rad_env, A, a, x, P, W, fx, fy, cutoff, cm);
           }
         }
-        static_force<T, FL>(obs_env, R.N, x, P, W, fx, fy);
+        static_force<T, FL>(obs_env, N, x, P, W, fx, fy);
+        if (kBodies) {
+          __syncthreads();  // every agent has read this substep's shape poses
+          if (a == 0)
+            bodies_step(sbst + (k * G + le) * N, sbst + ((k + 1) * G + le) * N, sbc, obs_env, N,
+                        rec_env, rad_env, iden_env, A, W, R.body_clamp != 0);
+        }
         Agent<T> y;
         integrate_sel<T, FL>(x, a0, a1, fx, fy, P, W, y);
         x = y;
@@ -626,6 +850,9 @@ __global__ void __launch_bounds__(1024) rollout_bwd_kernel(const RolloutArgs<T> 
       for (int k = S - 1; k >= 0; --k) {
         T* xy_env = sxy + (k * G + le) * NP4;
         T4* rec_env = srec + k * GA + le * A;
+        const BodyS<T>* bk = sbst + (k * G + le) * N;
+        if (kBodies && a == 0 && k < S - 1)
+          set_body_poses(R, ec, t == 0 && k == 0 && !R.poses_from_bodies, bk, sbc, obs_env);
         const T* ow = sown + (size_t(k) * GA + tid) * 4;
         const T4 rr = rec_env[a];
         Agent<T> in{rr.x, rr.y, ow[0], rr.z, rr.w, ow[1], ow[2]};
@@ -639,8 +866,22 @@ __global__ void __launch_bounds__(1024) rollout_bwd_kernel(const RolloutArgs<T> 
         if (FL & F_TRUNC) cut_env[a] = R.cutoff[ws];
         const unsigned cm = (FL & F_MASK) ? R.cmask[ws] : 0u;
         __syncthreads();
-        force_vjp<T, FL, AS>(xy_env, rec_env, fb_env, cut_env, rad_env, iden_env, obs_env, R.N, A,
-                             a, cm, in, P, W, gfx, gfy, gin);
+        force_vjp<T, FL, AS>(xy_env, rec_env, fb_env, cut_env, rad_env, iden_env, obs_env, sbc,
+                             sgpose + size_t(tid) * N, N, A, a, cm, in, P, W, gfx, gfy, gin);
+        if (kBodies) {
+          __syncthreads();  // shape-pose cotangents of every agent are in
+          if (a == 0)
+            bodies_step_vjp(bk, sbc, obs_env, N, rec_env, rad_env, iden_env, A, W,
+                            R.body_clamp != 0, !(t == 0 && k == 0 && !R.poses_from_bodies),
+                            sgpose + size_t(le) * A * N,
+                            sgag + le * A, sgshape + le * N, sgbody + le * N, sgbnew + le * N);
+          __syncthreads();  // reaction cotangents of every agent are in
+          const T4 gr = sgag[tid];
+          gin.px += gr.x;
+          gin.py += gr.y;
+          gin.vx += gr.z;
+          gin.vy += gr.w;
+        }
         g = gin;
         out = in;
         fbuf ^= 1;

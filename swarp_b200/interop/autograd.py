@@ -86,19 +86,34 @@ class Trajectory(Sequence):
         return TorchState(*(f[t] for f in self.stacked), *self.extra)
 
 
+class BodyState(NamedTuple):
+    """Movable-body state per obstacle slot (only body-root slots are meaningful)."""
+
+    pos: torch.Tensor  # [n_envs, n_obstacles, 2]
+    angle: torch.Tensor  # [n_envs, n_obstacles]
+    vel: torch.Tensor  # [n_envs, n_obstacles, 2]
+    ang_vel: torch.Tensor  # [n_envs, n_obstacles]
+
+
 class _RolloutFn(torch.autograd.Function):
-    """``(actions [T,E,A,D], five state tensors) -> (final five, trajectory five [T,...])``."""
+    """``(actions [T,E,A,D], five state tensors) -> (final five, trajectory five [T,...],
+    final body state four)``; the body outputs are empty when no body moves."""
 
     @staticmethod
-    def forward(ctx, stepper: Stepper, actions, pos, theta, vel, speed, ang_vel):
+    def forward(ctx, stepper: Stepper, moving: bool, actions, pos, theta, vel, speed, ang_vel):
         state5 = tuple(t.contiguous() for t in (pos, theta, vel, speed, ang_vel))
         acts = actions.contiguous()
-        traj, fin, _, ws = stepper.rollout_forward(state5, acts, final=True)
+        traj, fin, _, rec = stepper.rollout_forward(state5, acts, final=True, moving_bodies=moving)
         ctx.stepper = stepper
-        ctx.ws = ws
+        ctx.rec = rec
         ctx.set_materialize_grads(False)
         ctx.save_for_backward(acts, *state5, *traj)
-        return (*fin, *traj)
+        if rec.moving:
+            body = tuple(x[-1] for x in rec.body_traj)
+        else:
+            body = tuple(acts.new_empty(0) for _ in range(4))
+            ctx.mark_non_differentiable(*body)
+        return (*fin, *traj, *body)
 
     @staticmethod
     def backward(ctx, *grads):
@@ -106,8 +121,10 @@ class _RolloutFn(torch.autograd.Function):
         state5, traj5 = tuple(rest[:5]), tuple(rest[5:10])
         gfin = tuple(None if g is None else g.contiguous() for g in grads[:5])
         gtraj = tuple(None if g is None else g.contiguous() for g in grads[5:10])
-        g_act, g_init = ctx.stepper.rollout_backward(state5, acts, traj5, gtraj, gfin, ctx.ws)
-        return (None, g_act, *g_init)
+        gbody = grads[10:14] if ctx.rec.moving and any(g is not None for g in grads[10:14]) else None
+        g_act, g_init = ctx.stepper.rollout_backward(state5, acts, traj5, gtraj, gfin, ctx.rec,
+                                                     gbody_final=gbody)
+        return (None, None, g_act, *g_init)
 
 
 def _run(stepper: Stepper, state: TorchState, actions_seq: torch.Tensor):
@@ -118,19 +135,25 @@ def _run(stepper: Stepper, state: TorchState, actions_seq: torch.Tensor):
         actions_seq.requires_grad or any(t.requires_grad for t in core)
     )
     extra = tuple(state[5:])
+    # Reference rule: movable bodies advance on untaped steps; on taped ones only when
+    # the stepper opts in (bodies_in_grad), which also makes them differentiable.
+    moving = stepper.any_movable and (not grad_mode or stepper.bodies_in_grad)
     if grad_mode:
-        out = _RolloutFn.apply(stepper, actions_seq, *core)
-        fin, traj = out[:5], out[5:]
+        out = _RolloutFn.apply(stepper, moving, actions_seq, *core)
+        fin, traj, body = out[:5], out[5:10], out[10:14]
     else:
         with torch.no_grad():
             core_c = tuple(t.contiguous() for t in core)
-            traj, fin, _, _ = stepper.rollout_forward(core_c, actions_seq.contiguous(), final=True)
-    return TorchState(*fin, *extra), traj, extra
+            traj, fin, _, rec = stepper.rollout_forward(core_c, actions_seq.contiguous(), final=True,
+                                                        moving_bodies=moving)
+            body = tuple(x[-1] for x in rec.body_traj) if rec.moving else None
+    body_state = BodyState(*body) if moving else None
+    return TorchState(*fin, *extra), traj, extra, body_state
 
 
 def warp_step(stepper: Stepper, state: TorchState, actions: torch.Tensor, slot=None) -> TorchState:
     """Differentiable env step: ``state, actions [E,A,act_dim] -> next state``."""
-    fin, _, _ = _run(stepper, state, actions.unsqueeze(0))
+    fin, _, _, _ = _run(stepper, state, actions.unsqueeze(0))
     return fin
 
 
@@ -151,8 +174,26 @@ def rollout(
         ring.reset()
         for _ in range(T):
             ring.acquire()
-    fin, traj, extra = _run(stepper, state, actions_seq)
+    fin, traj, extra, _ = _run(stepper, state, actions_seq)
     return fin, Trajectory(tuple(traj), extra)
+
+
+def rollout_bodies(
+    stepper: Stepper,
+    state: TorchState,
+    actions_seq: torch.Tensor,
+) -> tuple[TorchState, Trajectory, BodyState | None]:
+    """:func:`rollout` that also returns the movable bodies' final state.
+
+    With ``stepper.bodies_in_grad`` (or under ``torch.no_grad()``) the bodies advance
+    through the rollout, and in grad mode their final state is differentiable: a loss
+    on it back-propagates through the body dynamics and the agent contacts into the
+    actions and the initial agent state (bodies made of circle shapes). The body state
+    the rollout starts from is ``stepper.body_state``, which the rollout advances.
+    ``None`` is returned when no body moves.
+    """
+    fin, traj, extra, body = _run(stepper, state, actions_seq)
+    return fin, Trajectory(tuple(traj), extra), body
 
 
 @dataclass
