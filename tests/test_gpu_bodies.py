@@ -118,7 +118,7 @@ def test_compound_circle_body_forward_and_adjoint_f64():
     close(body.angle[:, 0], body_r[-1].body_angle[:, 0], 1e-10, "body angle")
     close(body.vel[:, 0], body_r[-1].body_vel[:, 0], 1e-10, "body vel")
     # the body moved
-    assert float((body.pos[:, 0].cpu() - ob.body_pos[:, 0]).norm(dim=-1).max()) > 1e-3
+    assert float((body.pos[:, 0].detach().cpu() - ob.body_pos[:, 0]).norm(dim=-1).max()) > 1e-3
     close(a.grad, a_ref.grad, 1e-9, "grad actions")
     close(s[0].grad, s_ref[0].grad, 1e-9, "grad init pos")
     assert float(a.grad.abs().max()) > 0
