@@ -1,15 +1,18 @@
 """Benchmark: forward + adjoint (BPTT) env-steps/s of the fused B200 rollout.
 
-One "step" is one full BPTT pass of the hot path over one batch: ``rollout`` of H=64 env
-steps for 16,000 navigation envs x 16 holonomic agents (config 2 of the reference's
-benchmark set), then the gradient of sum(||pos_H - goal||^2) w.r.t. all actions, through
-the public API (``swarp_b200.interop.autograd.rollout`` + ``torch.autograd.grad``).
-Inputs are synthetic and seeded (uniform starts/goals in the arena, uniform [-1, 1]
-actions); every step's inputs and outputs exceed L2 (actions 131 MB, trajectory 459 MB).
+One "step" is one full BPTT pass of the hot path over one batch: ``rollout`` of H env
+steps, then the gradient of the config's loss w.r.t. all actions, through the public API
+(``swarp_b200.interop.autograd.rollout`` / ``rollout_bodies`` + ``torch.autograd.grad``).
+The default workload is config 2 of the reference's benchmark set (the headline): 16,000
+navigation envs x 16 holonomic agents, H=64, loss sum(||pos_H - goal||^2). ``--config``
+selects configs 1-5 (config 1: 1024 x 8, H=32; 3: heterogeneous fleet 8192 x 32 with 10
+circle/box/segment obstacles per env, H=50; 4: 4096 x 4 agents pushing one movable
+3-circle body, H=100, loss sum ||body_pos_H - goal||; 5: dense swarm 2048 x 256, H=32,
+K=32 within 0.15, overflow flag tracked). Inputs are synthetic and seeded.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl reference]
 
-N > 1 runs under torchrun, one rank per GPU, each rank stepping its own 16,000 envs
+N > 1 runs under torchrun, one rank per GPU, each rank stepping its own batch of envs
 (weak scaling); the only collective is one NCCL all-reduce of (loss, ||grad||^2) per
 step. ``--impl reference`` times the CPU restatement of the reference (oracle/cpu_port.c,
 all host threads) on the same workload, metric and unit.
@@ -19,12 +22,14 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
 import sys
 import threading
 import time
+from dataclasses import dataclass, field
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
@@ -32,38 +37,155 @@ sys.path.insert(0, ROOT)
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-E_PER_GPU, N_AGENTS, HORIZON, DT = 16000, 16, 64, 0.05
-METRIC = "fwd+bwd env-steps/s, 16k envs x 16 agents, BPTT H=64"
 UNIT = "env-steps/s"
-BYTES_PER_AGENT_STEP = 80  # algorithmic: fwd 8 + 28, adjoint 8 + 28 + 8 (fp32)
-FWD_BYTES, BWD_BYTES = 36, 44
+FWD_BYTES, BWD_BYTES = 36, 44  # algorithmic fp32 bytes per agent-step: fwd 8 + 28, adjoint 8 + 28 + 8
+BYTES_PER_AGENT_STEP = FWD_BYTES + BWD_BYTES
+BODY_BYTES_PER_ENV_STEP = 48  # config 4: body pos/angle/vel/ang_vel written fwd, read bwd
+DT = 0.05
+HEADLINE_METRIC = "fwd+bwd env-steps/s, 16k envs×16 agents, BPTT H=64; % of HBM roofline"
 
 
-def world_config():
+@dataclass
+class Workload:
+    """One benchmark configuration: stepper, seeded host inputs and the loss."""
+
+    cid: int
+    name: str
+    E: int
+    A: int
+    H: int
+    stepper: object
+    pos: np.ndarray
+    theta: np.ndarray
+    goal: np.ndarray
+    acts: np.ndarray
+    body: bool = False
+    cpu_spec: dict = field(default_factory=dict)
+
+    @property
+    def metric(self) -> str:
+        if self.cid == 2:
+            return HEADLINE_METRIC
+        return f"fwd+bwd env-steps/s, config {self.cid}, BPTT H={self.H}"
+
+    @property
+    def algo_bytes_per_env_step(self) -> int:
+        return BYTES_PER_AGENT_STEP * self.A + (BODY_BYTES_PER_ENV_STEP if self.body else 0)
+
+
+def nav_world(A: int, radius: float = 0.05, neighbor_radius: float | None = None,
+              max_neighbors: int | None = None):
+    """NavigationScenario.make_world constants (reference swarp/scenarios/navigation.py:127-141):
+    margin 0.5 r, reach 2 r + margin, soft walls at +-1, K = min(32, max(4, A))."""
     from swarp_b200.core.config import WorldConfig
 
-    # NavigationScenario.make_world defaults at radius 0.05 (reference
-    # swarp/scenarios/navigation.py:127-141): margin 0.5 r, reach 2 r + margin, soft walls.
-    r = 0.05
-    margin = 0.5 * r
+    margin = 0.5 * radius
     return WorldConfig(collisions=True, collision_k=100.0, collision_c=1.0, collision_margin=margin,
                        bounds=(-1.0, 1.0, -1.0, 1.0), bounds_mode="soft",
-                       neighbor_radius=2 * r + margin, max_neighbors=min(32, max(4, N_AGENTS)))
+                       neighbor_radius=neighbor_radius or 2 * radius + margin,
+                       max_neighbors=max_neighbors or min(32, max(4, A)))
 
 
-def agent_configs():
-    from swarp_b200.dynamics.base import AgentConfig
+def build_workload(cid: int, rank: int = 0, dev="cuda:0", n_envs: int | None = None,
+                   make_stepper: bool = True) -> Workload:
+    """The seeded synthetic inputs of config ``cid`` (rank-dependent seeds)."""
+    from swarp_b200.core.config import ObstacleKind, Obstacles, WorldConfig
+    from swarp_b200.core.stepper import Stepper
+    from swarp_b200.dynamics.base import AgentConfig, DynamicsModel
 
-    return [AgentConfig(radius=0.05, max_speed=1.0, max_accel=2.0) for _ in range(N_AGENTS)]
-
-
-def synthetic_inputs(E: int, seed: int):
-    """Starts/goals U[-0.95, 0.95]^2, actions U[-1, 1] (numpy, float32)."""
-    rng = np.random.default_rng(seed)
-    pos = rng.uniform(-0.95, 0.95, (E, N_AGENTS, 2)).astype(np.float32)
-    goal = rng.uniform(-0.95, 0.95, (E, N_AGENTS, 2)).astype(np.float32)
-    acts = rng.uniform(-1.0, 1.0, (HORIZON, E, N_AGENTS, 2)).astype(np.float32)
-    return pos, goal, acts
+    rng = np.random.default_rng(7919 * cid + rank)
+    f32 = np.float32
+    obstacles = None
+    body = False
+    if cid in (1, 2, 5):
+        E, A, H = {1: (1024, 8, 32), 2: (16000, 16, 64), 5: (2048, 256, 32)}[cid]
+        E = n_envs or E
+        cfgs = [AgentConfig(radius=0.05, max_speed=1.0, max_accel=2.0) for _ in range(A)]
+        if cid == 5:
+            world = nav_world(A, neighbor_radius=0.15, max_neighbors=32)
+            pos = np.clip(rng.normal(0.0, 0.6, (E, A, 2)), -1.0, 1.0).astype(f32)
+            name = ("config5: dense swarm, holonomic VELOCITY, 2048 envs x 256 agents, "
+                    "N(0, 0.6^2) starts, R=0.15, K=32, H=32")
+        else:
+            world = nav_world(A)
+            pos = rng.uniform(-0.95, 0.95, (E, A, 2)).astype(f32)
+            name = (f"config{cid}: navigation, holonomic VELOCITY, {E} envs x {A} agents, "
+                    f"H={H}, dt=0.05, soft walls, agent contacts, K={A}")
+        theta = np.zeros((E, A), f32)
+        goal = rng.uniform(-0.95, 0.95, (E, A, 2)).astype(f32)
+        acts = rng.uniform(-1.0, 1.0, (H, E, A, 2)).astype(f32)
+    elif cid == 3:
+        E, A, H = n_envs or 8192, 32, 50
+        models = rng.permutation(np.arange(A) % 3)
+        kinds = [DynamicsModel.HOLONOMIC, DynamicsModel.DIFF_DRIVE, DynamicsModel.KINEMATIC_BICYCLE]
+        cfgs = [AgentConfig(model=kinds[m]) for m in models]
+        world = nav_world(A)
+        pos = rng.uniform(-0.95, 0.95, (E, A, 2)).astype(f32)
+        theta = rng.uniform(-math.pi, math.pi, (E, A)).astype(f32)
+        goal = rng.uniform(-0.95, 0.95, (E, A, 2)).astype(f32)
+        acts = rng.uniform(-1.0, 1.0, (H, E, A, 2)).astype(f32)
+        # 4 circles, 2 boxes, 4 segments; sizes per obstacle index (shared by envs),
+        # poses per env (reference obstacle layout, swarp/core/config.py:155-166).
+        shape = np.array([0, 0, 0, 0, 1, 1, 2, 2, 2, 2], np.int32)
+        radius = np.concatenate([rng.uniform(0.05, 0.15, 4), np.zeros(2), np.full(4, 0.02)])
+        half = np.zeros((10, 2))
+        half[4:6] = rng.uniform(0.05, 0.15, (2, 2))
+        half[6:, 0] = rng.uniform(0.1, 0.3, 4)
+        obstacles = Obstacles(
+            pos=torch.from_numpy(rng.uniform(-1.0, 1.0, (E, 10, 2)).astype(f32)),
+            radius=torch.from_numpy(radius.astype(f32)), shape=torch.from_numpy(shape),
+            angle=torch.from_numpy(rng.uniform(0.0, math.pi, (E, 10)).astype(f32)),
+            half_extents=torch.from_numpy(half.astype(f32)))
+        name = ("config3: heterogeneous fleet (1/3 holonomic, diff-drive, bicycle), 8192 envs x "
+                "32 agents, 4 circle + 2 box + 4 segment obstacles per env, H=50, K=32")
+    elif cid == 4:
+        E, A, H = n_envs or 4096, 4, 100
+        body = True
+        cfgs = [AgentConfig(radius=0.05, max_speed=1.0, max_accel=2.0) for _ in range(A)]
+        world = WorldConfig(collisions=True, collision_k=100.0, collision_c=5.0,
+                            collision_margin=0.025, bounds=(-1.0, 1.0, -1.0, 1.0),
+                            bounds_mode="soft", neighbor_radius=0.125, max_neighbors=4)
+        r, d = 0.08, 0.12
+        mass = float(rng.uniform(1.0, 5.0))
+        inertia = mass * (0.5 * r * r + 2.0 * d * d / 3.0)  # parallel-axis sum of 3 discs
+        ang = rng.uniform(-0.5, 0.5, E)
+        cen = rng.uniform(-0.3, 0.3, (E, 2))
+        off = np.array([[-d, 0.0], [0.0, 0.0], [d, 0.0]])
+        ca, sa = np.cos(ang)[:, None], np.sin(ang)[:, None]
+        opos = np.stack([cen[:, None, 0] + ca * off[:, 0] - sa * off[:, 1],
+                         cen[:, None, 1] + sa * off[:, 0] + ca * off[:, 1]], -1)
+        obstacles = Obstacles(
+            pos=torch.from_numpy(opos.astype(f32)), radius=torch.full((3,), r),
+            shape=torch.zeros(3, dtype=torch.int32),
+            angle=torch.from_numpy(np.repeat(ang[:, None], 3, 1).astype(f32)),
+            kind=torch.full((3,), int(ObstacleKind.MOVABLE), dtype=torch.int32),
+            mass=torch.full((3,), mass), inertia=torch.full((3,), inertia),
+            body=torch.zeros(3, dtype=torch.int32), body_offset=torch.from_numpy(off.astype(f32)),
+            half_extents=torch.zeros(3, 2))
+        a_ang = rng.uniform(0.0, 2 * math.pi, (E, A))
+        a_rad = rng.uniform(0.2, 0.28, (E, A))
+        pos = (cen[:, None, :] + np.stack([np.cos(a_ang), np.sin(a_ang)], -1) * a_rad[..., None])
+        pos = pos.astype(f32)
+        theta = np.zeros((E, A), f32)
+        goal = rng.uniform(-0.5, 0.5, (E, 2)).astype(f32)
+        push = goal[:, None, :] - pos
+        push /= np.linalg.norm(push, axis=-1, keepdims=True)
+        acts = (push[None] + 0.3 * rng.standard_normal((H, E, A, 2))).astype(f32)
+        name = ("config4: transport pushing, 4096 envs x 4 holonomic agents + one movable "
+                "3-circle body (mass U[1,5]), H=100, loss sum ||body_pos_H - goal||")
+    else:
+        raise ValueError(f"unknown config {cid}")
+    st = None
+    if make_stepper:
+        st = Stepper(cfgs, dt=DT, device=dev, dtype=torch.float32, world=world)
+        if obstacles is not None:
+            st.set_obstacles(obstacles)
+        if body:
+            st.bodies_in_grad = True
+        if cid == 5:
+            st.track_neighbor_overflow = True
+    cpu_spec = {"configs": cfgs, "world": world, "obstacles": obstacles}
+    return Workload(cid, name, E, A, H, st, pos, theta, goal, acts, body, cpu_spec)
 
 
 # ------------------------------------------------------------------ clocks
@@ -89,6 +211,11 @@ class ClockSampler:
             self._t.start()
         except (OSError, FileNotFoundError):
             self.proc = None
+            return self
+        t0 = time.monotonic()  # nvidia-smi takes a moment to start: wait for its first sample
+        while not self.lines and self.proc.poll() is None and time.monotonic() - t0 < 5.0:
+            time.sleep(0.01)
+        self._first = len(self.lines)
         return self
 
     def _read(self):
@@ -106,7 +233,8 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
+        # samples taken during the timed region (plus the one just before it)
+        for line in self.lines[max(0, getattr(self, "_first", 0) - 1):]:
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
                 continue
@@ -122,29 +250,15 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+class _Null:
+    def __enter__(self):
+        return None
+
+    def __exit__(self, *exc):
+        return False
+
+
 # ------------------------------------------------------------------ CPU side
-def cpu_rollout_sample(E: int, threads: int, seed: int = 0):
-    """One fwd+adjoint rollout of E envs on the C restatement; returns seconds."""
-    from oracle import cpu_port
-
-    pos, goal, acts = synthetic_inputs(E, seed)
-    z = np.zeros((E, N_AGENTS), np.float32)
-    from swarp_b200.dynamics.base import param_rows
-
-    w = world_config()
-    t0 = time.perf_counter()
-    traj, _, _ = cpu_port.rollout(
-        params=param_rows(agent_configs()), model_tag=[0] * N_AGENTS, ctrl_mode=[0] * N_AGENTS,
-        dt=DT, substeps=1, collisions=True, k=w.collision_k, c=w.collision_c,
-        margin=w.collision_margin, max_overlap=0.0, neighbor_radius=w.neighbor_radius,
-        max_neighbors=w.max_neighbors, bounds_mode=1, bounds=w.bounds,
-        init=[pos, z, np.zeros_like(pos), z, z], actions=acts,
-        grad_final_pos=np.zeros_like(pos), threads=threads, dtype=np.float32)
-    # The adjoint's work does not depend on the cotangent values, so the sample seeds it
-    # with zeros instead of 2 (pos_H - goal) (which would need the forward first).
-    return time.perf_counter() - t0
-
-
 def host_threads() -> int:
     try:
         return len(os.sched_getaffinity(0))
@@ -152,48 +266,114 @@ def host_threads() -> int:
         return os.cpu_count() or 1
 
 
-def calibrate_cpu(target_s: float, threads: int) -> int:
+def cpu_rollout_sample(cid: int, E: int, threads: int, seed: int = 0) -> float:
+    """One fwd+adjoint rollout of E envs of config ``cid`` on the CPU; returns seconds.
+
+    Configs 1, 2, 3, 5 run the OpenMP C restatement (oracle/cpu_port.c). Config 4 (movable
+    bodies, which that port does not model) runs the float32 torch restatement
+    (oracle/torch_ref.py) with torch's intra-op threads."""
+    wl = build_workload(cid, rank=seed, n_envs=E, make_stepper=False)
+    if cid == 4:
+        return _torch_oracle_sample(wl, threads)
+    from oracle import cpu_port
+    from swarp_b200.dynamics.base import param_rows
+
+    w = wl.cpu_spec["world"]
+    cfgs = wl.cpu_spec["configs"]
+    obs = None
+    o = wl.cpu_spec["obstacles"]
+    if o is not None:
+        r = o.resolve("cpu", torch.float64)
+        obs = {"pos": r.pos.numpy(), "angle": r.angle.expand(E, -1).numpy(),
+               "vel": r.vel.numpy(), "ang_vel": r.ang_vel.numpy(), "radius": r.radius.numpy(),
+               "half": r.half_extents.numpy(), "shape": r.shape.numpy()}
+    z = np.zeros((wl.E, wl.A), np.float32)
+    t0 = time.perf_counter()
+    cpu_port.rollout(
+        params=param_rows(cfgs), model_tag=[int(c.model) for c in cfgs],
+        ctrl_mode=[int(c.ctrl_mode) for c in cfgs], dt=DT, substeps=1, collisions=True,
+        k=w.collision_k, c=w.collision_c, margin=w.collision_margin, max_overlap=0.0,
+        neighbor_radius=w.neighbor_radius, max_neighbors=w.max_neighbors, bounds_mode=1,
+        bounds=w.bounds, init=[wl.pos, wl.theta, np.zeros_like(wl.pos), z, z], actions=wl.acts,
+        grad_final_pos=np.zeros_like(wl.pos), obstacles=obs, threads=threads, dtype=np.float32)
+    # The adjoint's work does not depend on the cotangent values, so the sample seeds it
+    # with zeros instead of 2 (pos_H - goal) (which would need the forward first).
+    return time.perf_counter() - t0
+
+
+def _torch_oracle_sample(wl: Workload, threads: int) -> float:
+    from oracle import torch_ref as R
+    from swarp_b200.dynamics.base import param_rows
+
+    torch.set_num_threads(threads)
+    cfgs, w, o = wl.cpu_spec["configs"], wl.cpu_spec["world"], wl.cpu_spec["obstacles"]
+    f = torch.float32
+    ro = o.resolve("cpu", f)
+    rw = R.RefWorld(params=torch.tensor(param_rows(cfgs), dtype=f),
+                    model_tag=[int(c.model) for c in cfgs], ctrl_mode=[int(c.ctrl_mode) for c in cfgs],
+                    dt=DT, substeps=1, collisions=True, k=w.collision_k, c=w.collision_c,
+                    margin=w.collision_margin, max_overlap=0.0, neighbor_radius=w.neighbor_radius,
+                    max_neighbors=w.max_neighbors, bounds=w.bounds, soft_walls=True,
+                    clamp_bounds=False, lin_damping=w.obstacle_linear_damping,
+                    ang_damping=w.obstacle_angular_damping, bodies_move=True)
+    rob = R.RefObstacles(pos=ro.pos, angle=ro.angle.expand(wl.E, -1), vel=ro.vel, ang_vel=ro.ang_vel,
+                         radius=ro.radius, half=ro.half_extents, shape=ro.shape.tolist(),
+                         kind=ro.kind.tolist(), mass=ro.mass, inertia=ro.inertia,
+                         body=ro.body.tolist(), body_off=ro.body_offset)
+    rob = R.seed_bodies(rob)
+    pos = torch.from_numpy(wl.pos)
+    z = torch.zeros(wl.E, wl.A)
+    acts = torch.from_numpy(wl.acts).requires_grad_(True)
+    t0 = time.perf_counter()
+    _, _, body_traj = R.rollout((pos, z, torch.zeros_like(pos), z, z), acts, rw, rob)
+    loss = (body_traj[-1].body_pos[:, 0] - torch.from_numpy(wl.goal)).norm(dim=-1).sum()
+    loss.backward()
+    return time.perf_counter() - t0
+
+
+def calibrate_cpu(cid: int, target_s: float, threads: int, e_max: int) -> int:
     E = max(threads, 8)
     while True:
-        dt = cpu_rollout_sample(E, threads)
-        if dt >= target_s / 4 or E >= E_PER_GPU:
-            return min(E_PER_GPU, max(1, int(E * target_s / max(dt, 1e-6))))
+        dt = cpu_rollout_sample(cid, E, threads)
+        if dt >= target_s / 4 or E >= e_max:
+            return min(e_max, max(1, int(E * target_s / max(dt, 1e-6))))
         E *= 4
 
 
-def cpu_baseline_block(target_s: float = 2.0, repeats: int = 3) -> dict:
+def cpu_baseline_block(wl: Workload, target_s: float = 2.0, repeats: int = 3) -> dict:
     threads = host_threads()
-    E = calibrate_cpu(target_s, threads)
-    times = [cpu_rollout_sample(E, threads, seed=i) for i in range(repeats)]
+    E = calibrate_cpu(wl.cid, target_s, threads, wl.E)
+    times = [cpu_rollout_sample(wl.cid, E, threads, seed=i) for i in range(repeats)]
     t = statistics.median(times)
-    return {"value": E * HORIZON / t, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{E} envs x {N_AGENTS} agents x H={HORIZON}, fwd+adjoint, float32, "
-                      f"C restatement (oracle/cpu_port.c, OpenMP {threads} threads), median of "
-                      f"{repeats}"}
+    port = ("float32 torch restatement (oracle/torch_ref.py)" if wl.cid == 4 else
+            f"C restatement (oracle/cpu_port.c, OpenMP {threads} threads)")
+    return {"value": E * wl.H / t, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{E} envs x {wl.A} agents x H={wl.H}, fwd+adjoint, float32, {port}, "
+                      f"median of {repeats}"}
 
 
 def run_reference(args, rank: int, world: int) -> None:
     if rank != 0:
         return
     threads = host_threads()
-    E = calibrate_cpu(0.05, threads)  # ~50 ms per step keeps --steps runs to minutes
+    wl = build_workload(args.config, make_stepper=False)
+    E = calibrate_cpu(args.config, 0.05, threads, wl.E)  # ~50 ms per step: runs end in minutes
     for i in range(args.warmup):
-        cpu_rollout_sample(E, threads, seed=i)
+        cpu_rollout_sample(args.config, E, threads, seed=i)
     t0 = time.perf_counter()
     for i in range(args.steps):
-        cpu_rollout_sample(E, threads, seed=i)
+        cpu_rollout_sample(args.config, E, threads, seed=i)
     dt = time.perf_counter() - t0
-    value = E * HORIZON * args.steps / dt
+    value = E * wl.H * args.steps / dt
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "impl": "reference", "metric": wl.metric, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": "config2-sample: navigation, holonomic, 16 agents/env, H=64, "
-                               f"{E} envs per step (bounded CPU sample)",
-                   "n_agents": N_AGENTS, "horizon": HORIZON, "dt": DT},
+        "config": {"workload": wl.name + f" (bounded CPU sample: {E} envs per step)",
+                   "n_agents": wl.A, "horizon": wl.H, "dt": DT},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{E} envs per step, C restatement of the reference "
+                         "sample": f"{E} envs per step, CPU restatement of the reference "
                                    "(the reference's Warp path cannot be installed here)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -201,12 +381,13 @@ def run_reference(args, rank: int, world: int) -> None:
 
 
 # ------------------------------------------------------------------ GPU side
-def profile_traffic():
+def profile_traffic(cid: int):
     """DRAM bytes per launch of the adjoint kernel from the committed ncu summary, if any."""
     path = os.path.join(ROOT, "profiles", "rollout_bwd_config2.md")
+    key = f"traffic_bytes_per_launch_config{cid}:"
     try:
         for line in open(path):
-            if line.startswith("traffic_bytes_per_launch_config2:"):
+            if line.startswith(key):
                 return float(line.split(":")[1])
     except OSError:
         pass
@@ -216,8 +397,9 @@ def profile_traffic():
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5])
     ap.add_argument("--impl", default="swarp_b200", choices=["swarp_b200", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=30)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -240,113 +422,149 @@ def main() -> None:
             dist.destroy_process_group()
         return
 
-    from swarp_b200.core.stepper import Stepper
-    from swarp_b200.interop.autograd import TorchState, rollout
+    from swarp_b200.core.sharding import reduce_loss_and_grad_norm
+    from swarp_b200.interop.autograd import TorchState, rollout, rollout_bodies
+    from swarp_b200.interop.graphs import GraphedRollout
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    st = Stepper(agent_configs(), dt=DT, device=dev, dtype=torch.float32, world=world_config())
-    E = E_PER_GPU
-    pos_h, goal_h, acts_h = synthetic_inputs(E, seed=1000 + rank)
-    pos = torch.from_numpy(pos_h).to(dev)
-    goal = torch.from_numpy(goal_h).to(dev)
-    acts = torch.from_numpy(acts_h).to(dev).requires_grad_(True)
-    zero = torch.zeros(E, N_AGENTS, device=dev)
-    state = TorchState(pos, zero, torch.zeros(E, N_AGENTS, 2, device=dev), zero, zero)
-    red = torch.zeros(2, device=dev)
+    wl = build_workload(args.config, rank=rank, dev=dev)
+    st, E, A, H = wl.stepper, wl.E, wl.A, wl.H
+    pos = torch.from_numpy(wl.pos).to(dev)
+    theta = torch.from_numpy(wl.theta).to(dev)
+    goal = torch.from_numpy(wl.goal).to(dev)
+    acts = torch.from_numpy(wl.acts).to(dev).requires_grad_(True)
+    zero = torch.zeros(E, A, device=dev)
+    state = TorchState(pos, theta, torch.zeros(E, A, 2, device=dev), zero, zero)
+    snap = st.bodies_snapshot() if wl.body else None
 
-    # per-kernel device time: events around the two rollout launches
-    kern = {"fwd": [], "bwd": []}
-    record = {"on": False}
-    f_fwd, f_bwd = st.rollout_forward, st.rollout_backward
+    def loss_fn(final, _traj):
+        # sum ||pos_H - goal||^2 as one fused op (and one fused op in the backward)
+        return torch.nn.functional.mse_loss(final.pos, goal, reduction="sum")
 
-    def timed(name, fn):
-        def wrap(*a, **k):
-            if not record["on"]:
-                return fn(*a, **k)
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record()
-            out = fn(*a, **k)
-            e1.record()
-            kern[name].append((e0, e1))
-            return out
-        return wrap
-
-    st.rollout_forward = timed("fwd", f_fwd)
-    st.rollout_backward = timed("bwd", f_bwd)
-
-    def bptt_step(state, acts, goal):
-        final, _ = rollout(st, state, acts)
-        loss = ((final.pos - goal) ** 2).sum()
+    def eager_step(state, acts):
+        """The drop-in path: rollout (or rollout_bodies) + autograd.grad, all eager."""
+        if wl.body:
+            st.restore_bodies(snap)  # every step pushes the same body from the same pose
+            _, _, body = rollout_bodies(st, state, acts)
+            loss = (body.pos[:, 0] - goal).norm(dim=-1).sum()
+        else:
+            final, traj = rollout(st, state, acts)
+            loss = loss_fn(final, traj)
         (g,) = torch.autograd.grad(loss, [acts])
         if dist is not None:
-            red[0] = loss.detach()
-            red[1] = g.square().sum()
-            dist.all_reduce(red)
-        return loss, g
+            loss = reduce_loss_and_grad_norm(loss, g)[0]
+        return loss
 
     for _ in range(args.warmup):
-        bptt_step(state, acts, goal)
+        eager_step(state, acts)
     torch.cuda.synchronize()
 
-    # ---- timed region (device time, max over ranks)
-    if dist is not None:
-        dist.barrier()
+    # ---- per-kernel device time: the two rollout kernels back to back (GPU-bound loop)
+    s5 = tuple(state[:5])
+    a_d = acts.detach()
+    n_k = max(20, min(args.steps, 200))
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(n_k)]
+    for i in range(n_k + 3):
+        if wl.body:
+            st.restore_bodies(snap)
+        if i >= 3:
+            ev[i - 3][0].record()
+        traj, fin, _, rec = st.rollout_forward(s5, a_d, final=True)
+        if i >= 3:
+            ev[i - 3][1].record()
+        # cotangent only on the final positions, as the BPTT loss gives
+        st.rollout_backward(s5, a_d, traj, (None,) * 5, (fin[0], None, None, None, None), rec)
+        if i >= 3:
+            ev[i - 3][2].record()
     torch.cuda.synchronize()
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        record["on"] = True
-        ev0.record()
-        for _ in range(args.steps):
-            bptt_step(state, acts, goal)
-        ev1.record()
+    t_fwd = statistics.median(e[0].elapsed_time(e[1]) for e in ev)
+    t_bwd = statistics.median(e[1].elapsed_time(e[2]) for e in ev)
+
+    # ---- the timed step: one CUDA-graph replay of the whole BPTT step (one launch from
+    # the host), then the (loss, ||g||^2) all-reduce across ranks
+    graphed = None
+    if not wl.body:
+        graphed = GraphedRollout(st, state, acts, loss_fn, grad_norm=dist is not None, warmup=3)
+
+        def step():
+            graphed()
+            if dist is not None:
+                dist.all_reduce(graphed.loss_and_grad_norm)
+    else:
+        def step():
+            eager_step(state, acts)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    def timed_loop(fn, n, sample_clocks):
+        if dist is not None:
+            dist.barrier()
         torch.cuda.synchronize()
-        record["on"] = False
-    if dist is not None:
-        dist.barrier()
-    ms = ev0.elapsed_time(ev1)
-    t_fwd = statistics.mean(a.elapsed_time(b) for a, b in kern["fwd"])
-    t_bwd = statistics.mean(a.elapsed_time(b) for a, b in kern["bwd"])
-    ms_t = torch.tensor([ms, t_fwd, t_bwd], device=dev, dtype=torch.float64)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) if sample_clocks else _Null() as clk:
+            e0.record()
+            for _ in range(n):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        return e0.elapsed_time(e1), clk
+
+    ms, clocks = timed_loop(step, args.steps, True)
+    n_eager = max(20, min(args.steps, 200))
+    for _ in range(3):
+        eager_step(state, acts)
+    ms_eager, _ = timed_loop(lambda: eager_step(state, acts), n_eager, False)
+    ms_t = torch.tensor([ms, t_fwd, t_bwd, ms_eager], device=dev, dtype=torch.float64)
     if dist is not None:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-    ms, t_fwd, t_bwd = (float(x) for x in ms_t.cpu())
+    ms, t_fwd, t_bwd, ms_eager = (float(x) for x in ms_t.cpu())
     ms_per_step = ms / args.steps
-    value = world * E * HORIZON / (ms_per_step / 1e3)
+    value = world * E * H / (ms_per_step / 1e3)
+    value_eager = world * E * H / (ms_eager / n_eager / 1e3)
+    overflow = None
+    if st.track_neighbor_overflow:
+        ov = st.rollout_overflow()
+        overflow = {"agents_over_K": int(ov.sum()), "max_true_count":
+                    int(st.last_true_count_max.max()), "K": st.world.max_neighbors}
 
-    # ---- end to end: host inputs (pinned) -> device, step, loss -> host
-    pin_acts = torch.from_numpy(acts_h).pin_memory()
-    pin_pos = torch.from_numpy(pos_h).pin_memory()
-    pin_goal = torch.from_numpy(goal_h).pin_memory()
-    d_acts = torch.empty_like(acts)
-    h2d = pin_acts.numel() * 4 + pin_pos.numel() * 4 + pin_goal.numel() * 4
+    # ---- end to end: host inputs (pinned) -> device, step, loss -> host, through the
+    # public API (GraphedRollout call, or rollout_bodies for config 4)
+    pin = [torch.from_numpy(x).pin_memory() for x in (wl.acts, wl.pos, wl.theta, wl.goal)]
+    h2d = sum(p.numel() * p.element_size() for p in pin)
     d2h = 8
-    losses = []
-    for i in range(args.e2e_steps + 3):
-        if i == 3:
+    d_acts = torch.empty_like(acts)
+
+    def e2e_step():
+        if graphed is not None:
+            goal.copy_(pin[3], non_blocking=True)
+            graphed(TorchState(pin[1], pin[2], None, None, None), pin[0])  # vel etc. stay 0
+            loss = graphed.loss
             if dist is not None:
-                dist.barrier()
-            torch.cuda.synchronize()
-            e2e0 = torch.cuda.Event(enable_timing=True)
-            e2e0.record()
-        d_acts.copy_(pin_acts, non_blocking=True)
-        p = pin_pos.to(dev, non_blocking=True)
-        gl = pin_goal.to(dev, non_blocking=True)
-        a = d_acts.detach().requires_grad_(True)
-        s0 = TorchState(p, zero, torch.zeros_like(p), zero, zero)
-        loss, _ = bptt_step(s0, a, gl)
-        losses.append(float(loss.detach().to("cpu", torch.float64)))
-    e2e1 = torch.cuda.Event(enable_timing=True)
-    e2e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = torch.tensor([e2e0.elapsed_time(e2e1) / args.e2e_steps], device=dev,
-                          dtype=torch.float64)
+                dist.all_reduce(graphed.loss_and_grad_norm)
+                loss = graphed.loss_and_grad_norm[0]
+        else:
+            d_acts.copy_(pin[0], non_blocking=True)
+            p, th, gl = (x.to(dev, non_blocking=True) for x in pin[1:])
+            goal.copy_(gl)
+            a = d_acts.detach().requires_grad_(True)
+            loss = eager_step(TorchState(p, th, torch.zeros_like(p), zero, zero), a)
+        return float(loss.detach().to("cpu", torch.float64))
+
+    for _ in range(3):
+        e2e_step()
+    e2e_total, _ = timed_loop(e2e_step, args.e2e_steps, False)
+    e2e_ms = torch.tensor([e2e_total / args.e2e_steps], device=dev, dtype=torch.float64)
     if dist is not None:
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_value = world * E * HORIZON / (float(e2e_ms.item()) / 1e3)
+    e2e_value = world * E * H / (float(e2e_ms.item()) / 1e3)
 
+    if graphed is not None:
+        graphed.release()  # before the process group goes: the graph follows NCCL work
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -360,39 +578,45 @@ def main() -> None:
     else:
         peak = 6650.0
         peak_src = "fallback"
-    agent_steps = E * N_AGENTS * HORIZON
-    bwd_gbs = BWD_BYTES * agent_steps / (t_bwd / 1e3) / 1e9
-    fwd_gbs = FWD_BYTES * agent_steps / (t_fwd / 1e3) / 1e9
-    step_gbs = BYTES_PER_AGENT_STEP * agent_steps / ((t_fwd + t_bwd) / 1e3) / 1e9
+    agent_steps = E * A * H
+    body_b = (BODY_BYTES_PER_ENV_STEP // 2) * E * H if wl.body else 0
+    bwd_gbs = (BWD_BYTES * agent_steps + body_b) / (t_bwd / 1e3) / 1e9
+    fwd_gbs = (FWD_BYTES * agent_steps + body_b) / (t_fwd / 1e3) / 1e9
+    step_gbs = wl.algo_bytes_per_env_step * E * H / ((t_fwd + t_bwd) / 1e3) / 1e9
     dom = "bwd" if t_bwd >= t_fwd else "fwd"
-    traffic = profile_traffic()
     roof = {"bound": "hbm", "kernel": f"rollout_{dom}_kernel<float,...>",
             "achieved": bwd_gbs if dom == "bwd" else fwd_gbs, "peak": peak, "unit": "GB/s",
             "peak_source": peak_src}
     roof["frac"] = roof["achieved"] / peak
-    roof["traffic"] = traffic if dom == "bwd" else None
+    roof["traffic"] = profile_traffic(args.config) if dom == "bwd" else None
+    cfg = {"workload": wl.name, "config_id": args.config, "n_envs_per_gpu": E, "n_agents": A,
+           "horizon": H, "parallelism": f"env-sharded dp{world}",
+           "l2": "inputs larger than L2" if wl.acts.nbytes + 28 * agent_steps > 126e6 else
+                 "inputs smaller than L2 (small config; no flush)"}
     line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "metric": wl.metric, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config2: navigation, holonomic VELOCITY, 16000 envs x 16 agents "
-                               "per GPU, H=64, dt=0.05, soft walls, agent contacts",
-                   "n_envs_per_gpu": E, "n_agents": N_AGENTS, "horizon": HORIZON,
-                   "parallelism": f"env-sharded dp{world}",
-                   "l2": "inputs larger than L2 (actions 131 MB, trajectory 459 MB per step)"},
+        "config": cfg,
         "roofline": roof,
         "roofline_step": {"bound": "hbm", "achieved": step_gbs, "peak": peak, "unit": "GB/s",
                           "frac": step_gbs / peak,
-                          "bytes_per_agent_step": BYTES_PER_AGENT_STEP,
+                          "bytes_per_env_step": wl.algo_bytes_per_env_step,
                           "fwd_ms": t_fwd, "bwd_ms": t_bwd, "fwd_gbs": fwd_gbs,
                           "bwd_gbs": bwd_gbs},
         "clocks": clocks.summary(),
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": 2 * args.steps,
+        "timed_path": ("one CUDA-graph replay of the whole BPTT step per step "
+                       "(swarp_b200.interop.graphs.GraphedRollout)" if graphed is not None else
+                       "eager rollout_bodies + autograd.grad"),
+        "value_eager": value_eager,
     }
+    if overflow is not None:
+        line["neighbor_overflow"] = overflow
     if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline_block()
+        line["cpu_baseline"] = cpu_baseline_block(wl)
     print(json.dumps(line), flush=True)
 
 

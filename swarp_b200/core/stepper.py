@@ -139,6 +139,11 @@ class Stepper:
         #: and only no-grad steps integrate them. True integrates them on grad rollouts
         #: as well and differentiates through them (bodies of circle shapes).
         self.bodies_in_grad = False
+        #: When set, every rollout also records, per agent, the largest uncapped in-radius
+        #: neighbor count over its substeps (``last_true_count_max`` [E, A] int32);
+        #: :meth:`rollout_overflow` compares it with ``max_neighbors``.
+        self.track_neighbor_overflow = False
+        self.last_true_count_max: torch.Tensor | None = None
         #: Body state per obstacle slot (pos [E,N,2], angle [E,N], vel [E,N,2],
         #: ang_vel [E,N]); only body-root slots are meaningful.
         self.body_state: tuple[torch.Tensor, ...] | None = None
@@ -261,6 +266,26 @@ class Stepper:
             oc.poses_from_bodies = int(self._poses_from_bodies)
         return wc
 
+    def rollout_overflow(self) -> torch.Tensor | None:
+        """Bool ``[E, A]``: the agent had more in-radius neighbors than ``max_neighbors``
+        on some substep of the last rollout (needs ``track_neighbor_overflow``)."""
+        if self.last_true_count_max is None:
+            return None
+        return self.last_true_count_max > self.world.max_neighbors
+
+    def bodies_snapshot(self):
+        """Opaque copy of the movable-body state (body poses/velocities and the placed
+        shapes) that :meth:`restore_bodies` reinstates, e.g. to restart an episode."""
+        bs = None if self.body_state is None else tuple(t.clone() for t in self.body_state)
+        return (self.obstacles, bs, self._poses_from_bodies)
+
+    def restore_bodies(self, snapshot) -> None:
+        obstacles, bs, from_bodies = snapshot
+        self.obstacles = obstacles
+        self.body_state = None if bs is None else tuple(t.clone() for t in bs)
+        self._poses_from_bodies = from_bodies
+        self._wc_cache.clear()
+
     def _advance_bodies(self, body_traj) -> None:
         """After a rollout that moved the bodies: the final body state becomes the stepper's,
         and the moving shapes are re-placed on it (as the reference's body pass leaves its
@@ -340,8 +365,10 @@ class Stepper:
         else:
             traj = out
         fin = tuple(torch.empty_like(t[0]) for t in traj) if final else None
+        true_count = true_count or self.track_neighbor_overflow
         tmax = (torch.empty(E, self.n_agents, dtype=torch.int32, device=self.device)
-                if true_count else None)
+                if true_count and self.collisions else None)
+        self.last_true_count_max = tmax
         nbytes = int(lib.swarp_rollout_workspace_bytes(C.byref(wc), H))
         ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=self.device)
         bi = bt = None

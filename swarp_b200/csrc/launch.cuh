@@ -4,7 +4,10 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <cstdint>
+#include <mutex>
 #include <type_traits>
+#include <unordered_map>
 
 #include "rollout.cuh"
 
@@ -21,13 +24,32 @@ int launch_neighbors(int E, int A, int G, int K, T r2, const T* pos, int* idx, i
 
 #ifdef SWARP_DEFINE_LAUNCHERS
 
+// Raise a kernel's dynamic shared-memory limit once per size (per device): the attribute
+// call is not stream-ordered, so keeping it off the common launch path also keeps launches
+// inside CUDA-graph capture free of it after the first (uncaptured) call of a shape.
+template <typename K>
+inline bool ensure_smem_limit(K kernel, size_t smem) {
+  if (smem <= 48 * 1024) return true;
+  static std::mutex mu;
+  static std::unordered_map<long long, size_t> raised;  // (device, kernel) -> limit set
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  const long long key = (static_cast<long long>(dev) << 56) ^
+                        static_cast<long long>(reinterpret_cast<uintptr_t>(kernel));
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = raised.find(key);
+  if (it != raised.end() && it->second >= smem) return true;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess)
+    return false;
+  raised[key] = smem;
+  return true;
+}
+
 template <typename K>
 inline int launch_kernel(K kernel, int grid, int block, size_t smem, cudaStream_t st,
                          const void* arg) {
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-          cudaSuccess)
-    return kErrCuda;
+  if (!ensure_smem_limit(kernel, smem)) return kErrCuda;
   void* args[] = {const_cast<void*>(arg)};
   return cudaLaunchKernel(reinterpret_cast<const void*>(kernel), dim3(grid), dim3(block), args, smem,
                           st) == cudaSuccess

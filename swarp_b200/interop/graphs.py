@@ -1,0 +1,95 @@
+"""A whole BPTT step captured in one CUDA graph.
+
+One eager BPTT step through :func:`~swarp_b200.interop.autograd.rollout` is two fused
+kernels on the device but a few hundred microseconds of host work (autograd bookkeeping,
+the loss ops, the adjoint's engine hand-off). At the benchmark sizes that host time is
+the same order as the kernels, so a training loop, and every rank of a multi-GPU job, is
+then limited by Python. :class:`GraphedRollout` records the step once (forward kernel,
+the user's loss, ``autograd.grad``, the adjoint kernel, the squared gradient norm) and
+replays it with one graph launch. This is the B200-side counterpart of the reference's
+CUDA-graph runtime (``swarp/core/stepper.py`` persistent buffers + ``wp.capture_*``),
+which captures the forward step only.
+
+Shapes, the stepper's configuration and the loss are fixed at capture; inputs are
+copied into the graph's static buffers on each call.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Callable
+
+import torch
+
+from swarp_b200.core.stepper import Stepper
+from swarp_b200.interop.autograd import TorchState, Trajectory, rollout
+
+
+class GraphedRollout:
+    """``loss_fn(final, trajectory) -> scalar`` differentiated w.r.t. the actions (and,
+    with ``wrt_state``, the five initial-state fields), captured as one CUDA graph.
+
+    ``state`` / ``actions`` give the shapes and the first inputs. Calling the object
+    (optionally with new inputs, device or pinned host tensors of the same shapes) replays
+    the graph and returns ``(loss, grad_actions)``: static tensors overwritten by the
+    next call. With ``grad_norm`` (default), ``loss_and_grad_norm`` is a static
+    ``[loss, ||grad_actions||^2]`` pair in the stepper's dtype, ready for a single
+    all-reduce across ranks (``None`` otherwise).
+    """
+
+    def __init__(self, stepper: Stepper, state: TorchState, actions: torch.Tensor,
+                 loss_fn: Callable[[TorchState, Trajectory], torch.Tensor], *,
+                 wrt_state: bool = False, grad_norm: bool = True, warmup: int = 3) -> None:
+        if stepper.any_movable:
+            raise NotImplementedError(
+                "GraphedRollout does not capture movable bodies: their state advances on the "
+                "host side between rollouts; use rollout_bodies eagerly")
+        dev = stepper.device
+        self.stepper = stepper
+        self.loss_fn = loss_fn
+        self.wrt_state = wrt_state
+        self.grad_norm = grad_norm
+        # Static leaves, detached from any history the given inputs carry: a backward that
+        # reached back into the caller's graph would leave the capture stream.
+        self.actions = actions.detach().to(dev, copy=True).requires_grad_(True)
+        self.state = TorchState(*(t.detach().to(dev, copy=True) for t in tuple(state)[:5]))
+        if wrt_state:
+            for t in self.state[:5]:
+                t.requires_grad_(True)
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(max(1, warmup)):
+                self._body()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.loss, self.grads, self.loss_and_grad_norm = self._body()
+        self.grad_actions = self.grads[0]
+        self.grad_state = TorchState(*self.grads[1:6]) if wrt_state else None
+
+    def _body(self):
+        fin, traj = rollout(self.stepper, self.state, self.actions)
+        loss = self.loss_fn(fin, traj)
+        wrt = [self.actions] + (list(self.state[:5]) if self.wrt_state else [])
+        grads = torch.autograd.grad(loss, wrt)
+        pair = None
+        if self.grad_norm:
+            g = grads[0].reshape(-1)
+            pair = torch.stack([loss.detach(), torch.dot(g, g)])
+        return loss.detach(), grads, pair
+
+    def __call__(self, state: TorchState | None = None, actions: torch.Tensor | None = None):
+        with torch.no_grad():
+            if actions is not None:
+                self.actions.copy_(actions, non_blocking=True)
+            if state is not None:
+                for dst, src in zip(self.state[:5], tuple(state)[:5], strict=True):
+                    if src is not None:  # None keeps that field's current contents
+                        dst.copy_(src, non_blocking=True)
+        self.graph.replay()
+        return self.loss, self.grad_actions
+
+    def release(self) -> None:
+        """Free the graph (and its memory pool) now rather than at garbage collection."""
+        self.graph.reset()
+        self.graph = None
