@@ -422,7 +422,7 @@ def main() -> None:
             dist.destroy_process_group()
         return
 
-    from swarp_b200.core.sharding import reduce_loss_and_grad_norm
+    from swarp_b200.core.sharding import PairReducer, reduce_loss_and_grad_norm
     from swarp_b200.interop.autograd import TorchState, rollout, rollout_bodies
     from swarp_b200.interop.graphs import GraphedRollout
 
@@ -483,14 +483,17 @@ def main() -> None:
 
     # ---- the timed step: one CUDA-graph replay of the whole BPTT step (one launch from
     # the host), then the (loss, ||g||^2) all-reduce across ranks
-    graphed = None
+    graphed = reducer = None
     if not wl.body:
-        graphed = GraphedRollout(st, state, acts, loss_fn, grad_norm=dist is not None, warmup=3)
+        graphed = GraphedRollout(st, state, acts, loss_fn,
+                                 grad_norm="fused" if dist is not None else False, warmup=3)
+
+        reducer = PairReducer(graphed.loss_and_grad_norm) if dist is not None else None
 
         def step():
             graphed()
-            if dist is not None:
-                dist.all_reduce(graphed.loss_and_grad_norm)
+            if reducer is not None:  # overlaps the next step's rollout
+                reducer(graphed.loss_and_grad_norm)
     else:
         def step():
             eager_step(state, acts)
@@ -498,7 +501,7 @@ def main() -> None:
         step()
     torch.cuda.synchronize()
 
-    def timed_loop(fn, n, sample_clocks):
+    def timed_loop(fn, n, sample_clocks, finish=None):
         if dist is not None:
             dist.barrier()
         torch.cuda.synchronize()
@@ -508,13 +511,16 @@ def main() -> None:
             e0.record()
             for _ in range(n):
                 fn()
+            if finish is not None:
+                finish()  # the compute stream waits for work still on other streams
             e1.record()
             torch.cuda.synchronize()
         if dist is not None:
             dist.barrier()
         return e0.elapsed_time(e1), clk
 
-    ms, clocks = timed_loop(step, args.steps, True)
+    ms, clocks = timed_loop(step, args.steps, True,
+                            finish=reducer.drain if reducer is not None else None)
     n_eager = max(20, min(args.steps, 200))
     for _ in range(3):
         eager_step(state, acts)

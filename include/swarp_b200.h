@@ -114,8 +114,9 @@ typedef struct {
   swarp_obstacles_t obstacles;
 } swarp_world_t;
 
-/* Bytes of device workspace swarp_rollout_fwd fills and swarp_rollout_bwd reads
- * for this world and horizon (0 when none is needed). */
+/* Bytes of device workspace for this world and horizon: the contact checkpoint that
+ * swarp_rollout_fwd fills and swarp_rollout_bwd reads, then the adjoint's per-CTA
+ * partial sums for adj_actions_sqnorm (0 for an invalid world). */
 size_t swarp_rollout_workspace_bytes(const swarp_world_t* w, int32_t horizon);
 
 /* Forward rollout of `horizon` steps from `init`.
@@ -138,14 +139,18 @@ int swarp_rollout_fwd(const swarp_world_t* w, int32_t horizon, swarp_state_t ini
  * workspace). Cotangents: adj_traj [T, ...] and adj_final (any field may be NULL =
  * zero), adj_bodies_final (fields may be NULL; body pos/angle/vel/ang_vel after the
  * last step). Outputs: adj_actions [T, E, A, act_dim] and adj_init (all five fields
- * required). Deterministic: no atomics, fixed summation order. Moving bodies are
- * differentiated when all their shapes are circles (SWARP_ERR_UNSUPPORTED otherwise). */
+ * required); adj_actions_sqnorm (NULL = not computed): one scalar of the world's dtype,
+ * the sum of squares of adj_actions, reduced in the kernel's epilogue (the per-CTA
+ * partials go to the workspace's tail) instead of a second pass over adj_actions.
+ * Deterministic: no atomics, fixed summation order. Moving bodies are differentiated
+ * when all their shapes are circles (SWARP_ERR_UNSUPPORTED otherwise). The fused norm
+ * has no counterpart in the reference (its callers compute it from the gradient). */
 int swarp_rollout_bwd(const swarp_world_t* w, int32_t horizon, swarp_state_t init,
                       const void* actions, swarp_state_t traj, swarp_state_t adj_traj,
                       swarp_state_t adj_final, swarp_bodies_t bodies_init,
                       swarp_bodies_t bodies_traj, swarp_bodies_t adj_bodies_final,
-                      void* adj_actions, swarp_state_t adj_init, const void* workspace,
-                      size_t workspace_bytes, void* stream);
+                      void* adj_actions, swarp_state_t adj_init, void* adj_actions_sqnorm,
+                      void* workspace, size_t workspace_bytes, void* stream);
 
 /* Padded within-radius neighbor lists of positions pos [E, A, 2] (brute force, ascending
  * agent index, capped at max_neighbors): idx [E, A, K] int32 (unused slots untouched),

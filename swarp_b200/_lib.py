@@ -75,7 +75,7 @@ SIGNATURES = {
                                     C.c_void_p]),
     "swarp_rollout_bwd": (C.c_int, [C.POINTER(WorldC), C.c_int32, State, C.c_void_p, State, State,
                                     State, Bodies, Bodies, Bodies, C.c_void_p, State, C.c_void_p,
-                                    C.c_size_t, C.c_void_p]),
+                                    C.c_void_p, C.c_size_t, C.c_void_p]),
     "swarp_neighbors": (C.c_int, [C.POINTER(WorldC), C.c_void_p, C.c_void_p, C.c_void_p,
                                   C.c_void_p, C.c_void_p]),
     "swarp_rollout_noalloc": (C.c_int, [C.POINTER(WorldC), C.c_int32, State, C.c_void_p, State,

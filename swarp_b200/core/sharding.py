@@ -42,3 +42,39 @@ def reduce_loss_and_grad_norm(loss: torch.Tensor, grads, group=None) -> torch.Te
     if dist.is_available() and dist.is_initialized():
         dist.all_reduce(pair, op=dist.ReduceOp.SUM, group=group)
     return pair
+
+
+class PairReducer:
+    """Asynchronous per-step all-reduce of a small ``[loss, ||g||^2]`` pair.
+
+    Each call copies the pair into one of ``depth`` ring buffers and starts its all-reduce
+    on the collective's own stream without making the compute stream wait, so the next
+    rollout overlaps the reduction. The compute stream waits for a reduction only when its
+    buffer comes round again (``depth`` steps later). ``result(i)`` is the reduced pair of
+    the ``i``-th call from the end (0 = latest), valid after :meth:`drain`.
+    """
+
+    def __init__(self, like: torch.Tensor, depth: int = 3, group=None) -> None:
+        self.bufs = [torch.zeros(2, dtype=like.dtype, device=like.device) for _ in range(depth)]
+        self.works: list = [None] * depth
+        self.group = group
+        self.n = 0
+
+    def __call__(self, pair: torch.Tensor) -> None:
+        i = self.n % len(self.bufs)
+        if self.works[i] is not None:
+            self.works[i].wait()  # stream-ordered: the buffer's previous reduction is done
+        self.bufs[i].copy_(pair)
+        dist = torch.distributed
+        if dist.is_available() and dist.is_initialized():
+            self.works[i] = dist.all_reduce(self.bufs[i], group=self.group, async_op=True)
+        self.n += 1
+
+    def drain(self) -> None:
+        for i, w in enumerate(self.works):
+            if w is not None:
+                w.wait()
+                self.works[i] = None
+
+    def result(self, back: int = 0) -> torch.Tensor:
+        return self.bufs[(self.n - 1 - back) % len(self.bufs)]

@@ -144,6 +144,12 @@ class Stepper:
         #: :meth:`rollout_overflow` compares it with ``max_neighbors``.
         self.track_neighbor_overflow = False
         self.last_true_count_max: torch.Tensor | None = None
+        #: When set, every adjoint rollout also reduces sum(grad_actions^2) in its epilogue
+        #: into ``last_grad_sqnorm`` (a 0-d tensor of the stepper's dtype): the squared norm
+        #: of the gradient that flows into the actions through the rollout, without a
+        #: second pass over it.
+        self.track_grad_norm = False
+        self.last_grad_sqnorm: torch.Tensor | None = None
         #: Body state per obstacle slot (pos [E,N,2], angle [E,N], vel [E,N,2],
         #: ang_vel [E,N]); only body-root slots are meaningful.
         self.body_state: tuple[torch.Tensor, ...] | None = None
@@ -407,12 +413,16 @@ class Stepper:
         if gbody_final is not None:
             keep = tuple(None if x is None else x.contiguous() for x in gbody_final)
             gb = _lib.Bodies(*(_lib.ptr(x) for x in keep))
+        sq = None
+        if self.track_grad_norm:
+            sq = torch.empty((), dtype=self.dtype, device=self.device)
+            self.last_grad_sqnorm = sq
         rc = lib.swarp_rollout_bwd(
             C.byref(rec.wc), actions.shape[0], _lib.state_c(state5), actions.data_ptr(),
             _lib.state_c(traj5), _lib.state_c(gtraj5), _lib.state_c(gfin5),
             _lib.Bodies(*(_lib.ptr(x) for x in rec.body_init)) if rec.body_init else _lib.Bodies(),
             _lib.Bodies(*(_lib.ptr(x) for x in rec.body_traj)) if rec.body_traj else _lib.Bodies(),
-            gb, g_act.data_ptr(), _lib.state_c(g_init), ws.data_ptr(), ws.numel(),
+            gb, g_act.data_ptr(), _lib.state_c(g_init), _lib.ptr(sq), ws.data_ptr(), ws.numel(),
             _lib.stream_ptr(self.device),
         )
         _lib.check(rc, "swarp_rollout_bwd")

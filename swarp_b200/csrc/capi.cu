@@ -14,7 +14,7 @@ using namespace swarp;
 
 namespace {
 
-constexpr int kAbiVersion = 2;
+constexpr int kAbiVersion = 3;
 
 int threads_target() {
   static int v = [] {
@@ -166,6 +166,22 @@ void set_state_out(const swarp_state_t& s, T*& p, T*& th, T*& v, T*& sp, T*& w) 
   w = static_cast<T*>(s.ang_vel);
 }
 
+// Workspace: [contact checkpoint cells (F_TRUNC cutoffs / F_MASK masks)] then, 256-byte
+// aligned, one partial sum per adjoint CTA for the fused ||grad_actions||^2 epilogue.
+size_t partials_offset(const swarp_world_t* w, int horizon) {
+  const size_t cells = (size_t)horizon * w->substeps * (size_t)w->n_envs * w->n_agents;
+  const int fl = flags_of(w);
+  size_t b = 0;
+  if (fl & F_TRUNC) b = cells * sizeof(int16_t);  // list cutoffs
+  if (fl & F_MASK) b = cells * sizeof(uint32_t);  // contact masks
+  return (b + 255) & ~size_t(255);
+}
+size_t partials_bytes(const swarp_world_t* w) {
+  const int G = envs_per_cta(w->n_agents, w->n_envs);
+  const size_t n = (size_t)(w->n_envs + G - 1) / G;
+  return n * (w->dtype == SWARP_F32 ? sizeof(float) : sizeof(double));
+}
+
 template <typename T>
 int fwd_typed(const swarp_world_t* w, int horizon, swarp_state_t init, const void* actions,
               swarp_state_t traj, swarp_state_t fin, int32_t* true_max, swarp_bodies_t bi,
@@ -192,7 +208,7 @@ template <typename T>
 int bwd_typed(const swarp_world_t* w, int horizon, swarp_state_t init, const void* actions,
               swarp_state_t traj, swarp_state_t gtraj, swarp_state_t gfin, swarp_bodies_t bi,
               swarp_bodies_t bt, swarp_bodies_t gbf, void* gact, swarp_state_t ginit,
-              const void* ws, cudaStream_t st) {
+              void* gsq, void* ws, cudaStream_t st) {
   RolloutArgs<T> R;
   fill_common<T>(w, horizon, R);
   set_bodies<T>(bi, R.bi_pos, R.bi_ang, R.bi_vel, R.bi_om);
@@ -209,8 +225,12 @@ int bwd_typed(const swarp_world_t* w, int horizon, swarp_state_t init, const voi
   R.g_act = static_cast<T*>(gact);
   set_state_out<T>(ginit, R.gi_pos, R.gi_th, R.gi_vel, R.gi_s, R.gi_w);
   const int fl = flags_of(w);
-  R.cutoff = (fl & F_TRUNC) ? const_cast<int16_t*>(static_cast<const int16_t*>(ws)) : nullptr;
-  R.cmask = (fl & F_MASK) ? const_cast<uint32_t*>(static_cast<const uint32_t*>(ws)) : nullptr;
+  R.cutoff = (fl & F_TRUNC) ? static_cast<int16_t*>(ws) : nullptr;
+  R.cmask = (fl & F_MASK) ? static_cast<uint32_t*>(ws) : nullptr;
+  R.gsq_out = static_cast<T*>(gsq);
+  R.gsq_partial = gsq ? reinterpret_cast<T*>(static_cast<unsigned char*>(ws) +
+                                             partials_offset(w, horizon))
+                      : nullptr;
   return launch_bwd<T>(R, fl, st);
 }
 
@@ -229,11 +249,7 @@ extern "C" {
 
 size_t swarp_rollout_workspace_bytes(const swarp_world_t* w, int32_t horizon) {
   if (validate_world(w, horizon) != SWARP_OK) return 0;
-  const size_t cells = (size_t)horizon * w->substeps * (size_t)w->n_envs * w->n_agents;
-  const int fl = flags_of(w);
-  if (fl & F_TRUNC) return cells * sizeof(int16_t);  // list cutoffs
-  if (fl & F_MASK) return cells * sizeof(uint32_t);  // contact masks
-  return 0;
+  return partials_offset(w, horizon) + partials_bytes(w);
 }
 
 int swarp_rollout_fwd(const swarp_world_t* w, int32_t horizon, swarp_state_t init,
@@ -262,8 +278,8 @@ int swarp_rollout_bwd(const swarp_world_t* w, int32_t horizon, swarp_state_t ini
                       const void* actions, swarp_state_t traj, swarp_state_t adj_traj,
                       swarp_state_t adj_final, swarp_bodies_t bodies_init,
                       swarp_bodies_t bodies_traj, swarp_bodies_t adj_bodies_final,
-                      void* adj_actions, swarp_state_t adj_init, const void* workspace,
-                      size_t workspace_bytes, void* stream) {
+                      void* adj_actions, swarp_state_t adj_init, void* adj_actions_sqnorm,
+                      void* workspace, size_t workspace_bytes, void* stream) {
   int rc = validate_world(w, horizon);
   if (rc != SWARP_OK) return rc;
   if (flags_of(w) & F_BODIES) {
@@ -273,14 +289,18 @@ int swarp_rollout_bwd(const swarp_world_t* w, int32_t horizon, swarp_state_t ini
   if (!state_complete(init) || !state_complete(traj) || !state_complete(adj_init) || !actions ||
       !adj_actions)
     return SWARP_ERR_INVALID_ARG;
-  const size_t need = swarp_rollout_workspace_bytes(w, horizon);
+  // the checkpoint cells are read; the partials (only with adj_actions_sqnorm) are written
+  const size_t need = adj_actions_sqnorm ? swarp_rollout_workspace_bytes(w, horizon)
+                                         : partials_offset(w, horizon);
   if (need > 0 && (!workspace || workspace_bytes < need)) return SWARP_ERR_WORKSPACE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (w->dtype == SWARP_F32)
     return bwd_typed<float>(w, horizon, init, actions, traj, adj_traj, adj_final, bodies_init,
-                            bodies_traj, adj_bodies_final, adj_actions, adj_init, workspace, st);
+                            bodies_traj, adj_bodies_final, adj_actions, adj_init,
+                            adj_actions_sqnorm, workspace, st);
   return bwd_typed<double>(w, horizon, init, actions, traj, adj_traj, adj_final, bodies_init,
-                           bodies_traj, adj_bodies_final, adj_actions, adj_init, workspace, st);
+                           bodies_traj, adj_bodies_final, adj_actions, adj_init,
+                           adj_actions_sqnorm, workspace, st);
 }
 
 int swarp_neighbors(const swarp_world_t* w, const void* pos, int32_t* idx, int32_t* count,

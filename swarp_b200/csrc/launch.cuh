@@ -66,8 +66,11 @@ int run_fwd(const RolloutArgs<T>& R, cudaStream_t st) {
 template <typename T, int FL, int AS>
 int run_bwd(const RolloutArgs<T>& R, cudaStream_t st) {
   const Layout<T> L(R.G, R.A, R.N, R.S, true, (FL & F_BODIES) != 0);
-  return launch_kernel(rollout_bwd_kernel<T, FL, AS>, (R.E + R.G - 1) / R.G, R.G * R.A, L.total,
-                       st, &R);
+  const int grid = (R.E + R.G - 1) / R.G;
+  const int rc = launch_kernel(rollout_bwd_kernel<T, FL, AS>, grid, R.G * R.A, L.total, st, &R);
+  if (rc != 0 || !R.gsq_partial) return rc;
+  sum_partials_kernel<T><<<1, 256, 0, st>>>(R.gsq_partial, grid, R.gsq_out);
+  return cudaGetLastError() == cudaSuccess ? 0 : kErrCuda;
 }
 
 // Every valid flag combination: no contacts, contacts, truncating contacts, checkpointed

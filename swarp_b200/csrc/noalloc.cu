@@ -67,5 +67,5 @@ extern "C" int swarp_rollout_noalloc(const swarp_world_t* w, int32_t horizon, sw
                              scratch, need, stream);
   if (rc != SWARP_OK) return rc;
   return swarp_rollout_bwd(w, horizon, init, actions, traj, adj_traj, adj_final, none, none, none,
-                           adj_actions, adj_init, scratch, need, stream);
+                           adj_actions, adj_init, nullptr, scratch, need, stream);
 }

@@ -65,6 +65,10 @@ template <typename T> struct RolloutArgs {
   const T *gf_pos, *gf_th, *gf_vel, *gf_s, *gf_w;  // cotangent of final (nullable)
   T* g_act;
   T *gi_pos, *gi_th, *gi_vel, *gi_s, *gi_w;
+  // optional fused epilogue: per-CTA partial sums of g_act^2 (workspace [gridDim.x]) and
+  // the reduced total (one scalar); both null when the norm is not requested
+  T* gsq_partial;
+  T* gsq_out;
   // movable bodies (F_BODIES): per-shape constants, state per shape slot [E, N] at t = 0
   // and after every step [H, E, N], cotangent of the final body state (nullable)
   const int *o_kind, *o_body;
@@ -687,6 +691,38 @@ __device__ __forceinline__ void bodies_step_vjp(const BodyS<T>* st, const BodyC<
   for (int o = 0; o < N; ++o) gbody[o] = gbnew[o];
 }
 
+// Deterministic CTA sum (fixed shuffle tree, then warp sums in warp order) stored by
+// thread 0. Every thread of the block must call it.
+template <typename T>
+__device__ __forceinline__ void block_sum_store(T v, T* out) {
+  __shared__ T warp_sums[32];
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (lane == 0) warp_sums[wid] = v;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    T s = T(0);
+    const int nw = (blockDim.x + 31) >> 5;
+    for (int i = 0; i < nw; ++i) s += warp_sums[i];
+    *out = s;
+  }
+}
+
+// Sum of the per-CTA partials in a fixed order (one block), accumulated in double.
+template <typename T>
+__global__ void __launch_bounds__(256) sum_partials_kernel(const T* partial, int n, T* out) {
+  __shared__ double acc[256];
+  double s = 0.0;
+  for (int i = threadIdx.x; i < n; i += 256) s += static_cast<double>(partial[i]);
+  acc[threadIdx.x] = s;
+  __syncthreads();
+  for (int w = 128; w > 0; w >>= 1) {
+    if (threadIdx.x < w) acc[threadIdx.x] += acc[threadIdx.x + w];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *out = static_cast<T>(acc[0]);
+}
+
 template <typename T, int FL, int AS>
 __global__ void __launch_bounds__(1024) rollout_bwd_kernel(const RolloutArgs<T> R) {
   using T2 = typename V2<T>::t;
@@ -768,6 +804,7 @@ __global__ void __launch_bounds__(1024) rollout_bwd_kernel(const RolloutArgs<T> 
   load_action(R, (long long)(H - 1) * EA + ia, a0, a1);
   if ((FL & F_MASK) && S == 1) cm0 = R.cmask[(long long)(H - 1) * EA + ia];
   int fbuf = 0;
+  T gsq = T(0);  // this agent's sum over the horizon of ||d loss / d action||^2
   for (int t = H - 1; t >= 0; --t) {
     if (has_gt) add_cotangent(R.gt_pos, R.gt_th, R.gt_vel, R.gt_s, R.gt_w, (long long)t * EA + ia, g);
     Agent<T> pcur{};
@@ -889,6 +926,7 @@ __global__ void __launch_bounds__(1024) rollout_bwd_kernel(const RolloutArgs<T> 
     }
     if (valid) {
       const long long ja = (long long)t * EA + ia;
+      gsq = Num<T>::fma_(ga0, ga0, Num<T>::fma_(ga1, ga1, gsq));
       if (R.act_dim == 2) {
         reinterpret_cast<T2*>(R.g_act)[ja] = T2{ga0, ga1};
       } else {
@@ -904,6 +942,7 @@ __global__ void __launch_bounds__(1024) rollout_bwd_kernel(const RolloutArgs<T> 
     cm0 = pcm;
   }
   if (valid) store_state(R.gi_pos, R.gi_th, R.gi_vel, R.gi_s, R.gi_w, ia, g);
+  if (R.gsq_partial) block_sum_store(gsq, R.gsq_partial + blockIdx.x);
 }
 
 // ============================================================ neighbor lists

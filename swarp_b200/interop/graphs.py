@@ -33,12 +33,15 @@ class GraphedRollout:
     the graph and returns ``(loss, grad_actions)``: static tensors overwritten by the
     next call. With ``grad_norm`` (default), ``loss_and_grad_norm`` is a static
     ``[loss, ||grad_actions||^2]`` pair in the stepper's dtype, ready for a single
-    all-reduce across ranks (``None`` otherwise).
+    all-reduce across ranks (``None`` otherwise). ``grad_norm="fused"`` takes the norm
+    from the adjoint kernel's epilogue instead of a second pass over the gradient; it
+    equals the exact norm when the loss depends on the actions only through the rollout.
     """
 
     def __init__(self, stepper: Stepper, state: TorchState, actions: torch.Tensor,
                  loss_fn: Callable[[TorchState, Trajectory], torch.Tensor], *,
-                 wrt_state: bool = False, grad_norm: bool = True, warmup: int = 3) -> None:
+                 wrt_state: bool = False, grad_norm: bool | str = True,
+                 warmup: int = 3) -> None:
         if stepper.any_movable:
             raise NotImplementedError(
                 "GraphedRollout does not capture movable bodies: their state advances on the "
@@ -47,7 +50,11 @@ class GraphedRollout:
         self.stepper = stepper
         self.loss_fn = loss_fn
         self.wrt_state = wrt_state
+        if grad_norm not in (True, False, "fused"):
+            raise ValueError(f"grad_norm must be True, False or 'fused'; got {grad_norm!r}")
         self.grad_norm = grad_norm
+        if grad_norm == "fused":
+            stepper.track_grad_norm = True
         # Static leaves, detached from any history the given inputs carry: a backward that
         # reached back into the caller's graph would leave the capture stream.
         self.actions = actions.detach().to(dev, copy=True).requires_grad_(True)
@@ -73,7 +80,9 @@ class GraphedRollout:
         wrt = [self.actions] + (list(self.state[:5]) if self.wrt_state else [])
         grads = torch.autograd.grad(loss, wrt)
         pair = None
-        if self.grad_norm:
+        if self.grad_norm == "fused":
+            pair = torch.stack([loss.detach(), self.stepper.last_grad_sqnorm])
+        elif self.grad_norm:
             g = grads[0].reshape(-1)
             pair = torch.stack([loss.detach(), torch.dot(g, g)])
         return loss.detach(), grads, pair

@@ -42,7 +42,7 @@ def test_error_strings_and_version(lib):
     lib.swarp_error_string.restype = C.c_char_p
     assert lib.swarp_error_string(0) == b"ok"
     assert b"unsupported" in lib.swarp_error_string(-2)
-    assert lib.swarp_abi_version() == 2
+    assert lib.swarp_abi_version() == 3
 
 
 def test_invalid_world_is_rejected_without_a_gpu(lib):

@@ -77,3 +77,40 @@ def test_graphed_rollout_rejects_movable_bodies():
     state, _, acts = _inputs(2, 2, 3, 0)
     with pytest.raises(NotImplementedError):
         GraphedRollout(st, state, acts, lambda f, t: f.pos.sum())
+
+
+@pytest.mark.parametrize("dtype,substeps,A,K", [(torch.float32, 1, 16, 16), (torch.float64, 1, 40, 8),
+                                                (torch.float32, 3, 8, 8), (torch.float64, 2, 5, 4)])
+def test_fused_grad_sqnorm_matches_the_gradient(dtype, substeps, A, K):
+    """The adjoint epilogue's sum(grad_actions^2) equals the norm of the returned gradient
+    (fast path, truncating lists, substep recompute path)."""
+    E, T = 37, 9
+    world = WorldConfig(collision_k=100.0, collision_c=1.0, collision_margin=0.025,
+                        bounds=(-1.0, 1.0, -1.0, 1.0), bounds_mode="soft",
+                        neighbor_radius=0.3, max_neighbors=K)
+    st = Stepper([AgentConfig(radius=0.05, max_speed=1.0, max_accel=2.0)] * A, dt=0.05,
+                 substeps=substeps, device=DEV, dtype=dtype, world=world)
+    st.track_grad_norm = True
+    state, goal, acts = _inputs(E, A, T, 3)
+    state = TorchState(*(t.to(dtype) for t in state[:5]))
+    a = acts.to(dtype).requires_grad_(True)
+    fin, _ = rollout(st, state, a)
+    (g,) = torch.autograd.grad(((fin.pos - goal.to(dtype)) ** 2).sum(), [a])
+    want = float(g.double().square().sum())
+    got = float(st.last_grad_sqnorm)
+    assert got == pytest.approx(want, rel=1e-5 if dtype == torch.float32 else 1e-12)
+
+
+def test_fused_norm_in_graph_pair():
+    E, A, T = 64, 16, 8
+    st = Stepper([AgentConfig(radius=0.05, max_speed=1.0, max_accel=2.0)] * A, dt=0.05,
+                 device=DEV, world=WorldConfig(collision_margin=0.025, neighbor_radius=0.125,
+                                               max_neighbors=16))
+    state, goal, acts = _inputs(E, A, T, 4)
+    gr = GraphedRollout(st, state, acts, lambda f, t: ((f.pos - goal) ** 2).sum(),
+                        grad_norm="fused")
+    _, g = gr()
+    torch.cuda.synchronize()
+    assert gr.loss_and_grad_norm[1].item() == pytest.approx(float(g.double().square().sum()),
+                                                            rel=1e-5)
+    gr.release()

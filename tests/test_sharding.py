@@ -9,7 +9,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from swarp_b200.core.sharding import env_shard, reduce_loss_and_grad_norm
+from swarp_b200.core.sharding import PairReducer, env_shard, reduce_loss_and_grad_norm
 
 
 @pytest.mark.parametrize("n,w", [(16000, 1), (16000, 2), (16001, 4), (7, 7), (1025, 8)])
@@ -51,7 +51,11 @@ def _worker(rank, world, port, n_envs, out):
         loss_all = torch.rand(n_envs, generator=g, dtype=torch.float64)
         a, b = env_shard(n_envs, rank, world)
         pair = reduce_loss_and_grad_norm(loss_all[a:b].sum(), grads_all[a:b])
-        out[rank] = pair.tolist()
+        red = PairReducer(pair, depth=2)
+        for k in range(5):  # ring reuse: each step's pair is reduced on its own
+            red(torch.tensor([float(k), float(rank)], dtype=torch.float64))
+        red.drain()
+        out[rank] = pair.tolist() + red.result(0).tolist() + red.result(1).tolist()
     finally:
         dist.destroy_process_group()
 
@@ -68,5 +72,7 @@ def test_two_rank_allreduce_equals_whole_batch():
     grads_all = torch.randn(n_envs, 3, 2, generator=g, dtype=torch.float64)
     loss_all = torch.rand(n_envs, generator=g, dtype=torch.float64)
     expect = [float(loss_all.sum()), float(grads_all.square().sum())]
+    ranks_sum = float(sum(range(world)))
     for r in range(world):
-        assert results[r] == pytest.approx(expect, rel=1e-12)
+        assert results[r][:2] == pytest.approx(expect, rel=1e-12)
+        assert results[r][2:] == [4.0 * world, ranks_sum, 3.0 * world, ranks_sum]
