@@ -104,6 +104,9 @@ class Stepper:
             raise NotImplementedError("only the semi-implicit Euler integrator runs on the CUDA path")
         if world.wheel_contacts:
             raise NotImplementedError("wheel contacts are not on the CUDA path")
+        if world.obstacle_friction > 0.0:
+            raise NotImplementedError("floor friction of movable bodies (obstacle_friction) is "
+                                      "not on the CUDA path")
         self.params = torch.tensor(param_rows(self.configs), dtype=self.dtype, device=self.device)
         self.params_per_env: torch.Tensor | None = None
         self.model_tag = torch.tensor([int(c.model) for c in self.configs], dtype=torch.int32,
