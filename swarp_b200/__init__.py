@@ -51,6 +51,9 @@ from swarp_b200.interop.autograd import (
     rollout_bodies,
     warp_step,
 )
+from swarp_b200.core.sharding import PairReducer, env_shard, reduce_loss_and_grad_norm
+from swarp_b200.interop.compile import compiled_warp_step, register_stepper
+from swarp_b200.interop.graphs import GraphedRollout
 from swarp_b200.scenarios import SCENARIOS, NavigationScenario, make_scenario, scenario_class
 
 __version__ = "0.1.0"
@@ -81,7 +84,8 @@ def make(name: str, n_envs: int, **kwargs) -> Environment:
 
 __all__ = [
     "AgentConfig", "AgentShape", "BodyState", "ControlMode", "DynamicsModel", "Environment",
-    "GradRing", "Integrator", "NUM_PARAMS", "NavigationScenario", "ObstacleKind", "ObstacleShape",
+    "GradRing", "GraphedRollout", "PairReducer", "compiled_warp_step", "env_shard",
+    "reduce_loss_and_grad_norm", "register_stepper", "Integrator", "NUM_PARAMS", "NavigationScenario", "ObstacleKind", "ObstacleShape",
     "Obstacles", "PARAM_FIELDS", "P_HALF_X", "P_HALF_Y", "P_LF", "P_LR", "P_MASS", "P_MAX_ACCEL",
     "P_MAX_ANG_ACCEL", "P_MAX_ANG_VEL", "P_MAX_SPEED", "P_MAX_STEER", "P_MIN_SPEED", "P_RADIUS",
     "P_SHAPE", "SCENARIOS", "Stepper", "TorchState", "World", "WorldConfig", "action_bounds",

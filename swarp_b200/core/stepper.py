@@ -13,6 +13,8 @@ reference's Warp dtype argument has no meaning without Warp.
 from __future__ import annotations
 
 import ctypes as C
+import itertools
+import weakref
 from dataclasses import dataclass, replace
 
 import numpy as np
@@ -61,6 +63,22 @@ class RolloutRecord:
     moving: bool
 
 
+# Live steppers by integer handle (weak): the handle is how an op that cannot carry Python
+# objects (the ``swarp::step`` custom op) names its stepper. Assigned at construction so
+# that a traced program only ever reads ``stepper.handle``.
+_REGISTRY: "weakref.WeakValueDictionary[int, Stepper]" = weakref.WeakValueDictionary()
+_NEXT_HANDLE = itertools.count()
+
+
+def stepper_by_handle(handle: int) -> Stepper:
+    try:
+        return _REGISTRY[handle]
+    except KeyError:
+        raise RuntimeError(
+            f"no live Stepper has handle {handle}: it was garbage-collected; keep the "
+            "Environment/World (or the Stepper) alive while a compiled step uses it") from None
+
+
 class Stepper:
     """Owns per-agent parameters, interaction config and the rollout launches."""
 
@@ -92,6 +110,8 @@ class Stepper:
         self.dtype = _as_torch_dtype(dtype)
         self.torch_dtype = self.dtype
         self.world = world
+        self.handle = next(_NEXT_HANDLE)
+        _REGISTRY[self.handle] = self
         if self.n_agents > _lib.MAX_AGENTS:
             raise ValueError(f"{self.n_agents} agents per env exceed the {_lib.MAX_AGENTS} this "
                              "build runs in one CTA")
