@@ -403,6 +403,8 @@ def main() -> None:
     ap.add_argument("--impl", default="swarp_b200", choices=["swarp_b200", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=30)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--envs", type=int, default=None,
+                    help="override the config's envs per GPU (smaller cases for profiling)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -428,7 +430,7 @@ def main() -> None:
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    wl = build_workload(args.config, rank=rank, dev=dev)
+    wl = build_workload(args.config, rank=rank, dev=dev, n_envs=args.envs)
     st, E, A, H = wl.stepper, wl.E, wl.A, wl.H
     pos = torch.from_numpy(wl.pos).to(dev)
     theta = torch.from_numpy(wl.theta).to(dev)

@@ -18,7 +18,7 @@ CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libswarp_b200.so")
 SOURCES = ["capi.cu", "noalloc.cu", "k_fwd_f32.cu", "k_fwd_f64.cu", "k_bwd_f32.cu",
            "k_bwd_f64.cu"]
-DEPS = [*SOURCES, "launch.cuh", "rollout.cuh", "physics.cuh"]
+DEPS = [*SOURCES, "launch.cuh", "rollout.cuh", "physics.cuh", "bodies.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--extended-lambda", "-fmad=false",
          "-Xcompiler", "-fPIC", "-Xcompiler", "-O2"]
