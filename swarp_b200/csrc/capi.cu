@@ -27,7 +27,9 @@ int threads_target() {
 
 // Envs per CTA: whole envs, about threads_target() threads.
 int envs_per_cta(int A, int E) {
-  int G = A >= threads_target() ? 1 : threads_target() / A;
+  int target = threads_target();
+  if (A == 16 && target > kMaxThreadsAS16) target = kMaxThreadsAS16;  // see rollout_bwd_kernel
+  int G = A >= target ? 1 : target / A;
   if (G > E) G = E;
   return G < 1 ? 1 : G;
 }

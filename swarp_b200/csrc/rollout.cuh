@@ -42,6 +42,9 @@ enum : int {
   F_BODIES = 32,  // movable bodies integrated in the substep loop (with F_OBS)
 };
 
+// Largest CTA the 16-agent specializations are launched with (host: envs_per_cta).
+constexpr int kMaxThreadsAS16 = 256;
+
 template <typename T> struct RolloutArgs {
   int E, A, G, H, S, act_dim, N;
   WorldC<T> W;
@@ -548,6 +551,9 @@ __global__ void __launch_bounds__(1024) rollout_fwd_kernel(const RolloutArgs<T> 
   const T* rad_env = srad + le * A;
   const T* iden_env = siden + le * A;
   Obs<T>* obs_env = sobs + le * N;
+  // unrolled: the step's state and prefetched action rotate through registers instead of
+  // being copied at the end of each step (measured: 223.6 -> 203.1 us at 16000 x 16 x 64)
+#pragma unroll 4
   for (int t = 0; t < R.H; ++t) {
     if (t + 1 < R.H) load_action(R, (long long)(t + 1) * EA + ia, n0, n1);
     for (int k = 0; k < R.S; ++k) {
@@ -723,8 +729,11 @@ __global__ void __launch_bounds__(256) sum_partials_kernel(const T* partial, int
   if (threadIdx.x == 0) *out = static_cast<T>(acc[0]);
 }
 
+// The compile-time 16-agent instances run in CTAs of at most kMaxThreadsAS16 threads:
+// their adjoint then has up to 255 registers instead of 64 (measured 230 -> 224 us).
 template <typename T, int FL, int AS>
-__global__ void __launch_bounds__(1024) rollout_bwd_kernel(const RolloutArgs<T> R) {
+__global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : 1024)
+    rollout_bwd_kernel(const RolloutArgs<T> R) {
   using T2 = typename V2<T>::t;
   using T4 = typename V4<T>::t;
   constexpr bool kBodies = (FL & F_BODIES) != 0;
