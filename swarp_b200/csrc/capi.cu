@@ -19,8 +19,8 @@ constexpr int kAbiVersion = 3;
 int threads_target() {
   static int v = [] {
     const char* s = std::getenv("SWARP_CTA_THREADS");
-    int t = s ? std::atoi(s) : 128;
-    return (t >= 32 && t <= 1024) ? t : 128;
+    int t = s ? std::atoi(s) : 64;
+    return (t >= 32 && t <= 1024) ? t : 64;
   }();
   return v;
 }

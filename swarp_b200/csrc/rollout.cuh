@@ -151,6 +151,16 @@ __device__ __forceinline__ void load_state(const T* pos, const T* th, const T* v
   x.w = w[i];
 }
 
+// Position and velocity only (heading, speed and turn rate read as 0): what the adjoint of
+// a holonomic velocity-controlled step reads of its input and output states.
+template <typename T>
+__device__ __forceinline__ void load_state_pv(const T* pos, const T* vel, long long i, Agent<T>& x) {
+  using T2 = typename V2<T>::t;
+  const T2 p = reinterpret_cast<const T2*>(pos)[i];
+  const T2 v = reinterpret_cast<const T2*>(vel)[i];
+  x = Agent<T>{p.x, p.y, T(0), v.x, v.y, T(0), T(0)};
+}
+
 template <typename T>
 __device__ __forceinline__ void store_state(T* pos, T* th, T* vel, T* s, T* w, long long i,
                                             const Agent<T>& x) {
@@ -342,16 +352,22 @@ __device__ __forceinline__ unsigned scan_chunk(const float* xy_env, int c, int n
   const float2 PX = make_float2(px, px), PY = make_float2(py, py), M1 = make_float2(-1.f, -1.f);
   const float2 NT = make_float2(-thr, -thr);
   unsigned m = 0u;
-  constexpr int NPC = AS > 0 ? ((AS + 1) / 2 < 16 ? (AS + 1) / 2 : 16) : 16;
-#pragma unroll
-  for (int p = NPC - 1; p >= 0; --p) {
-    if (AS == 0 && p >= npairs) continue;
+  auto visit = [&](int p) {
     const float4 q = P[p];
     const float2 dx = __ffma2_rn(make_float2(q.x, q.y), M1, PX);
     const float2 dy = __ffma2_rn(make_float2(q.z, q.w), M1, PY);
     const float2 d = __ffma2_rn(dx, dx, __ffma2_rn(dy, dy, NT));
     m = __funnelshift_l(__float_as_uint(d.y), m, 1);
     m = __funnelshift_l(__float_as_uint(d.x), m, 1);
+  };
+  if constexpr (AS > 0) {
+    constexpr int NPC = (AS + 1) / 2 < 16 ? (AS + 1) / 2 : 16;
+#pragma unroll
+    for (int p = NPC - 1; p >= 0; --p) visit(p);
+  } else {
+    // only the chunk's real pairs (a predicated 16-pair unroll would issue all 16)
+#pragma unroll 4
+    for (int p = npairs - 1; p >= 0; --p) visit(p);
   }
   return m;
 }
@@ -359,10 +375,9 @@ template <int AS>
 __device__ __forceinline__ unsigned scan_chunk(const double* xy_env, int c, int npairs, double px,
                                                double py, double thr) {
   unsigned m = 0u;
-  constexpr int NPC = AS > 0 ? ((AS + 1) / 2 < 16 ? (AS + 1) / 2 : 16) : 16;
+  const int NPC = AS > 0 ? ((AS + 1) / 2 < 16 ? (AS + 1) / 2 : 16) : npairs;
 #pragma unroll 4
   for (int p = NPC - 1; p >= 0; --p) {
-    if (AS == 0 && p >= npairs) continue;
     const double* q = xy_env + (c * 16 + p) * 4;
     const double dx1 = px - q[1], dy1 = py - q[3];
     const double dx0 = px - q[0], dy0 = py - q[2];
@@ -800,16 +815,32 @@ __global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : 1024)
 
   Agent<T> g{};
   add_cotangent(R.gf_pos, R.gf_th, R.gf_vel, R.gf_s, R.gf_w, ia, g);
+  // One-substep holonomic velocity fleets without bodies: the step's adjoint reads only the
+  // positions and velocities of its input and output states (heading passes through,
+  // speed is recomputed from the velocity), so the other three fields are not loaded.
+  const bool pv_only = (FL & F_HOLOVEL) && S == 1 && !kBodies;
+  auto load_traj = [&](long long i, Agent<T>& x) {
+    if (pv_only)
+      load_state_pv(R.t_pos, R.t_vel, i, x);
+    else
+      load_state(R.t_pos, R.t_th, R.t_vel, R.t_s, R.t_w, i, x);
+  };
+  auto load_init = [&](Agent<T>& x) {
+    if (pv_only)
+      load_state_pv(R.i_pos, R.i_vel, ia, x);
+    else
+      load_state(R.i_pos, R.i_th, R.i_vel, R.i_s, R.i_w, ia, x);
+  };
   Agent<T> nxt;  // output state of step t
-  load_state(R.t_pos, R.t_th, R.t_vel, R.t_s, R.t_w, (long long)(H - 1) * EA + ia, nxt);
+  load_traj((long long)(H - 1) * EA + ia, nxt);
   // software pipeline: the inputs of step t are loaded during step t+1
   Agent<T> cur;
   T a0, a1;
   unsigned cm0 = 0u;
   if (H > 1)
-    load_state(R.t_pos, R.t_th, R.t_vel, R.t_s, R.t_w, (long long)(H - 2) * EA + ia, cur);
+    load_traj((long long)(H - 2) * EA + ia, cur);
   else
-    load_state(R.i_pos, R.i_th, R.i_vel, R.i_s, R.i_w, ia, cur);
+    load_init(cur);
   load_action(R, (long long)(H - 1) * EA + ia, a0, a1);
   if ((FL & F_MASK) && S == 1) cm0 = R.cmask[(long long)(H - 1) * EA + ia];
   int fbuf = 0;
@@ -821,9 +852,9 @@ __global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : 1024)
     unsigned pcm = 0u;
     if (t > 0) {
       if (t > 1)
-        load_state(R.t_pos, R.t_th, R.t_vel, R.t_s, R.t_w, (long long)(t - 2) * EA + ia, pcur);
+        load_traj((long long)(t - 2) * EA + ia, pcur);
       else
-        load_state(R.i_pos, R.i_th, R.i_vel, R.i_s, R.i_w, ia, pcur);
+        load_init(pcur);
       load_action(R, (long long)(t - 1) * EA + ia, pa0, pa1);
       if ((FL & F_MASK) && S == 1) pcm = R.cmask[(long long)(t - 1) * EA + ia];
     }
