@@ -383,7 +383,7 @@ def run_reference(args, rank: int, world: int) -> None:
 # ------------------------------------------------------------------ GPU side
 def profile_traffic(cid: int):
     """DRAM bytes per launch of the adjoint kernel from the committed ncu summary, if any."""
-    path = os.path.join(ROOT, "profiles", "rollout_bwd_config2.md")
+    path = os.path.join(ROOT, "profiles", "rollout_kernels_config2.md")
     key = f"traffic_bytes_per_launch_config{cid}:"
     try:
         for line in open(path):
@@ -615,7 +615,8 @@ def main() -> None:
         "clocks": clocks.summary(),
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
-        "gpu_launches": 2 * args.steps,
+        # forward + adjoint per step, plus the fused-norm reduction when ranks all-reduce it
+        "gpu_launches": (3 if reducer is not None else 2) * args.steps,
         "timed_path": ("one CUDA-graph replay of the whole BPTT step per step "
                        "(swarp_b200.interop.graphs.GraphedRollout)" if graphed is not None else
                        "eager rollout_bodies + autograd.grad"),
