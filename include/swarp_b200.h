@@ -112,6 +112,7 @@ typedef struct {
   int32_t fleet_models;      /* host-known bitmask of the DynamicsModel values in model_tag */
   int32_t fleet_modes;       /* host-known bitmask of the ControlMode values in ctrl_mode */
   swarp_obstacles_t obstacles;
+  int32_t integrator;        /* 0 semi-implicit Euler, 1 classic RK4 (dynamics/kernels.py:521-793) */
 } swarp_world_t;
 
 /* Bytes of device workspace for this world and horizon: the contact checkpoint that

@@ -134,6 +134,7 @@ class RefWorld:
     lin_damping: float = 10.0
     ang_damping: float = 10.0
     bodies_move: bool = True
+    rk4: bool = False  # Integrator.RK4 instead of semi-implicit Euler
 
     def col(self, j):
         """Parameter column ``j`` broadcastable to ``[E, A]``."""
@@ -430,6 +431,98 @@ def integrate(state, act, fx, fy, w: RefWorld):
     return (torch.stack([npx, npy], -1), nth, torch.stack([nvx, nvy], -1), ns, nw)
 
 
+def _rk4_deriv(px, py, th, vx, vy, s, om, a0, a1, tag, mode, c):
+    """``swarp/dynamics/kernels.py:420-518`` (``_deriv``): the continuous-time derivative of
+    each 2-D model's independent states; derived quantities have zero rate."""
+    zero = torch.zeros_like(th)
+    vel_mode = mode == VELOCITY
+    hax, hay = clamp_norm(a0, a1, c["max_accel"])
+    h = (vx, vy, zero, torch.where(vel_mode, zero, hax), torch.where(vel_mode, zero, hay), zero,
+         zero)
+    d = (s * torch.cos(th), s * torch.sin(th), om, zero, zero,
+         torch.where(vel_mode, zero, wclamp(a0, -c["max_accel"], c["max_accel"])),
+         torch.where(vel_mode, zero, wclamp(a1, -c["max_ang_acc"], c["max_ang_acc"])))
+    wb = c["l_f"] + c["l_r"]
+    delta = wclamp(a1, -c["max_steer"], c["max_steer"])
+    beta = torch.atan(torch.tan(delta) * c["l_r"] / wb)
+    b = (s * torch.cos(th + beta), s * torch.sin(th + beta),
+         s / wb * torch.cos(beta) * torch.tan(delta), zero, zero,
+         wclamp(a0, -c["max_accel"], c["max_accel"]), zero)
+    return tuple(torch.where(tag == HOLONOMIC, h[i],
+                             torch.where(tag == DIFF_DRIVE, d[i],
+                                         torch.where(tag == BICYCLE, b[i], zero)))
+                 for i in range(7))
+
+
+def integrate_rk4(state, act, fx, fy, w: RefWorld):
+    """``swarp/dynamics/kernels.py:521-793`` (``_integrate_rk4``) for one substep: classic
+    RK4 over four derivative evaluations with the actions held; velocity-mode commands set
+    the velocity-level state first; limits apply to the combined result; the contact force
+    enters as the Euler path's ``F/m dt`` velocity term (and ``F/m dt^2`` in the pose)."""
+    pos, th, vel, s, om = state
+    E, A = th.shape
+    dt = w.dt / w.substeps
+    a0, a1 = act[..., 0], act[..., 1]
+    col = lambda j: w.col(j).expand(E, A)  # noqa: E731
+    c = {"max_speed": col(P_MAX_SPEED), "min_speed": col(P_MIN_SPEED),
+         "max_accel": col(P_MAX_ACCEL), "max_ang_vel": col(P_MAX_ANG_VEL),
+         "max_ang_acc": col(P_MAX_ANG_ACCEL), "l_f": col(P_LF), "l_r": col(P_LR),
+         "max_steer": col(P_MAX_STEER), "mass": col(P_MASS)}
+    tag = torch.tensor(w.model_tag, device=th.device).unsqueeze(0).expand(E, A)
+    mode = torch.tensor(w.ctrl_mode, device=th.device).unsqueeze(0).expand(E, A)
+    servo = mode == SERVO
+    if bool(servo.any()):  # kernels.py:846-861: SERVO becomes its VELOCITY command
+        tv = wclamp(a0, -c["max_speed"], c["max_speed"]) * col(P_CMD_GAIN_V)
+        tw = wclamp(a1, -c["max_ang_vel"], c["max_ang_vel"]) * col(P_CMD_GAIN_W)
+        dv_, dw_ = c["max_accel"] * dt, c["max_ang_acc"] * dt
+        a0 = torch.where(servo, s + wclamp(tv - s, -dv_, dv_), a0)
+        a1 = torch.where(servo, om + wclamp(tw - om, -dw_, dw_), a1)
+        mode = torch.where(servo, torch.zeros_like(mode), mode)
+    px, py, vx, vy = pos[..., 0], pos[..., 1], vel[..., 0], vel[..., 1]
+    vel_mode = mode == VELOCITY
+    cvx, cvy = clamp_norm(a0, a1, c["max_speed"])
+    vx = torch.where(vel_mode & (tag == HOLONOMIC), cvx, vx)
+    vy = torch.where(vel_mode & (tag == HOLONOMIC), cvy, vy)
+    s = torch.where(vel_mode & (tag == DIFF_DRIVE), wclamp(a0, -c["max_speed"], c["max_speed"]), s)
+    om = torch.where(vel_mode & (tag == DIFF_DRIVE),
+                     wclamp(a1, -c["max_ang_vel"], c["max_ang_vel"]), om)
+    x = (px, py, th, vx, vy, s, om)
+    dt2, sixth = dt * 0.5, dt / 6.0
+    k1 = _rk4_deriv(*x, a0, a1, tag, mode, c)
+    k2 = _rk4_deriv(*(xi + ki * dt2 for xi, ki in zip(x, k1)), a0, a1, tag, mode, c)
+    k3 = _rk4_deriv(*(xi + ki * dt2 for xi, ki in zip(x, k2)), a0, a1, tag, mode, c)
+    k4 = _rk4_deriv(*(xi + ki * dt for xi, ki in zip(x, k3)), a0, a1, tag, mode, c)
+    ipx, ipy, ith, ivx, ivy, i_s, iom = (
+        xi + (q1 + q2 * 2.0 + q3 * 2.0 + q4) * sixth for xi, q1, q2, q3, q4 in zip(x, k1, k2, k3, k4))
+    k_dt = dt / c["mass"]
+    dvx, dvy = fx * k_dt, fy * k_dt
+    zero = torch.zeros_like(th)
+    ppx, ppy = ipx + dvx * dt, ipy + dvy * dt
+    hvx, hvy = clamp_norm(ivx, ivy, c["max_speed"])
+    hvx, hvy = hvx + dvx, hvy + dvy
+    h = (ppx, ppy, th, hvx, hvy, wlength(hvx, hvy), zero)
+    ds_ = wclamp(i_s, -c["max_speed"], c["max_speed"])
+    dw_ = wclamp(iom, -c["max_ang_vel"], c["max_ang_vel"])
+    d = (ppx, ppy, ith, ds_ * torch.cos(ith) + dvx, ds_ * torch.sin(ith) + dvy, ds_, dw_)
+    bs = wclamp(i_s, c["min_speed"], c["max_speed"])
+    wb = c["l_f"] + c["l_r"]
+    delta = wclamp(a1, -c["max_steer"], c["max_steer"])
+    beta = torch.atan(torch.tan(delta) * c["l_r"] / wb)
+    bw = bs / wb * torch.cos(beta) * torch.tan(delta)
+    b = (ppx, ppy, ith, bs * torch.cos(ith + beta) + dvx, bs * torch.sin(ith + beta) + dvy, bs, bw)
+    hold = (pos[..., 0], pos[..., 1], th, vel[..., 0], vel[..., 1], state[3], state[4])
+    out = [torch.where(tag == HOLONOMIC, h[i], torch.where(tag == DIFF_DRIVE, d[i],
+                                                            torch.where(tag == BICYCLE, b[i], hold[i])))
+           for i in range(7)]
+    npx, npy, nth, nvx, nvy, ns, nw = out
+    if w.clamp_bounds:
+        x0, x1, y0, y1 = w.bounds
+        r = col(P_RADIUS)
+        npx = wclamp(npx, x0 + r, x1 - r)
+        npy = wclamp(npy, y0 + r, y1 - r)
+    return (torch.stack([npx, npy], -1), nth, torch.stack([nvx, nvy], -1), ns, nw)
+
+
 # -------------------------------------------------------------------------- bodies
 
 
@@ -663,7 +756,7 @@ def step(state, act, w: RefWorld, obs: RefObstacles | None = None):
             obs_next = body_pass(state, obs, w)
         else:
             obs_next = obs
-        state = integrate(state, act, fx, fy, w)
+        state = (integrate_rk4 if w.rk4 else integrate)(state, act, fx, fy, w)
         obs = obs_next
     return state, obs, tmax
 

@@ -64,6 +64,7 @@ class WorldC(C.Structure):
         ("model_tag", C.c_void_p), ("ctrl_mode", C.c_void_p),
         ("fleet_models", C.c_int32), ("fleet_modes", C.c_int32),
         ("obstacles", ObstaclesC),
+        ("integrator", C.c_int32),
     ]
 
 

@@ -4,8 +4,8 @@ Field names, defaults and validation mirror the reference
 (``swarp/core/config.py``: ``ObstacleShape`` ``:118-127``, ``ObstacleKind``
 ``:130-141``, ``Obstacles`` ``:144-283``, ``WorldConfig`` ``:286-427``) because they
 are the public configuration surface scenarios pass in. Options that select paths
-this package does not run on the GPU (``wheel_contacts``, floor friction,
-``Integrator.RK4``, the ``grid``/``uniform_grid`` neighbor backends) are accepted
+this package does not run on the GPU (``wheel_contacts``, floor friction, the
+``grid``/``uniform_grid`` neighbor backends) are accepted
 for compatibility and rejected by :class:`~swarp_b200.core.stepper.Stepper` when
 they would change the physics.
 """

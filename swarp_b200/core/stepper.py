@@ -120,8 +120,8 @@ class Stepper:
                 raise NotImplementedError("the 6-DOF drone model is not on the CUDA path yet")
             if c.shape == AgentShape.BOX:
                 raise NotImplementedError("box agents (OBB contacts) are not on the CUDA path yet")
-        if world.integrator != Integrator.EULER:
-            raise NotImplementedError("only the semi-implicit Euler integrator runs on the CUDA path")
+        if world.integrator not in (Integrator.EULER, Integrator.RK4):
+            raise NotImplementedError(f"integrator {world.integrator} is not on the CUDA path")
         if world.wheel_contacts:
             raise NotImplementedError("wheel contacts are not on the CUDA path")
         if world.obstacle_friction > 0.0:
@@ -260,6 +260,7 @@ class Stepper:
         wc.neighbor_radius = self.neighbor_radius
         wc.max_neighbors = w.max_neighbors
         wc.bounds_mode = 1 if self._soft_walls else (2 if self._clamp else 0)
+        wc.integrator = 1 if w.integrator == Integrator.RK4 else 0
         b = w.bounds if w.bounds is not None else (0.0, 0.0, 0.0, 0.0)
         wc.bounds = (C.c_double * 4)(*b)
         wc.lin_damping = w.obstacle_linear_damping

@@ -14,7 +14,7 @@ using namespace swarp;
 
 namespace {
 
-constexpr int kAbiVersion = 3;
+constexpr int kAbiVersion = 4;
 
 int threads_target() {
   static int v = [] {
@@ -56,6 +56,7 @@ int validate_world(const swarp_world_t* w, int horizon) {
   if (w->fleet_models & ~0x7) return SWARP_ERR_UNSUPPORTED;  // drone / unknown tags
   if (w->fleet_models == 0 || w->fleet_modes == 0 || (w->fleet_modes & ~0x7)) return SWARP_ERR_INVALID_ARG;
   if (w->bounds_mode < 0 || w->bounds_mode > 2) return SWARP_ERR_INVALID_ARG;
+  if (w->integrator < 0 || w->integrator > 1) return SWARP_ERR_INVALID_ARG;
   if (w->collisions) {
     if (w->max_neighbors < 1 || !(w->neighbor_radius > 0.0)) return SWARP_ERR_INVALID_ARG;
     if (w->n_agents > 32767) return SWARP_ERR_TOO_MANY_AGENTS;
@@ -88,6 +89,7 @@ int flags_of(const swarp_world_t* w) {
     fl |= F_OBS;
     if (w->obstacles.any_movable && w->obstacles.bodies_move) fl |= F_BODIES;
   }
+  if (w->integrator == 1) fl |= F_RK4;
   if (w->fleet_models == 1 && w->fleet_modes == 1) fl |= F_HOLOVEL;
   return fl;
 }

@@ -1,0 +1,6 @@
+// Kernel instances: fwd rollout, float, RK4 integrator.
+#define SWARP_DEFINE_LAUNCHERS
+#include "launch.cuh"
+namespace swarp {
+template int launch_fwd_part<float, F_RK4>(const RolloutArgs<float>&, int, cudaStream_t);
+}  // namespace swarp

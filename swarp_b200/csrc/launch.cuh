@@ -16,8 +16,16 @@ namespace swarp {
 constexpr int kErrUnsupported = -2;
 constexpr int kErrCuda = -4;
 
-template <typename T> int launch_fwd(const RolloutArgs<T>& R, int fl, cudaStream_t st);
-template <typename T> int launch_bwd(const RolloutArgs<T>& R, int fl, cudaStream_t st);
+// The instances are split by integrator (RB = 0: Euler cases, RB = F_RK4: the same cases
+// with RK4) so that each half compiles in a translation unit of its own (k_*.cu).
+template <typename T, int RB> int launch_fwd_part(const RolloutArgs<T>& R, int fl, cudaStream_t st);
+template <typename T, int RB> int launch_bwd_part(const RolloutArgs<T>& R, int fl, cudaStream_t st);
+template <typename T> inline int launch_fwd(const RolloutArgs<T>& R, int fl, cudaStream_t st) {
+  return (fl & F_RK4) ? launch_fwd_part<T, F_RK4>(R, fl, st) : launch_fwd_part<T, 0>(R, fl, st);
+}
+template <typename T> inline int launch_bwd(const RolloutArgs<T>& R, int fl, cudaStream_t st) {
+  return (fl & F_RK4) ? launch_bwd_part<T, F_RK4>(R, fl, st) : launch_bwd_part<T, 0>(R, fl, st);
+}
 template <typename T>
 int launch_neighbors(int E, int A, int G, int K, T r2, const T* pos, int* idx, int* cnt, int* tru,
                      cudaStream_t st);
@@ -76,11 +84,13 @@ int run_bwd(const RolloutArgs<T>& R, cudaStream_t st) {
 // Every valid flag combination: no contacts, contacts, truncating contacts, checkpointed
 // contacts; each with/without obstacles and with/without the holonomic-velocity fleet;
 // moving bodies (always with obstacles) with each contact mode and fleet kind.
-#define SWARP_FLAG_CASES(X)                                                                \
-  X(0) X(4) X(8) X(12) X(1) X(5) X(9) X(13) X(3) X(7) X(11) X(15) X(17) X(21) X(25) X(29) \
-  X(36) X(37) X(39) X(53) X(44) X(45) X(47) X(61)
+#define SWARP_FLAG_CASES_EULER(X, R)                                                           \
+  X(R + 0) X(R + 4) X(R + 8) X(R + 12) X(R + 1) X(R + 5) X(R + 9) X(R + 13) X(R + 3) X(R + 7) \
+  X(R + 11) X(R + 15) X(R + 17) X(R + 21) X(R + 25) X(R + 29) X(R + 36) X(R + 37) X(R + 39)   \
+  X(R + 53) X(R + 44) X(R + 45) X(R + 47) X(R + 61)
+// (each instantiated once with R = 0 and once with R = F_RK4)
 
-template <typename T> int launch_fwd(const RolloutArgs<T>& R, int fl, cudaStream_t st) {
+template <typename T, int RB> int launch_fwd_part(const RolloutArgs<T>& R, int fl, cudaStream_t st) {
   const bool a16 = std::is_same<T, float>::value && R.A == 16;
   switch (fl) {
 #define SWARP_X(F)                                                          \
@@ -88,13 +98,13 @@ template <typename T> int launch_fwd(const RolloutArgs<T>& R, int fl, cudaStream
     if constexpr (std::is_same<T, float>::value && ((F) & F_COLL))          \
       if (a16) return run_fwd<T, F, 16>(R, st);                             \
     return run_fwd<T, F, 0>(R, st);
-    SWARP_FLAG_CASES(SWARP_X)
+    SWARP_FLAG_CASES_EULER(SWARP_X, RB)
 #undef SWARP_X
   }
   return kErrUnsupported;
 }
 
-template <typename T> int launch_bwd(const RolloutArgs<T>& R, int fl, cudaStream_t st) {
+template <typename T, int RB> int launch_bwd_part(const RolloutArgs<T>& R, int fl, cudaStream_t st) {
   const bool a16 = std::is_same<T, float>::value && R.A == 16;
   switch (fl) {
 #define SWARP_X(F)                                                          \
@@ -102,7 +112,7 @@ template <typename T> int launch_bwd(const RolloutArgs<T>& R, int fl, cudaStream
     if constexpr (std::is_same<T, float>::value && ((F) & F_COLL))          \
       if (a16) return run_bwd<T, F, 16>(R, st);                             \
     return run_bwd<T, F, 0>(R, st);
-    SWARP_FLAG_CASES(SWARP_X)
+    SWARP_FLAG_CASES_EULER(SWARP_X, RB)
 #undef SWARP_X
   }
   return kErrUnsupported;

@@ -767,4 +767,318 @@ __device__ __forceinline__ void integrate_vjp(const Agent<T>& in, T a0, T a1, co
   }
 }
 
+// ------------------------------------------------------------------- RK4
+// Classic RK4 over the 2-D models' independent states (swarp/dynamics/kernels.py:420-793):
+// the derivative holds the actions; velocity-mode commands first set the velocity-level
+// state; the limits apply to the combined result; the contact force enters as the Euler
+// path's F/m dt on the velocity (and F/m dt^2 on the pose). The adjoint recomputes the
+// four stages from the substep input and walks them backwards.
+template <typename T>
+__device__ __forceinline__ Agent<T> rk4_axpy(const Agent<T>& x, const Agent<T>& k, T h) {
+  return Agent<T>{x.px + k.px * h, x.py + k.py * h, x.th + k.th * h, x.vx + k.vx * h,
+                  x.vy + k.vy * h, x.s + k.s * h, x.w + k.w * h};
+}
+
+// Steering terms of the bicycle (constant over a step): tan(delta), beta, wheelbase.
+template <typename T> struct Steer {
+  T td, beta, cb, sb, wb;
+};
+template <typename T>
+__device__ __forceinline__ Steer<T> steer_of(T c1, const AgentP<T>& P) {
+  Steer<T> q;
+  q.wb = P.l_f + P.l_r;
+  q.td = Num<T>::tan_(wclamp(c1, -P.max_steer, P.max_steer));
+  q.beta = Num<T>::atan_(q.td * P.l_r / q.wb);
+  q.cb = Num<T>::cos_(q.beta);
+  q.sb = Num<T>::sin_(q.beta);
+  return q;
+}
+
+template <typename T>
+__device__ __forceinline__ Agent<T> rk4_deriv(const Agent<T>& x, T c0, T c1, int mode,
+                                               const AgentP<T>& P, const Steer<T>& q) {
+  Agent<T> d{T(0), T(0), T(0), T(0), T(0), T(0), T(0)};
+  if (P.tag == TAG_HOLONOMIC) {
+    d.px = x.vx;
+    d.py = x.vy;
+    if (mode != MODE_VELOCITY) clamp_norm(c0, c1, P.max_accel, d.vx, d.vy);
+  } else if (P.tag == TAG_DIFF_DRIVE) {
+    d.px = x.s * Num<T>::cos_(x.th);
+    d.py = x.s * Num<T>::sin_(x.th);
+    d.th = x.w;
+    if (mode != MODE_VELOCITY) {
+      d.s = wclamp(c0, -P.max_accel, P.max_accel);
+      d.w = wclamp(c1, -P.max_ang_accel, P.max_ang_accel);
+    }
+  } else {
+    const T ang = x.th + q.beta;
+    d.px = x.s * Num<T>::cos_(ang);
+    d.py = x.s * Num<T>::sin_(ang);
+    d.th = x.s / q.wb * q.cb * q.td;
+    d.s = wclamp(c0, -P.max_accel, P.max_accel);
+  }
+  return d;
+}
+
+// Adjoint of rk4_deriv at x for the cotangent gk: adds into gx, the command cotangents
+// (gc0, gc1) and, for the bicycle, the cotangents of beta and tan(delta).
+template <typename T>
+__device__ __forceinline__ void rk4_deriv_vjp(const Agent<T>& x, const Agent<T>& gk, T c0, T c1,
+                                              int mode, const AgentP<T>& P, const Steer<T>& q,
+                                              Agent<T>& gx, T& gc0, T& gc1, T& gbeta, T& gtd) {
+  if (P.tag == TAG_HOLONOMIC) {
+    gx.vx += gk.px;
+    gx.vy += gk.py;
+    if (mode != MODE_VELOCITY) {
+      T r0, r1;
+      clamp_norm_vjp(c0, c1, P.max_accel, gk.vx, gk.vy, r0, r1);
+      gc0 += r0;
+      gc1 += r1;
+    }
+  } else if (P.tag == TAG_DIFF_DRIVE) {
+    const T c = Num<T>::cos_(x.th), sn = Num<T>::sin_(x.th);
+    gx.s += gk.px * c + gk.py * sn;
+    gx.th += x.s * (c * gk.py - sn * gk.px);
+    gx.w += gk.th;
+    if (mode != MODE_VELOCITY) {
+      if (clamp_pass(c0, -P.max_accel, P.max_accel)) gc0 += gk.s;
+      if (clamp_pass(c1, -P.max_ang_accel, P.max_ang_accel)) gc1 += gk.w;
+    }
+  } else {
+    const T ang = x.th + q.beta;
+    const T ca = Num<T>::cos_(ang), sa = Num<T>::sin_(ang);
+    // dth = ((s / wb) * cos(beta)) * tan(delta)
+    gx.s += gk.px * ca + gk.py * sa + gk.th * q.td * q.cb / q.wb;
+    const T gang = x.s * (ca * gk.py - sa * gk.px);
+    gx.th += gang;
+    gbeta += gang - gk.th * q.td * (x.s / q.wb) * q.sb;
+    gtd += gk.th * (x.s / q.wb) * q.cb;
+    if (clamp_pass(c0, -P.max_accel, P.max_accel)) gc0 += gk.s;
+  }
+}
+
+// The four stages from the substep input: x (after the velocity-mode command), the
+// stage states x2..x4, the slopes k1..k4 and the combined independent state xi.
+template <typename T> struct Rk4Stages {
+  Agent<T> x, x2, x3, x4, k1, k2, k3, k4, xi;
+  T c0, c1;
+  int mode;
+  Steer<T> q;
+};
+template <typename T>
+__device__ __forceinline__ void rk4_stages(const Agent<T>& in, T a0, T a1, const AgentP<T>& P,
+                                           T dt, Rk4Stages<T>& R) {
+  R.mode = P.mode;
+  R.c0 = a0;
+  R.c1 = a1;
+  if (R.mode == MODE_SERVO) {
+    servo_cmd(a0, a1, in.s, in.w, P, dt, R.c0, R.c1);
+    R.mode = MODE_VELOCITY;
+  }
+  R.q = steer_of(R.c1, P);
+  R.x = in;
+  if (R.mode == MODE_VELOCITY) {
+    if (P.tag == TAG_HOLONOMIC) {
+      clamp_norm(R.c0, R.c1, P.max_speed, R.x.vx, R.x.vy);
+    } else if (P.tag == TAG_DIFF_DRIVE) {
+      R.x.s = wclamp(R.c0, -P.max_speed, P.max_speed);
+      R.x.w = wclamp(R.c1, -P.max_ang_vel, P.max_ang_vel);
+    }
+  }
+  const T h = dt * T(0.5), sixth = dt / T(6);
+  R.k1 = rk4_deriv(R.x, R.c0, R.c1, R.mode, P, R.q);
+  R.x2 = rk4_axpy(R.x, R.k1, h);
+  R.k2 = rk4_deriv(R.x2, R.c0, R.c1, R.mode, P, R.q);
+  R.x3 = rk4_axpy(R.x, R.k2, h);
+  R.k3 = rk4_deriv(R.x3, R.c0, R.c1, R.mode, P, R.q);
+  R.x4 = rk4_axpy(R.x, R.k3, dt);
+  R.k4 = rk4_deriv(R.x4, R.c0, R.c1, R.mode, P, R.q);
+  auto comb = [&](T x, T a, T b, T c, T d) { return x + (a + b * T(2) + c * T(2) + d) * sixth; };
+  R.xi = Agent<T>{comb(R.x.px, R.k1.px, R.k2.px, R.k3.px, R.k4.px),
+                  comb(R.x.py, R.k1.py, R.k2.py, R.k3.py, R.k4.py),
+                  comb(R.x.th, R.k1.th, R.k2.th, R.k3.th, R.k4.th),
+                  comb(R.x.vx, R.k1.vx, R.k2.vx, R.k3.vx, R.k4.vx),
+                  comb(R.x.vy, R.k1.vy, R.k2.vy, R.k3.vy, R.k4.vy),
+                  comb(R.x.s, R.k1.s, R.k2.s, R.k3.s, R.k4.s),
+                  comb(R.x.w, R.k1.w, R.k2.w, R.k3.w, R.k4.w)};
+}
+
+template <typename T>
+__device__ __forceinline__ void integrate_rk4_fwd(const Agent<T>& in, T a0, T a1, T fx, T fy,
+                                                  const AgentP<T>& P, const WorldC<T>& W,
+                                                  Agent<T>& out) {
+  const T dt = W.dt;
+  Rk4Stages<T> R;
+  rk4_stages(in, a0, a1, P, dt, R);
+  const Agent<T>& xi = R.xi;
+  const T dvx = fx * P.dt_over_m, dvy = fy * P.dt_over_m;
+  out.px = xi.px + dvx * dt;
+  out.py = xi.py + dvy * dt;
+  if (P.tag == TAG_HOLONOMIC) {
+    T vx, vy;
+    clamp_norm(xi.vx, xi.vy, P.max_speed, vx, vy);
+    vx = vx + dvx;
+    vy = vy + dvy;
+    out.th = in.th;
+    out.vx = vx;
+    out.vy = vy;
+    out.s = norm2(vx, vy);
+    out.w = T(0);
+  } else if (P.tag == TAG_DIFF_DRIVE) {
+    const T so = wclamp(xi.s, -P.max_speed, P.max_speed);
+    out.w = wclamp(xi.w, -P.max_ang_vel, P.max_ang_vel);
+    out.th = xi.th;
+    out.vx = so * Num<T>::cos_(xi.th) + dvx;
+    out.vy = so * Num<T>::sin_(xi.th) + dvy;
+    out.s = so;
+  } else {
+    const T so = wclamp(xi.s, P.min_speed, P.max_speed);
+    const Steer<T>& q = R.q;
+    out.th = xi.th;
+    out.w = so / q.wb * q.cb * q.td;
+    out.vx = so * Num<T>::cos_(xi.th + q.beta) + dvx;
+    out.vy = so * Num<T>::sin_(xi.th + q.beta) + dvy;
+    out.s = so;
+  }
+  if (W.bounds_mode == BOUNDS_CLAMP) {
+    out.px = wclamp(out.px, W.bx0 + P.radius, W.bx1 - P.radius);
+    out.py = wclamp(out.py, W.by0 + P.radius, W.by1 - P.radius);
+  }
+}
+
+// Adjoint of integrate_rk4_fwd (same contract as integrate_vjp: gin overwritten, force
+// cotangent written, action cotangent added). `out` is the substep's stored output: the
+// position clamp's side test uses it (strictly inside the interval: not clamped; on its
+// boundary: the pre-clamp position rebuilt from the stored velocity decides).
+template <typename T>
+__device__ __forceinline__ void integrate_rk4_vjp(const Agent<T>& in, T a0, T a1, const Agent<T>& out,
+                                                  const Agent<T>& g, const AgentP<T>& P,
+                                                  const WorldC<T>& W, Agent<T>& gin, T& gfx, T& gfy,
+                                                  T& ga0, T& ga1) {
+  const T dt = W.dt;
+  Rk4Stages<T> R;
+  rk4_stages(in, a0, a1, P, dt, R);
+  const Agent<T>& xi = R.xi;
+  const Steer<T>& q = R.q;
+  // ---- output map: cotangent of xi, of the force term and of the steering
+  Agent<T> gxi{T(0), T(0), T(0), T(0), T(0), T(0), T(0)};
+  T gc0 = T(0), gc1 = T(0), gbeta = T(0), gtd = T(0);
+  T gpx = g.px, gpy = g.py;
+  T vbx, vby;  // velocity without the force term
+  if (P.tag == TAG_HOLONOMIC) {
+    clamp_norm(xi.vx, xi.vy, P.max_speed, vbx, vby);
+  } else if (P.tag == TAG_DIFF_DRIVE) {
+    const T so = wclamp(xi.s, -P.max_speed, P.max_speed);
+    vbx = so * Num<T>::cos_(xi.th);
+    vby = so * Num<T>::sin_(xi.th);
+  } else {
+    const T so = wclamp(xi.s, P.min_speed, P.max_speed);
+    vbx = so * Num<T>::cos_(xi.th + q.beta);
+    vby = so * Num<T>::sin_(xi.th + q.beta);
+  }
+  if (W.bounds_mode == BOUNDS_CLAMP) {
+    const T lox = W.bx0 + P.radius, hix = W.bx1 - P.radius;
+    const T loy = W.by0 + P.radius, hiy = W.by1 - P.radius;
+    const T prex = xi.px + (out.vx - vbx) * dt, prey = xi.py + (out.vy - vby) * dt;
+    const bool px_in = (out.px > lox && out.px < hix) || clamp_pass(prex, lox, hix);
+    const bool py_in = (out.py > loy && out.py < hiy) || clamp_pass(prey, loy, hiy);
+    if (!px_in) gpx = T(0);
+    if (!py_in) gpy = T(0);
+  }
+  gxi.px = gpx;
+  gxi.py = gpy;
+  // p = xi.p + dv * dt, v = vb + dv, dv = F * dt / m
+  T gvx = g.vx, gvy = g.vy;
+  if (P.tag == TAG_HOLONOMIC) {
+    const T n2 = dot2(out.vx, out.vy, out.vx, out.vy);  // s = |v|
+    if (n2 > T(0)) {
+      const T qq = g.s * Num<T>::rsqrt_(n2);
+      gvx += out.vx * qq;
+      gvy += out.vy * qq;
+    }
+  }
+  gfx = (gvx + gpx * dt) * P.dt_over_m;
+  gfy = (gvy + gpy * dt) * P.dt_over_m;
+  if (P.tag == TAG_HOLONOMIC) {
+    clamp_norm_vjp(xi.vx, xi.vy, P.max_speed, gvx, gvy, gxi.vx, gxi.vy);
+    gxi.th = g.th;  // heading passes through
+  } else if (P.tag == TAG_DIFF_DRIVE) {
+    const T so = wclamp(xi.s, -P.max_speed, P.max_speed);
+    const T c = Num<T>::cos_(xi.th), sn = Num<T>::sin_(xi.th);
+    const T gso = g.s + gvx * c + gvy * sn;
+    gxi.th = g.th + so * (c * gvy - sn * gvx);
+    gxi.s = clamp_pass(xi.s, -P.max_speed, P.max_speed) ? gso : T(0);
+    gxi.w = clamp_pass(xi.w, -P.max_ang_vel, P.max_ang_vel) ? g.w : T(0);
+  } else {
+    const T so = wclamp(xi.s, P.min_speed, P.max_speed);
+    const T ang = xi.th + q.beta;
+    const T ca = Num<T>::cos_(ang), sa = Num<T>::sin_(ang);
+    // w = ((so / wb) * cos(beta)) * tan(delta)
+    const T gso = g.s + gvx * ca + gvy * sa + g.w * q.td * q.cb / q.wb;
+    const T gang = so * (ca * gvy - sa * gvx);
+    gxi.th = g.th + gang;
+    gbeta += gang - g.w * q.td * (so / q.wb) * q.sb;
+    gtd += g.w * (so / q.wb) * q.cb;
+    gxi.s = clamp_pass(xi.s, P.min_speed, P.max_speed) ? gso : T(0);
+  }
+  // ---- combine: xi = x + (k1 + 2 k2 + 2 k3 + k4) * dt / 6
+  const T h = dt * T(0.5), sixth = dt / T(6);
+  auto scale = [](const Agent<T>& v, T c) {
+    return Agent<T>{v.px * c, v.py * c, v.th * c, v.vx * c, v.vy * c, v.s * c, v.w * c};
+  };
+  auto add = [](Agent<T>& a, const Agent<T>& b) {
+    a.px += b.px; a.py += b.py; a.th += b.th; a.vx += b.vx; a.vy += b.vy; a.s += b.s; a.w += b.w;
+  };
+  const Agent<T> gS = scale(gxi, sixth);
+  Agent<T> gx = gxi;
+  Agent<T> gk1 = gS, gk2 = scale(gS, T(2)), gk3 = scale(gS, T(2));
+  const Agent<T> gk4 = gS;
+  Agent<T> gst{T(0), T(0), T(0), T(0), T(0), T(0), T(0)};
+  rk4_deriv_vjp(R.x4, gk4, R.c0, R.c1, R.mode, P, q, gst, gc0, gc1, gbeta, gtd);
+  add(gx, gst);
+  add(gk3, scale(gst, dt));
+  gst = Agent<T>{T(0), T(0), T(0), T(0), T(0), T(0), T(0)};
+  rk4_deriv_vjp(R.x3, gk3, R.c0, R.c1, R.mode, P, q, gst, gc0, gc1, gbeta, gtd);
+  add(gx, gst);
+  add(gk2, scale(gst, h));
+  gst = Agent<T>{T(0), T(0), T(0), T(0), T(0), T(0), T(0)};
+  rk4_deriv_vjp(R.x2, gk2, R.c0, R.c1, R.mode, P, q, gst, gc0, gc1, gbeta, gtd);
+  add(gx, gst);
+  add(gk1, scale(gst, h));
+  gst = Agent<T>{T(0), T(0), T(0), T(0), T(0), T(0), T(0)};
+  rk4_deriv_vjp(R.x, gk1, R.c0, R.c1, R.mode, P, q, gst, gc0, gc1, gbeta, gtd);
+  add(gx, gst);
+  // ---- velocity-mode command: it replaced the velocity-level input state
+  gin = gx;
+  if (R.mode == MODE_VELOCITY) {
+    if (P.tag == TAG_HOLONOMIC) {
+      T r0, r1;
+      clamp_norm_vjp(R.c0, R.c1, P.max_speed, gx.vx, gx.vy, r0, r1);
+      gc0 += r0;
+      gc1 += r1;
+      gin.vx = gin.vy = T(0);
+    } else if (P.tag == TAG_DIFF_DRIVE) {
+      if (clamp_pass(R.c0, -P.max_speed, P.max_speed)) gc0 += gx.s;
+      if (clamp_pass(R.c1, -P.max_ang_vel, P.max_ang_vel)) gc1 += gx.w;
+      gin.s = gin.w = T(0);
+    }
+  }
+  // ---- steering: beta = atan(tan(delta) * l_r / wb), tan(delta) with delta = clamp(c1)
+  if (P.tag == TAG_BICYCLE) {
+    const T z = q.td * P.l_r / q.wb;
+    gtd += gbeta / (T(1) + z * z) * P.l_r / q.wb;
+    const T gdelta = gtd * (T(1) + q.td * q.td);
+    if (clamp_pass(R.c1, -P.max_steer, P.max_steer)) gc1 += gdelta;
+  }
+  if (P.mode == MODE_SERVO) {
+    T gs = T(0), gw = T(0);
+    servo_cmd_vjp(a0, a1, in.s, in.w, P, dt, gc0, gc1, ga0, ga1, gs, gw);
+    gin.s += gs;
+    gin.w += gw;
+  } else {
+    ga0 += gc0;
+    ga1 += gc1;
+  }
+}
+
 }  // namespace swarp

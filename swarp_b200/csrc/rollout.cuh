@@ -40,6 +40,7 @@ enum : int {
   F_HOLOVEL = 8,  // every agent is holonomic / VELOCITY
   F_MASK = 16,    // contact masks checkpointed (A <= 32, no truncation)
   F_BODIES = 32,  // movable bodies integrated in the substep loop (with F_OBS)
+  F_RK4 = 64,     // classic RK4 integrator instead of semi-implicit Euler
 };
 
 // Largest CTA the 16-agent specializations are launched with (host: envs_per_cta).
@@ -478,14 +479,15 @@ __device__ __forceinline__ void static_force(const Obs<T>* sobs, int N, const Ag
 template <typename T, int FL>
 __device__ __forceinline__ void integrate_sel(const Agent<T>& in, T a0, T a1, T fx, T fy,
                                               const AgentP<T>& P, const WorldC<T>& W, Agent<T>& out) {
+  AgentP<T> Q = P;
   if (FL & F_HOLOVEL) {
-    AgentP<T> Q = P;
     Q.tag = TAG_HOLONOMIC;
     Q.mode = MODE_VELOCITY;
-    integrate_fwd(in, a0, a1, fx, fy, Q, W, out);
-  } else {
-    integrate_fwd(in, a0, a1, fx, fy, P, W, out);
   }
+  if (FL & F_RK4)
+    integrate_rk4_fwd(in, a0, a1, fx, fy, Q, W, out);
+  else
+    integrate_fwd(in, a0, a1, fx, fy, Q, W, out);
 }
 
 template <typename T, int FL>
@@ -493,14 +495,15 @@ __device__ __forceinline__ void integrate_vjp_sel(const Agent<T>& in, T a0, T a1
                                                   const Agent<T>& g, const AgentP<T>& P,
                                                   const WorldC<T>& W, Agent<T>& gin, T& gfx, T& gfy,
                                                   T& ga0, T& ga1) {
+  AgentP<T> Q = P;
   if (FL & F_HOLOVEL) {
-    AgentP<T> Q = P;
     Q.tag = TAG_HOLONOMIC;
     Q.mode = MODE_VELOCITY;
-    integrate_vjp(in, a0, a1, out, g, Q, W, gin, gfx, gfy, ga0, ga1);
-  } else {
-    integrate_vjp(in, a0, a1, out, g, P, W, gin, gfx, gfy, ga0, ga1);
   }
+  if (FL & F_RK4)
+    integrate_rk4_vjp(in, a0, a1, out, g, Q, W, gin, gfx, gfy, ga0, ga1);
+  else
+    integrate_vjp(in, a0, a1, out, g, Q, W, gin, gfx, gfy, ga0, ga1);
 }
 
 // Pad slot of an odd-sized env: never within any radius.

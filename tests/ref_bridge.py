@@ -5,6 +5,7 @@ from __future__ import annotations
 import torch
 
 from oracle import torch_ref as R
+from swarp_b200.dynamics.base import Integrator
 
 D = torch.float64
 
@@ -30,6 +31,7 @@ def ref_world(stepper, n_envs: int | None = None) -> R.RefWorld:
         clamp_bounds=stepper._clamp,
         lin_damping=w.obstacle_linear_damping,
         ang_damping=w.obstacle_angular_damping,
+        rk4=w.integrator == Integrator.RK4,
     )
 
 

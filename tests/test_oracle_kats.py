@@ -314,3 +314,74 @@ def test_gradcheck_oracle_with_collisions_and_walls():
 
     inputs = tuple(t.clone().requires_grad_(True) for t in (*st, acts))
     assert torch.autograd.gradcheck(fn, inputs, eps=1e-6, atol=1e-5)
+
+
+# --------------------------------------------------------------------- RK4
+# reference tests/unit/test_dynamics.py:261-298 (RK4 arm), :484-560
+
+
+def _dd_circle_final(dt, N, rk4):
+    cfg = AgentConfig(model=DynamicsModel.DIFF_DRIVE, ctrl_mode=ControlMode.VELOCITY,
+                      max_speed=5.0, max_ang_vel=5.0)
+    s, w = 1.3, 0.9
+    traj = run(world([cfg], dt, collisions=False, rk4=rk4), state_of([[0.2, -0.1]], theta=[0.3]),
+               np.tile(np.array([s, w]), (N, 1, 1)))
+    th = 0.3 + w * dt * N
+    exact = np.array([0.2 + (s / w) * (np.sin(th) - np.sin(0.3)),
+                      -0.1 - (s / w) * (np.cos(th) - np.cos(0.3))])
+    return np.linalg.norm(traj[-1][0][0, 0].numpy() - exact)
+
+
+def test_rk4_convergence_order():
+    """On the circular diff-drive trajectory RK4 converges ~dt^4, Euler ~dt^1."""
+    e_rk, e_rk2 = _dd_circle_final(2.0 / 100, 100, True), _dd_circle_final(2.0 / 200, 200, True)
+    e_eu, e_eu2 = _dd_circle_final(2.0 / 100, 100, False), _dd_circle_final(2.0 / 200, 200, False)
+    assert np.log2(e_rk / e_rk2) > 3.5
+    assert 0.8 < np.log2(e_eu / e_eu2) < 1.3
+    assert e_rk < e_eu * 1e-3
+
+
+def test_rk4_matches_euler_on_straight_line():
+    cfg = AgentConfig(model=DynamicsModel.HOLONOMIC, ctrl_mode=ControlMode.VELOCITY, max_speed=2.0)
+    acts = np.tile(np.array([0.7, -0.4]), (20, 1, 1))
+    eu = run(world([cfg], 0.05, collisions=False), state_of([[0.0, 0.0]]), acts)
+    rk = run(world([cfg], 0.05, collisions=False, rk4=True), state_of([[0.0, 0.0]]), acts)
+    np.testing.assert_allclose(rk[-1][0].numpy(), eu[-1][0].numpy(), atol=1e-12)
+
+
+def test_rk4_bicycle_min_speed_stops_but_creeps():
+    """min_speed = 0 stops the car under full braking; RK4 applies limits to the combined
+    result only, so (unlike Euler) its pose still moves after the speed reaches zero."""
+    cfg = AgentConfig(model=DynamicsModel.KINEMATIC_BICYCLE, max_speed=5.0, max_accel=1.0,
+                      l_f=1.25, l_r=1.25, max_steer=0.6, min_speed=0.0)
+    init = state_of([[0.0, 0.0]], vel=[[0.5, 0.0]], speed=[0.5])
+    acts = np.tile(np.array([-1.0, 0.3]), (30, 1, 1))
+    traj = run(world([cfg], 0.1, collisions=False, rk4=True), init, acts)
+    speeds = np.array([s[3][0, 0].item() for s in traj])
+    assert speeds.min() == 0.0 and speeds[-1] == 0.0
+    rev = AgentConfig(model=DynamicsModel.KINEMATIC_BICYCLE, max_speed=5.0, max_accel=1.0,
+                      l_f=1.25, l_r=1.25, max_steer=0.6)
+    traj_rev = run(world([rev], 0.1, collisions=False, rk4=True), init, acts)
+    assert traj_rev[-1][3][0, 0].item() < 0.0
+
+
+@pytest.mark.parametrize("model,mode", [
+    (DynamicsModel.HOLONOMIC, ControlMode.VELOCITY), (DynamicsModel.HOLONOMIC, ControlMode.ACCELERATION),
+    (DynamicsModel.DIFF_DRIVE, ControlMode.VELOCITY), (DynamicsModel.DIFF_DRIVE, ControlMode.ACCELERATION),
+    (DynamicsModel.DIFF_DRIVE, ControlMode.SERVO), (DynamicsModel.KINEMATIC_BICYCLE, ControlMode.VELOCITY)])
+def test_gradcheck_oracle_rk4_step(model, mode):
+    """reference tests/unit/test_gradients.py:77-108: the RK4 step is differentiable."""
+    cfgs = [AgentConfig(model=model, ctrl_mode=mode, max_speed=BIG, max_accel=BIG, max_ang_vel=BIG,
+                        max_ang_accel=BIG, max_steer=1.0, l_f=0.16, l_r=0.14) for _ in range(2)]
+    w = world(cfgs, 0.1, collisions=False, rk4=True)
+    g = torch.Generator().manual_seed(1)
+    st = [torch.randn(2, 2, 2, generator=g, dtype=D), torch.randn(2, 2, generator=g, dtype=D),
+          torch.randn(2, 2, 2, generator=g, dtype=D), torch.randn(2, 2, generator=g, dtype=D),
+          torch.randn(2, 2, generator=g, dtype=D)]
+    st = [x.requires_grad_(True) for x in st]
+    a = (0.3 * torch.randn(2, 2, 2, generator=g, dtype=D)).requires_grad_(True)
+
+    def fn(p, th, v, s, om, act):
+        return R.step((p, th, v, s, om), act, w)[0]
+
+    assert torch.autograd.gradcheck(fn, (*st, a), eps=1e-6, atol=1e-5)
