@@ -6,6 +6,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <limits>
+#include <type_traits>
 
 #include "../../include/swarp_b200.h"
 #include "launch.cuh"
@@ -24,6 +25,34 @@ int threads_target() {
   }();
   return v;
 }
+
+// The two-agents-per-thread kernels (rollout_x2.cuh): on unless SWARP_X2=0.
+bool x2_enabled() {
+  static bool v = [] {
+    const char* s = std::getenv("SWARP_X2");
+    return !(s && s[0] == '0');
+  }();
+  return v;
+}
+bool aligned(const void* p, unsigned n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; }
+
+// Whether a float world can take the two-agents-per-thread kernels (their preconditions:
+// 16 agents, 2 action slots, checkpointed contact masks, no moving bodies, vector-aligned
+// fields; the adjoint also one substep per step).
+bool x2_ok(const RolloutArgs<float>& R, int fl, bool bwd) {
+  if (!x2_enabled() || R.A != 16 || R.act_dim != 2) return false;
+  if (!(fl & F_MASK) || (fl & (F_BODIES | F_TRUNC))) return false;
+  if (bwd && R.S != 1) return false;
+  const void* v16[] = {R.t_pos, R.t_vel, R.i_pos, R.i_vel, R.act, R.f_pos, R.f_vel, R.g_act};
+  for (const void* p : v16)
+    if (p && !aligned(p, 16)) return false;
+  const void* v8[] = {R.t_th, R.t_s, R.t_w, R.i_th, R.i_s, R.i_w, R.f_th, R.f_s, R.f_w,
+                      R.cmask, R.true_max};
+  for (const void* p : v8)
+    if (p && !aligned(p, 8)) return false;
+  return true;
+}
+int x2_envs_per_cta(int E) { return E < 8 ? E : 8; }  // 64 threads: the kernels' launch bound
 
 // Envs per CTA: whole envs, about threads_target() threads.
 int envs_per_cta(int A, int E) {
@@ -205,6 +234,12 @@ int fwd_typed(const swarp_world_t* w, int horizon, swarp_state_t init, const voi
   const int fl = flags_of(w);
   R.cutoff = (fl & F_TRUNC) ? static_cast<int16_t*>(ws) : nullptr;
   R.cmask = (fl & F_MASK) ? static_cast<uint32_t*>(ws) : nullptr;
+  if constexpr (std::is_same<T, float>::value) {
+    if (x2_ok(R, fl, false)) {
+      R.G = x2_envs_per_cta(R.E);
+      return launch_fwd_x2(R, fl, st);
+    }
+  }
   return launch_fwd<T>(R, fl, st);
 }
 
@@ -235,6 +270,12 @@ int bwd_typed(const swarp_world_t* w, int horizon, swarp_state_t init, const voi
   R.gsq_partial = gsq ? reinterpret_cast<T*>(static_cast<unsigned char*>(ws) +
                                              partials_offset(w, horizon))
                       : nullptr;
+  if constexpr (std::is_same<T, float>::value) {
+    if (x2_ok(R, fl, true)) {
+      R.G = x2_envs_per_cta(R.E);  // fewer CTAs than the partials buffer is sized for
+      return launch_bwd_x2(R, fl, st);
+    }
+  }
   return launch_bwd<T>(R, fl, st);
 }
 

@@ -20,6 +20,11 @@ constexpr int kErrCuda = -4;
 // with RK4) so that each half compiles in a translation unit of its own (k_*.cu).
 template <typename T, int RB> int launch_fwd_part(const RolloutArgs<T>& R, int fl, cudaStream_t st);
 template <typename T, int RB> int launch_bwd_part(const RolloutArgs<T>& R, int fl, cudaStream_t st);
+// Two agents per thread (float, A == 16, contact masks, no moving bodies; rollout_x2.cuh).
+// R.G counts envs per CTA of 8 threads each.
+int launch_fwd_x2(const RolloutArgs<float>& R, int fl, cudaStream_t st);
+int launch_bwd_x2(const RolloutArgs<float>& R, int fl, cudaStream_t st);
+
 template <typename T> inline int launch_fwd(const RolloutArgs<T>& R, int fl, cudaStream_t st) {
   return (fl & F_RK4) ? launch_fwd_part<T, F_RK4>(R, fl, st) : launch_fwd_part<T, 0>(R, fl, st);
 }
