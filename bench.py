@@ -592,7 +592,9 @@ def main() -> None:
     fwd_gbs = (FWD_BYTES * agent_steps + body_b) / (t_fwd / 1e3) / 1e9
     step_gbs = wl.algo_bytes_per_env_step * E * H / ((t_fwd + t_bwd) / 1e3) / 1e9
     dom = "bwd" if t_bwd >= t_fwd else "fwd"
-    roof = {"bound": "hbm", "kernel": f"rollout_{dom}_kernel<float,...>",
+    # 16-agent float worlds without moving bodies take the two-agents-per-thread instances
+    x2 = A == 16 and not wl.body and (dom == "fwd" or st.substeps == 1)
+    roof = {"bound": "hbm", "kernel": f"rollout_{dom}_{'x2_' if x2 else ''}kernel<...>",
             "achieved": bwd_gbs if dom == "bwd" else fwd_gbs, "peak": peak, "unit": "GB/s",
             "peak_source": peak_src}
     roof["frac"] = roof["achieved"] / peak
