@@ -39,6 +39,7 @@ import torch
 P_RADIUS, P_MASS, P_MAX_SPEED, P_MAX_ACCEL, P_MAX_ANG_VEL, P_MAX_ANG_ACCEL = 0, 1, 2, 3, 4, 5
 P_LF, P_LR, P_MAX_STEER, P_MIN_SPEED = 6, 7, 8, 16
 P_CMD_GAIN_V, P_CMD_GAIN_W = 20, 21
+P_SHAPE, P_HALF_X, P_HALF_Y = 17, 18, 19
 HOLONOMIC, DIFF_DRIVE, BICYCLE = 0, 1, 2
 VELOCITY, ACCELERATION, SERVO = 0, 1, 2
 CIRCLE, BOX, SEGMENT = 0, 1, 2
@@ -284,6 +285,214 @@ def wall_forces(px, py, vx, vy, ra, w: RefWorld, denom):
     return fx, fy
 
 
+# ------------------------------------------------------------------ box agents
+
+
+def _point_box(vx, vy, cx, cy, ca, sa, hx, hy):
+    """``swarp/core/collisions.py:270-288``: distance and closest point from an exterior
+    point to an oriented box (distance floored like pair_force's)."""
+    dx, dy = vx - cx, vy - cy
+    lx = ca * dx + sa * dy
+    ly = -sa * dx + ca * dy
+    clx = wclamp(lx, -hx, hx)
+    cly = wclamp(ly, -hy, hy)
+    ox, oy = lx - clx, ly - cly
+    d2 = ox * ox + oy * oy
+    dist = torch.sqrt(wmax(d2, torch.full_like(d2, EPS2)))
+    return dist, cx + (ca * clx - sa * cly), cy + (sa * clx + ca * cly)
+
+
+def obb_contact(cax, cay, tha, hax, hay, cbx, cby, thb, hbx, hby, reach):
+    """``swarp/core/collisions.py:311-444``: signed distance, unit normal (B to A) and
+    contact point of two oriented boxes. SAT over the four face normals first; beyond
+    ``reach`` no contact; disjoint within reach: the closest of the eight vertex-versus-
+    box distances; overlapping: the least-overlap axis and the middle of the overlap of
+    the two projections on its reference face. Branches are selected per element."""
+    caA, saA, caB, saB = torch.cos(tha), torch.sin(tha), torch.cos(thb), torch.sin(thb)
+    uA0, uA1 = (caA, saA), (-saA, caA)
+    uB0, uB1 = (caB, saB), (-saB, caB)
+    dot = lambda u, v: u[0] * v[0] + u[1] * v[1]  # noqa: E731
+    d = (cax - cbx, cay - cby)
+    a00, a01 = wabs(dot(uA0, uB0)), wabs(dot(uA0, uB1))
+    a10, a11 = wabs(dot(uA1, uB0)), wabs(dot(uA1, uB1))
+    dA0, dA1, dB0, dB1 = dot(d, uA0), dot(d, uA1), dot(d, uB0), dot(d, uB1)
+    gaps = [wabs(dA0) - hax - (hbx * a00 + hby * a01), wabs(dA1) - hay - (hbx * a10 + hby * a11),
+            wabs(dB0) - hbx - (hax * a00 + hay * a10), wabs(dB1) - hby - (hax * a01 + hay * a11)]
+    s = gaps[0]
+    axis = torch.zeros_like(s, dtype=torch.int64)
+    for i in (1, 2, 3):
+        take = gaps[i] > s
+        s = torch.where(take, gaps[i], s)
+        axis = torch.where(take, torch.full_like(axis, i), axis)
+    zero = torch.zeros_like(s)
+    # disjoint: vertices of A against B (flip +1), then of B against A (flip -1)
+    eA0 = (uA0[0] * hax, uA0[1] * hax)
+    eA1 = (uA1[0] * hay, uA1[1] * hay)
+    eB0 = (uB0[0] * hbx, uB0[1] * hbx)
+    eB1 = (uB1[0] * hby, uB1[1] * hby)
+    best = torch.full_like(s, 1.0e30)
+    bnx, bny, bxx, bxy = zero, zero, cax, cay
+    verts = []
+    for sx, sy in ((1, 1), (-1, 1), (-1, -1), (1, -1)):
+        verts.append(((cax + sx * eA0[0]) + sy * eA1[0], (cay + sx * eA0[1]) + sy * eA1[1],
+                      cbx, cby, caB, saB, hbx, hby, 1.0))
+    for sx, sy in ((1, 1), (-1, 1), (-1, -1), (1, -1)):
+        verts.append(((cbx + sx * eB0[0]) + sy * eB1[0], (cby + sx * eB0[1]) + sy * eB1[1],
+                      cax, cay, caA, saA, hax, hay, -1.0))
+    for vx, vy, cx, cy, ca, sa, hx, hy, flip in verts:
+        dist, qx, qy = _point_box(vx, vy, cx, cy, ca, sa, hx, hy)
+        take = dist < best
+        best = torch.where(take, dist, best)
+        bnx = torch.where(take, (vx - qx) * (flip / dist), bnx)
+        bny = torch.where(take, (vy - qy) * (flip / dist), bny)
+        bxx = torch.where(take, (vx + qx) * 0.5, bxx)
+        bxy = torch.where(take, (vy + qy) * 0.5, bxy)
+    # overlapping: the least-overlap axis, oriented B -> A, and its reference face
+    sel = lambda vals: torch.where(axis == 0, vals[0], torch.where(  # noqa: E731
+        axis == 1, vals[1], torch.where(axis == 2, vals[2], vals[3])))
+    ux = sel([uA0[0], uA1[0], uB0[0], uB1[0]])
+    uy = sel([uA0[1], uA1[1], uB0[1], uB1[1]])
+    tx = sel([uA1[0], uA0[0], uB1[0], uB0[0]])
+    ty = sel([uA1[1], uA0[1], uB1[1], uB0[1]])
+    dn = sel([dA0, dA1, dB0, dB1])
+    h_n = sel([hax, hay, hbx, hby])
+    h_t = sel([hay, hax, hby, hbx])
+    r_t = sel([hbx * a10 + hby * a11, hbx * a00 + hby * a01, hax * a01 + hay * a11,
+               hax * a00 + hay * a10])
+    sgn = torch.where(dn < 0, -torch.ones_like(dn), torch.ones_like(dn))
+    onx, ony = ux * sgn, uy * sgn
+    b_axis = axis >= 2
+    crx, cry = torch.where(b_axis, cbx, cax), torch.where(b_axis, cby, cay)
+    cix, ciy = torch.where(b_axis, cax, cbx), torch.where(b_axis, cay, cby)
+    xn = torch.where(b_axis, (cbx * onx + cby * ony) + h_n, (cax * onx + cay * ony) - h_n)
+    ct_ref = crx * tx + cry * ty
+    ct_inc = cix * tx + ciy * ty
+    lo = wmax(ct_ref - h_t, ct_inc - r_t)
+    hi = wmin(ct_ref + h_t, ct_inc + r_t)
+    mid = 0.5 * (lo + hi)
+    oxx, oxy = onx * xn + tx * mid, ony * xn + ty * mid
+    far = s > reach
+    disjoint = (~far) & (s > 0)
+    s_out = torch.where(disjoint, best, s)
+    nx = torch.where(far, zero, torch.where(disjoint, bnx, onx))
+    ny = torch.where(far, zero, torch.where(disjoint, bny, ony))
+    px = torch.where(far, cax, torch.where(disjoint, bxx, oxx))
+    py = torch.where(far, cay, torch.where(disjoint, bxy, oxy))
+    return s_out, nx, ny, px, py
+
+
+def obb_force(cax, cay, tha, hax, hay, vax, vay, wa, cbx, cby, thb, hbx, hby, vbx, vby, wb, reach,
+              k, c, denom, max_overlap):
+    """``swarp/core/collisions.py:447-486``: force on box A from box B (and the point)."""
+    s, nx, ny, xx, xy = obb_contact(cax, cay, tha, hax, hay, cbx, cby, thb, hbx, hby, reach)
+    ov = reach - s
+    rax, ray = xx - cax, xy - cay
+    rbx, rby = xx - cbx, xy - cby
+    rvx = (vax + (-wa * ray)) - (vbx + (-wb * rby))
+    rvy = (vay + wa * rax) - (vby + wb * rbx)
+    cf = normal_coeff(ov, rvx * nx + rvy * ny, k, c, denom, max_overlap)
+    z = torch.zeros_like(s)
+    active = ov > 0
+    return torch.where(active, cf * nx, z), torch.where(active, cf * ny, z)
+
+
+def agent_pair_force(a_lt_b, box_a, box_b, pax, pay, tha, vax, vay, wa, ra, hax, hay,
+                     pbx, pby, thb, vbx, vby, wb, rb, hbx, hby, w: RefWorld, denom):
+    """``swarp/core/collisions.py:490-537``: the force on agent a from agent b for any
+    shapes: disc-disc pair_force; disc-box box_force (negated on the box); box-box
+    obb_force with the lower index as A on both agents, negated on the higher one."""
+    k, c, mo, m = w.k, w.c, w.max_overlap, w.margin
+    dd = pair_force(pax - pbx, pay - pby, vax - vbx, vay - vby, ra + rb + m, k, c, denom, mo)
+    db = box_force(pax, pay, vax, vay, pbx, pby, thb, hbx, hby, ra + m, k, c, denom, mo, vbx, vby, wb)
+    bd = box_force(pbx, pby, vbx, vby, pax, pay, tha, hax, hay, rb + m, k, c, denom, mo, vax, vay, wa)
+    lo = obb_force(pax, pay, tha, hax, hay, vax, vay, wa, pbx, pby, thb, hbx, hby, vbx, vby, wb, m,
+                   k, c, denom, mo)
+    hi = obb_force(pbx, pby, thb, hbx, hby, vbx, vby, wb, pax, pay, tha, hax, hay, vax, vay, wa, m,
+                   k, c, denom, mo)
+    out = []
+    for i in range(2):
+        bb = torch.where(a_lt_b, lo[i], -hi[i])
+        v = torch.where(box_a, torch.where(box_b, bb, -bd[i]), torch.where(box_b, db[i], dd[i]))
+        out.append(v)
+    return out[0], out[1]
+
+
+def box_obstacle_forces(px, py, th, vx, vy, om, hax, hay, obs, w: RefWorld, denom):
+    """``swarp/core/collisions.py:540-630``: obstacles on a box agent: BOX = obb_force with
+    reach = margin; SEGMENT = obb_force against the degenerate box (half_len, 0) with reach
+    = radius + margin; CIRCLE = -box_force with the circle centre as the point."""
+    fx = torch.zeros_like(px)
+    fy = torch.zeros_like(py)
+    if obs is None:
+        return fx, fy
+    k, c, m, mo = w.k, w.c, w.margin, w.max_overlap
+    ra = wlength(hax, hay)
+    for o in range(obs.n):
+        st = int(obs.shape[o])
+        cx, cy = obs.pos[:, o, 0].unsqueeze(1), obs.pos[:, o, 1].unsqueeze(1)
+        ang = obs.angle[:, o].unsqueeze(1)
+        vox, voy = obs.vel[:, o, 0].unsqueeze(1), obs.vel[:, o, 1].unsqueeze(1)
+        omo = obs.ang_vel[:, o].unsqueeze(1)
+        r_o, hx, hy = obs.radius[o], obs.half[o, 0], obs.half[o, 1]
+        apart = bounds_apart(px - cx, py - cy, ra + m + shape_bound(st, r_o, hx, hy))
+        if st == BOX:
+            gx, gy = obb_force(px, py, th, hax, hay, vx, vy, om, cx, cy, ang, hx + 0 * cx,
+                               hy + 0 * cx, vox, voy, omo, m, k, c, denom, mo)
+        elif st == SEGMENT:
+            gx, gy = obb_force(px, py, th, hax, hay, vx, vy, om, cx, cy, ang, hx + 0 * cx, 0 * cx,
+                               vox, voy, omo, r_o + m, k, c, denom, mo)
+        else:
+            gx, gy = box_force(cx, cy, vox, voy, px, py, th, hax, hay, r_o + m, k, c, denom, mo,
+                               vx, vy, om)
+            gx, gy = -gx, -gy
+        z = torch.zeros_like(gx)
+        fx = fx + torch.where(apart, z, gx)
+        fy = fy + torch.where(apart, z, gy)
+    return fx, fy
+
+
+def _sgn0(x):
+    one = torch.ones_like(x)
+    return torch.where(x > 0, one, torch.where(x < 0, -one, torch.zeros_like(x)))
+
+
+def wall_forces_box(px, py, th, vx, vy, om, hax, hay, w: RefWorld, denom):
+    """``swarp/core/collisions.py:646-690``: walls against a box's support extents, damped by
+    the velocity of the touching support vertex."""
+    x0, x1, y0, y1 = w.bounds
+    k, c, m, mo = w.k, w.c, w.margin, w.max_overlap
+    ca, sa = torch.cos(th), torch.sin(th)
+    ex = hax * wabs(ca) + hay * wabs(sa)
+    ey = hax * wabs(sa) + hay * wabs(ca)
+    sc, ss = _sgn0(ca), _sgn0(sa)
+    rl_y = -sc * hax * sa + ss * hay * ca
+    rb_x = -ss * hax * ca + sc * hay * sa
+    z = torch.zeros_like(px)
+    fx, fy = z, z
+    pen = ex + m - (px - x0)
+    fx = fx + torch.where(pen > 0, normal_coeff(pen, vx - om * rl_y, k, c, denom, mo), z)
+    pen = ex + m - (x1 - px)
+    fx = fx + torch.where(pen > 0, -normal_coeff(pen, -(vx + om * rl_y), k, c, denom, mo), z)
+    pen = ey + m - (py - y0)
+    fy = fy + torch.where(pen > 0, normal_coeff(pen, vy + om * rb_x, k, c, denom, mo), z)
+    pen = ey + m - (y1 - py)
+    fy = fy + torch.where(pen > 0, -normal_coeff(pen, -(vy - om * rb_x), k, c, denom, mo), z)
+    return fx, fy
+
+
+def clamp_footprint(npx, npy, nth, w: RefWorld, col):
+    """``swarp/dynamics/kernels.py:80-99``: keep the footprint inside the bounds (a box by
+    its support extents at the new heading, a disc by its radius)."""
+    x0, x1, y0, y1 = w.bounds
+    r = col(P_RADIUS)
+    box = col(P_SHAPE) > 0.5
+    ca, sa = wabs(torch.cos(nth)), wabs(torch.sin(nth))
+    hx, hy = col(P_HALF_X), col(P_HALF_Y)
+    ex = torch.where(box, hx * ca + hy * sa, r)
+    ey = torch.where(box, hx * sa + hy * ca, r)
+    return wclamp(npx, x0 + ex, x1 - ex), wclamp(npy, y0 + ey, y1 - ey)
+
+
 # ------------------------------------------------------------------ neighbor lists
 
 
@@ -324,18 +533,29 @@ def collision_forces(state, w: RefWorld, obs: RefObstacles | None):
     fx = torch.zeros_like(px)
     fy = torch.zeros_like(py)
     true_count = torch.zeros(E, A, dtype=torch.int64, device=px.device)
+    box = w.col(P_SHAPE).expand(E, A) > 0.5
+    any_box = bool(box.any())
+    th, om = state[1], state[4]
+    hax, hay = w.col(P_HALF_X).expand(E, A), w.col(P_HALF_Y).expand(E, A)
     if w.collisions:
         in_list, _, _, true_count = brute_neighbors(pos.detach(), w.neighbor_radius,
                                                     w.max_neighbors)
+        ar = torch.arange(A, device=px.device).unsqueeze(0)
         for b in range(A):
             sel = in_list[:, :, b]
             if not bool(sel.any()):
                 continue
-            gx, gy = pair_force(
-                px - px[:, b : b + 1], py - py[:, b : b + 1],
-                vx - vx[:, b : b + 1], vy - vy[:, b : b + 1],
-                ra + ra[:, b : b + 1] + w.margin, w.k, w.c, denom, w.max_overlap,
-            )
+            sl = slice(b, b + 1)
+            if any_box:
+                gx, gy = agent_pair_force(
+                    ar < b, box, box[:, sl], px, py, th, vx, vy, om, ra, hax, hay,
+                    px[:, sl], py[:, sl], th[:, sl], vx[:, sl], vy[:, sl], om[:, sl], ra[:, sl],
+                    hax[:, sl], hay[:, sl], w, denom)
+            else:
+                gx, gy = pair_force(
+                    px - px[:, sl], py - py[:, sl], vx - vx[:, sl], vy - vy[:, sl],
+                    ra + ra[:, sl] + w.margin, w.k, w.c, denom, w.max_overlap,
+                )
             z = torch.zeros_like(gx)
             fx = fx + torch.where(sel, gx, z)
             fy = fy + torch.where(sel, gy, z)
@@ -343,6 +563,12 @@ def collision_forces(state, w: RefWorld, obs: RefObstacles | None):
     if w.soft_walls:
         wx, wy = wall_forces(px, py, vx, vy, ra, w, denom)
         sx, sy = sx + wx, sy + wy
+    if any_box:  # collisions.py:951-994: box agents take the oriented static forces
+        bx_, by_ = box_obstacle_forces(px, py, th, vx, vy, om, hax, hay, obs, w, denom)
+        if w.soft_walls:
+            wx, wy = wall_forces_box(px, py, th, vx, vy, om, hax, hay, w, denom)
+            bx_, by_ = bx_ + wx, by_ + wy
+        sx, sy = torch.where(box, bx_, sx), torch.where(box, by_, sy)
     return fx + sx, fy + sy, true_count
 
 
@@ -424,10 +650,7 @@ def integrate(state, act, fx, fy, w: RefWorld):
         out.append(v)
     npx, npy, nth, nvx, nvy, ns, nw = out
     if w.clamp_bounds:
-        x0, x1, y0, y1 = w.bounds
-        r = col(P_RADIUS)
-        npx = wclamp(npx, x0 + r, x1 - r)
-        npy = wclamp(npy, y0 + r, y1 - r)
+        npx, npy = clamp_footprint(npx, npy, nth, w, col)
     return (torch.stack([npx, npy], -1), nth, torch.stack([nvx, nvy], -1), ns, nw)
 
 
@@ -516,10 +739,7 @@ def integrate_rk4(state, act, fx, fy, w: RefWorld):
            for i in range(7)]
     npx, npy, nth, nvx, nvy, ns, nw = out
     if w.clamp_bounds:
-        x0, x1, y0, y1 = w.bounds
-        r = col(P_RADIUS)
-        npx = wclamp(npx, x0 + r, x1 - r)
-        npy = wclamp(npy, y0 + r, y1 - r)
+        npx, npy = clamp_footprint(npx, npy, nth, w, col)
     return (torch.stack([npx, npy], -1), nth, torch.stack([nvx, nvy], -1), ns, nw)
 
 
