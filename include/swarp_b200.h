@@ -113,6 +113,8 @@ typedef struct {
   int32_t fleet_modes;       /* host-known bitmask of the ControlMode values in ctrl_mode */
   swarp_obstacles_t obstacles;
   int32_t integrator;        /* 0 semi-implicit Euler, 1 classic RK4 (dynamics/kernels.py:521-793) */
+  int32_t box_agents;        /* host-known: some params row has shape BOX (P_SHAPE = 1); the
+                                oriented-box contacts of swarp/core/collisions.py:262-690 */
 } swarp_world_t;
 
 /* Bytes of device workspace for this world and horizon: the contact checkpoint that

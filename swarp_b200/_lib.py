@@ -65,6 +65,7 @@ class WorldC(C.Structure):
         ("fleet_models", C.c_int32), ("fleet_modes", C.c_int32),
         ("obstacles", ObstaclesC),
         ("integrator", C.c_int32),
+        ("box_agents", C.c_int32),
     ]
 
 

@@ -118,8 +118,6 @@ class Stepper:
         for c in self.configs:
             if c.model == DynamicsModel.DRONE:
                 raise NotImplementedError("the 6-DOF drone model is not on the CUDA path yet")
-            if c.shape == AgentShape.BOX:
-                raise NotImplementedError("box agents (OBB contacts) are not on the CUDA path yet")
         if world.integrator not in (Integrator.EULER, Integrator.RK4):
             raise NotImplementedError(f"integrator {world.integrator} is not on the CUDA path")
         if world.wheel_contacts:
@@ -127,6 +125,7 @@ class Stepper:
         if world.obstacle_friction > 0.0:
             raise NotImplementedError("floor friction of movable bodies (obstacle_friction) is "
                                       "not on the CUDA path")
+        self.box_agents = any(c.shape == AgentShape.BOX for c in self.configs)
         self.params = torch.tensor(param_rows(self.configs), dtype=self.dtype, device=self.device)
         self.params_per_env: torch.Tensor | None = None
         self.model_tag = torch.tensor([int(c.model) for c in self.configs], dtype=torch.int32,
@@ -190,6 +189,9 @@ class Stepper:
         self.n_obstacles = obs.n_obstacles
         moving = obs.kind[obs.body.long()] != 0  # shapes whose body root is movable
         self.any_movable = bool(moving.any().item())
+        if self.any_movable and self.box_agents:
+            raise NotImplementedError("box agents against movable obstacles are not on the CUDA "
+                                      "path")
         self.movable_shapes = 0
         self._poses_from_bodies = False
         if self.any_movable:
@@ -261,6 +263,7 @@ class Stepper:
         wc.max_neighbors = w.max_neighbors
         wc.bounds_mode = 1 if self._soft_walls else (2 if self._clamp else 0)
         wc.integrator = 1 if w.integrator == Integrator.RK4 else 0
+        wc.box_agents = int(self.box_agents)
         b = w.bounds if w.bounds is not None else (0.0, 0.0, 0.0, 0.0)
         wc.bounds = (C.c_double * 4)(*b)
         wc.lin_damping = w.obstacle_linear_damping

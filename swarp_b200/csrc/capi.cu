@@ -15,7 +15,7 @@ using namespace swarp;
 
 namespace {
 
-constexpr int kAbiVersion = 4;
+constexpr int kAbiVersion = 5;
 
 int threads_target() {
   static int v = [] {
@@ -41,7 +41,7 @@ bool aligned(const void* p, unsigned n) { return (reinterpret_cast<uintptr_t>(p)
 // fields; the adjoint also one substep per step).
 bool x2_ok(const RolloutArgs<float>& R, int fl, bool bwd) {
   if (!x2_enabled() || R.A != 16 || R.act_dim != 2) return false;
-  if (!(fl & F_MASK) || (fl & (F_BODIES | F_TRUNC))) return false;
+  if (!(fl & F_MASK) || (fl & (F_BODIES | F_TRUNC | F_BOXES))) return false;
   if (bwd && R.S != 1) return false;
   const void* v16[] = {R.t_pos, R.t_vel, R.i_pos, R.i_vel, R.act, R.f_pos, R.f_vel, R.g_act};
   for (const void* p : v16)
@@ -86,6 +86,7 @@ int validate_world(const swarp_world_t* w, int horizon) {
   if (w->fleet_models == 0 || w->fleet_modes == 0 || (w->fleet_modes & ~0x7)) return SWARP_ERR_INVALID_ARG;
   if (w->bounds_mode < 0 || w->bounds_mode > 2) return SWARP_ERR_INVALID_ARG;
   if (w->integrator < 0 || w->integrator > 1) return SWARP_ERR_INVALID_ARG;
+  if (w->box_agents < 0 || w->box_agents > 1) return SWARP_ERR_INVALID_ARG;
   if (w->collisions) {
     if (w->max_neighbors < 1 || !(w->neighbor_radius > 0.0)) return SWARP_ERR_INVALID_ARG;
     if (w->n_agents > 32767) return SWARP_ERR_TOO_MANY_AGENTS;
@@ -119,6 +120,7 @@ int flags_of(const swarp_world_t* w) {
     if (w->obstacles.any_movable && w->obstacles.bodies_move) fl |= F_BODIES;
   }
   if (w->integrator == 1) fl |= F_RK4;
+  if (w->box_agents) fl |= F_BOXES;
   if (w->fleet_models == 1 && w->fleet_modes == 1) fl |= F_HOLOVEL;
   return fl;
 }
@@ -307,6 +309,8 @@ int swarp_rollout_fwd(const swarp_world_t* w, int32_t horizon, swarp_state_t ini
   if (!state_complete(init) || !state_complete(traj) || !actions) return SWARP_ERR_INVALID_ARG;
   if ((flags_of(w) & F_BODIES) && (!bodies_complete(bodies_init) || !bodies_complete(bodies_traj)))
     return SWARP_ERR_INVALID_ARG;
+  // box agents against moving bodies: not built
+  if ((flags_of(w) & F_BOXES) && (flags_of(w) & F_BODIES)) return SWARP_ERR_UNSUPPORTED;
   const bool any_fin = final_out.pos || final_out.theta || final_out.vel || final_out.speed || final_out.ang_vel;
   if (any_fin && !state_complete(final_out)) return SWARP_ERR_INVALID_ARG;
   const size_t need = swarp_rollout_workspace_bytes(w, horizon);
@@ -327,6 +331,7 @@ int swarp_rollout_bwd(const swarp_world_t* w, int32_t horizon, swarp_state_t ini
                       void* workspace, size_t workspace_bytes, void* stream) {
   int rc = validate_world(w, horizon);
   if (rc != SWARP_OK) return rc;
+  if (flags_of(w) & F_BOXES) return SWARP_ERR_UNSUPPORTED;  // box-agent adjoint: not built
   if (flags_of(w) & F_BODIES) {
     if (!bodies_complete(bodies_init) || !bodies_complete(bodies_traj)) return SWARP_ERR_INVALID_ARG;
     if (w->obstacles.movable_shapes & ~(1 << SHAPE_CIRCLE)) return SWARP_ERR_UNSUPPORTED;

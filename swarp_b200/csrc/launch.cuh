@@ -17,7 +17,8 @@ constexpr int kErrUnsupported = -2;
 constexpr int kErrCuda = -4;
 
 // The instances are split by integrator (RB = 0: Euler cases, RB = F_RK4: the same cases
-// with RK4) so that each half compiles in a translation unit of its own (k_*.cu).
+// with RK4) and, for the forward, by whether box agents are present (RB | F_BOXES) so that
+// each part compiles in a translation unit of its own (k_*.cu).
 template <typename T, int RB> int launch_fwd_part(const RolloutArgs<T>& R, int fl, cudaStream_t st);
 template <typename T, int RB> int launch_bwd_part(const RolloutArgs<T>& R, int fl, cudaStream_t st);
 // Two agents per thread (float, A == 16, contact masks, no moving bodies; rollout_x2.cuh).
@@ -26,6 +27,9 @@ int launch_fwd_x2(const RolloutArgs<float>& R, int fl, cudaStream_t st);
 int launch_bwd_x2(const RolloutArgs<float>& R, int fl, cudaStream_t st);
 
 template <typename T> inline int launch_fwd(const RolloutArgs<T>& R, int fl, cudaStream_t st) {
+  if (fl & F_BOXES)
+    return (fl & F_RK4) ? launch_fwd_part<T, F_BOXES | F_RK4>(R, fl, st)
+                        : launch_fwd_part<T, F_BOXES>(R, fl, st);
   return (fl & F_RK4) ? launch_fwd_part<T, F_RK4>(R, fl, st) : launch_fwd_part<T, 0>(R, fl, st);
 }
 template <typename T> inline int launch_bwd(const RolloutArgs<T>& R, int fl, cudaStream_t st) {
@@ -72,7 +76,8 @@ inline int launch_kernel(K kernel, int grid, int block, size_t smem, cudaStream_
 
 template <typename T, int FL, int AS>
 int run_fwd(const RolloutArgs<T>& R, cudaStream_t st) {
-  const Layout<T> L(R.G, R.A, R.N, R.S, false, (FL & F_BODIES) != 0);
+  const Layout<T> L(R.G, R.A, R.N, R.S, false, (FL & F_BODIES) != 0,
+                    (FL & F_BOXES) != 0 && (FL & F_COLL) != 0);
   return launch_kernel(rollout_fwd_kernel<T, FL, AS>, (R.E + R.G - 1) / R.G, R.G * R.A, L.total,
                        st, &R);
 }
@@ -95,17 +100,24 @@ int run_bwd(const RolloutArgs<T>& R, cudaStream_t st) {
   X(R + 53) X(R + 44) X(R + 45) X(R + 47) X(R + 61)
 // (each instantiated once with R = 0 and once with R = F_RK4)
 
+// Box-agent worlds: the cases without moving bodies (R = F_BOXES, F_BOXES | F_RK4).
+#define SWARP_FLAG_CASES_BOXES(X, R)                                                           \
+  X(R + 0) X(R + 4) X(R + 8) X(R + 12) X(R + 1) X(R + 5) X(R + 9) X(R + 13) X(R + 3) X(R + 7) \
+  X(R + 11) X(R + 15) X(R + 17) X(R + 21) X(R + 25) X(R + 29)
+
 template <typename T, int RB> int launch_fwd_part(const RolloutArgs<T>& R, int fl, cudaStream_t st) {
   const bool a16 = std::is_same<T, float>::value && R.A == 16;
-  switch (fl) {
 #define SWARP_X(F)                                                          \
   case F:                                                                   \
     if constexpr (std::is_same<T, float>::value && ((F) & F_COLL))          \
       if (a16) return run_fwd<T, F, 16>(R, st);                             \
     return run_fwd<T, F, 0>(R, st);
-    SWARP_FLAG_CASES_EULER(SWARP_X, RB)
-#undef SWARP_X
+  if constexpr ((RB & F_BOXES) != 0) {
+    switch (fl) { SWARP_FLAG_CASES_BOXES(SWARP_X, RB) }
+  } else {
+    switch (fl) { SWARP_FLAG_CASES_EULER(SWARP_X, RB) }
   }
+#undef SWARP_X
   return kErrUnsupported;
 }
 

@@ -77,6 +77,8 @@ template <typename T> struct AgentP {
   T dt_over_m;  // sub_dt / mass  (the reference's force * (dt / mass))
   T inv_denom;  // 1 / (1 + c * sub_dt / mass): implicit damping denominator, inverted once
   int tag, mode;
+  int box;     // shape BOX (else disc)
+  T hx, hy;    // box half extents
 };
 
 // World constants of one launch.
@@ -253,7 +255,7 @@ __device__ __forceinline__ bool bounds_apart(T dx, T dy, T reach) {
 
 // Box SDF contact (collisions.py:174-260): force on an agent at p with velocity v.
 template <typename T>
-__device__ __forceinline__ void box_force(T px, T py, T vx, T vy, const Obs<T>& o, T reach, T inv_denom,
+__device__ __forceinline__ bool box_force(T px, T py, T vx, T vy, const Obs<T>& o, T reach, T inv_denom,
                                           const WorldC<T>& W, T& fx, T& fy) {
   fx = T(0);
   fy = T(0);
@@ -291,7 +293,9 @@ __device__ __forceinline__ void box_force(T px, T py, T vx, T vy, const Obs<T>& 
     T cf = normal_coeff(overlap, vn, inv_denom, W);
     fx = cf * nx;
     fy = cf * ny;
+    return true;
   }
+  return false;
 }
 
 template <typename T>
@@ -577,7 +581,21 @@ __device__ __forceinline__ void servo_cmd_vjp(T a0, T a1, T s, T w, const AgentP
 // One semi-implicit Euler substep of a 2-D agent under force (fx, fy).
 // p_new = p + v_new * dt is an explicit fma in both directions, so the adjoint
 // reconstructs the pre-clamp position bit for bit from the stored output velocity.
-template <typename T>
+// Hard clamp of the new position (dynamics/kernels.py:80-99, clamp_footprint): a disc is
+// inset by its radius, a box (kBox worlds) by its support extents at the new heading.
+template <typename T, bool kBox>
+__device__ __forceinline__ void clamp_footprint(Agent<T>& out, const AgentP<T>& P, const WorldC<T>& W) {
+  T ex = P.radius, ey = P.radius;
+  if (kBox && P.box) {
+    const T ca = fabs(Num<T>::cos_(out.th)), sa = fabs(Num<T>::sin_(out.th));
+    ex = P.hx * ca + P.hy * sa;
+    ey = P.hx * sa + P.hy * ca;
+  }
+  out.px = wclamp(out.px, W.bx0 + ex, W.bx1 - ex);
+  out.py = wclamp(out.py, W.by0 + ey, W.by1 - ey);
+}
+
+template <typename T, bool kBox = false>
 __device__ __forceinline__ void integrate_fwd(const Agent<T>& in, T a0, T a1, T fx, T fy,
                                               const AgentP<T>& P, const WorldC<T>& W, Agent<T>& out) {
   const T dt = W.dt;
@@ -643,10 +661,7 @@ __device__ __forceinline__ void integrate_fwd(const Agent<T>& in, T a0, T a1, T 
     out.s = sn;
     out.w = wn;
   }
-  if (W.bounds_mode == BOUNDS_CLAMP) {
-    out.px = wclamp(out.px, W.bx0 + P.radius, W.bx1 - P.radius);
-    out.py = wclamp(out.py, W.by0 + P.radius, W.by1 - P.radius);
-  }
+  if (W.bounds_mode == BOUNDS_CLAMP) clamp_footprint<T, kBox>(out, P, W);
 }
 
 // Adjoint of integrate_fwd. `out` is the substep's stored output (only its velocity
@@ -903,7 +918,7 @@ __device__ __forceinline__ void rk4_stages(const Agent<T>& in, T a0, T a1, const
                   comb(R.x.w, R.k1.w, R.k2.w, R.k3.w, R.k4.w)};
 }
 
-template <typename T>
+template <typename T, bool kBox = false>
 __device__ __forceinline__ void integrate_rk4_fwd(const Agent<T>& in, T a0, T a1, T fx, T fy,
                                                   const AgentP<T>& P, const WorldC<T>& W,
                                                   Agent<T>& out) {
@@ -940,10 +955,7 @@ __device__ __forceinline__ void integrate_rk4_fwd(const Agent<T>& in, T a0, T a1
     out.vy = so * Num<T>::sin_(xi.th + q.beta) + dvy;
     out.s = so;
   }
-  if (W.bounds_mode == BOUNDS_CLAMP) {
-    out.px = wclamp(out.px, W.bx0 + P.radius, W.bx1 - P.radius);
-    out.py = wclamp(out.py, W.by0 + P.radius, W.by1 - P.radius);
-  }
+  if (W.bounds_mode == BOUNDS_CLAMP) clamp_footprint<T, kBox>(out, P, W);
 }
 
 // Adjoint of integrate_rk4_fwd (same contract as integrate_vjp: gin overwritten, force

@@ -21,6 +21,7 @@
 // rescans, and with truncation the forward stores each list's cutoff index instead.
 #pragma once
 #include "bodies.cuh"
+#include "boxes.cuh"
 #include "physics.cuh"
 
 namespace swarp {
@@ -41,6 +42,7 @@ enum : int {
   F_MASK = 16,    // contact masks checkpointed (A <= 32, no truncation)
   F_BODIES = 32,  // movable bodies integrated in the substep loop (with F_OBS)
   F_RK4 = 64,     // classic RK4 integrator instead of semi-implicit Euler
+  F_BOXES = 128,  // some agents are oriented boxes (boxes.cuh)
 };
 
 // Largest CTA the 16-agent specializations are launched with (host: envs_per_cta).
@@ -87,8 +89,10 @@ template <typename T> struct RolloutArgs {
 // Shared-memory carve-up, identical on host (sizes) and device (pointers).
 template <typename T> struct Layout {
   int G, A, NP, nbuf, S;
-  size_t xy, rec, own, fb, cut, rad, iden, obs, bc, bst, gpose, gag, gbody, gbnew, gshape, total;
-  __host__ __device__ Layout(int G_, int A_, int N, int S_, bool bwd, bool bodies = false)
+  size_t xy, rec, own, fb, cut, rad, iden, obs, bc, bst, gpose, gag, gbody, gbnew, gshape, thw, shp,
+      total;
+  __host__ __device__ Layout(int G_, int A_, int N, int S_, bool bwd, bool bodies = false,
+                             bool boxes = false)
       : G(G_), A(A_), S(S_) {
     NP = (A + 1) / 2;
     nbuf = bwd ? (S > 2 ? S : 2) : 2;
@@ -111,6 +115,9 @@ template <typename T> struct Layout {
     gbody = bwd ? take(size_t(G) * NB * sizeof(BodyG<T>)) : 0;
     gbnew = bwd ? take(size_t(G) * NB * sizeof(BodyG<T>)) : 0;
     gshape = bwd ? take(size_t(G) * NB * 4 * sizeof(T)) : 0;
+    // box worlds: every agent's (heading, turn rate) per buffer and (box, hx, hy) once
+    thw = boxes ? take(size_t(nbuf) * GA * 2 * sizeof(T)) : 0;
+    shp = boxes ? take(size_t(GA) * 4 * sizeof(T)) : 0;
     total = off;
   }
 };
@@ -135,6 +142,9 @@ __device__ __forceinline__ void load_params(const RolloutArgs<T>& R, int e, int 
   P.mode = R.ctrl_mode[a];
   P.dt_over_m = R.W.dt / P.mass;
   P.inv_denom = T(1) / (T(1) + R.W.c * R.W.dt / P.mass);
+  P.box = row[17] > T(0.5);
+  P.hx = row[18];
+  P.hy = row[19];
 }
 
 template <typename T>
@@ -439,6 +449,45 @@ __device__ __forceinline__ int neighbor_force(const T* xy_env, const typename V4
   return total;
 }
 
+// Box worlds: the agent's pose as an oriented box (heading th, turn rate w).
+template <typename T>
+__device__ __forceinline__ Ob<T> ob_of(T px, T py, T th, T vx, T vy, T w, T hx, T hy) {
+  return Ob<T>{px, py, Num<T>::cos_(th), Num<T>::sin_(th), hx, hy, vx, vy, w};
+}
+
+// neighbor_force for worlds with box agents: the same capped list, each pair through the
+// shape dispatch (disc-disc, disc-box, box-box). thw_env holds every agent's (th, w) of
+// the substep, shp_env its (box, hx, hy).
+template <typename T, int FL, int AS>
+__device__ __forceinline__ int neighbor_force_box(const T* xy_env, const typename V4<T>::t* rec_env,
+                                                  const typename V2<T>::t* thw_env,
+                                                  const typename V4<T>::t* shp_env,
+                                                  const T* rad_env, int A, int a, const Agent<T>& x,
+                                                  const AgentP<T>& P, const WorldC<T>& W, T& fx,
+                                                  T& fy, int& cutoff, unsigned& cmask) {
+  int listed = 0;
+  cutoff = A;
+  cmask = 0u;
+  const Ob<T> oa = ob_of(x.px, x.py, x.th, x.vx, x.vy, x.w, P.hx, P.hy);
+  const bool box_a = P.box != 0;
+  const int total = for_each_in_radius<T, AS>(xy_env, rec_env, A, a, x.px, x.py, W.r2_thr,
+                                              [&](int b, const typename V4<T>::t& q) {
+    if (FL & F_TRUNC) {
+      if (listed >= W.K) return;
+      ++listed;
+      if (listed == W.K) cutoff = b;
+    }
+    const auto tw = thw_env[b];
+    const auto sh = shp_env[b];
+    const Ob<T> ob = ob_of(q.x, q.y, tw.x, q.z, q.w, tw.y, sh.y, sh.z);
+    if (pair_force_shaped(a, b, box_a, oa, P.radius, sh.x > T(0.5), ob, rad_env[b], P.inv_denom,
+                          W, fx, fy))
+      cmask |= 1u << (b & 31);
+  });
+  if ((FL & F_TRUNC) && total <= W.K) cutoff = A;
+  return total;
+}
+
 // Contact force from a checkpointed contact mask (ascending b, the forward's order).
 template <typename T>
 __device__ __forceinline__ void mask_force(const typename V4<T>::t* rec_env, const T* rad_env,
@@ -457,6 +506,12 @@ __device__ __forceinline__ void mask_force(const typename V4<T>::t* rec_env, con
 template <typename T, int FL>
 __device__ __forceinline__ void static_force(const Obs<T>* sobs, int N, const Agent<T>& x,
                                              const AgentP<T>& P, const WorldC<T>& W, T& fx, T& fy) {
+  if ((FL & F_BOXES) && P.box) {  // collisions.py:951-994: the oriented static forces
+    box_static_force((FL & F_OBS) ? sobs : nullptr, (FL & F_OBS) ? N : 0,
+                     W.bounds_mode == BOUNDS_SOFT,
+                     ob_of(x.px, x.py, x.th, x.vx, x.vy, x.w, P.hx, P.hy), P.inv_denom, W, fx, fy);
+    return;
+  }
   T sx = T(0), sy = T(0);
   if (FL & F_OBS) {
     for (int o = 0; o < N; ++o) {
@@ -484,10 +539,11 @@ __device__ __forceinline__ void integrate_sel(const Agent<T>& in, T a0, T a1, T 
     Q.tag = TAG_HOLONOMIC;
     Q.mode = MODE_VELOCITY;
   }
+  constexpr bool kBox = (FL & F_BOXES) != 0;
   if (FL & F_RK4)
-    integrate_rk4_fwd(in, a0, a1, fx, fy, Q, W, out);
+    integrate_rk4_fwd<T, kBox>(in, a0, a1, fx, fy, Q, W, out);
   else
-    integrate_fwd(in, a0, a1, fx, fy, Q, W, out);
+    integrate_fwd<T, kBox>(in, a0, a1, fx, fy, Q, W, out);
 }
 
 template <typename T, int FL>
@@ -523,6 +579,8 @@ __global__ void __launch_bounds__(1024) rollout_fwd_kernel(const RolloutArgs<T> 
   using T4 = typename V4<T>::t;
   constexpr bool kBodies = (FL & F_BODIES) != 0;
   constexpr bool kShare = (FL & (F_COLL | F_BODIES)) != 0;  // agent records in smem each substep
+  constexpr bool kBoxes = (FL & F_BOXES) != 0 && (FL & F_COLL) != 0;  // shapes meet in pairs
+  using T2 = typename V2<T>::t;
   extern __shared__ __align__(16) unsigned char smem[];
   const int A = AS > 0 ? AS : R.A;
   const int G = R.G, GA = G * A, N = R.N;
@@ -532,8 +590,10 @@ __global__ void __launch_bounds__(1024) rollout_fwd_kernel(const RolloutArgs<T> 
   const int e = e0 + le;
   const bool valid = e < R.E;
   const int ec = valid ? e : R.E - 1;
-  const Layout<T> L(G, A, N, R.S, false, kBodies);
+  const Layout<T> L(G, A, N, R.S, false, kBodies, kBoxes);
   const int NP4 = L.NP * 4;
+  T2* sthw = reinterpret_cast<T2*>(smem + L.thw);  // [2][G*A] (th, w), box worlds
+  T4* sshp = reinterpret_cast<T4*>(smem + L.shp);  // [G*A] (box, hx, hy, -)
   T* sxy = reinterpret_cast<T*>(smem + L.xy);
   T4* srec = reinterpret_cast<T4*>(smem + L.rec);
   T* srad = reinterpret_cast<T*>(smem + L.rad);
@@ -547,6 +607,7 @@ __global__ void __launch_bounds__(1024) rollout_fwd_kernel(const RolloutArgs<T> 
   const WorldC<T> W = R.W;
   srad[tid] = P.radius;
   siden[tid] = P.inv_denom;
+  if (kBoxes) sshp[tid] = T4{P.box ? T(1) : T(0), P.hx, P.hy, T(0)};
   if (FL & F_OBS) load_obstacles(R, sobs, e0);
   if (FL & F_COLL) init_pads(sxy, 2, G, A);
   if (kBodies) {
@@ -558,6 +619,8 @@ __global__ void __launch_bounds__(1024) rollout_fwd_kernel(const RolloutArgs<T> 
     set_body_poses(R, ec, false, sbst + le * N, sbc, sobs + le * N);
   __syncthreads();
 
+  const T2* thw_env0 = sthw + le * A;
+  const T4* shp_env = sshp + le * A;
   const long long ia = (long long)ec * A + a;
   const long long EA = (long long)R.E * A;
   Agent<T> x;
@@ -581,13 +644,19 @@ __global__ void __launch_bounds__(1024) rollout_fwd_kernel(const RolloutArgs<T> 
       if (kShare) {
         if (FL & F_COLL) put_xy(xy_env, a, x.px, x.py);
         rec_env[a] = T4{x.px, x.py, x.vx, x.vy};
+        if (kBoxes) sthw[buf * GA + le * A + a] = T2{x.th, x.w};
         __syncthreads();
       }
       if (FL & F_COLL) {
         int cutoff;
         unsigned cm;
-        const int tc = neighbor_force<T, FL, AS>(xy_env, rec_env, rad_env, A, a, x, P, W, fx, fy,
-                                                 cutoff, cm);
+        int tc;
+        if (kBoxes)
+          tc = neighbor_force_box<T, FL, AS>(xy_env, rec_env, thw_env0 + buf * GA, shp_env, rad_env,
+                                             A, a, x, P, W, fx, fy, cutoff, cm);
+        else
+          tc = neighbor_force<T, FL, AS>(xy_env, rec_env, rad_env, A, a, x, P, W, fx, fy, cutoff,
+                                         cm);
         tmax = max(tmax, tc);
         const long long ws = ((long long)t * R.S + k) * EA + ia;
         if ((FL & F_TRUNC) && valid) R.cutoff[ws] = (int16_t)cutoff;

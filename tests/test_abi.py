@@ -42,7 +42,7 @@ def test_error_strings_and_version(lib):
     lib.swarp_error_string.restype = C.c_char_p
     assert lib.swarp_error_string(0) == b"ok"
     assert b"unsupported" in lib.swarp_error_string(-2)
-    assert lib.swarp_abi_version() == 4
+    assert lib.swarp_abi_version() == 5
 
 
 def test_invalid_world_is_rejected_without_a_gpu(lib):
@@ -87,6 +87,7 @@ int main(void) {
   F(swarp_world_t, obstacles); F(swarp_obstacles_t, pos); F(swarp_obstacles_t, any_movable);
   F(swarp_obstacles_t, bodies_move); F(swarp_obstacles_t, movable_shapes);
   F(swarp_obstacles_t, poses_from_bodies); F(swarp_world_t, integrator);
+  F(swarp_world_t, box_agents);
   return 0;
 }
 """
