@@ -59,12 +59,17 @@ def wmin(a, b):
 
 
 def wclamp(x, lo, hi):
-    """Warp ``clamp``: value ``min(max(lo, x), hi)``; gradient to ``x`` iff lo <= x <= hi."""
+    """Warp ``clamp``: value ``min(max(lo, x), hi)``; Warp's adjoint routes the gradient to
+    ``lo`` where x < lo, to ``hi`` where x > hi and to ``x`` otherwise (the bounds carry a
+    gradient only where they depend on the state, e.g. a box's support extents at its
+    heading in the footprint clamp). The routing terms are exact zeros in value."""
     x_t = torch.as_tensor(x)
     lo = torch.as_tensor(lo, dtype=x_t.dtype, device=x_t.device)
     hi = torch.as_tensor(hi, dtype=x_t.dtype, device=x_t.device)
     val = torch.minimum(torch.maximum(lo, x_t), hi).detach()
-    return torch.where((x_t >= lo) & (x_t <= hi), x_t, val)
+    route = torch.where(x_t < lo, lo - lo.detach(),
+                        torch.where(x_t > hi, hi - hi.detach(), x_t - x_t.detach()))
+    return val + route
 
 
 def wabs(x):

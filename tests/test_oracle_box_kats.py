@@ -206,3 +206,20 @@ def test_gradcheck_through_box_contacts():
     out = R.step(tuple(s), acts, w)[0]
     (gth,) = torch.autograd.grad(out[0][0, 0].sum(), [s[1]])
     assert gth[0, 1].abs() > 1e-6
+
+
+def test_gradcheck_through_the_footprint_clamp():
+    """A box pinned against a wall by the footprint clamp: its position follows the
+    support extent at the new heading, so the clamped coordinate carries a gradient into
+    the heading (Warp's clamp adjoint routes it to the bound)."""
+    cfgs = [box(0.2, 0.1, model=DynamicsModel.DIFF_DRIVE, max_ang_vel=BIG, max_accel=BIG)]
+    w = world(cfgs, bounds=(-1.0, 1.0, -1.0, 1.0), mode="clamp")
+    s = [x.clone().requires_grad_(True) for x in state([[-0.95, 0.97]], [0.9], [[-0.5, 0.3]], [1.0])]
+    acts = torch.tensor([[[0.3, 0.8]]], dtype=D, requires_grad=True)
+    out = R.step(tuple(s), acts, w)[0]
+    ex, ey = _extents(0.2, 0.1, float(out[1][0, 0]))
+    close(out[0][0, 0].detach(), [-1.0 + ex, 1.0 - ey], atol=1e-12)  # both coordinates clamped
+    assert torch.autograd.gradcheck(lambda *x: R.step(tuple(x[:5]), x[5], w)[0], (*s, acts),
+                                    eps=1e-6, atol=1e-5)
+    (gth,) = torch.autograd.grad(out[0][0, 0, 0], [s[1]])
+    assert gth.abs().max() > 0.05
