@@ -331,7 +331,7 @@ int swarp_rollout_bwd(const swarp_world_t* w, int32_t horizon, swarp_state_t ini
                       void* workspace, size_t workspace_bytes, void* stream) {
   int rc = validate_world(w, horizon);
   if (rc != SWARP_OK) return rc;
-  if (flags_of(w) & F_BOXES) return SWARP_ERR_UNSUPPORTED;  // box-agent adjoint: not built
+  if ((flags_of(w) & F_BOXES) && (flags_of(w) & F_BODIES)) return SWARP_ERR_UNSUPPORTED;
   if (flags_of(w) & F_BODIES) {
     if (!bodies_complete(bodies_init) || !bodies_complete(bodies_traj)) return SWARP_ERR_INVALID_ARG;
     if (w->obstacles.movable_shapes & ~(1 << SHAPE_CIRCLE)) return SWARP_ERR_UNSUPPORTED;

@@ -33,6 +33,9 @@ template <typename T> inline int launch_fwd(const RolloutArgs<T>& R, int fl, cud
   return (fl & F_RK4) ? launch_fwd_part<T, F_RK4>(R, fl, st) : launch_fwd_part<T, 0>(R, fl, st);
 }
 template <typename T> inline int launch_bwd(const RolloutArgs<T>& R, int fl, cudaStream_t st) {
+  if (fl & F_BOXES)
+    return (fl & F_RK4) ? launch_bwd_part<T, F_BOXES | F_RK4>(R, fl, st)
+                        : launch_bwd_part<T, F_BOXES>(R, fl, st);
   return (fl & F_RK4) ? launch_bwd_part<T, F_RK4>(R, fl, st) : launch_bwd_part<T, 0>(R, fl, st);
 }
 template <typename T>
@@ -83,7 +86,8 @@ int run_fwd(const RolloutArgs<T>& R, cudaStream_t st) {
 }
 template <typename T, int FL, int AS>
 int run_bwd(const RolloutArgs<T>& R, cudaStream_t st) {
-  const Layout<T> L(R.G, R.A, R.N, R.S, true, (FL & F_BODIES) != 0);
+  const Layout<T> L(R.G, R.A, R.N, R.S, true, (FL & F_BODIES) != 0,
+                    (FL & F_BOXES) != 0 && (FL & F_COLL) != 0);
   const int grid = (R.E + R.G - 1) / R.G;
   const int rc = launch_kernel(rollout_bwd_kernel<T, FL, AS>, grid, R.G * R.A, L.total, st, &R);
   if (rc != 0 || !R.gsq_partial) return rc;
@@ -123,15 +127,17 @@ template <typename T, int RB> int launch_fwd_part(const RolloutArgs<T>& R, int f
 
 template <typename T, int RB> int launch_bwd_part(const RolloutArgs<T>& R, int fl, cudaStream_t st) {
   const bool a16 = std::is_same<T, float>::value && R.A == 16;
-  switch (fl) {
 #define SWARP_X(F)                                                          \
   case F:                                                                   \
     if constexpr (std::is_same<T, float>::value && ((F) & F_COLL))          \
       if (a16) return run_bwd<T, F, 16>(R, st);                             \
     return run_bwd<T, F, 0>(R, st);
-    SWARP_FLAG_CASES_EULER(SWARP_X, RB)
-#undef SWARP_X
+  if constexpr ((RB & F_BOXES) != 0) {
+    switch (fl) { SWARP_FLAG_CASES_BOXES(SWARP_X, RB) }
+  } else {
+    switch (fl) { SWARP_FLAG_CASES_EULER(SWARP_X, RB) }
   }
+#undef SWARP_X
   return kErrUnsupported;
 }
 

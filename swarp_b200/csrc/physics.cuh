@@ -584,15 +584,40 @@ __device__ __forceinline__ void servo_cmd_vjp(T a0, T a1, T s, T w, const AgentP
 // Hard clamp of the new position (dynamics/kernels.py:80-99, clamp_footprint): a disc is
 // inset by its radius, a box (kBox worlds) by its support extents at the new heading.
 template <typename T, bool kBox>
+__device__ __forceinline__ void footprint_extents(T th, const AgentP<T>& P, T& ex, T& ey);
+template <typename T, bool kBox>
 __device__ __forceinline__ void clamp_footprint(Agent<T>& out, const AgentP<T>& P, const WorldC<T>& W) {
-  T ex = P.radius, ey = P.radius;
+  T ex, ey;
+  footprint_extents<T, kBox>(out.th, P, ex, ey);
+  out.px = wclamp(out.px, W.bx0 + ex, W.bx1 - ex);
+  out.py = wclamp(out.py, W.by0 + ey, W.by1 - ey);
+}
+
+// Adjoint of the box footprint clamp beyond the position gate: Warp's clamp adjoint sends
+// a clamped coordinate's gradient to its active bound (lo = b0 + e, hi = b1 - e), and the
+// support extents e = hx|cos| + hy|sin| (x), hx|sin| + hy|cos| (y) carry it into the new
+// heading th (abs with slope +1 at zero).
+template <typename T>
+__device__ __forceinline__ void box_clamp_vjp(int sidex, int sidey, T th, const AgentP<T>& P, T gpx,
+                                              T gpy, T& gth) {
+  const T gex = sidex < 0 ? gpx : (sidex > 0 ? -gpx : T(0));
+  const T gey = sidey < 0 ? gpy : (sidey > 0 ? -gpy : T(0));
+  const T c = Num<T>::cos_(th), s = Num<T>::sin_(th);
+  const T sc = c < T(0) ? T(-1) : T(1), ss = s < T(0) ? T(-1) : T(1);
+  const T dex = P.hx * (sc * -s) + P.hy * (ss * c);
+  const T dey = P.hx * (ss * c) + P.hy * (sc * -s);
+  gth += gex * dex + gey * dey;
+}
+// Support extents of the footprint at heading th (a disc: its radius).
+template <typename T, bool kBox>
+__device__ __forceinline__ void footprint_extents(T th, const AgentP<T>& P, T& ex, T& ey) {
+  ex = P.radius;
+  ey = P.radius;
   if (kBox && P.box) {
-    const T ca = fabs(Num<T>::cos_(out.th)), sa = fabs(Num<T>::sin_(out.th));
+    const T ca = fabs(Num<T>::cos_(th)), sa = fabs(Num<T>::sin_(th));
     ex = P.hx * ca + P.hy * sa;
     ey = P.hx * sa + P.hy * ca;
   }
-  out.px = wclamp(out.px, W.bx0 + ex, W.bx1 - ex);
-  out.py = wclamp(out.py, W.by0 + ey, W.by1 - ey);
 }
 
 template <typename T, bool kBox = false>
@@ -668,19 +693,26 @@ __device__ __forceinline__ void integrate_fwd(const Agent<T>& in, T a0, T a1, T 
 // and speed are read). Writes the gradients that flow straight to the substep input
 // into gin (overwriting), the force cotangent into (gfx, gfy) and adds the action
 // cotangent into (ga0, ga1).
-template <typename T>
+template <typename T, bool kBox = false>
 __device__ __forceinline__ void integrate_vjp(const Agent<T>& in, T a0, T a1, const Agent<T>& out,
-                                              const Agent<T>& g, const AgentP<T>& P,
+                                              const Agent<T>& g_out, const AgentP<T>& P,
                                               const WorldC<T>& W, Agent<T>& gin, T& gfx, T& gfy,
                                               T& ga0, T& ga1) {
   const T dt = W.dt;
+  Agent<T> g = g_out;
   gin.px = gin.py = gin.th = gin.vx = gin.vy = gin.s = gin.w = T(0);
   // bounds clamp on the new position
   T gpx = g.px, gpy = g.py;
   if (W.bounds_mode == BOUNDS_CLAMP) {
     T pxn = Num<T>::fma_(out.vx, dt, in.px), pyn = Num<T>::fma_(out.vy, dt, in.py);
-    if (!clamp_pass(pxn, W.bx0 + P.radius, W.bx1 - P.radius)) gpx = T(0);
-    if (!clamp_pass(pyn, W.by0 + P.radius, W.by1 - P.radius)) gpy = T(0);
+    T ex, ey;
+    footprint_extents<T, kBox>(out.th, P, ex, ey);
+    const T lox = W.bx0 + ex, hix = W.bx1 - ex, loy = W.by0 + ey, hiy = W.by1 - ey;
+    if (!clamp_pass(pxn, lox, hix)) gpx = T(0);
+    if (!clamp_pass(pyn, loy, hiy)) gpy = T(0);
+    if (kBox && P.box)
+      box_clamp_vjp(pxn < lox ? -1 : (pxn > hix ? 1 : 0), pyn < loy ? -1 : (pyn > hiy ? 1 : 0),
+                    out.th, P, g.px, g.py, g.th);
   }
   int mode = P.mode;
   T c0 = a0, c1 = a1;
@@ -962,12 +994,13 @@ __device__ __forceinline__ void integrate_rk4_fwd(const Agent<T>& in, T a0, T a1
 // cotangent written, action cotangent added). `out` is the substep's stored output: the
 // position clamp's side test uses it (strictly inside the interval: not clamped; on its
 // boundary: the pre-clamp position rebuilt from the stored velocity decides).
-template <typename T>
+template <typename T, bool kBox = false>
 __device__ __forceinline__ void integrate_rk4_vjp(const Agent<T>& in, T a0, T a1, const Agent<T>& out,
-                                                  const Agent<T>& g, const AgentP<T>& P,
+                                                  const Agent<T>& g_out, const AgentP<T>& P,
                                                   const WorldC<T>& W, Agent<T>& gin, T& gfx, T& gfy,
                                                   T& ga0, T& ga1) {
   const T dt = W.dt;
+  Agent<T> g = g_out;
   Rk4Stages<T> R;
   rk4_stages(in, a0, a1, P, dt, R);
   const Agent<T>& xi = R.xi;
@@ -989,13 +1022,19 @@ __device__ __forceinline__ void integrate_rk4_vjp(const Agent<T>& in, T a0, T a1
     vby = so * Num<T>::sin_(xi.th + q.beta);
   }
   if (W.bounds_mode == BOUNDS_CLAMP) {
-    const T lox = W.bx0 + P.radius, hix = W.bx1 - P.radius;
-    const T loy = W.by0 + P.radius, hiy = W.by1 - P.radius;
+    T ex, ey;
+    footprint_extents<T, kBox>(out.th, P, ex, ey);
+    const T lox = W.bx0 + ex, hix = W.bx1 - ex;
+    const T loy = W.by0 + ey, hiy = W.by1 - ey;
     const T prex = xi.px + (out.vx - vbx) * dt, prey = xi.py + (out.vy - vby) * dt;
     const bool px_in = (out.px > lox && out.px < hix) || clamp_pass(prex, lox, hix);
     const bool py_in = (out.py > loy && out.py < hiy) || clamp_pass(prey, loy, hiy);
     if (!px_in) gpx = T(0);
     if (!py_in) gpy = T(0);
+    // a clamped coordinate sits on its bound: below the upper one it is the lower one
+    if (kBox && P.box)
+      box_clamp_vjp(px_in ? 0 : (out.px < hix ? -1 : 1), py_in ? 0 : (out.py < hiy ? -1 : 1),
+                    out.th, P, g.px, g.py, g.th);
   }
   gxi.px = gpx;
   gxi.py = gpy;

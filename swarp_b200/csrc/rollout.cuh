@@ -22,6 +22,7 @@
 #pragma once
 #include "bodies.cuh"
 #include "boxes.cuh"
+#include "boxes_vjp.cuh"
 #include "physics.cuh"
 
 namespace swarp {
@@ -503,6 +504,27 @@ __device__ __forceinline__ void mask_force(const typename V4<T>::t* rec_env, con
   }
 }
 
+// mask_force for worlds with box agents (pair_force_shaped on every listed contact).
+template <typename T>
+__device__ __forceinline__ void mask_force_box(const typename V4<T>::t* rec_env,
+                                               const typename V2<T>::t* thw_env,
+                                               const typename V4<T>::t* shp_env, const T* rad_env,
+                                               unsigned m, int a, const Agent<T>& x,
+                                               const AgentP<T>& P, const WorldC<T>& W, T& fx,
+                                               T& fy) {
+  const Ob<T> oa = ob_of(x.px, x.py, x.th, x.vx, x.vy, x.w, P.hx, P.hy);
+  while (m) {
+    const int b = __ffs(m) - 1;
+    m &= m - 1u;
+    const auto q = rec_env[b];
+    const auto tw = thw_env[b];
+    const auto sh = shp_env[b];
+    const Ob<T> ob = ob_of(q.x, q.y, tw.x, q.z, q.w, tw.y, sh.y, sh.z);
+    pair_force_shaped(a, b, P.box != 0, oa, P.radius, sh.x > T(0.5), ob, rad_env[b], P.inv_denom,
+                      W, fx, fy);
+  }
+}
+
 template <typename T, int FL>
 __device__ __forceinline__ void static_force(const Obs<T>* sobs, int N, const Agent<T>& x,
                                              const AgentP<T>& P, const WorldC<T>& W, T& fx, T& fy) {
@@ -556,10 +578,11 @@ __device__ __forceinline__ void integrate_vjp_sel(const Agent<T>& in, T a0, T a1
     Q.tag = TAG_HOLONOMIC;
     Q.mode = MODE_VELOCITY;
   }
+  constexpr bool kBox = (FL & F_BOXES) != 0;
   if (FL & F_RK4)
-    integrate_rk4_vjp(in, a0, a1, out, g, Q, W, gin, gfx, gfy, ga0, ga1);
+    integrate_rk4_vjp<T, kBox>(in, a0, a1, out, g, Q, W, gin, gfx, gfy, ga0, ga1);
   else
-    integrate_vjp(in, a0, a1, out, g, Q, W, gin, gfx, gfy, ga0, ga1);
+    integrate_vjp<T, kBox>(in, a0, a1, out, g, Q, W, gin, gfx, gfy, ga0, ga1);
 }
 
 // Pad slot of an odd-sized env: never within any radius.
@@ -743,6 +766,58 @@ __device__ __forceinline__ void force_vjp(const T* xy_env, const typename V4<T>:
                    gin.vx, gin.vy);
 }
 
+// force_vjp for worlds with box agents (no moving bodies): every contact through the
+// shape dispatch's VJP (boxes_vjp.cuh), into all six state gradients of agent a.
+template <typename T, int FL, int AS>
+__device__ __forceinline__ void force_vjp_box(const T* xy_env, const typename V4<T>::t* rec_env,
+                                              const typename V2<T>::t* thw_env,
+                                              const typename V4<T>::t* shp_env,
+                                              const typename V2<T>::t* fb_env, const int* cut_env,
+                                              const T* rad_env, const T* iden_env,
+                                              const Obs<T>* sobs, int N, int A, int a,
+                                              unsigned cmask, const Agent<T>& x,
+                                              const AgentP<T>& P, const WorldC<T>& W, T gfx, T gfy,
+                                              Agent<T>& gin) {
+  using T4 = typename V4<T>::t;
+  const Ob<T> oa = ob_of(x.px, x.py, x.th, x.vx, x.vy, x.w, P.hx, P.hy);
+  const bool box_a = P.box != 0;
+  auto pair = [&](int b, const T4& q, bool own, bool cross) {
+    const auto tw = thw_env[b];
+    const auto sh = shp_env[b];
+    const auto gb = fb_env[b];
+    const Ob<T> ob = ob_of(q.x, q.y, tw.x, q.z, q.w, tw.y, sh.y, sh.z);
+    pair_shaped_vjp(a, b, box_a, oa, x.th, P.radius, P.inv_denom, own ? gfx : T(0),
+                    own ? gfy : T(0), sh.x > T(0.5), ob, tw.x, rad_env[b], iden_env[b],
+                    cross ? gb.x : T(0), cross ? gb.y : T(0), W, gin);
+  };
+  if (FL & F_MASK) {
+    unsigned m = cmask;
+    while (m) {
+      const int b = __ffs(m) - 1;
+      m &= m - 1u;
+      pair(b, rec_env[b], true, true);
+    }
+  } else if (FL & F_COLL) {
+    const int cut_a = (FL & F_TRUNC) ? cut_env[a] : A;
+    for_each_in_radius<T, AS>(xy_env, rec_env, A, a, x.px, x.py, W.r2_thr,
+                              [&](int b, const T4& q) {
+      pair(b, q, !(FL & F_TRUNC) || b <= cut_a, !(FL & F_TRUNC) || a <= cut_env[b]);
+    });
+  }
+  if (box_a) {
+    box_static_vjp((FL & F_OBS) ? sobs : nullptr, (FL & F_OBS) ? N : 0,
+                   W.bounds_mode == BOUNDS_SOFT, oa, x.th, P.inv_denom, gfx, gfy, W, gin);
+    return;
+  }
+  if (FL & F_OBS)
+    for (int o = 0; o < N; ++o)
+      obstacle_force_vjp(x.px, x.py, x.vx, x.vy, P.radius, P.inv_denom, sobs[o], gfx, gfy, W,
+                         gin.px, gin.py, gin.vx, gin.vy);
+  if (W.bounds_mode == BOUNDS_SOFT)
+    wall_force_vjp(x.px, x.py, x.vx, x.vy, P.radius, P.inv_denom, gfx, gfy, W, gin.px, gin.py,
+                   gin.vx, gin.vy);
+}
+
 // Adjoint of one env's body substep (one thread): consumes the cotangent of the bodies'
 // output states (gbody) and the agents' shape-pose cotangents (gpose [A][N]); writes the
 // cotangent of the input states back to gbody and the agents' (pos, vel) cotangents
@@ -824,6 +899,7 @@ __global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : 1024)
   using T2 = typename V2<T>::t;
   using T4 = typename V4<T>::t;
   constexpr bool kBodies = (FL & F_BODIES) != 0;
+  constexpr bool kBoxes = (FL & F_BOXES) != 0 && (FL & F_COLL) != 0;  // shapes meet in pairs
   extern __shared__ __align__(16) unsigned char smem[];
   const int A = AS > 0 ? AS : R.A;
   const int G = R.G, GA = G * A, S = R.S, N = R.N;
@@ -833,7 +909,9 @@ __global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : 1024)
   const int e = e0 + le;
   const bool valid = e < R.E;
   const int ec = valid ? e : R.E - 1;
-  const Layout<T> L(G, A, N, S, true, kBodies);
+  const Layout<T> L(G, A, N, S, true, kBodies, kBoxes);
+  T2* sthw = reinterpret_cast<T2*>(smem + L.thw);  // [nbuf][GA] (th, w), box worlds
+  T4* sshp = reinterpret_cast<T4*>(smem + L.shp);  // [GA] (box, hx, hy, -)
   const int NP4 = L.NP * 4;
   T* sxy = reinterpret_cast<T*>(smem + L.xy);       // [nbuf][G][NP*4] scan tables
   T4* srec = reinterpret_cast<T4*>(smem + L.rec);   // [nbuf][GA] (x, y, vx, vy)
@@ -859,6 +937,7 @@ __global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : 1024)
   const WorldC<T> W = R.W;
   srad[tid] = P.radius;
   siden[tid] = P.inv_denom;
+  if (kBoxes) sshp[tid] = T4{P.box ? T(1) : T(0), P.hx, P.hy, T(0)};
   if (FL & F_OBS) load_obstacles(R, sobs, e0);
   if (kScan) init_pads(sxy, L.nbuf, G, A);
   if (kBodies) {
@@ -883,6 +962,7 @@ __global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : 1024)
   const T* rad_env = srad + le * A;
   const T* iden_env = siden + le * A;
   Obs<T>* obs_env = sobs + le * N;
+  const T4* shp_env = sshp + le * A;
   const bool has_gt = R.gt_pos || R.gt_th || R.gt_vel || R.gt_s || R.gt_w;
 
   Agent<T> g{};
@@ -943,12 +1023,18 @@ __global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : 1024)
       if (FL & F_COLL) {
         if (kScan) put_xy(xy_env, a, cur.px, cur.py);
         rec_env[a] = T4{cur.px, cur.py, cur.vx, cur.vy};
+        if (kBoxes) sthw[fbuf * GA + le * A + a] = T2{cur.th, cur.w};
         fb_env[a] = T2{gfx, gfy};
         if (FL & F_TRUNC) cut_env[a] = R.cutoff[(long long)t * EA + ia];
         __syncthreads();
       }
-      force_vjp<T, FL, AS>(xy_env, rec_env, fb_env, cut_env, rad_env, iden_env, obs_env, sbc,
-                           nullptr, N, A, a, cm0, cur, P, W, gfx, gfy, gin);
+      if (FL & F_BOXES)
+        force_vjp_box<T, FL, AS>(xy_env, rec_env, sthw + fbuf * GA + le * A, shp_env, fb_env,
+                                 cut_env, rad_env, iden_env, obs_env, N, A, a, cm0, cur, P, W, gfx,
+                                 gfy, gin);
+      else
+        force_vjp<T, FL, AS>(xy_env, rec_env, fb_env, cut_env, rad_env, iden_env, obs_env, sbc,
+                             nullptr, N, A, a, cm0, cur, P, W, gfx, gfy, gin);
       g = gin;
       fbuf ^= 1;
     } else {
@@ -968,6 +1054,7 @@ __global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : 1024)
         T4* rec_env = srec + k * GA + le * A;
         if (kScan) put_xy(xy_env, a, x.px, x.py);
         rec_env[a] = T4{x.px, x.py, x.vx, x.vy};
+        if (kBoxes) sthw[k * GA + le * A + a] = T2{x.th, x.w};
         T* ow = sown + (size_t(k) * GA + tid) * 4;
         ow[0] = x.th;
         ow[1] = x.s;
@@ -976,12 +1063,22 @@ __global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : 1024)
         T fx = T(0), fy = T(0);
         if (kShare) __syncthreads();
         if (FL & F_COLL) {
+          const T2* thw_env = sthw + k * GA + le * A;
           if (FL & F_MASK) {
-            mask_force(rec_env, rad_env, R.cmask[((long long)t * S + k) * EA + ia], x, P, W, fx, fy);
+            const unsigned cmk = R.cmask[((long long)t * S + k) * EA + ia];
+            if (kBoxes)
+              mask_force_box(rec_env, thw_env, shp_env, rad_env, cmk, a, x, P, W, fx, fy);
+            else
+              mask_force(rec_env, rad_env, cmk, x, P, W, fx, fy);
           } else {
             int cutoff;
             unsigned cm;
-            neighbor_force<T, FL, AS>(xy_env, rec_env, rad_env, A, a, x, P, W, fx, fy, cutoff, cm);
+            if (kBoxes)
+              neighbor_force_box<T, FL, AS>(xy_env, rec_env, thw_env, shp_env, rad_env, A, a, x, P,
+                                            W, fx, fy, cutoff, cm);
+            else
+              neighbor_force<T, FL, AS>(xy_env, rec_env, rad_env, A, a, x, P, W, fx, fy, cutoff,
+                                        cm);
           }
         }
         static_force<T, FL>(obs_env, N, x, P, W, fx, fy);
@@ -1015,8 +1112,13 @@ __global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : 1024)
         if (FL & F_TRUNC) cut_env[a] = R.cutoff[ws];
         const unsigned cm = (FL & F_MASK) ? R.cmask[ws] : 0u;
         __syncthreads();
-        force_vjp<T, FL, AS>(xy_env, rec_env, fb_env, cut_env, rad_env, iden_env, obs_env, sbc,
-                             sgpose + size_t(tid) * N, N, A, a, cm, in, P, W, gfx, gfy, gin);
+        if (FL & F_BOXES)
+          force_vjp_box<T, FL, AS>(xy_env, rec_env, sthw + k * GA + le * A, shp_env, fb_env,
+                                   cut_env, rad_env, iden_env, obs_env, N, A, a, cm, in, P, W, gfx,
+                                   gfy, gin);
+        else
+          force_vjp<T, FL, AS>(xy_env, rec_env, fb_env, cut_env, rad_env, iden_env, obs_env, sbc,
+                               sgpose + size_t(tid) * N, N, A, a, cm, in, P, W, gfx, gfy, gin);
         if (kBodies) {
           __syncthreads();  // shape-pose cotangents of every agent are in
           if (a == 0)

@@ -299,3 +299,69 @@ def test_sixteen_agent_fleet_f32():
     st = stepper(cfgs, dtype=torch.float32, c=1.0, bounds=(-0.6, 0.6, -0.6, 0.6), dt=0.05)
     check_fwd(st, rand_scene(24, 16, 12, spread=0.55), rand_actions(4, 24, 16, 13),
               rtol=1e-5, dtype=torch.float32)
+
+
+# ------------------------------------------------------------ adjoint
+from test_gpu_parity import check  # noqa: E402
+
+
+@pytest.mark.parametrize("rk4", [False, True], ids=["euler", "rk4"])
+def test_grad_mixed_fleet_obstacles_soft_walls_f64(rk4):
+    cfgs = mixed_fleet(9, 21)
+    st = stepper(cfgs, c=1.0, bounds=(-0.45, 0.45, -0.45, 0.45), dt=0.05, rk4=rk4)
+    E = 4
+    st.set_obstacles(obstacle_mix(E, 22))
+    check(st, rand_scene(E, 9, 23), rand_actions(6, E, 9, 24, scale=1.5), seed=25, final=True)
+
+
+@pytest.mark.parametrize("rk4", [False, True], ids=["euler", "rk4"])
+def test_grad_footprint_clamp_f64(rk4):
+    """Boxes held inside the bounds by the footprint clamp: the clamped coordinates'
+    gradients flow into the heading through the support extents."""
+    cfgs = mixed_fleet(6, 31)
+    st = stepper(cfgs, c=1.0, bounds=(-0.25, 0.25, -0.25, 0.25), mode="clamp", dt=0.05, rk4=rk4)
+    check(st, rand_scene(5, 6, 32, spread=0.3), rand_actions(6, 5, 6, 33, scale=2.0), seed=34)
+
+
+def test_grad_substeps_and_saturation_f64():
+    cfgs = mixed_fleet(7, 41)
+    reach = 2.0 * max(x.radius for x in cfgs) + MARGIN
+    world = WorldConfig(collision_k=K, collision_c=1.0, collision_margin=MARGIN,
+                        contact_max_overlap=0.02, neighbor_radius=reach,
+                        bounds=(-0.4, 0.4, -0.4, 0.4))
+    st = Stepper(cfgs, dt=0.06, substeps=3, device=DEV, dtype=D, world=world)
+    st.set_obstacles(obstacle_mix(3, 42))
+    check(st, rand_scene(3, 7, 43), rand_actions(5, 3, 7, 44), seed=45, final=True)
+
+
+def test_grad_truncated_lists_f64():
+    cfgs = mixed_fleet(12, 51)
+    st = stepper(cfgs, c=0.5, dt=0.05, max_neighbors=3, neighbor_radius=0.3)
+    check(st, rand_scene(3, 12, 52, spread=0.2), rand_actions(5, 3, 12, 53), seed=54)
+
+
+def test_grad_reference_gradcheck_scene_f64():
+    """The reference's gradcheck scene (two boxes on a face contact and a disc)."""
+    ha, hb = (0.2, 0.1), (0.15, 0.08)
+    tha, thb = 0.3, 1.0
+    n = np.array([-math.sin(tha), math.cos(tha)])
+    t = np.array([math.cos(tha), math.sin(tha)])
+    ub0, ub1 = np.array([math.cos(thb), math.sin(thb)]), np.array([-math.sin(thb), math.cos(thb)])
+    rb = hb[0] * abs(ub0 @ n) + hb[1] * abs(ub1 @ n)
+    pos = np.array([[0.0, 0.0], n * (ha[1] + rb - 0.01), -n * (ha[1] + 0.06 - 0.01) + 0.05 * t])
+    cfgs = [box(*ha, model=DynamicsModel.DIFF_DRIVE, max_ang_vel=BIG, max_accel=BIG),
+            box(*hb, model=DynamicsModel.DIFF_DRIVE, max_ang_vel=BIG, max_accel=BIG,
+                ctrl_mode=ControlMode.ACCELERATION, max_ang_accel=BIG),
+            disc(0.06, max_accel=BIG)]
+    st = stepper(cfgs, c=1.0)
+    rng = np.random.default_rng(0)
+    s5 = state(pos, [tha, thb, 0.0], 0.1 * rng.normal(size=(3, 2)), 0.5 * rng.normal(size=3))
+    acts = torch.tensor([[[[0.1, 0.4], [0.05, -0.3], [0.1, 0.0]]]], dtype=D).repeat(3, 1, 1, 1)
+    check(st, s5, acts, seed=61, final=True)
+
+
+def test_grad_sixteen_agent_fleet_f32():
+    cfgs = mixed_fleet(16, 71)
+    st = stepper(cfgs, dtype=torch.float32, c=1.0, bounds=(-0.6, 0.6, -0.6, 0.6), dt=0.05)
+    check(st, rand_scene(24, 16, 72, spread=0.55), rand_actions(4, 24, 16, 73), seed=74,
+          dtype=torch.float32, rtol_f=1e-5, rtol_g=1e-4)
