@@ -19,10 +19,14 @@ What it restates (reference = ddebenedittis/swarp, paths relative to that projec
 * ``swarp/core/neighbors.py:76-97``    ``_brute_force`` (ascending index, cap, true count)
 * ``swarp/core/bodies.py:79-127,167-255,367-569`` movable compound-body pass
 * ``swarp/core/stepper.py:549-648``    substep order: neighbors, forces, bodies, integrate
+* ``swarp/dynamics/kernels.py:102-163,349-369,494-508,758-768`` the 6-DOF drone (Euler, RK4)
+* ``swarp/core/collisions.py:262-690`` box agents; ``swarp/dynamics/kernels.py:80-99``
+  footprint clamp
 
 Gradients come from torch autograd over this restatement. Warp's adjoint conventions
 at kinks are reproduced with ``torch.where`` forms: ``max(a, b)`` sends the gradient
-to ``b`` on a tie, ``clamp`` passes it to ``x`` on the closed interval, ``length`` and
+to ``b`` on a tie, ``clamp`` passes it to ``x`` on the closed interval (else to the active
+bound), ``length`` and
 ``abs`` follow Warp's ``adj_length`` (zero at the zero vector) and ``adj_abs`` (+1 at
 0). Movable bodies are not differentiated by the reference (its body pass is
 untaped, ``swarp/core/bodies.py:40-43``); here they are, which makes this module the
@@ -40,7 +44,8 @@ P_RADIUS, P_MASS, P_MAX_SPEED, P_MAX_ACCEL, P_MAX_ANG_VEL, P_MAX_ANG_ACCEL = 0, 
 P_LF, P_LR, P_MAX_STEER, P_MIN_SPEED = 6, 7, 8, 16
 P_CMD_GAIN_V, P_CMD_GAIN_W = 20, 21
 P_SHAPE, P_HALF_X, P_HALF_Y = 17, 18, 19
-HOLONOMIC, DIFF_DRIVE, BICYCLE = 0, 1, 2
+P_THRUST_MAX, P_ARM, P_IXX, P_IYY, P_IZZ, P_KAPPA, P_GRAVITY = 9, 10, 11, 12, 13, 14, 15
+HOLONOMIC, DIFF_DRIVE, BICYCLE, DRONE = 0, 1, 2, 3
 VELOCITY, ACCELERATION, SERVO = 0, 1, 2
 CIRCLE, BOX, SEGMENT = 0, 1, 2
 EPS2 = 1.0e-10
@@ -529,7 +534,7 @@ def brute_neighbors(pos, radius: float, max_neighbors: int):
 
 def collision_forces(state, w: RefWorld, obs: RefObstacles | None):
     """``swarp/core/collisions.py:818-881``: neighbor gather in list order + static."""
-    pos, _, vel, _, _ = state
+    pos, _, vel, _, _ = state[:5]
     px, py = pos[..., 0], pos[..., 1]
     vx, vy = vel[..., 0], vel[..., 1]
     E, A = px.shape
@@ -589,7 +594,7 @@ def clamp_norm(x, y, limit):
 
 def integrate(state, act, fx, fy, w: RefWorld):
     """``swarp/dynamics/kernels.py:166-275,395-403`` for one substep, per agent model."""
-    pos, th, vel, s, om = state
+    pos, th, vel, s, om = state[:5]
     E, A = th.shape
     dt = w.dt / w.substeps
     a0, a1 = act[..., 0], act[..., 1]
@@ -653,10 +658,19 @@ def integrate(state, act, fx, fy, w: RefWorld):
                         torch.where(tag == DIFF_DRIVE, d[i],
                                     torch.where(tag == BICYCLE, b[i], hold[i])))
         out.append(v)
+    drone = None
+    if len(state) == 9:  # kernels.py:349-369: the 6-DOF branch; 2-D agents pass it through
+        a2, a3 = _act_slot(act, 2), _act_slot(act, 3)
+        dr = _drone_euler(px, py, vx, vy, dvx, dvy, state[5:], a0, a1, a2, a3, col, dt)
+        is_d = tag == DRONE
+        for i, j in ((0, 0), (1, 1), (3, 2), (4, 3)):
+            out[i] = torch.where(is_d, dr[j], out[i])
+        drone = _merge_drone(is_d, dr[4:], state[5:])
     npx, npy, nth, nvx, nvy, ns, nw = out
     if w.clamp_bounds:
         npx, npy = clamp_footprint(npx, npy, nth, w, col)
-    return (torch.stack([npx, npy], -1), nth, torch.stack([nvx, nvy], -1), ns, nw)
+    res = (torch.stack([npx, npy], -1), nth, torch.stack([nvx, nvy], -1), ns, nw)
+    return res if drone is None else res + drone
 
 
 def _rk4_deriv(px, py, th, vx, vy, s, om, a0, a1, tag, mode, c):
@@ -687,7 +701,7 @@ def integrate_rk4(state, act, fx, fy, w: RefWorld):
     RK4 over four derivative evaluations with the actions held; velocity-mode commands set
     the velocity-level state first; limits apply to the combined result; the contact force
     enters as the Euler path's ``F/m dt`` velocity term (and ``F/m dt^2`` in the pose)."""
-    pos, th, vel, s, om = state
+    pos, th, vel, s, om = state[:5]
     E, A = th.shape
     dt = w.dt / w.substeps
     a0, a1 = act[..., 0], act[..., 1]
@@ -742,10 +756,136 @@ def integrate_rk4(state, act, fx, fy, w: RefWorld):
     out = [torch.where(tag == HOLONOMIC, h[i], torch.where(tag == DIFF_DRIVE, d[i],
                                                             torch.where(tag == BICYCLE, b[i], hold[i])))
            for i in range(7)]
+    drone = None
+    if len(state) == 9:  # kernels.py:494-518, 758-768: the drone's RK4 over its 6-DOF state
+        a2, a3 = _act_slot(act, 2), _act_slot(act, 3)
+        dr = _drone_rk4(pos[..., 0], pos[..., 1], vel[..., 0], vel[..., 1], dvx, dvy, state[5:],
+                        a0, a1, a2, a3, col, dt)
+        is_d = tag == DRONE
+        for i, j in ((0, 0), (1, 1), (3, 2), (4, 3)):
+            out[i] = torch.where(is_d, dr[j], out[i])
+        drone = _merge_drone(is_d, dr[4:], state[5:])
     npx, npy, nth, nvx, nvy, ns, nw = out
     if w.clamp_bounds:
         npx, npy = clamp_footprint(npx, npy, nth, w, col)
-    return (torch.stack([npx, npy], -1), nth, torch.stack([nvx, nvy], -1), ns, nw)
+    res = (torch.stack([npx, npy], -1), nth, torch.stack([nvx, nvy], -1), ns, nw)
+    return res if drone is None else res + drone
+
+
+# -------------------------------------------------------------------------- drone
+
+
+def _act_slot(act, j):
+    """``swarp/dynamics/kernels.py:797-810`` (``_load_actions``): slot j, zero past act_dim."""
+    return act[..., j] if act.shape[-1] > j else torch.zeros_like(act[..., 0])
+
+
+def _cross3(ax, ay, az, bx, by, bz):
+    return ay * bz - az * by, az * bx - ax * bz, ax * by - ay * bx
+
+
+def _quat_rotate(qx, qy, qz, qw, vx, vy, vz):
+    """``swarp/dynamics/kernels.py:107-114``: v rotated by the unit quaternion (x, y, z, w),
+    ``v + w t + u x t`` with ``t = 2 u x v``."""
+    cx, cy, cz = _cross3(qx, qy, qz, vx, vy, vz)
+    tx, ty, tz = 2.0 * cx, 2.0 * cy, 2.0 * cz
+    ux, uy, uz = _cross3(qx, qy, qz, tx, ty, tz)
+    return vx + qw * tx + ux, vy + qw * ty + uy, vz + qw * tz + uz
+
+
+def _quat_deriv(qx, qy, qz, qw, wx, wy, wz):
+    """``swarp/dynamics/kernels.py:117-126``: ``0.5 q (x) (w, 0)`` (Hamilton)."""
+    return (0.5 * (qw * wx + qy * wz - qz * wy), 0.5 * (qw * wy - qx * wz + qz * wx),
+            0.5 * (qw * wz + qx * wy - qy * wx), 0.5 * (-qx * wx - qy * wy - qz * wz))
+
+
+def _normalize4(q):
+    """Warp ``normalize`` of a 4-vector: q / |q| (zero for the zero vector)."""
+    n2 = q[0] * q[0] + q[1] * q[1] + q[2] * q[2] + q[3] * q[3]
+    pos = n2 > 0
+    n = torch.where(pos, torch.sqrt(torch.where(pos, n2, torch.ones_like(n2))), torch.ones_like(n2))
+    return tuple(torch.where(pos, x / n, torch.zeros_like(x)) for x in q)
+
+
+def _drone_rates(f0, f1, f2, f3, q, br, col):
+    """``swarp/dynamics/kernels.py:130-163``: world acceleration and body angular
+    acceleration of a "+" quadrotor (rotors 0/2 on body x, 1/3 on body y)."""
+    mass, g = col(P_MASS), col(P_GRAVITY)
+    arm, kappa = col(P_ARM), col(P_KAPPA)
+    ixx, iyy, izz = col(P_IXX), col(P_IYY), col(P_IZZ)
+    thrust = f0 + f1 + f2 + f3
+    z0 = torch.zeros_like(thrust)
+    fx, fy, fz = _quat_rotate(*q, z0, z0, thrust)
+    acc = (fx / mass - 0.0, fy / mass - 0.0, fz / mass - g)
+    tx = arm * (f1 - f3)
+    ty = arm * (f2 - f0)
+    tz = kappa * (f0 - f1 + f2 - f3)
+    bx, by, bz = br
+    ang = ((tx - (izz - iyy) * by * bz) / ixx, (ty - (ixx - izz) * bz * bx) / iyy,
+           (tz - (iyy - ixx) * bx * by) / izz)
+    return acc, ang
+
+
+def _thrusts(a0, a1, a2, a3, col):
+    tmax = col(P_THRUST_MAX)
+    z = torch.zeros_like(tmax)
+    return tuple(wclamp(a, z, tmax) for a in (a0, a1, a2, a3))
+
+
+def _drone_euler(px, py, vx, vy, dvx, dvy, d, a0, a1, a2, a3, col, dt):
+    """``swarp/dynamics/kernels.py:349-369``: semi-implicit Euler of the 6-DOF state (rates
+    and velocities first, then attitude with the new rates and positions with the new
+    velocities). Returns (px, py, vx, vy, z, vz, attitude, body_rates)."""
+    z, vz, att, br = d
+    q = tuple(att[..., i] for i in range(4))
+    b = tuple(br[..., i] for i in range(3))
+    acc, ang = _drone_rates(*_thrusts(a0, a1, a2, a3, col), q, b, col)
+    nb = tuple(b[i] + ang[i] * dt for i in range(3))
+    nvz = vz + acc[2] * dt
+    nvx = vx + acc[0] * dt + dvx
+    nvy = vy + acc[1] * dt + dvy
+    qd = _quat_deriv(*q, *nb)
+    nq = _normalize4(tuple(q[i] + qd[i] * dt for i in range(4)))
+    return (px + nvx * dt, py + nvy * dt, nvx, nvy, z + nvz * dt, nvz,
+            torch.stack(nq, -1), torch.stack(nb, -1))
+
+
+def _drone_deriv(vx, vy, vz, q, b, f, col):
+    """The drone rows of ``_deriv`` (``swarp/dynamics/kernels.py:494-508``)."""
+    acc, ang = _drone_rates(*f, q, b, col)
+    return (vx, vy, acc[0], acc[1], vz, acc[2], _quat_deriv(*q, *b), ang)
+
+
+def _drone_rk4(px, py, vx, vy, dvx, dvy, d, a0, a1, a2, a3, col, dt):
+    """``swarp/dynamics/kernels.py:521-793`` for a drone: RK4 over (p, v, z, vz, q, rates)
+    with the thrusts held, the contact force as the Euler path's F/m dt velocity term,
+    the attitude renormalized after the combine."""
+    z, vz, att, br = d
+    f = _thrusts(a0, a1, a2, a3, col)
+    x = [px, py, vx, vy, z, vz] + [att[..., i] for i in range(4)] + [br[..., i] for i in range(3)]
+
+    def deriv(x):
+        k = _drone_deriv(x[2], x[3], x[5], tuple(x[6:10]), tuple(x[10:13]), f, col)
+        return [k[0], k[1], k[2], k[3], k[4], k[5], *k[6], *k[7]]
+
+    dt2, sixth = dt * 0.5, dt / 6.0
+    k1 = deriv(x)
+    k2 = deriv([xi + ki * dt2 for xi, ki in zip(x, k1)])
+    k3 = deriv([xi + ki * dt2 for xi, ki in zip(x, k2)])
+    k4 = deriv([xi + ki * dt for xi, ki in zip(x, k3)])
+    xi = [x0 + (q1 + q2 * 2.0 + q3 * 2.0 + q4) * sixth for x0, q1, q2, q3, q4 in zip(x, k1, k2, k3, k4)]
+    nq = _normalize4(tuple(xi[6:10]))
+    return (xi[0] + dvx * dt, xi[1] + dvy * dt, xi[2] + dvx, xi[3] + dvy, xi[4], xi[5],
+            torch.stack(nq, -1), torch.stack(xi[10:13], -1))
+
+
+def _merge_drone(is_d, new, old):
+    """Drone agents take the new 6-DOF fields, every other agent passes them through."""
+    out = []
+    for n, o in zip(new, old):
+        m = is_d if n.dim() == is_d.dim() else is_d.unsqueeze(-1)
+        out.append(torch.where(m, n, o))
+    return tuple(out)
 
 
 # -------------------------------------------------------------------------- bodies
@@ -827,7 +967,7 @@ def body_pass(state, obs: RefObstacles, w: RefWorld):
     body, as in every configuration here, the two readings coincide).
     Returns a new :class:`RefObstacles`.
     """
-    pos, _, vel, _, _ = state
+    pos, _, vel, _, _ = state[:5]
     px, py = pos[..., 0], pos[..., 1]
     vx, vy = vel[..., 0], vel[..., 1]
     E, A = px.shape

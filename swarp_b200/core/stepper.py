@@ -107,6 +107,9 @@ class Stepper:
             raise RuntimeError(
                 f"swarp_b200 steps only on CUDA devices (got {device!r}); there is no CPU path"
             )
+        if self.device.index is None:  # "cuda" means the current device, as in torch
+            self.device = torch.device(
+                "cuda", torch.cuda.current_device() if torch.cuda.is_available() else 0)
         self.dtype = _as_torch_dtype(dtype)
         self.torch_dtype = self.dtype
         self.world = world

@@ -376,3 +376,13 @@ def test_env_independence_full_size_f32():
     st0 = tuple(t[sub_idx].detach().cpu().double() for t in state)
     r1, _, _ = R.step(st0, acts[0, sub_idx].cpu().double(), w)
     close(full[1][sub_idx].cpu().double(), r1[0], 1e-5, "step-1 pos")
+
+
+def test_bare_cuda_device_string():
+    """device="cuda" names the current device, as in torch."""
+    st = Stepper(cfgs_of(DynamicsModel.HOLONOMIC, ControlMode.VELOCITY, 3), dt=0.05, device="cuda",
+                 dtype=torch.float64, world=WorldConfig())
+    assert st.device == torch.device("cuda", torch.cuda.current_device())
+    s = TorchState(*(t.to(DEV) for t in rand_state(2, 3, 91)))
+    fin, traj = rollout(st, s, rand_actions(2, 2, 3, 92).to(DEV))
+    assert traj[-1][0].shape == (2, 3, 2)
