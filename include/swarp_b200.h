@@ -55,6 +55,12 @@ typedef struct {
   void* vel;
   void* speed;
   void* ang_vel;
+  /* 6-DOF drone fields (swarp/core/state.py WorldState.z/vz/attitude/body_rates); read and
+   * written only in worlds with drone agents (fleet_models bit 3), NULL otherwise */
+  void* z;          /* [.., E, A]    */
+  void* vz;         /* [.., E, A]    */
+  void* attitude;   /* [.., E, A, 4] unit quaternion (x, y, z, w), body to world */
+  void* body_rates; /* [.., E, A, 3] */
 } swarp_state_t;
 
 /* Obstacle set (E envs, N shapes). Poses and motion are per env, extents per shape.

@@ -28,7 +28,9 @@ MAX_AGENTS = 1024
 
 class State(C.Structure):
     _fields_ = [("pos", C.c_void_p), ("theta", C.c_void_p), ("vel", C.c_void_p),
-                ("speed", C.c_void_p), ("ang_vel", C.c_void_p)]
+                ("speed", C.c_void_p), ("ang_vel", C.c_void_p),
+                ("z", C.c_void_p), ("vz", C.c_void_p), ("attitude", C.c_void_p),
+                ("body_rates", C.c_void_p)]
 
 
 class ObstaclesC(C.Structure):
@@ -125,7 +127,7 @@ def ptr(t: torch.Tensor | None) -> int | None:
 
 
 def state_c(fields) -> State:
-    """``State`` of five tensors (or Nones)."""
+    """``State`` of five (2-D) or nine (with the drone fields) tensors or Nones."""
     return State(*(ptr(t) for t in fields))
 
 

@@ -19,9 +19,10 @@ LIB = os.path.join(HERE, "libswarp_b200.so")
 SOURCES = ["capi.cu", "noalloc.cu", "k_fwd_f32.cu", "k_fwd_f64.cu", "k_bwd_f32.cu",
            "k_bwd_f64.cu", "k_fwd_f32_rk4.cu", "k_fwd_f64_rk4.cu", "k_bwd_f32_rk4.cu",
            "k_bwd_f64_rk4.cu", "k_x2_f32.cu", "k_fwd_f32_box.cu", "k_fwd_f64_box.cu",
-           "k_bwd_f32_box.cu", "k_bwd_f64_box.cu"]
+           "k_bwd_f32_box.cu", "k_bwd_f64_box.cu", "k_fwd_f32_drone.cu", "k_fwd_f64_drone.cu",
+           "k_bwd_f32_drone.cu", "k_bwd_f64_drone.cu"]
 DEPS = [*SOURCES, "launch.cuh", "rollout.cuh", "rollout_x2.cuh", "physics.cuh", "bodies.cuh",
-        "boxes.cuh", "boxes_vjp.cuh"]
+        "boxes.cuh", "boxes_vjp.cuh", "drone.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--extended-lambda", "-fmad=false",
          "-Xcompiler", "-fPIC", "-Xcompiler", "-O2"]

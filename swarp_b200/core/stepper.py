@@ -118,9 +118,9 @@ class Stepper:
         if self.n_agents > _lib.MAX_AGENTS:
             raise ValueError(f"{self.n_agents} agents per env exceed the {_lib.MAX_AGENTS} this "
                              "build runs in one CTA")
-        for c in self.configs:
-            if c.model == DynamicsModel.DRONE:
-                raise NotImplementedError("the 6-DOF drone model is not on the CUDA path yet")
+        # 6-DOF drones carry four more state fields (z, vz, attitude, body rates)
+        self.has_drones = any(c.model == DynamicsModel.DRONE for c in self.configs)
+        self.n_state = 9 if self.has_drones else 5
         if world.integrator not in (Integrator.EULER, Integrator.RK4):
             raise NotImplementedError(f"integrator {world.integrator} is not on the CUDA path")
         if world.wheel_contacts:
@@ -129,6 +129,8 @@ class Stepper:
             raise NotImplementedError("floor friction of movable bodies (obstacle_friction) is "
                                       "not on the CUDA path")
         self.box_agents = any(c.shape == AgentShape.BOX for c in self.configs)
+        if self.has_drones and self.box_agents:
+            raise NotImplementedError("box agents and drones in one fleet are not on the CUDA path")
         self.params = torch.tensor(param_rows(self.configs), dtype=self.dtype, device=self.device)
         self.params_per_env: torch.Tensor | None = None
         self.model_tag = torch.tensor([int(c.model) for c in self.configs], dtype=torch.int32,
@@ -192,9 +194,9 @@ class Stepper:
         self.n_obstacles = obs.n_obstacles
         moving = obs.kind[obs.body.long()] != 0  # shapes whose body root is movable
         self.any_movable = bool(moving.any().item())
-        if self.any_movable and self.box_agents:
-            raise NotImplementedError("box agents against movable obstacles are not on the CUDA "
-                                      "path")
+        if self.any_movable and (self.box_agents or self.has_drones):
+            raise NotImplementedError("box agents or drones against movable obstacles are not on "
+                                      "the CUDA path")
         self.movable_shapes = 0
         self._poses_from_bodies = False
         if self.any_movable:
@@ -362,8 +364,9 @@ class Stepper:
         if actions.shape[-2] != self.n_agents or actions.shape[-1] < 2:
             raise ValueError(f"actions must be [..., n_envs, {self.n_agents}, act_dim>=2]; got "
                              f"{tuple(actions.shape)}")
-        shapes = [(E, self.n_agents, 2), (E, self.n_agents), (E, self.n_agents, 2),
-                  (E, self.n_agents), (E, self.n_agents)]
+        A = self.n_agents
+        shapes = [(E, A, 2), (E, A), (E, A, 2), (E, A), (E, A), (E, A), (E, A), (E, A, 4),
+                  (E, A, 3)][:self.n_state]
         for t, shp in zip(state, shapes, strict=True):
             if tuple(t.shape) != shp:
                 raise ValueError(f"state field of shape {tuple(t.shape)}, expected {shp}")
@@ -381,10 +384,11 @@ class Stepper:
                         out=None, true_count: bool = False, moving_bodies: bool = True):
         """Run the forward rollout kernel.
 
-        ``state5`` are the five contiguous initial-state tensors, ``actions`` is
-        ``[T, E, A, act_dim]``. Movable bodies (if any) advance when ``moving_bodies``; the
+        ``state5`` are the ``n_state`` contiguous initial-state tensors (five, or nine with
+        the drone fields z, vz, attitude, body_rates when the fleet has drones), ``actions``
+        is ``[T, E, A, act_dim]``. Movable bodies (if any) advance when ``moving_bodies``; the
         stepper then carries their final state. Returns ``(traj5, final5 | None,
-        true_max | None, record)`` with ``traj5`` stacked ``[T, E, A(,2)]`` and ``record``
+        true_max | None, record)`` with ``traj5`` stacked ``[T, E, A(,k)]`` and ``record``
         the :class:`RolloutRecord` the adjoint needs.
         """
         lib = _lib.load()
@@ -395,9 +399,13 @@ class Stepper:
             wc.obstacles.bodies_move = int(moving)
         opts = {"device": self.device, "dtype": self.dtype}
         if out is None:
-            traj = (torch.empty(H, E, self.n_agents, 2, **opts), torch.empty(H, E, self.n_agents, **opts),
-                    torch.empty(H, E, self.n_agents, 2, **opts), torch.empty(H, E, self.n_agents, **opts),
-                    torch.empty(H, E, self.n_agents, **opts))
+            A = self.n_agents
+            traj = (torch.empty(H, E, A, 2, **opts), torch.empty(H, E, A, **opts),
+                    torch.empty(H, E, A, 2, **opts), torch.empty(H, E, A, **opts),
+                    torch.empty(H, E, A, **opts))
+            if self.has_drones:
+                traj = traj + (torch.empty(H, E, A, **opts), torch.empty(H, E, A, **opts),
+                               torch.empty(H, E, A, 4, **opts), torch.empty(H, E, A, 3, **opts))
         else:
             traj = out
         fin = tuple(torch.empty_like(t[0]) for t in traj) if final else None

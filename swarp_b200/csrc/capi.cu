@@ -15,7 +15,7 @@ using namespace swarp;
 
 namespace {
 
-constexpr int kAbiVersion = 5;
+constexpr int kAbiVersion = 6;
 
 int threads_target() {
   static int v = [] {
@@ -41,7 +41,7 @@ bool aligned(const void* p, unsigned n) { return (reinterpret_cast<uintptr_t>(p)
 // fields; the adjoint also one substep per step).
 bool x2_ok(const RolloutArgs<float>& R, int fl, bool bwd) {
   if (!x2_enabled() || R.A != 16 || R.act_dim != 2) return false;
-  if (!(fl & F_MASK) || (fl & (F_BODIES | F_TRUNC | F_BOXES))) return false;
+  if (!(fl & F_MASK) || (fl & (F_BODIES | F_TRUNC | F_BOXES | F_DRONE))) return false;
   if (bwd && R.S != 1) return false;
   const void* v16[] = {R.t_pos, R.t_vel, R.i_pos, R.i_vel, R.act, R.f_pos, R.f_vel, R.g_act};
   for (const void* p : v16)
@@ -82,8 +82,10 @@ int validate_world(const swarp_world_t* w, int horizon) {
   if (w->n_agents > SWARP_MAX_AGENTS) return SWARP_ERR_TOO_MANY_AGENTS;
   if (!(w->dt > 0.0)) return SWARP_ERR_INVALID_ARG;
   if (!w->params || !w->model_tag || !w->ctrl_mode) return SWARP_ERR_INVALID_ARG;
-  if (w->fleet_models & ~0x7) return SWARP_ERR_UNSUPPORTED;  // drone / unknown tags
+  if (w->fleet_models & ~0xF) return SWARP_ERR_UNSUPPORTED;  // unknown tags
   if (w->fleet_models == 0 || w->fleet_modes == 0 || (w->fleet_modes & ~0x7)) return SWARP_ERR_INVALID_ARG;
+  // drones together with box agents (exclusive in the reference) or moving bodies: not built
+  if ((w->fleet_models & 0x8) && w->box_agents) return SWARP_ERR_UNSUPPORTED;
   if (w->bounds_mode < 0 || w->bounds_mode > 2) return SWARP_ERR_INVALID_ARG;
   if (w->integrator < 0 || w->integrator > 1) return SWARP_ERR_INVALID_ARG;
   if (w->box_agents < 0 || w->box_agents > 1) return SWARP_ERR_INVALID_ARG;
@@ -105,6 +107,7 @@ int validate_world(const swarp_world_t* w, int horizon) {
 bool state_complete(const swarp_state_t& s) {
   return s.pos && s.theta && s.vel && s.speed && s.ang_vel;
 }
+bool drone_complete(const swarp_state_t& s) { return s.z && s.vz && s.attitude && s.body_rates; }
 
 int flags_of(const swarp_world_t* w) {
   int fl = 0;
@@ -121,6 +124,7 @@ int flags_of(const swarp_world_t* w) {
   }
   if (w->integrator == 1) fl |= F_RK4;
   if (w->box_agents) fl |= F_BOXES;
+  if (w->fleet_models & 0x8) fl |= F_DRONE;
   if (w->fleet_models == 1 && w->fleet_modes == 1) fl |= F_HOLOVEL;
   return fl;
 }
@@ -200,6 +204,10 @@ void set_state_out(const swarp_state_t& s, T*& p, T*& th, T*& v, T*& sp, T*& w) 
   sp = static_cast<T*>(s.speed);
   w = static_cast<T*>(s.ang_vel);
 }
+template <typename Q> DroneF<Q> drone_of(const swarp_state_t& s) {
+  return DroneF<Q>{static_cast<Q*>(s.z), static_cast<Q*>(s.vz), static_cast<Q*>(s.attitude),
+                   static_cast<Q*>(s.body_rates)};
+}
 
 // Workspace: [contact checkpoint cells (F_TRUNC cutoffs / F_MASK masks)] then, 256-byte
 // aligned, one partial sum per adjoint CTA for the fused ||grad_actions||^2 epilogue.
@@ -232,6 +240,9 @@ int fwd_typed(const swarp_world_t* w, int horizon, swarp_state_t init, const voi
   R.act = static_cast<const T*>(actions);
   set_state_out<T>(traj, R.t_pos, R.t_th, R.t_vel, R.t_s, R.t_w);
   set_state_out<T>(fin, R.f_pos, R.f_th, R.f_vel, R.f_s, R.f_w);
+  R.i_d = drone_of<const T>(init);
+  R.t_d = drone_of<T>(traj);
+  R.f_d = drone_of<T>(fin);
   R.true_max = true_max;
   const int fl = flags_of(w);
   R.cutoff = (fl & F_TRUNC) ? static_cast<int16_t*>(ws) : nullptr;
@@ -265,6 +276,11 @@ int bwd_typed(const swarp_world_t* w, int horizon, swarp_state_t init, const voi
   set_state<T>(gfin, R.gf_pos, R.gf_th, R.gf_vel, R.gf_s, R.gf_w);
   R.g_act = static_cast<T*>(gact);
   set_state_out<T>(ginit, R.gi_pos, R.gi_th, R.gi_vel, R.gi_s, R.gi_w);
+  R.i_d = drone_of<const T>(init);
+  R.t_d = drone_of<T>(traj);
+  R.gt_d = drone_of<const T>(gtraj);
+  R.gf_d = drone_of<const T>(gfin);
+  R.gi_d = drone_of<T>(ginit);
   const int fl = flags_of(w);
   R.cutoff = (fl & F_TRUNC) ? static_cast<int16_t*>(ws) : nullptr;
   R.cmask = (fl & F_MASK) ? static_cast<uint32_t*>(ws) : nullptr;
@@ -313,6 +329,11 @@ int swarp_rollout_fwd(const swarp_world_t* w, int32_t horizon, swarp_state_t ini
   if ((flags_of(w) & F_BOXES) && (flags_of(w) & F_BODIES)) return SWARP_ERR_UNSUPPORTED;
   const bool any_fin = final_out.pos || final_out.theta || final_out.vel || final_out.speed || final_out.ang_vel;
   if (any_fin && !state_complete(final_out)) return SWARP_ERR_INVALID_ARG;
+  if (flags_of(w) & F_DRONE) {
+    if ((flags_of(w) & F_BODIES)) return SWARP_ERR_UNSUPPORTED;
+    if (!drone_complete(init) || !drone_complete(traj)) return SWARP_ERR_INVALID_ARG;
+    if (any_fin && !drone_complete(final_out)) return SWARP_ERR_INVALID_ARG;
+  }
   const size_t need = swarp_rollout_workspace_bytes(w, horizon);
   if (need > 0 && (!workspace || workspace_bytes < need)) return SWARP_ERR_WORKSPACE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -332,6 +353,11 @@ int swarp_rollout_bwd(const swarp_world_t* w, int32_t horizon, swarp_state_t ini
   int rc = validate_world(w, horizon);
   if (rc != SWARP_OK) return rc;
   if ((flags_of(w) & F_BOXES) && (flags_of(w) & F_BODIES)) return SWARP_ERR_UNSUPPORTED;
+  if (flags_of(w) & F_DRONE) {
+    if (flags_of(w) & F_BODIES) return SWARP_ERR_UNSUPPORTED;
+    if (!drone_complete(init) || !drone_complete(traj) || !drone_complete(adj_init))
+      return SWARP_ERR_INVALID_ARG;
+  }
   if (flags_of(w) & F_BODIES) {
     if (!bodies_complete(bodies_init) || !bodies_complete(bodies_traj)) return SWARP_ERR_INVALID_ARG;
     if (w->obstacles.movable_shapes & ~(1 << SHAPE_CIRCLE)) return SWARP_ERR_UNSUPPORTED;

@@ -27,12 +27,18 @@ int launch_fwd_x2(const RolloutArgs<float>& R, int fl, cudaStream_t st);
 int launch_bwd_x2(const RolloutArgs<float>& R, int fl, cudaStream_t st);
 
 template <typename T> inline int launch_fwd(const RolloutArgs<T>& R, int fl, cudaStream_t st) {
+  if (fl & F_DRONE)
+    return (fl & F_RK4) ? launch_fwd_part<T, F_DRONE | F_RK4>(R, fl, st)
+                        : launch_fwd_part<T, F_DRONE>(R, fl, st);
   if (fl & F_BOXES)
     return (fl & F_RK4) ? launch_fwd_part<T, F_BOXES | F_RK4>(R, fl, st)
                         : launch_fwd_part<T, F_BOXES>(R, fl, st);
   return (fl & F_RK4) ? launch_fwd_part<T, F_RK4>(R, fl, st) : launch_fwd_part<T, 0>(R, fl, st);
 }
 template <typename T> inline int launch_bwd(const RolloutArgs<T>& R, int fl, cudaStream_t st) {
+  if (fl & F_DRONE)
+    return (fl & F_RK4) ? launch_bwd_part<T, F_DRONE | F_RK4>(R, fl, st)
+                        : launch_bwd_part<T, F_DRONE>(R, fl, st);
   if (fl & F_BOXES)
     return (fl & F_RK4) ? launch_bwd_part<T, F_BOXES | F_RK4>(R, fl, st)
                         : launch_bwd_part<T, F_BOXES>(R, fl, st);
@@ -87,7 +93,7 @@ int run_fwd(const RolloutArgs<T>& R, cudaStream_t st) {
 template <typename T, int FL, int AS>
 int run_bwd(const RolloutArgs<T>& R, cudaStream_t st) {
   const Layout<T> L(R.G, R.A, R.N, R.S, true, (FL & F_BODIES) != 0,
-                    (FL & F_BOXES) != 0 && (FL & F_COLL) != 0);
+                    (FL & F_BOXES) != 0 && (FL & F_COLL) != 0, (FL & F_DRONE) != 0);
   const int grid = (R.E + R.G - 1) / R.G;
   const int rc = launch_kernel(rollout_bwd_kernel<T, FL, AS>, grid, R.G * R.A, L.total, st, &R);
   if (rc != 0 || !R.gsq_partial) return rc;
@@ -104,6 +110,11 @@ int run_bwd(const RolloutArgs<T>& R, cudaStream_t st) {
   X(R + 53) X(R + 44) X(R + 45) X(R + 47) X(R + 61)
 // (each instantiated once with R = 0 and once with R = F_RK4)
 
+// Drone worlds: the contact and obstacle cases without moving bodies (R = F_DRONE,
+// F_DRONE | F_RK4); a drone fleet is never a holonomic-velocity fleet.
+#define SWARP_FLAG_CASES_DRONE(X, R) \
+  X(R + 0) X(R + 4) X(R + 1) X(R + 5) X(R + 3) X(R + 7) X(R + 17) X(R + 21)
+
 // Box-agent worlds: the cases without moving bodies (R = F_BOXES, F_BOXES | F_RK4).
 #define SWARP_FLAG_CASES_BOXES(X, R)                                                           \
   X(R + 0) X(R + 4) X(R + 8) X(R + 12) X(R + 1) X(R + 5) X(R + 9) X(R + 13) X(R + 3) X(R + 7) \
@@ -116,7 +127,9 @@ template <typename T, int RB> int launch_fwd_part(const RolloutArgs<T>& R, int f
     if constexpr (std::is_same<T, float>::value && ((F) & F_COLL))          \
       if (a16) return run_fwd<T, F, 16>(R, st);                             \
     return run_fwd<T, F, 0>(R, st);
-  if constexpr ((RB & F_BOXES) != 0) {
+  if constexpr ((RB & F_DRONE) != 0) {
+    switch (fl) { SWARP_FLAG_CASES_DRONE(SWARP_X, RB) }
+  } else if constexpr ((RB & F_BOXES) != 0) {
     switch (fl) { SWARP_FLAG_CASES_BOXES(SWARP_X, RB) }
   } else {
     switch (fl) { SWARP_FLAG_CASES_EULER(SWARP_X, RB) }
@@ -132,7 +145,9 @@ template <typename T, int RB> int launch_bwd_part(const RolloutArgs<T>& R, int f
     if constexpr (std::is_same<T, float>::value && ((F) & F_COLL))          \
       if (a16) return run_bwd<T, F, 16>(R, st);                             \
     return run_bwd<T, F, 0>(R, st);
-  if constexpr ((RB & F_BOXES) != 0) {
+  if constexpr ((RB & F_DRONE) != 0) {
+    switch (fl) { SWARP_FLAG_CASES_DRONE(SWARP_X, RB) }
+  } else if constexpr ((RB & F_BOXES) != 0) {
     switch (fl) { SWARP_FLAG_CASES_BOXES(SWARP_X, RB) }
   } else {
     switch (fl) { SWARP_FLAG_CASES_EULER(SWARP_X, RB) }

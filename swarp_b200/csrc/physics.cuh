@@ -60,7 +60,7 @@ template <typename T> __device__ __forceinline__ T len2(T x, T y) { return Num<T
 template <typename T> struct Eps2 { static constexpr T v = T(1.0e-10); };
 
 // Model / mode / shape tags (values of the reference enums).
-enum : int { TAG_HOLONOMIC = 0, TAG_DIFF_DRIVE = 1, TAG_BICYCLE = 2 };
+enum : int { TAG_HOLONOMIC = 0, TAG_DIFF_DRIVE = 1, TAG_BICYCLE = 2, TAG_DRONE = 3 };
 enum : int { MODE_VELOCITY = 0, MODE_ACCELERATION = 1, MODE_SERVO = 2 };
 enum : int { SHAPE_CIRCLE = 0, SHAPE_BOX = 1, SHAPE_SEGMENT = 2 };
 enum : int { BOUNDS_NONE = 0, BOUNDS_SOFT = 1, BOUNDS_CLAMP = 2 };
@@ -79,6 +79,7 @@ template <typename T> struct AgentP {
   int tag, mode;
   int box;     // shape BOX (else disc)
   T hx, hy;    // box half extents
+  T tmax, arm, ixx, iyy, izz, kappa, grav;  // drone: rotor thrust limit, geometry, gravity
 };
 
 // World constants of one launch.

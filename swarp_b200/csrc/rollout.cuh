@@ -23,6 +23,7 @@
 #include "bodies.cuh"
 #include "boxes.cuh"
 #include "boxes_vjp.cuh"
+#include "drone.cuh"
 #include "physics.cuh"
 
 namespace swarp {
@@ -44,10 +45,16 @@ enum : int {
   F_BODIES = 32,  // movable bodies integrated in the substep loop (with F_OBS)
   F_RK4 = 64,     // classic RK4 integrator instead of semi-implicit Euler
   F_BOXES = 128,  // some agents are oriented boxes (boxes.cuh)
+  F_DRONE = 256,  // some agents are 6-DOF drones (drone.cuh)
 };
 
 // Largest CTA the 16-agent specializations are launched with (host: envs_per_cta).
 constexpr int kMaxThreadsAS16 = 256;
+
+// The four drone field arrays of one state (null when the world has no drones).
+template <typename P> struct DroneF {
+  P *z, *vz, *att, *br;
+};
 
 template <typename T> struct RolloutArgs {
   int E, A, G, H, S, act_dim, N;
@@ -85,15 +92,21 @@ template <typename T> struct RolloutArgs {
   const T *gb_pos, *gb_ang, *gb_vel, *gb_om;
   int body_clamp;
   int poses_from_bodies;
+  // drone fields (F_DRONE): z, vz [.., E, A], attitude [.., E, A, 4], body rates [.., E, A, 3]
+  // of the init, trajectory, final, their cotangents and the init cotangent
+  DroneF<const T> i_d;
+  DroneF<T> t_d, f_d;
+  DroneF<const T> gt_d, gf_d;
+  DroneF<T> gi_d;
 };
 
 // Shared-memory carve-up, identical on host (sizes) and device (pointers).
 template <typename T> struct Layout {
   int G, A, NP, nbuf, S;
   size_t xy, rec, own, fb, cut, rad, iden, obs, bc, bst, gpose, gag, gbody, gbnew, gshape, thw, shp,
-      total;
+      dro, total;
   __host__ __device__ Layout(int G_, int A_, int N, int S_, bool bwd, bool bodies = false,
-                             bool boxes = false)
+                             bool boxes = false, bool drone = false)
       : G(G_), A(A_), S(S_) {
     NP = (A + 1) / 2;
     nbuf = bwd ? (S > 2 ? S : 2) : 2;
@@ -119,6 +132,8 @@ template <typename T> struct Layout {
     // box worlds: every agent's (heading, turn rate) per buffer and (box, hx, hy) once
     thw = boxes ? take(size_t(nbuf) * GA * 2 * sizeof(T)) : 0;
     shp = boxes ? take(size_t(GA) * 4 * sizeof(T)) : 0;
+    // drone worlds, adjoint: every substep's drone state of the recomputed chain
+    dro = (bwd && drone) ? take(size_t(S) * GA * sizeof(Drone<T>)) : 0;
     total = off;
   }
 };
@@ -146,6 +161,13 @@ __device__ __forceinline__ void load_params(const RolloutArgs<T>& R, int e, int 
   P.box = row[17] > T(0.5);
   P.hx = row[18];
   P.hy = row[19];
+  P.tmax = row[9];
+  P.arm = row[10];
+  P.ixx = row[11];
+  P.iyy = row[12];
+  P.izz = row[13];
+  P.kappa = row[14];
+  P.grav = row[15];
 }
 
 template <typename T>
@@ -214,6 +236,60 @@ __device__ __forceinline__ void load_action(const RolloutArgs<T>& R, long long i
   } else {
     a0 = R.act[i * R.act_dim];
     a1 = R.act[i * R.act_dim + 1];
+  }
+}
+
+// Action slots 2 and 3 (a drone's rotors 2, 3); zero past act_dim (kernels.py:797-810).
+template <typename T>
+__device__ __forceinline__ void load_action23(const RolloutArgs<T>& R, long long i, T& a2, T& a3) {
+  a2 = R.act_dim > 2 ? R.act[i * R.act_dim + 2] : T(0);
+  a3 = R.act_dim > 3 ? R.act[i * R.act_dim + 3] : T(0);
+}
+
+template <typename T>
+__device__ __forceinline__ void load_drone(const DroneF<const T>& F, long long i, Drone<T>& d) {
+  d.z = F.z[i];
+  d.vz = F.vz[i];
+  d.qx = F.att[4 * i];
+  d.qy = F.att[4 * i + 1];
+  d.qz = F.att[4 * i + 2];
+  d.qw = F.att[4 * i + 3];
+  d.bx = F.br[3 * i];
+  d.by = F.br[3 * i + 1];
+  d.bz = F.br[3 * i + 2];
+}
+template <typename T>
+__device__ __forceinline__ void load_drone(const DroneF<T>& F, long long i, Drone<T>& d) {
+  load_drone(DroneF<const T>{F.z, F.vz, F.att, F.br}, i, d);
+}
+template <typename T>
+__device__ __forceinline__ void store_drone(const DroneF<T>& F, long long i, const Drone<T>& d) {
+  F.z[i] = d.z;
+  F.vz[i] = d.vz;
+  F.att[4 * i] = d.qx;
+  F.att[4 * i + 1] = d.qy;
+  F.att[4 * i + 2] = d.qz;
+  F.att[4 * i + 3] = d.qw;
+  F.br[3 * i] = d.bx;
+  F.br[3 * i + 1] = d.by;
+  F.br[3 * i + 2] = d.bz;
+}
+// Cotangent fields may be absent (NULL = zero), each array on its own.
+template <typename T>
+__device__ __forceinline__ void add_drone_cotangent(const DroneF<const T>& F, long long i,
+                                                    Drone<T>& g) {
+  if (F.z) g.z += F.z[i];
+  if (F.vz) g.vz += F.vz[i];
+  if (F.att) {
+    g.qx += F.att[4 * i];
+    g.qy += F.att[4 * i + 1];
+    g.qz += F.att[4 * i + 2];
+    g.qw += F.att[4 * i + 3];
+  }
+  if (F.br) {
+    g.bx += F.br[3 * i];
+    g.by += F.br[3 * i + 1];
+    g.bz += F.br[3 * i + 2];
   }
 }
 
@@ -585,6 +661,62 @@ __device__ __forceinline__ void integrate_vjp_sel(const Agent<T>& in, T a0, T a1
     integrate_vjp<T, kBox>(in, a0, a1, out, g, Q, W, gin, gfx, gfy, ga0, ga1);
 }
 
+// Drone worlds: a drone agent takes the 6-DOF substep (rotor slots a0..a3, the servo
+// rewrite of slots 0/1 first, as the reference's kernels apply it to every SERVO agent),
+// every other agent its 2-D model with the drone fields passed through.
+template <typename T, int FL>
+__device__ __forceinline__ void integrate_drone_sel(const Agent<T>& in, const Drone<T>& d, T a0,
+                                                    T a1, T a2, T a3, T fx, T fy,
+                                                    const AgentP<T>& P, const WorldC<T>& W,
+                                                    Agent<T>& out, Drone<T>& dout) {
+  if (P.tag != TAG_DRONE) {
+    integrate_sel<T, FL>(in, a0, a1, fx, fy, P, W, out);
+    dout = d;
+    return;
+  }
+  T a[4] = {a0, a1, a2, a3};
+  if (P.mode == MODE_SERVO) servo_cmd(a0, a1, in.s, in.w, P, W.dt, a[0], a[1]);
+  if (FL & F_RK4)
+    drone_rk4_fwd(in, d, a, fx, fy, P, W, out, dout);
+  else
+    drone_euler_fwd(in, d, a, fx, fy, P, W, out, dout);
+}
+
+// Adjoint of integrate_drone_sel; same contract as integrate_vjp_sel, plus the drone
+// fields' cotangents (gd in, gdin out) and the action slots 2, 3 (ga2, ga3 added).
+template <typename T, int FL>
+__device__ __forceinline__ void integrate_vjp_drone_sel(const Agent<T>& in, const Drone<T>& d,
+                                                        T a0, T a1, T a2, T a3,
+                                                        const Agent<T>& out, const Agent<T>& g,
+                                                        const Drone<T>& gd, const AgentP<T>& P,
+                                                        const WorldC<T>& W, Agent<T>& gin,
+                                                        Drone<T>& gdin, T& gfx, T& gfy, T& ga0,
+                                                        T& ga1, T& ga2, T& ga3) {
+  if (P.tag != TAG_DRONE) {
+    integrate_vjp_sel<T, FL>(in, a0, a1, out, g, P, W, gin, gfx, gfy, ga0, ga1);
+    gdin = gd;
+    return;
+  }
+  T ac[4] = {a0, a1, a2, a3};
+  const bool servo = P.mode == MODE_SERVO;
+  if (servo) servo_cmd(a0, a1, in.s, in.w, P, W.dt, ac[0], ac[1]);
+  T gac[4] = {T(0), T(0), T(0), T(0)};
+  gfx = T(0);
+  gfy = T(0);
+  if (FL & F_RK4)
+    drone_rk4_vjp(in, d, ac, out, g, gd, P, W, gin, gdin, gfx, gfy, gac);
+  else
+    drone_euler_vjp(in, d, ac, out, g, gd, P, W, gin, gdin, gfx, gfy, gac);
+  if (servo) {
+    servo_cmd_vjp(a0, a1, in.s, in.w, P, W.dt, gac[0], gac[1], ga0, ga1, gin.s, gin.w);
+  } else {
+    ga0 += gac[0];
+    ga1 += gac[1];
+  }
+  ga2 += gac[2];
+  ga3 += gac[3];
+}
+
 // Pad slot of an odd-sized env: never within any radius.
 template <typename T>
 __device__ __forceinline__ void init_pads(T* xy, int nbuf, int G, int A) {
@@ -648,10 +780,15 @@ __global__ void __launch_bounds__(1024) rollout_fwd_kernel(const RolloutArgs<T> 
   const long long EA = (long long)R.E * A;
   Agent<T> x;
   load_state(R.i_pos, R.i_th, R.i_vel, R.i_s, R.i_w, ia, x);
+  constexpr bool kDrone = (FL & F_DRONE) != 0;
+  Drone<T> xd{};
+  if (kDrone) load_drone(R.i_d, ia, xd);
   int tmax = 0;
   int buf = 0;
   T a0, a1, n0 = T(0), n1 = T(0);
+  T a2 = T(0), a3 = T(0), n2 = T(0), n3 = T(0);  // drone rotor slots
   load_action(R, ia, a0, a1);
+  if (kDrone) load_action23(R, ia, a2, a3);
   const T* rad_env = srad + le * A;
   const T* iden_env = siden + le * A;
   Obs<T>* obs_env = sobs + le * N;
@@ -660,6 +797,7 @@ __global__ void __launch_bounds__(1024) rollout_fwd_kernel(const RolloutArgs<T> 
 #pragma unroll 4
   for (int t = 0; t < R.H; ++t) {
     if (t + 1 < R.H) load_action(R, (long long)(t + 1) * EA + ia, n0, n1);
+    if (kDrone && t + 1 < R.H) load_action23(R, (long long)(t + 1) * EA + ia, n2, n3);
     for (int k = 0; k < R.S; ++k) {
       T fx = T(0), fy = T(0);
       T* xy_env = sxy + (buf * G + le) * NP4;
@@ -694,18 +832,28 @@ __global__ void __launch_bounds__(1024) rollout_fwd_kernel(const RolloutArgs<T> 
       }
       if (kShare) buf ^= 1;
       Agent<T> y;
-      integrate_sel<T, FL>(x, a0, a1, fx, fy, P, W, y);
+      if (kDrone) {
+        Drone<T> yd;
+        integrate_drone_sel<T, FL>(x, xd, a0, a1, a2, a3, fx, fy, P, W, y, yd);
+        xd = yd;
+      } else {
+        integrate_sel<T, FL>(x, a0, a1, fx, fy, P, W, y);
+      }
       x = y;
     }
     if (valid) store_state(R.t_pos, R.t_th, R.t_vel, R.t_s, R.t_w, (long long)t * EA + ia, x);
+    if (kDrone && valid) store_drone(R.t_d, (long long)t * EA + ia, xd);
     if (kBodies && a == 0 && valid)
       store_bodies(R.bt_pos, R.bt_ang, R.bt_vel, R.bt_om, ((long long)t * R.E + e) * N, N,
                    sbst + le * N);
     a0 = n0;
     a1 = n1;
+    a2 = n2;
+    a3 = n3;
   }
   if (valid) {
     if (R.f_pos) store_state(R.f_pos, R.f_th, R.f_vel, R.f_s, R.f_w, ia, x);
+    if (kDrone && R.f_d.z) store_drone(R.f_d, ia, xd);
     if (R.true_max) R.true_max[ia] = tmax;
   }
 }
@@ -909,9 +1057,11 @@ __global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : 1024)
   const int e = e0 + le;
   const bool valid = e < R.E;
   const int ec = valid ? e : R.E - 1;
-  const Layout<T> L(G, A, N, S, true, kBodies, kBoxes);
+  constexpr bool kDrone = (FL & F_DRONE) != 0;
+  const Layout<T> L(G, A, N, S, true, kBodies, kBoxes, kDrone);
   T2* sthw = reinterpret_cast<T2*>(smem + L.thw);  // [nbuf][GA] (th, w), box worlds
   T4* sshp = reinterpret_cast<T4*>(smem + L.shp);  // [GA] (box, hx, hy, -)
+  Drone<T>* sdro = reinterpret_cast<Drone<T>*>(smem + L.dro);  // [S][GA], drone worlds
   const int NP4 = L.NP * 4;
   T* sxy = reinterpret_cast<T*>(smem + L.xy);       // [nbuf][G][NP*4] scan tables
   T4* srec = reinterpret_cast<T4*>(smem + L.rec);   // [nbuf][GA] (x, y, vx, vy)
@@ -964,9 +1114,12 @@ __global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : 1024)
   Obs<T>* obs_env = sobs + le * N;
   const T4* shp_env = sshp + le * A;
   const bool has_gt = R.gt_pos || R.gt_th || R.gt_vel || R.gt_s || R.gt_w;
+  const bool has_gtd = kDrone && (R.gt_d.z || R.gt_d.vz || R.gt_d.att || R.gt_d.br);
 
   Agent<T> g{};
   add_cotangent(R.gf_pos, R.gf_th, R.gf_vel, R.gf_s, R.gf_w, ia, g);
+  Drone<T> gd{};  // cotangent of the drone fields
+  if (kDrone) add_drone_cotangent(R.gf_d, ia, gd);
   // One-substep holonomic velocity fleets without bodies: the step's adjoint reads only the
   // positions and velocities of its input and output states (heading passes through,
   // speed is recomputed from the velocity), so the other three fields are not loaded.
@@ -994,13 +1147,24 @@ __global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : 1024)
   else
     load_init(cur);
   load_action(R, (long long)(H - 1) * EA + ia, a0, a1);
+  Drone<T> curd{};
+  T a2 = T(0), a3 = T(0);
+  if (kDrone) {
+    if (H > 1)
+      load_drone(R.t_d, (long long)(H - 2) * EA + ia, curd);
+    else
+      load_drone(R.i_d, ia, curd);
+    load_action23(R, (long long)(H - 1) * EA + ia, a2, a3);
+  }
   if ((FL & F_MASK) && S == 1) cm0 = R.cmask[(long long)(H - 1) * EA + ia];
   int fbuf = 0;
   T gsq = T(0);  // this agent's sum over the horizon of ||d loss / d action||^2
   for (int t = H - 1; t >= 0; --t) {
     if (has_gt) add_cotangent(R.gt_pos, R.gt_th, R.gt_vel, R.gt_s, R.gt_w, (long long)t * EA + ia, g);
+    if (has_gtd) add_drone_cotangent(R.gt_d, (long long)t * EA + ia, gd);
     Agent<T> pcur{};
-    T pa0 = T(0), pa1 = T(0);
+    Drone<T> pcurd{};
+    T pa0 = T(0), pa1 = T(0), pa2 = T(0), pa3 = T(0);
     unsigned pcm = 0u;
     if (t > 0) {
       if (t > 1)
@@ -1008,14 +1172,28 @@ __global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : 1024)
       else
         load_init(pcur);
       load_action(R, (long long)(t - 1) * EA + ia, pa0, pa1);
+      if (kDrone) {
+        if (t > 1)
+          load_drone(R.t_d, (long long)(t - 2) * EA + ia, pcurd);
+        else
+          load_drone(R.i_d, ia, pcurd);
+        load_action23(R, (long long)(t - 1) * EA + ia, pa2, pa3);
+      }
       if ((FL & F_MASK) && S == 1) pcm = R.cmask[(long long)(t - 1) * EA + ia];
     }
-    T ga0 = T(0), ga1 = T(0);
+    T ga0 = T(0), ga1 = T(0), ga2 = T(0), ga3 = T(0);
 
     if (S == 1 && !kBodies) {
       Agent<T> gin;
       T gfx, gfy;
-      integrate_vjp_sel<T, FL>(cur, a0, a1, nxt, g, P, W, gin, gfx, gfy, ga0, ga1);
+      if (kDrone) {
+        Drone<T> gdin;
+        integrate_vjp_drone_sel<T, FL>(cur, curd, a0, a1, a2, a3, nxt, g, gd, P, W, gin, gdin, gfx,
+                                       gfy, ga0, ga1, ga2, ga3);
+        gd = gdin;
+      } else {
+        integrate_vjp_sel<T, FL>(cur, a0, a1, nxt, g, P, W, gin, gfx, gfy, ga0, ga1);
+      }
       T* xy_env = sxy + (fbuf * G + le) * NP4;
       T4* rec_env = srec + fbuf * GA + le * A;
       T2* fb_env = sfb + fbuf * GA + le * A;
@@ -1049,11 +1227,13 @@ __global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : 1024)
         set_body_poses(R, ec, t == 0 && !R.poses_from_bodies, b0, sbc, obs_env);
       }
       Agent<T> x = cur;
+      Drone<T> xd = curd;
       for (int k = 0; k < S; ++k) {
         T* xy_env = sxy + (k * G + le) * NP4;
         T4* rec_env = srec + k * GA + le * A;
         if (kScan) put_xy(xy_env, a, x.px, x.py);
         rec_env[a] = T4{x.px, x.py, x.vx, x.vy};
+        if (kDrone) sdro[size_t(k) * GA + tid] = xd;
         if (kBoxes) sthw[k * GA + le * A + a] = T2{x.th, x.w};
         T* ow = sown + (size_t(k) * GA + tid) * 4;
         ow[0] = x.th;
@@ -1089,7 +1269,13 @@ __global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : 1024)
                         rec_env, rad_env, iden_env, A, W, R.body_clamp != 0);
         }
         Agent<T> y;
-        integrate_sel<T, FL>(x, a0, a1, fx, fy, P, W, y);
+        if (kDrone) {
+          Drone<T> yd;
+          integrate_drone_sel<T, FL>(x, xd, a0, a1, a2, a3, fx, fy, P, W, y, yd);
+          xd = yd;
+        } else {
+          integrate_sel<T, FL>(x, a0, a1, fx, fy, P, W, y);
+        }
         x = y;
       }
       Agent<T> out = nxt;
@@ -1104,7 +1290,14 @@ __global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : 1024)
         Agent<T> in{rr.x, rr.y, ow[0], rr.z, rr.w, ow[1], ow[2]};
         Agent<T> gin;
         T gfx, gfy;
-        integrate_vjp_sel<T, FL>(in, a0, a1, out, g, P, W, gin, gfx, gfy, ga0, ga1);
+        if (kDrone) {
+          Drone<T> gdin;
+          integrate_vjp_drone_sel<T, FL>(in, sdro[size_t(k) * GA + tid], a0, a1, a2, a3, out, g, gd,
+                                         P, W, gin, gdin, gfx, gfy, ga0, ga1, ga2, ga3);
+          gd = gdin;
+        } else {
+          integrate_vjp_sel<T, FL>(in, a0, a1, out, g, P, W, gin, gfx, gfy, ga0, ga1);
+        }
         T2* fb_env = sfb + fbuf * GA + le * A;
         int* cut_env = scut + fbuf * GA + le * A;
         fb_env[a] = T2{gfx, gfy};
@@ -1141,21 +1334,29 @@ __global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : 1024)
     if (valid) {
       const long long ja = (long long)t * EA + ia;
       gsq = Num<T>::fma_(ga0, ga0, Num<T>::fma_(ga1, ga1, gsq));
+      if (kDrone) gsq = Num<T>::fma_(ga2, ga2, Num<T>::fma_(ga3, ga3, gsq));
       if (R.act_dim == 2) {
         reinterpret_cast<T2*>(R.g_act)[ja] = T2{ga0, ga1};
       } else {
         R.g_act[ja * R.act_dim] = ga0;
         R.g_act[ja * R.act_dim + 1] = ga1;
-        for (int j = 2; j < R.act_dim; ++j) R.g_act[ja * R.act_dim + j] = T(0);
+        for (int j = 2; j < R.act_dim; ++j)
+          R.g_act[ja * R.act_dim + j] = (kDrone && j == 2) ? ga2 : ((kDrone && j == 3) ? ga3 : T(0));
       }
     }
     nxt = cur;
     cur = pcur;
     a0 = pa0;
     a1 = pa1;
+    if (kDrone) {
+      curd = pcurd;
+      a2 = pa2;
+      a3 = pa3;
+    }
     cm0 = pcm;
   }
   if (valid) store_state(R.gi_pos, R.gi_th, R.gi_vel, R.gi_s, R.gi_w, ia, g);
+  if (kDrone && valid) store_drone(R.gi_d, ia, gd);
   if (R.gsq_partial) block_sum_store(gsq, R.gsq_partial + blockIdx.x);
 }
 

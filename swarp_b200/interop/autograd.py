@@ -96,16 +96,18 @@ class BodyState(NamedTuple):
 
 
 class _RolloutFn(torch.autograd.Function):
-    """``(actions [T,E,A,D], five state tensors) -> (final five, trajectory five [T,...],
-    final body state four)``; the body outputs are empty when no body moves."""
+    """``(actions [T,E,A,D], n state tensors) -> (final n, trajectory n [T,...], final body
+    state four)`` with n = ``stepper.n_state`` (five, nine with the drone fields); the body
+    outputs are empty when no body moves."""
 
     @staticmethod
-    def forward(ctx, stepper: Stepper, moving: bool, actions, pos, theta, vel, speed, ang_vel):
-        state5 = tuple(t.contiguous() for t in (pos, theta, vel, speed, ang_vel))
+    def forward(ctx, stepper: Stepper, moving: bool, actions, *state):
+        state5 = tuple(t.contiguous() for t in state)
         acts = actions.contiguous()
         traj, fin, _, rec = stepper.rollout_forward(state5, acts, final=True, moving_bodies=moving)
         ctx.stepper = stepper
         ctx.rec = rec
+        ctx.n = len(state5)
         ctx.set_materialize_grads(False)
         ctx.save_for_backward(acts, *state5, *traj)
         if rec.moving:
@@ -118,10 +120,12 @@ class _RolloutFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, *grads):
         acts, *rest = ctx.saved_tensors
-        state5, traj5 = tuple(rest[:5]), tuple(rest[5:10])
-        gfin = tuple(None if g is None else g.contiguous() for g in grads[:5])
-        gtraj = tuple(None if g is None else g.contiguous() for g in grads[5:10])
-        gbody = grads[10:14] if ctx.rec.moving and any(g is not None for g in grads[10:14]) else None
+        n = ctx.n
+        state5, traj5 = tuple(rest[:n]), tuple(rest[n:2 * n])
+        gfin = tuple(None if g is None else g.contiguous() for g in grads[:n])
+        gtraj = tuple(None if g is None else g.contiguous() for g in grads[n:2 * n])
+        gb = grads[2 * n:2 * n + 4]
+        gbody = gb if ctx.rec.moving and any(g is not None for g in gb) else None
         g_act, g_init = ctx.stepper.rollout_backward(state5, acts, traj5, gtraj, gfin, ctx.rec,
                                                      gbody_final=gbody)
         return (None, None, g_act, *g_init)
@@ -129,18 +133,19 @@ class _RolloutFn(torch.autograd.Function):
 
 def _run(stepper: Stepper, state: TorchState, actions_seq: torch.Tensor):
     state = fill_state_defaults(state)
-    core = tuple(state[:5])
+    n = stepper.n_state
+    core = tuple(state[:n])
     stepper._check_inputs(core, actions_seq, horizon_dim=True)
     grad_mode = torch.is_grad_enabled() and (
         actions_seq.requires_grad or any(t.requires_grad for t in core)
     )
-    extra = tuple(state[5:])
+    extra = tuple(state[n:])
     # Reference rule: movable bodies advance on untaped steps; on taped ones only when
     # the stepper opts in (bodies_in_grad), which also makes them differentiable.
     moving = stepper.any_movable and (not grad_mode or stepper.bodies_in_grad)
     if grad_mode:
         out = _RolloutFn.apply(stepper, moving, actions_seq, *core)
-        fin, traj, body = out[:5], out[5:10], out[10:14]
+        fin, traj, body = out[:n], out[n:2 * n], out[2 * n:2 * n + 4]
     else:
         with torch.no_grad():
             core_c = tuple(t.contiguous() for t in core)

@@ -46,6 +46,9 @@ class GraphedRollout:
             raise NotImplementedError(
                 "GraphedRollout does not capture movable bodies: their state advances on the "
                 "host side between rollouts; use rollout_bodies eagerly")
+        if stepper.has_drones:
+            raise NotImplementedError("GraphedRollout captures 2-D fleets; run a fleet with "
+                                      "drones through rollout eagerly")
         dev = stepper.device
         self.stepper = stepper
         self.loss_fn = loss_fn

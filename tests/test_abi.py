@@ -42,7 +42,7 @@ def test_error_strings_and_version(lib):
     lib.swarp_error_string.restype = C.c_char_p
     assert lib.swarp_error_string(0) == b"ok"
     assert b"unsupported" in lib.swarp_error_string(-2)
-    assert lib.swarp_abi_version() == 5
+    assert lib.swarp_abi_version() == 6
 
 
 def test_invalid_world_is_rejected_without_a_gpu(lib):
@@ -60,10 +60,14 @@ def test_invalid_world_is_rejected_without_a_gpu(lib):
     assert rc == -1
     w.dtype, w.n_envs, w.n_agents, w.act_dim, w.substeps, w.dt = 0, 2, 3, 2, 1, 0.1
     w.params, w.model_tag, w.ctrl_mode = 8, 8, 8  # non-null placeholders, never dereferenced
-    w.fleet_models, w.fleet_modes = 1 << 3, 1  # a drone fleet
+    w.fleet_models, w.fleet_modes = 1 << 4, 1  # an unknown model tag
     rc = fwd(C.byref(w), 4, _lib.State(), None, _lib.State(), _lib.State(), None, _lib.Bodies(),
              _lib.Bodies(), None, 0, None)
     assert rc == -2
+    w.fleet_models = 1 << 3  # a drone fleet without its drone state fields
+    rc = fwd(C.byref(w), 4, _lib.State(), None, _lib.State(), _lib.State(), None, _lib.Bodies(),
+             _lib.Bodies(), None, 0, None)
+    assert rc == -1
     w.fleet_models = 1
     w.n_agents = 5000
     rc = fwd(C.byref(w), 4, _lib.State(), None, _lib.State(), _lib.State(), None, _lib.Bodies(),
@@ -87,7 +91,7 @@ int main(void) {
   F(swarp_world_t, obstacles); F(swarp_obstacles_t, pos); F(swarp_obstacles_t, any_movable);
   F(swarp_obstacles_t, bodies_move); F(swarp_obstacles_t, movable_shapes);
   F(swarp_obstacles_t, poses_from_bodies); F(swarp_world_t, integrator);
-  F(swarp_world_t, box_agents);
+  F(swarp_world_t, box_agents); F(swarp_state_t, z); F(swarp_state_t, body_rates);
   return 0;
 }
 """
@@ -109,5 +113,5 @@ def test_ctypes_layout_matches_c(tmp_path):
         if "." not in key:
             continue
         struct, field = key.split(".")
-        cls = _lib.WorldC if struct == "swarp_world_t" else _lib.ObstaclesC
+        cls = {"swarp_world_t": _lib.WorldC, "swarp_state_t": _lib.State}.get(struct, _lib.ObstaclesC)
         assert getattr(cls, field).offset == int(val), key
