@@ -88,6 +88,9 @@ __device__ __forceinline__ ObbContact<T> obb_contact(const Ob<T>& A, const Ob<T>
   } else if (r.s > T(0)) {
     r.branch = 1;
     T best = T(1.0e30);
+    // unrolled, so that which box is `own` is known at compile time (a reference chosen at
+    // run time would put both boxes in local memory)
+#pragma unroll
     for (int v = 0; v < 8; ++v) {
       const Ob<T>& own = v < 4 ? A : B;
       const Ob<T>& other = v < 4 ? B : A;
@@ -122,10 +125,10 @@ __device__ __forceinline__ ObbContact<T> obb_contact(const Ob<T>& A, const Ob<T>
     r.nx = ux * sgn;
     r.ny = uy * sgn;
     const bool bref = r.axis >= 2;
-    const Ob<T>& ref = bref ? B : A;
-    const Ob<T>& inc = bref ? A : B;
+    const T rcx = bref ? B.cx : A.cx, rcy = bref ? B.cy : A.cy;  // reference box centre
+    const T icx = bref ? A.cx : B.cx, icy = bref ? A.cy : B.cy;  // incident box centre
     const T xn = bref ? (B.cx * r.nx + B.cy * r.ny) + hn : (A.cx * r.nx + A.cy * r.ny) - hn;
-    const T ct_ref = ref.cx * tx + ref.cy * ty, ct_inc = inc.cx * tx + inc.cy * ty;
+    const T ct_ref = rcx * tx + rcy * ty, ct_inc = icx * tx + icy * ty;
     const T lo = wmax(ct_ref - ht, ct_inc - rt), hi = wmin(ct_ref + ht, ct_inc + rt);
     const T mid = T(0.5) * (lo + hi);
     r.px = r.nx * xn + tx * mid;
@@ -173,6 +176,14 @@ __device__ __forceinline__ bool pair_force_shaped(int a, int b, bool box_a, cons
     return pair_force_add(dx, dy, dot2(dx, dy, dx, dy), oa.vx - ob.vx, oa.vy - ob.vy,
                           ra + rb + W.margin, inv_denom, W, fx, fy);
   }
+  // Broad phase: a box lies within its circumradius of its centre, so centres farther apart
+  // than the two bounds plus the contact reach cannot touch (the exact test below would find
+  // no overlap; the same slack as bounds_apart keeps every borderline pair).
+  const T bnd_a = box_a ? norm2(oa.hx, oa.hy) : ra, bnd_b = box_b ? norm2(ob.hx, ob.hy) : rb;
+  const T reach = box_a && box_b ? W.margin : (box_a ? rb : ra) + W.margin;
+  if (bounds_apart(oa.cx - ob.cx, oa.cy - ob.cy, (box_a ? bnd_a : T(0)) + (box_b ? bnd_b : T(0)) +
+                                                     reach))
+    return false;
   T gx, gy;
   bool on;
   if (!box_a) {

@@ -246,8 +246,8 @@ __device__ __forceinline__ void obb_geom_dual(const ObbD<T>& A, const ObbD<T>& B
   using D = Dual<T, 3>;
   if (c.branch == 1) {
     const bool ownA = c.vert < 4;
-    const ObbD<T>& own = ownA ? A : B;
-    const ObbD<T>& oth = ownA ? B : A;
+    const ObbD<T> own = ownA ? A : B;  // values, not a run-time reference (local memory)
+    const ObbD<T> oth = ownA ? B : A;
     const T flip = ownA ? T(1) : T(-1);
     const int v = c.vert & 3;
     const D e0x = own.ca * own.hx, e0y = own.sa * own.hx;
@@ -313,10 +313,10 @@ __device__ __forceinline__ void obb_geom_dual(const ObbD<T>& A, const ObbD<T>& B
   nx = ux * sgn;
   ny = uy * sgn;
   const bool bref = c.axis >= 2;
-  const ObbD<T>& ref = bref ? B : A;
-  const ObbD<T>& inc = bref ? A : B;
+  const D rcx = bref ? B.cx : A.cx, rcy = bref ? B.cy : A.cy;
+  const D icx = bref ? A.cx : B.cx, icy = bref ? A.cy : B.cy;
   const D xn = bref ? (B.cx * nx + B.cy * ny) + hn : (A.cx * nx + A.cy * ny) - hn;
-  const D ct_ref = ref.cx * tx + ref.cy * ty, ct_inc = inc.cx * tx + inc.cy * ty;
+  const D ct_ref = rcx * tx + rcy * ty, ct_inc = icx * tx + icy * ty;
   const D lo = dmax(ct_ref - ht, ct_inc - rt), hi = dmin(ct_ref + ht, ct_inc + rt);
   const D mid = T(0.5) * (lo + hi);
   px = nx * xn + tx * mid;
@@ -427,7 +427,14 @@ __device__ __forceinline__ void pair_shaped_vjp(int a, int b, bool box_a, const 
   if (!box_a && !box_b) {
     pair_vjp_sym(oa.cx - ob.cx, oa.cy - ob.cy, oa.vx - ob.vx, oa.vy - ob.vy, ra + rb + W.margin,
                  ida, gax, gay, idb, gbx, gby, W, gin.px, gin.py, gin.vx, gin.vy);
-  } else if (!box_a) {
+    return;
+  }
+  // the forward's broad phase (pair_force_shaped): such pairs carry no force
+  const T reach = box_a && box_b ? W.margin : (box_a ? rb : ra) + W.margin;
+  if (bounds_apart(oa.cx - ob.cx, oa.cy - ob.cy, (box_a ? norm2(oa.hx, oa.hy) : T(0)) +
+                                                     (box_b ? norm2(ob.hx, ob.hy) : T(0)) + reach))
+    return;
+  if (!box_a) {
     sdf_contact_vjp(oa.cx, oa.cy, oa.vx, oa.vy, ob, thb, true, ra + W.margin, ida, gax, gay, idb,
                     gbx, gby, W, gin);
   } else if (!box_b) {

@@ -183,7 +183,7 @@ def test_warp_step_and_default_drone_fields():
     acts = torch.full((2, 3, 4), HOVER, dtype=D, device=DEV)
     out = warp_step(st, s5, acts)
     assert out.z.shape == (2, 3) and out.attitude.shape == (2, 3, 4)
-    ref = R.step(tuple(t.cpu() for t in (*s5, torch.zeros(2, 3, device=DEV, dtype=D),
+    ref = R.step(tuple(t.cpu() for t in (*tuple(s5)[:5], torch.zeros(2, 3, device=DEV, dtype=D),
                                          torch.zeros(2, 3, device=DEV, dtype=D),
                                          torch.tensor([0, 0, 0, 1.0], dtype=D, device=DEV).expand(2, 3, 4),
                                          torch.zeros(2, 3, 3, device=DEV, dtype=D))),
