@@ -60,7 +60,7 @@ __device__ __forceinline__ void box_vertex(const Ob<T>& b, int v, T& x, T& y) {
 }
 
 template <typename T>
-__device__ __forceinline__ ObbContact<T> obb_contact(const Ob<T>& A, const Ob<T>& B, T reach) {
+__device__ __noinline__ ObbContact<T> obb_contact(const Ob<T>& A, const Ob<T>& B, T reach) {
   const T dx = A.cx - B.cx, dy = A.cy - B.cy;
   // unit axes: uA0 = (caA, saA), uA1 = (-saA, caA), likewise B
   const T a00 = fabs(A.ca * B.ca + A.sa * B.sa);
@@ -88,25 +88,26 @@ __device__ __forceinline__ ObbContact<T> obb_contact(const Ob<T>& A, const Ob<T>
   } else if (r.s > T(0)) {
     r.branch = 1;
     T best = T(1.0e30);
-    // unrolled, so that which box is `own` is known at compile time (a reference chosen at
-    // run time would put both boxes in local memory)
-#pragma unroll
-    for (int v = 0; v < 8; ++v) {
-      const Ob<T>& own = v < 4 ? A : B;
-      const Ob<T>& other = v < 4 ? B : A;
-      const T flip = v < 4 ? T(1) : T(-1);
-      T vx, vy, qx, qy;
-      box_vertex(own, v & 3, vx, vy);
-      const T dist = point_box(vx, vy, other, qx, qy);
-      if (dist < best) {
-        best = dist;
-        r.nx = (vx - qx) * (flip / dist);
-        r.ny = (vy - qy) * (flip / dist);
-        r.px = (vx + qx) * T(0.5);
-        r.py = (vy + qy) * T(0.5);
-        r.vert = v;
+    // the vertices of A against B, then of B against A (two loops, so that which box
+    // owns the vertex is known at compile time)
+    auto scan = [&](const Ob<T>& own, const Ob<T>& other, T flip, int v0) {
+#pragma unroll 1
+      for (int v = 0; v < 4; ++v) {
+        T vx, vy, qx, qy;
+        box_vertex(own, v, vx, vy);
+        const T dist = point_box(vx, vy, other, qx, qy);
+        if (dist < best) {
+          best = dist;
+          r.nx = (vx - qx) * (flip / dist);
+          r.ny = (vy - qy) * (flip / dist);
+          r.px = (vx + qx) * T(0.5);
+          r.py = (vy + qy) * T(0.5);
+          r.vert = v0 + v;
+        }
       }
-    }
+    };
+    scan(A, B, T(1), 0);
+    scan(B, A, T(-1), 4);
     r.s = best;
   } else {
     r.branch = 2;
@@ -140,7 +141,7 @@ __device__ __forceinline__ ObbContact<T> obb_contact(const Ob<T>& A, const Ob<T>
 // Force on box A from box B (spring-damper along the contact normal, damped by the two
 // material points' closing velocity at the contact point). Returns whether in contact.
 template <typename T>
-__device__ __forceinline__ bool obb_force(const Ob<T>& A, const Ob<T>& B, T reach, T inv_denom,
+__device__ __noinline__ bool obb_force(const Ob<T>& A, const Ob<T>& B, T reach, T inv_denom,
                                           const WorldC<T>& W, T& fx, T& fy) {
   const ObbContact<T> c = obb_contact(A, B, reach);
   fx = T(0);
@@ -154,6 +155,15 @@ __device__ __forceinline__ bool obb_force(const Ob<T>& A, const Ob<T>& B, T reac
   fx = cf * c.nx;
   fy = cf * c.ny;
   return true;
+}
+
+// box_force for agent pairs, kept out of line: the box paths are the cold, large part of
+// a box world's contact pass, and one copy of their code per kernel keeps the hot loop in
+// the instruction cache.
+template <typename T>
+__device__ __noinline__ bool box_force_pair(T px, T py, T vx, T vy, const Obs<T>& o, T reach,
+                                            T inv_denom, const WorldC<T>& W, T& fx, T& fy) {
+  return box_force(px, py, vx, vy, o, reach, inv_denom, W, fx, fy);
 }
 
 // Obs (the SDF law's box description) of an agent box.
@@ -187,9 +197,9 @@ __device__ __forceinline__ bool pair_force_shaped(int a, int b, bool box_a, cons
   T gx, gy;
   bool on;
   if (!box_a) {
-    on = box_force(oa.cx, oa.cy, oa.vx, oa.vy, obs_of(ob), ra + W.margin, inv_denom, W, gx, gy);
+    on = box_force_pair(oa.cx, oa.cy, oa.vx, oa.vy, obs_of(ob), ra + W.margin, inv_denom, W, gx, gy);
   } else if (!box_b) {
-    on = box_force(ob.cx, ob.cy, ob.vx, ob.vy, obs_of(oa), rb + W.margin, inv_denom, W, gx, gy);
+    on = box_force_pair(ob.cx, ob.cy, ob.vx, ob.vy, obs_of(oa), rb + W.margin, inv_denom, W, gx, gy);
     gx = -gx;
     gy = -gy;
   } else if (a < b) {
@@ -206,7 +216,7 @@ __device__ __forceinline__ bool pair_force_shaped(int a, int b, bool box_a, cons
 
 // Obstacles and walls on a box agent (collisions.py:540-690), obstacles first.
 template <typename T>
-__device__ __forceinline__ void box_static_force(const Obs<T>* sobs, int N, bool walls,
+__device__ __noinline__ void box_static_force(const Obs<T>* sobs, int N, bool walls,
                                                  const Ob<T>& oa, T inv_denom,
                                                  const WorldC<T>& W, T& fx, T& fy) {
   T sx = T(0), sy = T(0);

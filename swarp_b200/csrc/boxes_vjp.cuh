@@ -327,7 +327,7 @@ __device__ __forceinline__ void obb_geom_dual(const ObbD<T>& A, const ObbD<T>& B
 // gA/gB their cotangents) into the own box's state gradient (own = A or B; the other
 // box's state is constant). thA/thB are the headings the Ob poses were built from.
 template <typename T>
-__device__ __forceinline__ void obb_contact_vjp(const Ob<T>& A, T thA, const Ob<T>& B, T thB,
+__device__ __noinline__ void obb_contact_vjp(const Ob<T>& A, T thA, const Ob<T>& B, T thB,
                                                 bool ownA, T reach, T idA, T gAx, T gAy, T idB,
                                                 T gBx, T gBy, const WorldC<T>& W,
                                                 Agent<T>& gin) {
@@ -359,7 +359,7 @@ __device__ __forceinline__ void obb_contact_vjp(const Ob<T>& A, T thA, const Ob<
 // obstacle's) against box B (force cf_P n on the point, -cf_B n on the box); own = the
 // point (its position and velocity are variables 0, 1, 3, 4) or the box (all six).
 template <typename T>
-__device__ __forceinline__ void sdf_contact_vjp(T ppx, T ppy, T pvx, T pvy, const Ob<T>& B,
+__device__ __noinline__ void sdf_contact_vjp(T ppx, T ppy, T pvx, T pvy, const Ob<T>& B,
                                                 T thB, bool ownP, T reach, T idP, T gPx, T gPy,
                                                 T idB, T gBx, T gBy, const WorldC<T>& W,
                                                 Agent<T>& gin) {
@@ -450,7 +450,7 @@ __device__ __forceinline__ void pair_shaped_vjp(int a, int b, bool box_a, const 
 // VJP of box_static_force (obstacles, then the support-extent walls) of a box agent at
 // heading th with force cotangent (gfx, gfy).
 template <typename T>
-__device__ __forceinline__ void box_static_vjp(const Obs<T>* sobs, int N, bool walls,
+__device__ __noinline__ void box_static_vjp(const Obs<T>* sobs, int N, bool walls,
                                                const Ob<T>& oa, T th, T inv_denom, T gfx, T gfy,
                                                const WorldC<T>& W, Agent<T>& gin) {
   const T ra = norm2(oa.hx, oa.hy);

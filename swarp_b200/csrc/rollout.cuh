@@ -793,8 +793,11 @@ __global__ void __launch_bounds__(1024) rollout_fwd_kernel(const RolloutArgs<T> 
   const T* iden_env = siden + le * A;
   Obs<T>* obs_env = sobs + le * N;
   // unrolled: the step's state and prefetched action rotate through registers instead of
-  // being copied at the end of each step (measured: 223.6 -> 203.1 us at 16000 x 16 x 64)
-#pragma unroll 4
+  // being copied at the end of each step (measured: 223.6 -> 203.1 us at 16000 x 16 x 64);
+  // not for box and drone worlds, whose larger step body would then thrash the
+  // instruction cache (measured: ~77% of issue slots lost to instruction fetch)
+  constexpr int kUnrollT = (FL & (F_BOXES | F_DRONE)) ? 1 : 4;
+#pragma unroll kUnrollT
   for (int t = 0; t < R.H; ++t) {
     if (t + 1 < R.H) load_action(R, (long long)(t + 1) * EA + ia, n0, n1);
     if (kDrone && t + 1 < R.H) load_action23(R, (long long)(t + 1) * EA + ia, n2, n3);
