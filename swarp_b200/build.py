@@ -51,13 +51,22 @@ def build(force: bool = False, verbose: bool = False, extra: list[str] | None = 
     objdir = os.path.join(HERE, "_build")
     os.makedirs(objdir, exist_ok=True)
     objs, procs = [], []
+    # every translation unit includes every header: a header change rebuilds all of them,
+    # a change to one .cu file only that one (unless forced or given extra flags)
+    headers = [os.path.join(CSRC, d) for d in DEPS if not d.endswith(".cu")]
+    headers.append(os.path.join(ROOT, "include", "swarp_b200.h"))
+    newest_hdr = max(os.path.getmtime(h) for h in headers)
     for src in SOURCES:
         obj = os.path.join(objdir, src.replace(".cu", ".o"))
-        cmd = [nvcc(), *ARCH, *FLAGS, *(extra or []), "-c", "-o", obj, os.path.join(CSRC, src)]
+        objs.append(obj)
+        path = os.path.join(CSRC, src)
+        if (not force and not extra and os.path.exists(obj)
+                and os.path.getmtime(obj) > max(newest_hdr, os.path.getmtime(path))):
+            continue
+        cmd = [nvcc(), *ARCH, *FLAGS, *(extra or []), "-c", "-o", obj, path]
         if verbose:
             print(" ".join(cmd), flush=True)
         procs.append(subprocess.Popen(cmd))
-        objs.append(obj)
     failed = [p.args[-1] for p in procs if p.wait() != 0]
     if failed:
         raise RuntimeError(f"nvcc failed on {failed}")
