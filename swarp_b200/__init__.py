@@ -49,6 +49,7 @@ from swarp_b200.interop.autograd import (
     TorchState,
     rollout,
     rollout_bodies,
+    rollout_checkpointed,
     warp_step,
 )
 from swarp_b200.core.sharding import PairReducer, env_shard, reduce_loss_and_grad_norm
@@ -89,6 +90,6 @@ __all__ = [
     "Obstacles", "PARAM_FIELDS", "P_HALF_X", "P_HALF_Y", "P_LF", "P_LR", "P_MASS", "P_MAX_ACCEL",
     "P_MAX_ANG_ACCEL", "P_MAX_ANG_VEL", "P_MAX_SPEED", "P_MAX_STEER", "P_MIN_SPEED", "P_RADIUS",
     "P_SHAPE", "SCENARIOS", "Stepper", "TorchState", "World", "WorldConfig", "action_bounds",
-    "make", "make_scenario", "per_env_float_template", "rollout", "rollout_bodies",
+    "make", "make_scenario", "per_env_float_template", "rollout", "rollout_bodies", "rollout_checkpointed",
     "scenario_class", "warp_step", "__version__",
 ]

@@ -201,6 +201,79 @@ def rollout_bodies(
     return fin, Trajectory(tuple(traj), extra), body
 
 
+class _CheckpointedFn(torch.autograd.Function):
+    """``(actions [T,E,A,D], n state tensors) -> final n``, keeping only the state at
+    every ``every``-th step: the forward runs the fused rollout kernel one segment of
+    ``every`` steps at a time and drops each segment's trajectory; the backward re-runs
+    each segment from its checkpoint (the same kernels on the same inputs reproduce it bit
+    for bit) and runs the adjoint kernel over it, last segment first, handing the
+    cotangent of each segment's initial state to the segment before."""
+
+    @staticmethod
+    def forward(ctx, stepper: Stepper, every: int, actions, *state):
+        acts = actions.contiguous()
+        cur = tuple(t.contiguous() for t in state)
+        checkpoints = [cur]
+        T = acts.shape[0]
+        for t0 in range(0, T, every):
+            _, fin, _, _ = stepper.rollout_forward(cur, acts[t0:t0 + every], final=True,
+                                                   moving_bodies=False)
+            cur = fin
+            checkpoints.append(cur)
+        ctx.stepper, ctx.every, ctx.n = stepper, every, len(cur)
+        ctx.set_materialize_grads(False)
+        ctx.save_for_backward(acts, *(t for cp in checkpoints[:-1] for t in cp))
+        return cur
+
+    @staticmethod
+    def backward(ctx, *g_final):
+        acts, *flat = ctx.saved_tensors
+        n, every, st = ctx.n, ctx.every, ctx.stepper
+        checkpoints = [tuple(flat[i:i + n]) for i in range(0, len(flat), n)]
+        g = tuple(None if x is None else x.contiguous() for x in g_final)
+        g_act = torch.empty_like(acts)
+        for i in reversed(range(len(checkpoints))):
+            t0 = i * every
+            seg = acts[t0:t0 + every]
+            traj, _, _, rec = st.rollout_forward(checkpoints[i], seg, final=False,
+                                                 moving_bodies=False)
+            ga, g = st.rollout_backward(checkpoints[i], seg, traj, (None,) * n, g, rec)
+            g_act[t0:t0 + every] = ga
+        return (None, None, g_act, *g)
+
+
+def rollout_checkpointed(stepper: Stepper, state: TorchState, actions_seq: torch.Tensor,
+                         every: int = 8) -> TorchState:
+    """BPTT rollout that returns only the final state and keeps the state of every
+    ``every``-th step for the backward pass instead of the whole trajectory.
+
+    Memory for a T-step rollout is T/every checkpoints plus one ``every``-step segment,
+    against T steps for :func:`rollout`; the price is a second forward pass over the
+    horizon inside the backward. Gradients (w.r.t. ``state`` and ``actions_seq``) are the
+    same as :func:`rollout`'s for a loss on the final state, bit for bit. Fleets with
+    movable bodies are not accepted (their state advances on the host between rollouts).
+    """
+    if every < 1:
+        raise ValueError(f"every must be >= 1, got {every}")
+    if stepper.any_movable:
+        raise NotImplementedError("rollout_checkpointed does not take movable bodies; use "
+                                  "rollout_bodies")
+    state = fill_state_defaults(state)
+    n = stepper.n_state
+    core = tuple(state[:n])
+    stepper._check_inputs(core, actions_seq, horizon_dim=True)
+    extra = tuple(state[n:])
+    if torch.is_grad_enabled() and (actions_seq.requires_grad or
+                                    any(t.requires_grad for t in core)):
+        fin = _CheckpointedFn.apply(stepper, int(every), actions_seq, *core)
+    else:
+        with torch.no_grad():
+            _, fin, _, _ = stepper.rollout_forward(tuple(t.contiguous() for t in core),
+                                                   actions_seq.contiguous(), final=True,
+                                                   moving_bodies=False)
+    return TorchState(*fin, *extra)
+
+
 @dataclass
 class StepGradSlot:
     """One reserved step of a :class:`GradRing` (API compatibility)."""
