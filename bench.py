@@ -266,15 +266,37 @@ def host_threads() -> int:
         return os.cpu_count() or 1
 
 
-def cpu_rollout_sample(cid: int, E: int, threads: int, seed: int = 0) -> float:
-    """One fwd+adjoint rollout of E envs of config ``cid`` on the CPU; returns seconds.
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+@dataclass
+class CpuSample:
+    """The inputs of one CPU fwd+adjoint rollout of E envs of a config, generated before
+    any timing starts."""
+
+    cid: int
+    E: int
+    H: int
+    run: object  # callable(threads) -> seconds of the rollout + adjoint alone
+
+
+def cpu_prepare(cid: int, E: int, seed: int = 0) -> CpuSample:
+    """Seeded inputs of E envs of config ``cid`` for the CPU restatement (untimed).
 
     Configs 1, 2, 3, 5 run the OpenMP C restatement (oracle/cpu_port.c). Config 4 (movable
     bodies, which that port does not model) runs the float32 torch restatement
     (oracle/torch_ref.py) with torch's intra-op threads."""
     wl = build_workload(cid, rank=seed, n_envs=E, make_stepper=False)
+    rng = np.random.default_rng(1000 + seed)
     if cid == 4:
-        return _torch_oracle_sample(wl, threads)
+        return CpuSample(cid, E, wl.H, _torch_oracle_prep(wl))
     from oracle import cpu_port
     from swarp_b200.dynamics.base import param_rows
 
@@ -288,24 +310,29 @@ def cpu_rollout_sample(cid: int, E: int, threads: int, seed: int = 0) -> float:
                "vel": r.vel.numpy(), "ang_vel": r.ang_vel.numpy(), "radius": r.radius.numpy(),
                "half": r.half_extents.numpy(), "shape": r.shape.numpy()}
     z = np.zeros((wl.E, wl.A), np.float32)
-    t0 = time.perf_counter()
-    cpu_port.rollout(
-        params=param_rows(cfgs), model_tag=[int(c.model) for c in cfgs],
-        ctrl_mode=[int(c.ctrl_mode) for c in cfgs], dt=DT, substeps=1, collisions=True,
-        k=w.collision_k, c=w.collision_c, margin=w.collision_margin, max_overlap=0.0,
-        neighbor_radius=w.neighbor_radius, max_neighbors=w.max_neighbors, bounds_mode=1,
-        bounds=w.bounds, init=[wl.pos, wl.theta, np.zeros_like(wl.pos), z, z], actions=wl.acts,
-        grad_final_pos=np.zeros_like(wl.pos), obstacles=obs, threads=threads, dtype=np.float32)
-    # The adjoint's work does not depend on the cotangent values, so the sample seeds it
-    # with zeros instead of 2 (pos_H - goal) (which would need the forward first).
-    return time.perf_counter() - t0
+    init = [wl.pos, wl.theta, np.zeros_like(wl.pos), z, z]
+    # the adjoint's cotangent: seeded, nonzero (its work does not depend on the values:
+    # the C adjoint has no value-dependent early exit)
+    g_final = rng.standard_normal(wl.pos.shape).astype(np.float32)
+    kw = dict(params=param_rows(cfgs), model_tag=[int(c.model) for c in cfgs],
+              ctrl_mode=[int(c.ctrl_mode) for c in cfgs], dt=DT, substeps=1, collisions=True,
+              k=w.collision_k, c=w.collision_c, margin=w.collision_margin, max_overlap=0.0,
+              neighbor_radius=w.neighbor_radius, max_neighbors=w.max_neighbors, bounds_mode=1,
+              bounds=w.bounds, init=init, actions=wl.acts, grad_final_pos=g_final,
+              obstacles=obs, dtype=np.float32)
+
+    def run(threads: int) -> float:
+        t0 = time.perf_counter()
+        cpu_port.rollout(threads=threads, **kw)
+        return time.perf_counter() - t0
+
+    return CpuSample(cid, E, wl.H, run)
 
 
-def _torch_oracle_sample(wl: Workload, threads: int) -> float:
+def _torch_oracle_prep(wl: Workload):
     from oracle import torch_ref as R
     from swarp_b200.dynamics.base import param_rows
 
-    torch.set_num_threads(threads)
     cfgs, w, o = wl.cpu_spec["configs"], wl.cpu_spec["world"], wl.cpu_spec["obstacles"]
     f = torch.float32
     ro = o.resolve("cpu", f)
@@ -323,61 +350,94 @@ def _torch_oracle_sample(wl: Workload, threads: int) -> float:
     rob = R.seed_bodies(rob)
     pos = torch.from_numpy(wl.pos)
     z = torch.zeros(wl.E, wl.A)
-    acts = torch.from_numpy(wl.acts).requires_grad_(True)
-    t0 = time.perf_counter()
-    _, _, body_traj = R.rollout((pos, z, torch.zeros_like(pos), z, z), acts, rw, rob)
-    loss = (body_traj[-1].body_pos[:, 0] - torch.from_numpy(wl.goal)).norm(dim=-1).sum()
-    loss.backward()
-    return time.perf_counter() - t0
+    goal = torch.from_numpy(wl.goal)
+    acts0 = torch.from_numpy(wl.acts)
+
+    def run(threads: int) -> float:
+        torch.set_num_threads(threads)
+        acts = acts0.clone().requires_grad_(True)
+        t0 = time.perf_counter()
+        _, _, body_traj = R.rollout((pos, z, torch.zeros_like(pos), z, z), acts, rw, rob)
+        loss = (body_traj[-1].body_pos[:, 0] - goal).norm(dim=-1).sum()
+        loss.backward()
+        return time.perf_counter() - t0
+
+    return run
 
 
-def calibrate_cpu(cid: int, target_s: float, threads: int, e_max: int) -> int:
+def cpu_envs_for(cid: int, seconds: float, threads: int, e_max: int) -> int:
+    """Envs of config ``cid`` whose fwd+adjoint rollout takes about ``seconds`` on
+    ``threads`` threads (at most e_max), from timed calibration samples."""
     E = max(threads, 8)
     while True:
-        dt = cpu_rollout_sample(cid, E, threads)
-        if dt >= target_s / 4 or E >= e_max:
-            return min(e_max, max(1, int(E * target_s / max(dt, 1e-6))))
+        sample = cpu_prepare(cid, min(E, e_max))
+        dt = sample.run(threads)
+        if dt >= seconds / 4 or E >= e_max:
+            return min(e_max, max(1, int(min(E, e_max) * seconds / max(dt, 1e-6))))
         E *= 4
 
 
 def cpu_baseline_block(wl: Workload, target_s: float = 2.0, repeats: int = 3) -> dict:
+    """The CPU restatement on all host threads and on one, in this run (rank 0, N=1)."""
     threads = host_threads()
-    E = calibrate_cpu(wl.cid, target_s, threads, wl.E)
-    times = [cpu_rollout_sample(wl.cid, E, threads, seed=i) for i in range(repeats)]
-    t = statistics.median(times)
+    out = {}
+    for label, th in (("all", threads), ("one", 1)):
+        E = cpu_envs_for(wl.cid, target_s, th, wl.E)
+        samples = [cpu_prepare(wl.cid, E, seed=i) for i in range(repeats)]
+        times = [smp.run(th) for smp in samples]
+        out[label] = (E, E * wl.H / statistics.median(times))
     port = ("float32 torch restatement (oracle/torch_ref.py)" if wl.cid == 4 else
-            f"C restatement (oracle/cpu_port.c, OpenMP {threads} threads)")
-    return {"value": E * wl.H / t, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{E} envs x {wl.A} agents x H={wl.H}, fwd+adjoint, float32, {port}, "
-                      f"median of {repeats}"}
+            "C restatement (oracle/cpu_port.c, OpenMP)")
+    return {"value": out["all"][1], "unit": UNIT, "cores": threads, "kind": "port",
+            "threads": threads, "value_1core": out["one"][1], "cpu_model": cpu_model(),
+            "sample": f"{out['all'][0]} envs x {wl.A} agents x H={wl.H} on {threads} threads, "
+                      f"{out['one'][0]} envs on 1 thread; fwd+adjoint, float32, {port}; "
+                      f"inputs generated before timing; median of {repeats}"}
 
 
 def run_reference(args, rank: int, world: int) -> None:
+    """The CPU restatement of the reference's rollout + adjoint (the reference's own Warp
+    path cannot be installed here), all host threads, on this arm's workload: each step one
+    rollout of the config's full env count, unless that would not let ``--steps`` +
+    ``--warmup`` steps end within about two minutes (then a bounded env sample, stated in
+    ``cpu_baseline.sample``). Inputs are generated before the timed loop; only the
+    rollout + adjoint calls are timed."""
     if rank != 0:
         return
     threads = host_threads()
-    wl = build_workload(args.config, make_stepper=False)
-    E = calibrate_cpu(args.config, 0.05, threads, wl.E)  # ~50 ms per step: runs end in minutes
+    wl = build_workload(args.config, make_stepper=False, n_envs=args.envs)
+    budget = min(1.5, 120.0 / max(1, args.steps + args.warmup))
+    E = cpu_envs_for(args.config, budget, threads, wl.E)
+    samples = [cpu_prepare(args.config, E, seed=i) for i in range(2)]
     for i in range(args.warmup):
-        cpu_rollout_sample(args.config, E, threads, seed=i)
-    t0 = time.perf_counter()
-    for i in range(args.steps):
-        cpu_rollout_sample(args.config, E, threads, seed=i)
-    dt = time.perf_counter() - t0
+        samples[i % 2].run(threads)
+    times = [samples[i % 2].run(threads) for i in range(args.steps)]
+    dt = sum(times)
     value = E * wl.H * args.steps / dt
+    full = E == wl.E
     line = {
         "impl": "reference", "metric": wl.metric, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": wl.name + f" (bounded CPU sample: {E} envs per step)",
-                   "n_agents": wl.A, "horizon": wl.H, "dt": DT},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{E} envs per step, CPU restatement of the reference "
-                                   "(the reference's Warp path cannot be installed here)"},
+        "config": config_block(wl, world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "threads": threads,
+                         "kind": "port", "cpu_model": cpu_model(),
+                         "sample": (f"{E} envs per step ({'the full workload' if full else 'a bounded sample of the workload'}), "
+                                    "CPU restatement of the reference (oracle/cpu_port.c; "
+                                    "the reference's Warp path cannot be installed here), "
+                                    "inputs generated before timing")},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def config_block(wl: Workload, world: int) -> dict:
+    agent_steps = wl.E * wl.A * wl.H
+    return {"workload": wl.name, "config_id": wl.cid, "n_envs_per_gpu": wl.E, "n_agents": wl.A,
+            "horizon": wl.H, "parallelism": f"env-sharded dp{world}",
+            "l2": "inputs larger than L2" if wl.acts.nbytes + 28 * agent_steps > 126e6 else
+                  "inputs smaller than L2 (small config; no flush)"}
 
 
 # ------------------------------------------------------------------ GPU side
@@ -402,6 +462,8 @@ def main() -> None:
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5])
     ap.add_argument("--impl", default="swarp_b200", choices=["swarp_b200", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=30)
+    ap.add_argument("--e2e-chunks", type=int, default=8,
+                    help="env chunks the end-to-end leg pipelines host copies over")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--envs", type=int, default=None,
                     help="override the config's envs per GPU (smaller cases for profiling)")
@@ -508,7 +570,7 @@ def main() -> None:
         step()
     torch.cuda.synchronize()
 
-    def timed_loop(fn, n, sample_clocks, finish=None):
+    def timed_loop(fn, n, sample_clocks, finish=None, start=None):
         if dist is not None:
             dist.barrier()
         torch.cuda.synchronize()
@@ -516,6 +578,8 @@ def main() -> None:
         e1 = torch.cuda.Event(enable_timing=True)
         with ClockSampler(local) if sample_clocks else _Null() as clk:
             e0.record()
+            if start is not None:
+                start()  # work on other streams is ordered after e0
             for _ in range(n):
                 fn()
             if finish is not None:
@@ -545,36 +609,93 @@ def main() -> None:
         overflow = {"agents_over_K": int(ov.sum()), "max_true_count":
                     int(st.last_true_count_max.max()), "K": st.world.max_neighbors}
 
-    # ---- end to end: host inputs (pinned) -> device, step, loss -> host, through the
-    # public API (GraphedRollout call, or rollout_bodies for config 4)
+    # ---- collective: device time of the (loss, ||g||^2) all-reduce, back to back and
+    # when every step waits for its own (the pattern a ring of pending reductions avoids)
+    allreduce = None
+    if dist is not None:
+        buf = torch.zeros(2, device=dev, dtype=torch.float32)
+        for _ in range(20):
+            dist.all_reduce(buf)
+        n_ar = 100
+        ar_ms, _ = timed_loop(lambda: dist.all_reduce(buf), n_ar, False)
+
+        def step_wait():
+            graphed()
+            dist.all_reduce(graphed.loss_and_grad_norm)
+
+        for _ in range(3):
+            step_wait()
+        n_sw = max(20, min(args.steps, 200))
+        sw_ms, _ = timed_loop(step_wait, n_sw, False)
+        ar_t = torch.tensor([ar_ms / n_ar * 1e3, sw_ms / n_sw], device=dev, dtype=torch.float64)
+        dist.all_reduce(ar_t, op=dist.ReduceOp.MAX)
+        allreduce = {"us_per_allreduce_back_to_back": float(ar_t[0]),
+                     "ms_per_step_waiting_for_each_allreduce": float(ar_t[1]),
+                     "bytes": 8, "backend": "nccl"}
+
+    # ---- end to end through the public API with host buffers: every step copies its
+    # inputs (actions, start positions and headings, goals) from pinned host memory and
+    # its result (the action gradient and the loss) back to pinned host memory
     pin = [torch.from_numpy(x).pin_memory() for x in (wl.acts, wl.pos, wl.theta, wl.goal)]
     h2d = sum(p.numel() * p.element_size() for p in pin)
-    d2h = 8
-    d_acts = torch.empty_like(acts)
+    grad_h = torch.empty(wl.acts.shape, dtype=torch.float32).pin_memory()
+    streamed = None
+    if graphed is not None:
+        from swarp_b200.interop.streamed import StreamedRollout
 
-    def e2e_step():
-        if graphed is not None:
-            goal.copy_(pin[3], non_blocking=True)
-            graphed(TorchState(pin[1], pin[2], None, None, None), pin[0])  # vel etc. stay 0
-            loss = graphed.loss
-            if dist is not None:
-                dist.all_reduce(graphed.loss_and_grad_norm)
-                loss = graphed.loss_and_grad_norm[0]
-        else:
+        streamed = StreamedRollout(
+            st, E, H, 2, lambda fin, _traj, g: torch.nn.functional.mse_loss(
+                fin.pos, g, reduction="sum"), aux_like=[goal], chunks=args.e2e_chunks)
+        loss_h = torch.zeros(streamed.n_chunks, dtype=torch.float64).pin_memory()
+        d2h = grad_h.numel() * grad_h.element_size() + loss_h.numel() * 8
+
+        def e2e_step():
+            streamed(TorchState(pin[1], pin[2], None, None, None), pin[0], [pin[3]], grad_h,
+                     loss_h)
+
+        def e2e_begin():
+            streamed.begin()
+
+        def e2e_end():
+            streamed.end()
+    else:
+        loss_h = torch.zeros(1, dtype=torch.float64).pin_memory()
+        d2h = grad_h.numel() * grad_h.element_size() + 8
+        d_acts = torch.empty_like(acts)
+
+        def e2e_step():
             d_acts.copy_(pin[0], non_blocking=True)
             p, th, gl = (x.to(dev, non_blocking=True) for x in pin[1:])
             goal.copy_(gl)
             a = d_acts.detach().requires_grad_(True)
-            loss = eager_step(TorchState(p, th, torch.zeros_like(p), zero, zero), a)
-        return float(loss.detach().to("cpu", torch.float64))
+            st.restore_bodies(snap)
+            _, _, body = rollout_bodies(st, TorchState(p, th, torch.zeros_like(p), zero, zero), a)
+            loss = (body.pos[:, 0] - goal).norm(dim=-1).sum()
+            (g,) = torch.autograd.grad(loss, [a])
+            grad_h.copy_(g, non_blocking=True)
+            loss_h.copy_(loss.detach().double().reshape(1), non_blocking=True)
+
+        e2e_begin = e2e_end = None
 
     for _ in range(3):
+        if e2e_begin:
+            e2e_begin()
         e2e_step()
-    e2e_total, _ = timed_loop(e2e_step, args.e2e_steps, False)
+        if e2e_end:
+            e2e_end()
+    torch.cuda.synchronize()
+    e2e_total, _ = timed_loop(e2e_step, args.e2e_steps, False, finish=e2e_end, start=e2e_begin)
     e2e_ms = torch.tensor([e2e_total / args.e2e_steps], device=dev, dtype=torch.float64)
     if dist is not None:
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
     e2e_value = world * E * H / (float(e2e_ms.item()) / 1e3)
+    # the gradient that came back equals the device-timed step's (same envs, same inputs)
+    e2e_grad_ok = None
+    if graphed is not None:
+        graphed(TorchState(pin[1].to(dev), pin[2].to(dev), None, None, None), pin[0].to(dev))
+        e2e_grad_ok = bool(torch.equal(graphed.grad_actions.cpu(), grad_h))
+    if streamed is not None:
+        streamed.release()
 
     if graphed is not None:
         graphed.release()  # before the process group goes: the graph follows NCCL work
@@ -604,10 +725,7 @@ def main() -> None:
             "peak_source": peak_src}
     roof["frac"] = roof["achieved"] / peak
     roof["traffic"] = profile_traffic(args.config) if dom == "bwd" else None
-    cfg = {"workload": wl.name, "config_id": args.config, "n_envs_per_gpu": E, "n_agents": A,
-           "horizon": H, "parallelism": f"env-sharded dp{world}",
-           "l2": "inputs larger than L2" if wl.acts.nbytes + 28 * agent_steps > 126e6 else
-                 "inputs smaller than L2 (small config; no flush)"}
+    cfg = config_block(wl, world)
     line = {
         "metric": wl.metric, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
@@ -621,7 +739,13 @@ def main() -> None:
                           "bwd_gbs": bwd_gbs},
         "clocks": clocks.summary(),
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h},
+                "d2h_bytes_per_step": d2h,
+                "path": (f"StreamedRollout: {streamed.n_chunks if streamed else 1} env chunks, "
+                         "host-to-device copies, captured BPTT step and device-to-host copies "
+                         "of the action gradient and loss on three streams"
+                         if graphed is not None else
+                         "eager rollout_bodies + autograd.grad; gradient copied back"),
+                "grad_matches_device_step": e2e_grad_ok},
         # forward + adjoint per step, plus the fused-norm reduction when ranks all-reduce it
         "gpu_launches": (3 if reducer is not None else 2) * args.steps,
         "timed_path": ("one CUDA-graph replay of the whole BPTT step per step "
@@ -631,6 +755,8 @@ def main() -> None:
     }
     if overflow is not None:
         line["neighbor_overflow"] = overflow
+    if allreduce is not None:
+        line["allreduce"] = allreduce
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_block(wl)
     print(json.dumps(line), flush=True)

@@ -169,9 +169,9 @@ int swarp_neighbors(const swarp_world_t* w, const void* pos, int32_t* idx, int32
 
 /* Allocation-free BPTT rollout: swarp_rollout_fwd followed by swarp_rollout_bwd in one
  * call, for callers that cannot allocate device memory (a plugin under another
- * runtime's memory manager, such as an XLA/JAX custom call; a real-time loop or a
- * stream being captured into a CUDA graph, where cudaMalloc may synchronize the device).
- * This entry point has no counterpart in the reference. The two kernels' shared
+ * runtime's memory manager, such as an XLA/JAX custom call, must not allocate behind
+ * that manager's back; a real-time control loop cannot wait on cudaMalloc, which may
+ * synchronize the device). This entry point has no counterpart in the reference. The two kernels' shared
  * workspace lives in a static device array of SWARP_NOALLOC_SCRATCH_BYTES that the
  * library owns (one per GPU that loads it, held until the process exits); nothing else
  * is allocated. Arguments mean what they mean for swarp_rollout_fwd / _bwd (final_out,
@@ -179,13 +179,23 @@ int swarp_neighbors(const swarp_world_t* w, const void* pos, int32_t* idx, int32
  * Returns SWARP_ERR_SCRATCH_LIMIT when swarp_rollout_workspace_bytes() exceeds
  * SWARP_NOALLOC_SCRATCH_BYTES. The first call on each device resolves the array's
  * device address (cudaGetSymbolAddress) with that device current: make it before any
- * stream capture. All calls share the array, so calls that overlap on one GPU race on
- * it; serialize them. */
+ * stream capture. The address is kept for the life of the process: after a
+ * cudaDeviceReset of a device, do not call this entry point on that device again. All
+ * calls share the array, so calls that overlap on one GPU race on it; serialize them. */
 #define SWARP_NOALLOC_SCRATCH_BYTES (16u << 20)
 int swarp_rollout_noalloc(const swarp_world_t* w, int32_t horizon, swarp_state_t init,
                           const void* actions, swarp_state_t traj, swarp_state_t final_out,
                           swarp_state_t adj_traj, swarp_state_t adj_final, void* adj_actions,
                           swarp_state_t adj_init, void* stream);
+
+/* Strided asynchronous copy of `rows` rows of `row_bytes` each, between any two of host
+ * (pinned) and device memory (cudaMemcpy2DAsync, direction from the pointers), on
+ * `stream`. This is host plumbing with no counterpart in the reference: it moves one env
+ * slice of a [T, E, ...] array (T rows, one per step) in one call, which the streamed
+ * BPTT front end (swarp_b200.interop.streamed) uses to pipeline host inputs and gradients
+ * against the kernels env chunk by env chunk. */
+int swarp_copy_rows(void* dst, size_t dst_pitch, const void* src, size_t src_pitch,
+                    size_t row_bytes, size_t rows, void* stream);
 
 /* Static description of a return code. */
 const char* swarp_error_string(int code);

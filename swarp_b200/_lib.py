@@ -84,6 +84,8 @@ SIGNATURES = {
                                   C.c_void_p, C.c_void_p]),
     "swarp_rollout_noalloc": (C.c_int, [C.POINTER(WorldC), C.c_int32, State, C.c_void_p, State,
                                         State, State, State, C.c_void_p, State, C.c_void_p]),
+    "swarp_copy_rows": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_size_t,
+                                  C.c_size_t, C.c_void_p]),
     "swarp_error_string": (C.c_char_p, [C.c_int]),
     "swarp_abi_version": (C.c_int32, []),
 }

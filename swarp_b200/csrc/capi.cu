@@ -75,6 +75,19 @@ template <typename T> T radius_sq_threshold(double Rd) {
   return x;
 }
 
+// The packed scan's threshold: r2_thr widened by 2^-19 (float) / 2^-48 (double) relative,
+// i.e. >= 30 ulps, plus a tiny absolute term that covers underflow of dx^2 + dy^2 when
+// r2_thr is subnormal. Every in-radius pair tests negative against it (the scan's two
+// fused roundings err by < 3 ulps of the threshold), so the scan's set is a superset of
+// the exact one; the kernels filter it with the exact test.
+template <typename T> T radius_sq_scan_threshold(T thr) {
+  if (!(thr > T(0))) return thr;
+  const bool f = std::is_same<T, float>::value;
+  const T rel = f ? T(0x1p-19) : T(0x1p-48);
+  const T tiny = f ? T(0x1p-120) : T(0x1p-1000);
+  return std::nextafter(thr * (T(1) + rel) + tiny, std::numeric_limits<T>::infinity());
+}
+
 int validate_world(const swarp_world_t* w, int horizon) {
   if (!w || horizon < 1) return SWARP_ERR_INVALID_ARG;
   if (w->dtype != SWARP_F32 && w->dtype != SWARP_F64) return SWARP_ERR_INVALID_ARG;
@@ -146,6 +159,7 @@ void fill_common(const swarp_world_t* w, int horizon, RolloutArgs<T>& R) {
   W.margin = static_cast<T>(w->margin);
   W.max_overlap = static_cast<T>(w->max_overlap);
   W.r2_thr = w->collisions ? radius_sq_threshold<T>(w->neighbor_radius) : T(-1);
+  W.r2_scan = radius_sq_scan_threshold(W.r2_thr);
   W.bx0 = static_cast<T>(w->bounds[0]);
   W.bx1 = static_cast<T>(w->bounds[1]);
   W.by0 = static_cast<T>(w->bounds[2]);
@@ -302,7 +316,8 @@ int nbr_typed(const swarp_world_t* w, const void* pos, int32_t* idx, int32_t* co
               int32_t* true_count, cudaStream_t st) {
   const int E = w->n_envs, A = w->n_agents;
   const int G = envs_per_cta(A, E);
-  return launch_neighbors<T>(E, A, G, w->max_neighbors, radius_sq_threshold<T>(w->neighbor_radius),
+  const T thr = radius_sq_threshold<T>(w->neighbor_radius);
+  return launch_neighbors<T>(E, A, G, w->max_neighbors, radius_sq_scan_threshold(thr), thr,
                              static_cast<const T*>(pos), idx, count, true_count, st);
 }
 
@@ -404,6 +419,16 @@ const char* swarp_error_string(int code) {
              "scratch (SWARP_NOALLOC_SCRATCH_BYTES)";
     default: return "unknown error code";
   }
+}
+
+int swarp_copy_rows(void* dst, size_t dst_pitch, const void* src, size_t src_pitch,
+                    size_t row_bytes, size_t rows, void* stream) {
+  if (rows == 0 || row_bytes == 0) return SWARP_OK;
+  if (!dst || !src || dst_pitch < row_bytes || src_pitch < row_bytes) return SWARP_ERR_INVALID_ARG;
+  return cudaMemcpy2DAsync(dst, dst_pitch, src, src_pitch, row_bytes, rows, cudaMemcpyDefault,
+                           static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? SWARP_OK
+             : SWARP_ERR_CUDA;
 }
 
 int32_t swarp_abi_version(void) { return kAbiVersion; }

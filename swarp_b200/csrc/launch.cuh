@@ -45,8 +45,8 @@ template <typename T> inline int launch_bwd(const RolloutArgs<T>& R, int fl, cud
   return (fl & F_RK4) ? launch_bwd_part<T, F_RK4>(R, fl, st) : launch_bwd_part<T, 0>(R, fl, st);
 }
 template <typename T>
-int launch_neighbors(int E, int A, int G, int K, T r2, const T* pos, int* idx, int* cnt, int* tru,
-                     cudaStream_t st);
+int launch_neighbors(int E, int A, int G, int K, T r2_scan, T r2, const T* pos, int* idx, int* cnt,
+                     int* tru, cudaStream_t st);
 
 #ifdef SWARP_DEFINE_LAUNCHERS
 
@@ -157,15 +157,15 @@ template <typename T, int RB> int launch_bwd_part(const RolloutArgs<T>& R, int f
 }
 
 template <typename T>
-int launch_neighbors(int E, int A, int G, int K, T r2, const T* pos, int* idx, int* cnt, int* tru,
-                     cudaStream_t st) {
+int launch_neighbors(int E, int A, int G, int K, T r2_scan, T r2, const T* pos, int* idx, int* cnt,
+                     int* tru, cudaStream_t st) {
   const size_t smem = ((size_t(G) * ((A + 1) / 2) * 4 * sizeof(T) + 15) & ~size_t(15)) +
                       size_t(G) * A * 4 * sizeof(T);
   auto k = neighbors_kernel<T>;
   if (smem > 48 * 1024 &&
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return kErrCuda;
-  k<<<(E + G - 1) / G, G * A, smem, st>>>(E, A, G, K, r2, pos, idx, cnt, tru);
+  k<<<(E + G - 1) / G, G * A, smem, st>>>(E, A, G, K, r2_scan, r2, pos, idx, cnt, tru);
   return cudaGetLastError() == cudaSuccess ? 0 : kErrCuda;
 }
 

@@ -2,8 +2,8 @@
 //
 // Some callers cannot allocate device memory: a plugin running under another runtime's
 // memory manager (an XLA/JAX custom call, another framework's operator) must not create
-// allocations behind that manager's back, and a real-time control loop or a stream being
-// captured into a CUDA graph cannot afford cudaMalloc, which may synchronize the device.
+// allocations behind that manager's back, and a real-time control loop cannot wait on
+// cudaMalloc, which may synchronize the device.
 // For them this entry point runs the forward rollout and its adjoint back to back with
 // the workspace they share (per-substep contact masks or list cutoffs) placed in a
 // static device array that the library owns, instead of a buffer the caller allocates.
@@ -12,7 +12,9 @@
 // its own SWARP_NOALLOC_SCRATCH_BYTES copy until the process exits. Host code cannot use
 // the array's name as a device address (on the host it names a host-side shadow), so the
 // device address is resolved with cudaGetSymbolAddress, once per device, with that
-// device current, and cached. The forward writes every workspace cell the adjoint reads,
+// device current, on the first call there (which should therefore come before any stream
+// capture), and cached for the life of the process: a cudaDeviceReset destroys the array
+// with the context, after which this entry point must not be called on that device. The forward writes every workspace cell the adjoint reads,
 // so nothing in the array has to start at zero. All calls share the one array: calls
 // whose work overlaps on a GPU (different streams, or different host threads on one
 // device) race on it and must be serialized by the caller.

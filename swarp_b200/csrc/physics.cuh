@@ -59,6 +59,22 @@ template <typename T> __device__ __forceinline__ T len2(T x, T y) { return Num<T
 
 template <typename T> struct Eps2 { static constexpr T v = T(1.0e-10); };
 
+// Neighbor membership, the reference's wp.length(p_b - p_a) <= radius
+// (swarp/core/neighbors.py:91), as IEEE arithmetic rounds the expression without
+// contraction: sqrt(fl(fl(dx*dx) + fl(dy*dy))) <= R. The square root is correctly rounded
+// and monotone, so with thr = the largest T whose square root is <= R (computed on the
+// host) the test is fl(fl(dx*dx) + fl(dy*dy)) <= thr, bit for bit, with no square root.
+// The kernels' packed scan evaluates dx^2 + (dy^2 - thr') with two fused roundings, which
+// can differ from this sum within an ulp of the threshold; it runs with thr' = thr widened
+// by at least 8 ulps, so its set contains every member (the fused error is below
+// 3 ulps of thr), and this exact test then drops the extra candidates.
+__device__ __forceinline__ bool in_radius(float dx, float dy, float thr) {
+  return __fadd_rn(__fmul_rn(dx, dx), __fmul_rn(dy, dy)) <= thr;
+}
+__device__ __forceinline__ bool in_radius(double dx, double dy, double thr) {
+  return __dadd_rn(__dmul_rn(dx, dx), __dmul_rn(dy, dy)) <= thr;
+}
+
 // Model / mode / shape tags (values of the reference enums).
 enum : int { TAG_HOLONOMIC = 0, TAG_DIFF_DRIVE = 1, TAG_BICYCLE = 2, TAG_DRONE = 3 };
 enum : int { MODE_VELOCITY = 0, MODE_ACCELERATION = 1, MODE_SERVO = 2 };
@@ -86,7 +102,8 @@ template <typename T> struct AgentP {
 template <typename T> struct WorldC {
   T dt;  // sub-step
   T k, c, margin, max_overlap;
-  T r2_thr;  // largest d2 with sqrt(d2) <= neighbor_radius (exact membership test)
+  T r2_thr;   // largest d2 with sqrt(d2) <= neighbor_radius (exact membership test)
+  T r2_scan;  // r2_thr widened by >= 8 ulps: the fused scan's superset threshold
   T bx0, bx1, by0, by1;
   T lin_decay, ang_decay;  // movable bodies: 1 - damping * dt
   int K;                   // max_neighbors

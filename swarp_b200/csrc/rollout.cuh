@@ -429,10 +429,12 @@ __device__ __forceinline__ void get_xy(const T* xy_env, int j, T& x, T& y) {
   y = xy_env[xslot<T>(j) + 2];
 }
 
-// Membership mask of agents [32c, 32c + 32) of one env within the neighbor radius of
-// (px, py) (self not removed). Bit j is the sign of dx^2 + (dy^2 - R^2), shifted in with
-// one funnel shift per neighbor, neighbors visited in descending index. AS > 0: the env
-// has exactly AS agents (compile-time).
+// Candidate mask of agents [32c, 32c + 32) of one env near (px, py) (self not removed):
+// bit j is the sign of dx^2 + (dy^2 - thr), two fused roundings, shifted in with one
+// funnel shift per neighbor, neighbors visited in descending index. Called with the
+// widened threshold W.r2_scan, the mask is a superset of the exact in-radius set (see
+// in_radius); callers drop the few extra bits. AS > 0: the env has exactly AS agents
+// (compile-time).
 template <int AS>
 __device__ __forceinline__ unsigned scan_chunk(const float* xy_env, int c, int npairs, float px,
                                                float py, float thr) {
@@ -476,24 +478,28 @@ __device__ __forceinline__ unsigned scan_chunk(const double* xy_env, int c, int 
 }
 
 // Calls fn(b, q) for every agent b != a of the env within the neighbor radius, ascending
-// b, with q = b's (x, y, vx, vy) record. Returns the count of such agents.
+// b, with q = b's (x, y, vx, vy) record. Returns the count of such agents. thr_scan is
+// the scan's widened threshold, thr the exact one (in_radius).
 template <typename T, int AS, typename Fn>
 __device__ __forceinline__ int for_each_in_radius(const T* xy_env, const typename V4<T>::t* rec_env,
-                                                  int A, int a, T px, T py, T thr, Fn&& fn) {
+                                                  int A, int a, T px, T py, T thr_scan, T thr,
+                                                  Fn&& fn) {
   const int NP = (A + 1) / 2;
   int total = 0;
   const int nchunk = AS > 0 ? (AS + 31) / 32 : (A + 31) / 32;
   for (int c = 0; c < nchunk; ++c) {
     const int npairs = min(16, NP - c * 16);
-    unsigned m = scan_chunk<AS>(xy_env, c, npairs, px, py, thr);
+    unsigned m = scan_chunk<AS>(xy_env, c, npairs, px, py, thr_scan);
     const int rel = a - 32 * c;
     if (rel >= 0 && rel < 32) m &= ~(1u << rel);
-    total += __popc(m);
     while (m) {
       const int jj = __ffs(m) - 1;
       m &= m - 1u;
       const int b = 32 * c + jj;
-      fn(b, rec_env[b]);
+      const auto q = rec_env[b];
+      if (!in_radius(px - q.x, py - q.y, thr)) continue;
+      ++total;
+      fn(b, q);
     }
   }
   return total;
@@ -510,7 +516,7 @@ __device__ __forceinline__ int neighbor_force(const T* xy_env, const typename V4
   int listed = 0;
   cutoff = A;
   cmask = 0u;
-  const int total = for_each_in_radius<T, AS>(xy_env, rec_env, A, a, x.px, x.py, W.r2_thr,
+  const int total = for_each_in_radius<T, AS>(xy_env, rec_env, A, a, x.px, x.py, W.r2_scan, W.r2_thr,
                                               [&](int b, const typename V4<T>::t& q) {
     if (FL & F_TRUNC) {
       if (listed >= W.K) return;
@@ -547,7 +553,7 @@ __device__ __forceinline__ int neighbor_force_box(const T* xy_env, const typenam
   cmask = 0u;
   const Ob<T> oa = ob_of(x.px, x.py, x.th, x.vx, x.vy, x.w, P.hx, P.hy);
   const bool box_a = P.box != 0;
-  const int total = for_each_in_radius<T, AS>(xy_env, rec_env, A, a, x.px, x.py, W.r2_thr,
+  const int total = for_each_in_radius<T, AS>(xy_env, rec_env, A, a, x.px, x.py, W.r2_scan, W.r2_thr,
                                               [&](int b, const typename V4<T>::t& q) {
     if (FL & F_TRUNC) {
       if (listed >= W.K) return;
@@ -889,7 +895,7 @@ __device__ __forceinline__ void force_vjp(const T* xy_env, const typename V4<T>:
     }
   } else if (FL & F_COLL) {
     const int cut_a = (FL & F_TRUNC) ? cut_env[a] : A;
-    for_each_in_radius<T, AS>(xy_env, rec_env, A, a, x.px, x.py, W.r2_thr,
+    for_each_in_radius<T, AS>(xy_env, rec_env, A, a, x.px, x.py, W.r2_scan, W.r2_thr,
                               [&](int b, const T4& q) {
       const bool own = !(FL & F_TRUNC) || b <= cut_a;
       const bool cross = !(FL & F_TRUNC) || a <= cut_env[b];
@@ -950,7 +956,7 @@ __device__ __forceinline__ void force_vjp_box(const T* xy_env, const typename V4
     }
   } else if (FL & F_COLL) {
     const int cut_a = (FL & F_TRUNC) ? cut_env[a] : A;
-    for_each_in_radius<T, AS>(xy_env, rec_env, A, a, x.px, x.py, W.r2_thr,
+    for_each_in_radius<T, AS>(xy_env, rec_env, A, a, x.px, x.py, W.r2_scan, W.r2_thr,
                               [&](int b, const T4& q) {
       pair(b, q, !(FL & F_TRUNC) || b <= cut_a, !(FL & F_TRUNC) || a <= cut_env[b]);
     });
@@ -1365,7 +1371,7 @@ __global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : 1024)
 
 // ============================================================ neighbor lists
 template <typename T>
-__global__ void __launch_bounds__(1024) neighbors_kernel(int E, int A, int G, int K, T r2_thr,
+__global__ void __launch_bounds__(1024) neighbors_kernel(int E, int A, int G, int K, T r2_scan, T r2_thr,
                                                          const T* pos, int* idx, int* count,
                                                          int* true_count) {
   using T2 = typename V2<T>::t;
@@ -1387,7 +1393,7 @@ __global__ void __launch_bounds__(1024) neighbors_kernel(int E, int A, int G, in
   srec[tid] = T4{p.x, p.y, T(0), T(0)};
   __syncthreads();
   int listed = 0;
-  const int total = for_each_in_radius<T, 0>(xy_env, srec + le * A, A, a, p.x, p.y, r2_thr,
+  const int total = for_each_in_radius<T, 0>(xy_env, srec + le * A, A, a, p.x, p.y, r2_scan, r2_thr,
                                              [&](int b, const T4&) {
     if (listed < K) {
       if (valid) idx[ia * K + listed] = b;

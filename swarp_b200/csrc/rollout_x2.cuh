@@ -30,8 +30,9 @@ constexpr int kX2Threads = 8;     // threads per env
 #define SWARP_X2_BWD_MINB 10
 #endif
 
-// Both agents' in-radius masks over the env (self bits included): one 16-byte table
-// load per pair of candidates, shared by the two agents.
+// Both agents' candidate masks over the env (self bits included; a superset of the
+// in-radius sets at thr = W.r2_scan): one 16-byte table load per pair of candidates,
+// shared by the two agents.
 __device__ __forceinline__ void scan_pair16(const float* xy_env, const Agent<float>& x0,
                                             const Agent<float>& x1, float thr, unsigned& m0,
                                             unsigned& m1) {
@@ -56,18 +57,21 @@ __device__ __forceinline__ void scan_pair16(const float* xy_env, const Agent<flo
   }
 }
 
-// Contact force on agent a from the agents of its in-radius mask m (self removed),
-// ascending index; returns the contact mask.
+// Contact force on agent a from the members of its candidate mask m (self removed,
+// ascending index; candidates outside the exact radius skipped); returns the contact mask
+// and adds the member count to cnt.
 __device__ __forceinline__ unsigned contacts_of(const float4* rec_env, const float* rad_env,
                                                 unsigned m, const Agent<float>& x,
                                                 const AgentP<float>& P, const WorldC<float>& W,
-                                                float& fx, float& fy) {
+                                                float& fx, float& fy, int& cnt) {
   unsigned cm = 0u;
   while (m) {
     const int b = __ffs(m) - 1;
     m &= m - 1u;
     const float4 q = rec_env[b];
     const float dx = x.px - q.x, dy = x.py - q.y;
+    if (!in_radius(dx, dy, W.r2_thr)) continue;
+    ++cnt;
     if (pair_force_add(dx, dy, dot2(dx, dy, dx, dy), x.vx - q.z, x.vy - q.w,
                        P.radius + rad_env[b] + W.margin, P.inv_denom, W, fx, fy))
       cm |= 1u << b;
@@ -163,14 +167,15 @@ __global__ void __launch_bounds__(64, SWARP_X2_FWD_MINB) rollout_fwd_x2_kernel(c
       rec_env[a0 + 1] = make_float4(x1.px, x1.py, x1.vx, x1.vy);
       __syncthreads();
       unsigned m0, m1;
-      scan_pair16(xy_env, x0, x1, W.r2_thr, m0, m1);
+      scan_pair16(xy_env, x0, x1, W.r2_scan, m0, m1);
       m0 &= ~(1u << a0);
       m1 &= ~(1u << (a0 + 1));
-      tmax0 = max(tmax0, __popc(m0));
-      tmax1 = max(tmax1, __popc(m1));
       float fx0 = 0.f, fy0 = 0.f, fx1 = 0.f, fy1 = 0.f;
-      const unsigned c0 = contacts_of(rec_env, rad_env, m0, x0, P0, W, fx0, fy0);
-      const unsigned c1 = contacts_of(rec_env, rad_env, m1, x1, P1, W, fx1, fy1);
+      int n0 = 0, n1 = 0;
+      const unsigned c0 = contacts_of(rec_env, rad_env, m0, x0, P0, W, fx0, fy0, n0);
+      const unsigned c1 = contacts_of(rec_env, rad_env, m1, x1, P1, W, fx1, fy1, n1);
+      tmax0 = max(tmax0, n0);
+      tmax1 = max(tmax1, n1);
       if (valid)
         reinterpret_cast<uint2*>(R.cmask)[(((long long)t * R.S + k) * EA + ia) >> 1] =
             make_uint2(c0, c1);

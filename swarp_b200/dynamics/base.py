@@ -36,14 +36,16 @@ class ControlMode(IntEnum):
 
 
 class AgentShape(IntEnum):
-    """Agent footprint tag. Only ``DISC`` agents run on the CUDA path."""
+    """Agent footprint tag: a disc of ``radius`` or an oriented box of half extents
+    ``half_extents`` (both run on the CUDA path)."""
 
     DISC = 0
     BOX = 1
 
 
 class Integrator(Enum):
-    """Time integrator. Only semi-implicit ``EULER`` runs on the CUDA path."""
+    """Time integrator of every substep: semi-implicit ``EULER`` or classic ``RK4`` (both
+    run on the CUDA path)."""
 
     EULER = "euler"
     RK4 = "rk4"

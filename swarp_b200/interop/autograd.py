@@ -39,32 +39,25 @@ class TorchState(NamedTuple):
     body_rates: torch.Tensor | None = None
 
 
-_DRONE_DEFAULTS: dict[tuple, tuple[torch.Tensor, ...]] = {}
-
-
 def fill_state_defaults(state: TorchState) -> TorchState:
-    """Materialise absent drone fields as zeros (identity attitude).
-
-    The 2-D path never writes these fields, so the defaults of one batch shape are
-    allocated once and shared (read-only) by every state that omits them.
+    """Materialise absent drone fields as zeros (identity attitude), freshly allocated on
+    every call with the batch shape, device and dtype of ``pos`` (reference
+    ``swarp/interop/autograd.py:48-68``): the tensors a state returns are its own, so a
+    caller may edit them in place without touching any other state.
     """
     if all(t is not None for t in state):
         return state
     ref = state.pos
     E, A = ref.shape[0], ref.shape[1]
-    key = (E, A, ref.dtype, ref.device)
-    dflt = _DRONE_DEFAULTS.get(key)
-    if dflt is None:
-        opts = {"device": ref.device, "dtype": ref.dtype}
+    opts = {"device": ref.device, "dtype": ref.dtype}
+    z = state.z if state.z is not None else torch.zeros(E, A, **opts)
+    vz = state.vz if state.vz is not None else torch.zeros(E, A, **opts)
+    if state.attitude is not None:
+        att = state.attitude
+    else:
         att = torch.zeros(E, A, 4, **opts)
         att[..., 3] = 1.0
-        dflt = (torch.zeros(E, A, **opts), torch.zeros(E, A, **opts), att,
-                torch.zeros(E, A, 3, **opts))
-        _DRONE_DEFAULTS[key] = dflt
-    z = state.z if state.z is not None else dflt[0]
-    vz = state.vz if state.vz is not None else dflt[1]
-    att = state.attitude if state.attitude is not None else dflt[2]
-    br = state.body_rates if state.body_rates is not None else dflt[3]
+    br = state.body_rates if state.body_rates is not None else torch.zeros(E, A, 3, **opts)
     return state._replace(z=z, vz=vz, attitude=att, body_rates=br)
 
 

@@ -21,7 +21,7 @@ from collections.abc import Callable
 import torch
 
 from swarp_b200.core.stepper import Stepper
-from swarp_b200.interop.autograd import TorchState, Trajectory, rollout
+from swarp_b200.interop.autograd import TorchState, Trajectory, fill_state_defaults, rollout
 
 
 class GraphedRollout:
@@ -62,6 +62,9 @@ class GraphedRollout:
         # reached back into the caller's graph would leave the capture stream.
         self.actions = actions.detach().to(dev, copy=True).requires_grad_(True)
         self.state = TorchState(*(t.detach().to(dev, copy=True) for t in tuple(state)[:5]))
+        # the drone fields a 2-D fleet passes through, materialised once outside the capture
+        # (the graph then holds no allocation or fill of them)
+        self.state = fill_state_defaults(self.state)
         if wrt_state:
             for t in self.state[:5]:
                 t.requires_grad_(True)

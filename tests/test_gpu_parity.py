@@ -82,8 +82,14 @@ def run_cuda(stepper, state5, acts, weights, dtype, final_w=None):
 
 
 def close(got, ref, rtol, what):
+    """Max-normalised (|got - ref| <= rtol * (|ref| + max|ref|)) and elementwise: every
+    element with |ref| >= 1e-2 max|ref| within 10 rtol of itself."""
     scale = max(float(ref.abs().max()), 1e-30)
     torch.testing.assert_close(got, ref, rtol=rtol, atol=rtol * scale, msg=lambda m: f"{what}: {m}")
+    big = ref.abs() >= 1e-2 * scale
+    if bool(big.any()):
+        worst = float(((got - ref).abs()[big] / ref.abs()[big]).max())
+        assert worst <= 10 * rtol, f"{what}: elementwise relative error {worst:.3g}"
 
 
 def check(stepper, state5, acts, seed=0, dtype=torch.float64, rtol_f=1e-10, rtol_g=1e-10,
