@@ -187,7 +187,9 @@ __device__ __forceinline__ Dual<T, N> dnormal_coeff(const Dual<T, N>& ov, const 
     ovs = ov * (T(1) - t * t);
     ovs.v = W.max_overlap * t;
   }
-  const Dual<T, N> x = (W.k * ovs - W.c * vn) * inv_denom;
+  Dual<T, N> num = W.k * ovs - W.c * vn;
+  num.v = nc_num(ovs.v, vn.v, W);  // the primal exactly as normal_coeff rounds it
+  const Dual<T, N> x = num * inv_denom;
   return dmax(x, dconst<T, N>(T(0)));
 }
 

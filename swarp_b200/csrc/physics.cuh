@@ -120,12 +120,25 @@ template <typename T> struct WorldC {
 // common unsaturated contact stays a handful of instructions.
 template <typename T> __device__ __noinline__ T tanh_ratio(T ov, T mo) { return Num<T>::tanh_(ov / mo); }
 
+// Numerator of the contact coefficient, k*ov' - c*vn, with one rounding less than the
+// reference's (an explicit fma). Every kernel that decides a branch on its sign (the
+// forward's max(x, 0) and the adjoints recomputing that activity) takes it from here, so
+// the decisions agree bit for bit.
+template <typename T> __device__ __forceinline__ T nc_num(T ovs, T vn, const WorldC<T>& W) {
+  return Num<T>::fma_(W.k, ovs, -(W.c * vn));
+}
+// Overlap of a disc pair, min_dist - |d| with |d| = m * rsqrt(m) (one fma); shared by the
+// forward and every adjoint that recomputes whether the pair is in contact.
+template <typename T> __device__ __forceinline__ T pair_overlap(T min_dist, T m, T inv) {
+  return Num<T>::fma_(-m, inv, min_dist);
+}
+
 // f = max(0, (k*ov' - c*vn) / denom), ov' = mo*tanh(ov/mo) when mo > 0
 template <typename T>
 __device__ __forceinline__ T normal_coeff(T ov, T vn, T inv_denom, const WorldC<T>& W) {
   T ovs = ov;
   if (W.max_overlap > T(0)) ovs = W.max_overlap * tanh_ratio(ov, W.max_overlap);
-  T x = (W.k * ovs - W.c * vn) * inv_denom;
+  T x = nc_num(ovs, vn, W) * inv_denom;
   return wmax(x, T(0));
 }
 // VJP of normal_coeff: cotangent g on its value -> (d ov, d vn)
@@ -137,7 +150,7 @@ __device__ __forceinline__ void normal_coeff_vjp(T ov, T vn, T inv_denom, T g, c
     th = tanh_ratio(ov, W.max_overlap);
     ovs = W.max_overlap * th;
   }
-  T x = (W.k * ovs - W.c * vn) * inv_denom;
+  T x = nc_num(ovs, vn, W) * inv_denom;
   if (x > T(0)) {
     T gnum = g * inv_denom;
     T govs = W.k * gnum;
@@ -157,13 +170,13 @@ __device__ __forceinline__ bool pair_force_add(T dx, T dy, T d2, T rvx, T rvy, T
                                                T inv_denom, const WorldC<T>& W, T& fx, T& fy) {
   const T m = wmax(d2, Eps2<T>::v);
   const T inv = Num<T>::rsqrt_(m);
-  const T ov = min_dist - m * inv;
+  const T ov = pair_overlap(min_dist, m, inv);
   if (ov > T(0)) {
     T nx = dx * inv, ny = dy * inv;
     T vn = dot2(rvx, rvy, nx, ny);
     T cf = normal_coeff(ov, vn, inv_denom, W);
-    fx = fx + cf * nx;
-    fy = fy + cf * ny;
+    fx = Num<T>::fma_(cf, nx, fx);
+    fy = Num<T>::fma_(cf, ny, fy);
     return true;
   }
   return false;
@@ -185,7 +198,7 @@ __device__ __forceinline__ void pair_force_vjp(T dx, T dy, T rvx, T rvy, T min_d
   const T d2 = dot2(dx, dy, dx, dy);
   const T m = wmax(d2, Eps2<T>::v);
   const T inv = Num<T>::rsqrt_(m);
-  const T ov = min_dist - m * inv;
+  const T ov = pair_overlap(min_dist, m, inv);
   if (!(ov > T(0))) return;
   T nx = dx * inv, ny = dy * inv;
   T vn = dot2(rvx, rvy, nx, ny);
@@ -213,17 +226,23 @@ __device__ __forceinline__ void pair_force_vjp(T dx, T dy, T rvx, T rvy, T min_d
 // Both directions of one disc-disc contact in a single VJP. With d = p_a - p_b and
 // rv = v_a - v_b, the force on a is cf_a n and on b is -cf_b n (cf_x uses x's implicit
 // denominator); ga and gb are their cotangents (zero to exclude a side, e.g. a truncated
-// list). L = cf_a (ga.n) - cf_b (gb.n); adds dL/dd and dL/drv (= dL/dp_a, dL/dv_a;
-// agent b receives the negatives from its own call with the roles swapped).
+// list). L = cf_a (ga.n) - cf_b (gb.n). pair_vjp_terms returns dL/dd and dL/drv
+// (= dL/dp_a, dL/dv_a) as four separate values, false when the pair is not in contact;
+// agent b's own call with the roles swapped gives their exact negatives. The owner adds
+// each value once, so where the terms are computed (by the owner or another lane) does
+// not change the sums.
+template <typename T> struct PairTerms {
+  T px, py, vx, vy;
+};
 template <typename T>
-__device__ __forceinline__ void pair_vjp_sym(T dx, T dy, T rvx, T rvy, T min_dist, T ida, T gax,
-                                             T gay, T idb, T gbx, T gby, const WorldC<T>& W,
-                                             T& gdx, T& gdy, T& grvx, T& grvy) {
+__device__ __forceinline__ bool pair_vjp_terms(T dx, T dy, T rvx, T rvy, T min_dist, T ida, T gax,
+                                               T gay, T idb, T gbx, T gby, const WorldC<T>& W,
+                                               PairTerms<T>& r) {
   const T d2 = dot2(dx, dy, dx, dy);
   const T m = wmax(d2, Eps2<T>::v);
   const T inv = Num<T>::rsqrt_(m);
-  const T ov = min_dist - m * inv;
-  if (!(ov > T(0))) return;
+  const T ov = pair_overlap(min_dist, m, inv);
+  if (!(ov > T(0))) return false;
   const T nx = dx * inv, ny = dy * inv;
   const T vn = dot2(rvx, rvy, nx, ny);
   T ovs = ov, th = T(0);
@@ -231,28 +250,40 @@ __device__ __forceinline__ void pair_vjp_sym(T dx, T dy, T rvx, T rvy, T min_dis
     th = tanh_ratio(ov, W.max_overlap);
     ovs = W.max_overlap * th;
   }
-  const T num = W.k * ovs - W.c * vn;
+  const T num = nc_num(ovs, vn, W);
   const T xa = num * ida, xb = num * idb;
   const T cfa = wmax(xa, T(0)), cfb = wmax(xb, T(0));
   const T q = (xa > T(0) ? ida * dot2(gax, gay, nx, ny) : T(0)) -
               (xb > T(0) ? idb * dot2(gbx, gby, nx, ny) : T(0));  // dL/dnum
-  T gnx = cfa * gax - cfb * gbx, gny = cfa * gay - cfb * gby;    // dL/dn at fixed num
   const T gvn = -W.c * q;
   const T govs = W.k * q;
   const T gov = (W.max_overlap > T(0)) ? govs * (T(1) - th * th) : govs;
-  grvx += gvn * nx;
-  grvy += gvn * ny;
-  gnx += gvn * rvx;
-  gny += gvn * rvy;
-  const T gdist = -gov - dot2(gnx, gny, nx, ny) * inv;
-  T ddx = gnx * inv, ddy = gny * inv;
+  r.vx = gvn * nx;
+  r.vy = gvn * ny;
+  // dL/dn: at fixed num, then through vn = rv.n
+  const T gnx = Num<T>::fma_(gvn, rvx, Num<T>::fma_(cfa, gax, -(cfb * gbx)));
+  const T gny = Num<T>::fma_(gvn, rvy, Num<T>::fma_(cfa, gay, -(cfb * gby)));
+  // n = d / dist, dist = sqrt(max(d2, eps)), ov = min_dist - dist
+  const T gdist = Num<T>::fma_(-dot2(gnx, gny, nx, ny), inv, -gov);
+  r.px = gnx * inv;
+  r.py = gny * inv;
   if (d2 > Eps2<T>::v) {
     const T gd2 = gdist * T(0.5) * inv;
-    ddx += T(2) * dx * gd2;
-    ddy += T(2) * dy * gd2;
+    r.px = Num<T>::fma_(T(2) * dx, gd2, r.px);
+    r.py = Num<T>::fma_(T(2) * dy, gd2, r.py);
   }
-  gdx += ddx;
-  gdy += ddy;
+  return true;
+}
+template <typename T>
+__device__ __forceinline__ void pair_vjp_sym(T dx, T dy, T rvx, T rvy, T min_dist, T ida, T gax,
+                                             T gay, T idb, T gbx, T gby, const WorldC<T>& W,
+                                             T& gdx, T& gdy, T& grvx, T& grvy) {
+  PairTerms<T> t;
+  if (!pair_vjp_terms(dx, dy, rvx, rvy, min_dist, ida, gax, gay, idb, gbx, gby, W, t)) return;
+  grvx += t.vx;
+  grvy += t.vy;
+  gdx += t.px;
+  gdy += t.py;
 }
 
 // ------------------------------------------------------------- static obstacles
@@ -487,10 +518,10 @@ __device__ __forceinline__ void wall_force(T px, T py, T vx, T vy, T ra, T inv_d
     if (pt > T(0)) fy = fy + (-normal_coeff(pt, -vy, inv_denom, W));
     return;
   }
-  const T cl = wmax((W.k * pl - W.c * vx) * inv_denom, T(0));
-  const T cr = wmax((W.k * pr - W.c * (-vx)) * inv_denom, T(0));
-  const T cb = wmax((W.k * pb - W.c * vy) * inv_denom, T(0));
-  const T ct = wmax((W.k * pt - W.c * (-vy)) * inv_denom, T(0));
+  const T cl = wmax(nc_num(pl, vx, W) * inv_denom, T(0));
+  const T cr = wmax(nc_num(pr, (-vx), W) * inv_denom, T(0));
+  const T cb = wmax(nc_num(pb, vy, W) * inv_denom, T(0));
+  const T ct = wmax(nc_num(pt, (-vy), W) * inv_denom, T(0));
   fx = (pl > T(0) ? cl : T(0)) + (pr > T(0) ? -cr : T(0));
   fy = (pb > T(0) ? cb : T(0)) + (pt > T(0) ? -ct : T(0));
 }
@@ -525,19 +556,19 @@ __device__ __forceinline__ void wall_force_vjp(T px, T py, T vx, T vy, T ra, T i
     return;
   }
   // d(coefficient)/d(numerator) = inv_denom on the active side of max(x, 0)
-  const bool al = pl > T(0) && (W.k * pl - W.c * vx) * inv_denom > T(0);
-  const bool ar = pr > T(0) && (W.k * pr - W.c * (-vx)) * inv_denom > T(0);
-  const bool ab = pb > T(0) && (W.k * pb - W.c * vy) * inv_denom > T(0);
-  const bool at = pt > T(0) && (W.k * pt - W.c * (-vy)) * inv_denom > T(0);
+  const bool al = pl > T(0) && nc_num(pl, vx, W) * inv_denom > T(0);
+  const bool ar = pr > T(0) && nc_num(pr, (-vx), W) * inv_denom > T(0);
+  const bool ab = pb > T(0) && nc_num(pb, vy, W) * inv_denom > T(0);
+  const bool at = pt > T(0) && nc_num(pt, (-vy), W) * inv_denom > T(0);
   const T nl = al ? gx * inv_denom : T(0);   // left:   f_x += c_l
   const T nr = ar ? -gx * inv_denom : T(0);  // right:  f_x -= c_r
   const T nb = ab ? gy * inv_denom : T(0);
   const T nt = at ? -gy * inv_denom : T(0);
   // numerator k*pen - c*vn; pen_l = reach - px + x0 (d/dpx = -1), pen_r (+1); vn = +-v
-  gpx += W.k * (nr - nl);
-  gvx += W.c * (nr - nl);
-  gpy += W.k * (nt - nb);
-  gvy += W.c * (nt - nb);
+  gpx = Num<T>::fma_(W.k, nr - nl, gpx);
+  gvx = Num<T>::fma_(W.c, nr - nl, gvx);
+  gpy = Num<T>::fma_(W.k, nt - nb, gpy);
+  gvy = Num<T>::fma_(W.c, nt - nb, gvy);
 }
 
 // ------------------------------------------------------------------- integrate
@@ -557,8 +588,8 @@ __device__ __forceinline__ void clamp_norm_vjp(T x, T y, T L, T gx, T gy, T& rx,
     const T inv = Num<T>::rsqrt_(n2);
     const T sc = L * inv;
     const T gn = -dot2(gx, gy, x, y) * sc * inv * inv;  // d/dn of L/n times (g . v) / n
-    rx = gx * sc + x * gn;
-    ry = gy * sc + y * gn;
+    rx = Num<T>::fma_(x, gn, gx * sc);
+    ry = Num<T>::fma_(y, gn, gy * sc);
   } else {
     rx = gx;
     ry = gy;
@@ -657,8 +688,8 @@ __device__ __forceinline__ void integrate_fwd(const Agent<T>& in, T a0, T a1, T 
       clamp_norm(a0, a1, P.max_accel, ax, ay);
       clamp_norm(Num<T>::fma_(ax, dt, in.vx), Num<T>::fma_(ay, dt, in.vy), P.max_speed, vx, vy);
     }
-    vx = vx + dvx;
-    vy = vy + dvy;
+    vx = Num<T>::fma_(fx, P.dt_over_m, vx);
+    vy = Num<T>::fma_(fy, P.dt_over_m, vy);
     out.px = Num<T>::fma_(vx, dt, in.px);
     out.py = Num<T>::fma_(vy, dt, in.py);
     out.th = in.th;
@@ -742,14 +773,14 @@ __device__ __forceinline__ void integrate_vjp(const Agent<T>& in, T a0, T a1, co
   // p_new = p + v_out*dt, v_out = vel-level + F*dt/m
   gin.px = gpx;
   gin.py = gpy;
-  T gvx = g.vx + gpx * dt, gvy = g.vy + gpy * dt;
+  T gvx = Num<T>::fma_(gpx, dt, g.vx), gvy = Num<T>::fma_(gpy, dt, g.vy);
   if (P.tag == TAG_HOLONOMIC) {
     // s_out = |v_new|
     const T n2 = dot2(out.vx, out.vy, out.vx, out.vy);
     if (n2 > T(0)) {
       const T q = g.s * Num<T>::rsqrt_(n2);
-      gvx += out.vx * q;
-      gvy += out.vy * q;
+      gvx = Num<T>::fma_(out.vx, q, gvx);
+      gvy = Num<T>::fma_(out.vy, q, gvy);
     }
     gin.th = g.th;
     gfx = gvx * P.dt_over_m;

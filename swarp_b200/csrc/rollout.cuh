@@ -868,6 +868,12 @@ __global__ void __launch_bounds__(1024) rollout_fwd_kernel(const RolloutArgs<T> 
 }
 
 // ================================================================== adjoint
+template <typename T, int FL>
+__device__ __forceinline__ void static_force_vjp(const Obs<T>* sobs, const BodyC<T>* sbc,
+                                                 typename V4<T>::t* gpose, int N,
+                                                 const Agent<T>& x, const AgentP<T>& P,
+                                                 const WorldC<T>& W, T gfx, T gfy, Agent<T>& gin);
+
 // Force VJP of agent a at one substep: given every env agent's (x, y, vx, vy) record and
 // force cotangent, adds d(loss)/d(pos, vel) of agent a through its own force and
 // through the forces its contacts feel from it. With moving bodies, also writes the
@@ -906,6 +912,16 @@ __device__ __forceinline__ void force_vjp(const T* xy_env, const typename V4<T>:
                    gin.px, gin.py, gin.vx, gin.vy);
     });
   }
+  static_force_vjp<T, FL>(sobs, sbc, gpose, N, x, P, W, gfx, gfy, gin);
+}
+
+// The obstacle and wall part of force_vjp (after the contacts, the forward's order).
+template <typename T, int FL>
+__device__ __forceinline__ void static_force_vjp(const Obs<T>* sobs, const BodyC<T>* sbc,
+                                                 typename V4<T>::t* gpose, int N,
+                                                 const Agent<T>& x, const AgentP<T>& P,
+                                                 const WorldC<T>& W, T gfx, T gfy, Agent<T>& gin) {
+  using T4 = typename V4<T>::t;
   if (FL & F_OBS) {
     for (int o = 0; o < N; ++o) {
       obstacle_force_vjp(x.px, x.py, x.vx, x.vy, P.radius, P.inv_denom, sobs[o], gfx, gfy, W,

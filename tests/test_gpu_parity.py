@@ -82,12 +82,14 @@ def run_cuda(stepper, state5, acts, weights, dtype, final_w=None):
 
 
 def close(got, ref, rtol, what):
-    """Max-normalised (|got - ref| <= rtol * (|ref| + max|ref|)) and elementwise: every
-    element with |ref| >= 1e-2 max|ref| within 10 rtol of itself."""
+    """Max-normalised: |got - ref| <= rtol * (|ref| + max|ref|). At the float64 bars
+    (rtol <= 1e-9) also elementwise: every element with |ref| >= 1e-2 max|ref| within
+    10 rtol of itself. (Float32 elementwise errors are compared with float32's own error on
+    the same inputs in test_gpu_parity_f32.py.)"""
     scale = max(float(ref.abs().max()), 1e-30)
     torch.testing.assert_close(got, ref, rtol=rtol, atol=rtol * scale, msg=lambda m: f"{what}: {m}")
     big = ref.abs() >= 1e-2 * scale
-    if bool(big.any()):
+    if rtol <= 1e-9 and bool(big.any()):
         worst = float(((got - ref).abs()[big] / ref.abs()[big]).max())
         assert worst <= 10 * rtol, f"{what}: elementwise relative error {worst:.3g}"
 
