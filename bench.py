@@ -487,7 +487,7 @@ def main() -> None:
         return
 
     from swarp_b200.core.sharding import PairReducer, reduce_loss_and_grad_norm
-    from swarp_b200.interop.autograd import TorchState, rollout, rollout_bodies
+    from swarp_b200.interop.autograd import FusedGoalLoss, TorchState, rollout, rollout_bodies
     from swarp_b200.interop.graphs import GraphedRollout
 
     torch.cuda.set_device(local)
@@ -549,7 +549,9 @@ def main() -> None:
     # the host), then the (loss, ||g||^2) all-reduce across ranks
     graphed = reducer = None
     if not wl.body:
-        graphed = GraphedRollout(st, state, acts, loss_fn,
+        # the same loss fused into the rollout kernels (rollout_goal_loss): the step is the
+        # forward kernel, one small reduction and the adjoint kernel
+        graphed = GraphedRollout(st, state, acts, FusedGoalLoss(goal),
                                  grad_norm="fused" if dist is not None else False, warmup=3)
 
         # a ring of 8 pending reductions: on some 4-GPU boxes the 2-element all-reduce took
@@ -643,9 +645,7 @@ def main() -> None:
     if graphed is not None:
         from swarp_b200.interop.streamed import StreamedRollout
 
-        streamed = StreamedRollout(
-            st, E, H, 2, lambda fin, _traj, g: torch.nn.functional.mse_loss(
-                fin.pos, g, reduction="sum"), aux_like=[goal], chunks=args.e2e_chunks)
+        streamed = StreamedRollout(st, E, H, 2, "goal", aux_like=[goal], chunks=args.e2e_chunks)
         loss_h = torch.zeros(streamed.n_chunks, dtype=torch.float64).pin_memory()
         d2h = grad_h.numel() * grad_h.element_size() + loss_h.numel() * 8
 
@@ -746,10 +746,12 @@ def main() -> None:
                          if graphed is not None else
                          "eager rollout_bodies + autograd.grad; gradient copied back"),
                 "grad_matches_device_step": e2e_grad_ok},
-        # forward + adjoint per step, plus the fused-norm reduction when ranks all-reduce it
-        "gpu_launches": (3 if reducer is not None else 2) * args.steps,
+        # forward + loss reduction + adjoint per step, plus the fused-norm reduction when
+        # ranks all-reduce it
+        "gpu_launches": (4 if reducer is not None else 3) * args.steps,
         "timed_path": ("one CUDA-graph replay of the whole BPTT step per step "
-                       "(swarp_b200.interop.graphs.GraphedRollout)" if graphed is not None else
+                       "(swarp_b200.interop.graphs.GraphedRollout with the goal loss fused into "
+                       "the rollout kernels, rollout_goal_loss)" if graphed is not None else
                        "eager rollout_bodies + autograd.grad"),
         "value_eager": value_eager,
     }

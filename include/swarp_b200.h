@@ -123,6 +123,19 @@ typedef struct {
                                 oriented-box contacts of swarp/core/collisions.py:262-690 */
 } swarp_world_t;
 
+/* The fused goal loss L = sum over envs and agents of |pos_T - goal|^2 (pos_T: the
+ * positions after the last step). goal [E, A, 2] in the world's dtype, NULL = no loss.
+ * swarp_rollout_fwd writes L (one scalar of the world's dtype) to `loss`, reduced in a
+ * fixed order from per-CTA partials in the workspace's tail; swarp_rollout_bwd adds
+ * loss_grad[0] * dL/dpos_T (loss_grad: one device scalar, dL'/dL of the caller's loss)
+ * to the final-position cotangent. This is a fused fast path of the library: the
+ * reference's callers form such losses in torch after the rollout. */
+typedef struct {
+  const void* goal;
+  void* loss;             /* swarp_rollout_fwd output */
+  const void* loss_grad;  /* swarp_rollout_bwd input  */
+} swarp_goal_loss_t;
+
 /* Bytes of device workspace for this world and horizon: the contact checkpoint that
  * swarp_rollout_fwd fills and swarp_rollout_bwd reads, then the adjoint's per-CTA
  * partial sums for adj_actions_sqnorm (0 for an invalid world). */
@@ -136,13 +149,14 @@ size_t swarp_rollout_workspace_bytes(const swarp_world_t* w, int32_t horizon);
  *             within-radius neighbor count (overflow <=> > max_neighbors)
  *   bodies_init / bodies_traj: movable-body state at t=0 and after every step
  *             (required only when obstacles.any_movable)
+ *   goal_loss: the fused goal loss (goal NULL = none; loss required with a goal)
  *   workspace: device scratch of swarp_rollout_workspace_bytes() bytes, kept for the
  *             matching swarp_rollout_bwd call. */
 int swarp_rollout_fwd(const swarp_world_t* w, int32_t horizon, swarp_state_t init,
                       const void* actions, swarp_state_t traj, swarp_state_t final_out,
                       int32_t* true_count_max, swarp_bodies_t bodies_init,
-                      swarp_bodies_t bodies_traj, void* workspace, size_t workspace_bytes,
-                      void* stream);
+                      swarp_bodies_t bodies_traj, swarp_goal_loss_t goal_loss,
+                      void* workspace, size_t workspace_bytes, void* stream);
 
 /* Adjoint of swarp_rollout_fwd (same world, horizon, init, actions, traj, bodies and
  * workspace). Cotangents: adj_traj [T, ...] and adj_final (any field may be NULL =
@@ -153,13 +167,15 @@ int swarp_rollout_fwd(const swarp_world_t* w, int32_t horizon, swarp_state_t ini
  * partials go to the workspace's tail) instead of a second pass over adj_actions.
  * Deterministic: no atomics, fixed summation order. Moving bodies are differentiated
  * when all their shapes are circles (SWARP_ERR_UNSUPPORTED otherwise). The fused norm
- * has no counterpart in the reference (its callers compute it from the gradient). */
+ * has no counterpart in the reference (its callers compute it from the gradient).
+ * goal_loss: with a goal, loss_grad (required) seeds the goal loss's cotangent. */
 int swarp_rollout_bwd(const swarp_world_t* w, int32_t horizon, swarp_state_t init,
                       const void* actions, swarp_state_t traj, swarp_state_t adj_traj,
                       swarp_state_t adj_final, swarp_bodies_t bodies_init,
                       swarp_bodies_t bodies_traj, swarp_bodies_t adj_bodies_final,
                       void* adj_actions, swarp_state_t adj_init, void* adj_actions_sqnorm,
-                      void* workspace, size_t workspace_bytes, void* stream);
+                      swarp_goal_loss_t goal_loss, void* workspace, size_t workspace_bytes,
+                      void* stream);
 
 /* Padded within-radius neighbor lists of positions pos [E, A, 2] (brute force, ascending
  * agent index, capped at max_neighbors): idx [E, A, K] int32 (unused slots untouched),

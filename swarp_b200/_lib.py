@@ -51,6 +51,10 @@ class Bodies(C.Structure):
                 ("ang_vel", C.c_void_p)]
 
 
+class GoalLoss(C.Structure):
+    _fields_ = [("goal", C.c_void_p), ("loss", C.c_void_p), ("loss_grad", C.c_void_p)]
+
+
 class WorldC(C.Structure):
     _fields_ = [
         ("dtype", C.c_int32), ("n_envs", C.c_int32), ("n_agents", C.c_int32),
@@ -75,11 +79,11 @@ class WorldC(C.Structure):
 SIGNATURES = {
     "swarp_rollout_workspace_bytes": (C.c_size_t, [C.POINTER(WorldC), C.c_int32]),
     "swarp_rollout_fwd": (C.c_int, [C.POINTER(WorldC), C.c_int32, State, C.c_void_p, State, State,
-                                    C.c_void_p, Bodies, Bodies, C.c_void_p, C.c_size_t,
+                                    C.c_void_p, Bodies, Bodies, GoalLoss, C.c_void_p, C.c_size_t,
                                     C.c_void_p]),
     "swarp_rollout_bwd": (C.c_int, [C.POINTER(WorldC), C.c_int32, State, C.c_void_p, State, State,
                                     State, Bodies, Bodies, Bodies, C.c_void_p, State, C.c_void_p,
-                                    C.c_void_p, C.c_size_t, C.c_void_p]),
+                                    GoalLoss, C.c_void_p, C.c_size_t, C.c_void_p]),
     "swarp_neighbors": (C.c_int, [C.POINTER(WorldC), C.c_void_p, C.c_void_p, C.c_void_p,
                                   C.c_void_p, C.c_void_p]),
     "swarp_rollout_noalloc": (C.c_int, [C.POINTER(WorldC), C.c_int32, State, C.c_void_p, State,

@@ -381,7 +381,8 @@ class Stepper:
         return int(lib.swarp_rollout_workspace_bytes(C.byref(wc), horizon))
 
     def rollout_forward(self, state5, actions: torch.Tensor, *, final: bool = True,
-                        out=None, true_count: bool = False, moving_bodies: bool = True):
+                        out=None, true_count: bool = False, moving_bodies: bool = True,
+                        goal: torch.Tensor | None = None, loss_out: torch.Tensor | None = None):
         """Run the forward rollout kernel.
 
         ``state5`` are the ``n_state`` contiguous initial-state tensors (five, or nine with
@@ -389,7 +390,9 @@ class Stepper:
         is ``[T, E, A, act_dim]``. Movable bodies (if any) advance when ``moving_bodies``; the
         stepper then carries their final state. Returns ``(traj5, final5 | None,
         true_max | None, record)`` with ``traj5`` stacked ``[T, E, A(,k)]`` and ``record``
-        the :class:`RolloutRecord` the adjoint needs.
+        the :class:`RolloutRecord` the adjoint needs. With ``goal`` ``[E, A, 2]`` the kernel
+        also reduces the goal loss sum |pos_T - goal|^2 into ``loss_out`` (a 0-d tensor of
+        the stepper's dtype).
         """
         lib = _lib.load()
         H, E, _, D = actions.shape
@@ -427,6 +430,7 @@ class Stepper:
             _lib.state_c(fin) if fin else _lib.State(), _lib.ptr(tmax),
             _lib.Bodies(*(_lib.ptr(x) for x in bi)) if bi else _lib.Bodies(),
             _lib.Bodies(*(_lib.ptr(x) for x in bt)) if bt else _lib.Bodies(),
+            _lib.GoalLoss(_lib.ptr(goal), _lib.ptr(loss_out), None),
             ws.data_ptr(), nbytes, _lib.stream_ptr(self.device),
         )
         _lib.check(rc, "swarp_rollout_fwd")
@@ -435,11 +439,14 @@ class Stepper:
         return traj, fin, tmax, rec
 
     def rollout_backward(self, state5, actions, traj5, gtraj5, gfin5, record: RolloutRecord,
-                         gbody_final=None):
+                         gbody_final=None, goal: torch.Tensor | None = None,
+                         loss_grad: torch.Tensor | None = None):
         """Adjoint of :meth:`rollout_forward` for the same inputs and its ``record``.
 
         ``gbody_final``: cotangents of the final body state (pos, angle, vel, ang_vel;
-        entries may be None). Returns ``(grad_actions, grad_init5)``.
+        entries may be None). With ``goal``, ``loss_grad`` (a 0-d device tensor, the
+        cotangent of the goal loss) seeds that loss's gradient in the kernel. Returns
+        ``(grad_actions, grad_init5)``.
         """
         lib = _lib.load()
         g_act = torch.empty_like(actions)
@@ -460,7 +467,8 @@ class Stepper:
             _lib.state_c(traj5), _lib.state_c(gtraj5), _lib.state_c(gfin5),
             _lib.Bodies(*(_lib.ptr(x) for x in rec.body_init)) if rec.body_init else _lib.Bodies(),
             _lib.Bodies(*(_lib.ptr(x) for x in rec.body_traj)) if rec.body_traj else _lib.Bodies(),
-            gb, g_act.data_ptr(), _lib.state_c(g_init), _lib.ptr(sq), ws.data_ptr(), ws.numel(),
+            gb, g_act.data_ptr(), _lib.state_c(g_init), _lib.ptr(sq),
+            _lib.GoalLoss(_lib.ptr(goal), None, _lib.ptr(loss_grad)), ws.data_ptr(), ws.numel(),
             _lib.stream_ptr(self.device),
         )
         _lib.check(rc, "swarp_rollout_bwd")

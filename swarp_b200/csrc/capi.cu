@@ -15,7 +15,7 @@ using namespace swarp;
 
 namespace {
 
-constexpr int kAbiVersion = 6;
+constexpr int kAbiVersion = 7;
 
 int threads_target() {
   static int v = [] {
@@ -234,7 +234,8 @@ size_t partials_offset(const swarp_world_t* w, int horizon) {
   return (b + 255) & ~size_t(255);
 }
 size_t partials_bytes(const swarp_world_t* w) {
-  const int G = envs_per_cta(w->n_agents, w->n_envs);
+  // the CTA count of the generic or the two-agents-per-thread kernels, whichever is larger
+  const int G = std::min(envs_per_cta(w->n_agents, w->n_envs), x2_envs_per_cta(w->n_envs));
   const size_t n = (size_t)(w->n_envs + G - 1) / G;
   return n * (w->dtype == SWARP_F32 ? sizeof(float) : sizeof(double));
 }
@@ -242,9 +243,14 @@ size_t partials_bytes(const swarp_world_t* w) {
 template <typename T>
 int fwd_typed(const swarp_world_t* w, int horizon, swarp_state_t init, const void* actions,
               swarp_state_t traj, swarp_state_t fin, int32_t* true_max, swarp_bodies_t bi,
-              swarp_bodies_t bt, void* ws, cudaStream_t st) {
+              swarp_bodies_t bt, swarp_goal_loss_t gl, void* ws, cudaStream_t st) {
   RolloutArgs<T> R;
   fill_common<T>(w, horizon, R);
+  R.goal = static_cast<const T*>(gl.goal);
+  R.loss_out = static_cast<T*>(gl.loss);
+  R.loss_partial = gl.goal ? reinterpret_cast<T*>(static_cast<unsigned char*>(ws) +
+                                                  partials_offset(w, horizon))
+                           : nullptr;
   set_bodies<T>(bi, R.bi_pos, R.bi_ang, R.bi_vel, R.bi_om);
   R.bt_pos = static_cast<T*>(bt.pos);
   R.bt_ang = static_cast<T*>(bt.angle);
@@ -274,9 +280,11 @@ template <typename T>
 int bwd_typed(const swarp_world_t* w, int horizon, swarp_state_t init, const void* actions,
               swarp_state_t traj, swarp_state_t gtraj, swarp_state_t gfin, swarp_bodies_t bi,
               swarp_bodies_t bt, swarp_bodies_t gbf, void* gact, swarp_state_t ginit,
-              void* gsq, void* ws, cudaStream_t st) {
+              void* gsq, swarp_goal_loss_t gl, void* ws, cudaStream_t st) {
   RolloutArgs<T> R;
   fill_common<T>(w, horizon, R);
+  R.goal = static_cast<const T*>(gl.goal);
+  R.loss_grad = static_cast<const T*>(gl.loss_grad);
   set_bodies<T>(bi, R.bi_pos, R.bi_ang, R.bi_vel, R.bi_om);
   R.bt_pos = static_cast<T*>(bt.pos);
   R.bt_ang = static_cast<T*>(bt.angle);
@@ -333,10 +341,11 @@ size_t swarp_rollout_workspace_bytes(const swarp_world_t* w, int32_t horizon) {
 int swarp_rollout_fwd(const swarp_world_t* w, int32_t horizon, swarp_state_t init,
                       const void* actions, swarp_state_t traj, swarp_state_t final_out,
                       int32_t* true_count_max, swarp_bodies_t bodies_init,
-                      swarp_bodies_t bodies_traj, void* workspace, size_t workspace_bytes,
-                      void* stream) {
+                      swarp_bodies_t bodies_traj, swarp_goal_loss_t goal_loss, void* workspace,
+                      size_t workspace_bytes, void* stream) {
   int rc = validate_world(w, horizon);
   if (rc != SWARP_OK) return rc;
+  if (goal_loss.goal && !goal_loss.loss) return SWARP_ERR_INVALID_ARG;
   if (!state_complete(init) || !state_complete(traj) || !actions) return SWARP_ERR_INVALID_ARG;
   if ((flags_of(w) & F_BODIES) && (!bodies_complete(bodies_init) || !bodies_complete(bodies_traj)))
     return SWARP_ERR_INVALID_ARG;
@@ -354,9 +363,9 @@ int swarp_rollout_fwd(const swarp_world_t* w, int32_t horizon, swarp_state_t ini
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (w->dtype == SWARP_F32)
     return fwd_typed<float>(w, horizon, init, actions, traj, final_out, true_count_max, bodies_init,
-                            bodies_traj, workspace, st);
+                            bodies_traj, goal_loss, workspace, st);
   return fwd_typed<double>(w, horizon, init, actions, traj, final_out, true_count_max, bodies_init,
-                           bodies_traj, workspace, st);
+                           bodies_traj, goal_loss, workspace, st);
 }
 
 int swarp_rollout_bwd(const swarp_world_t* w, int32_t horizon, swarp_state_t init,
@@ -364,9 +373,11 @@ int swarp_rollout_bwd(const swarp_world_t* w, int32_t horizon, swarp_state_t ini
                       swarp_state_t adj_final, swarp_bodies_t bodies_init,
                       swarp_bodies_t bodies_traj, swarp_bodies_t adj_bodies_final,
                       void* adj_actions, swarp_state_t adj_init, void* adj_actions_sqnorm,
-                      void* workspace, size_t workspace_bytes, void* stream) {
+                      swarp_goal_loss_t goal_loss, void* workspace, size_t workspace_bytes,
+                      void* stream) {
   int rc = validate_world(w, horizon);
   if (rc != SWARP_OK) return rc;
+  if (goal_loss.goal && !goal_loss.loss_grad) return SWARP_ERR_INVALID_ARG;
   if ((flags_of(w) & F_BOXES) && (flags_of(w) & F_BODIES)) return SWARP_ERR_UNSUPPORTED;
   if (flags_of(w) & F_DRONE) {
     if (flags_of(w) & F_BODIES) return SWARP_ERR_UNSUPPORTED;
@@ -388,10 +399,10 @@ int swarp_rollout_bwd(const swarp_world_t* w, int32_t horizon, swarp_state_t ini
   if (w->dtype == SWARP_F32)
     return bwd_typed<float>(w, horizon, init, actions, traj, adj_traj, adj_final, bodies_init,
                             bodies_traj, adj_bodies_final, adj_actions, adj_init,
-                            adj_actions_sqnorm, workspace, st);
+                            adj_actions_sqnorm, goal_loss, workspace, st);
   return bwd_typed<double>(w, horizon, init, actions, traj, adj_traj, adj_final, bodies_init,
                            bodies_traj, adj_bodies_final, adj_actions, adj_init,
-                           adj_actions_sqnorm, workspace, st);
+                           adj_actions_sqnorm, goal_loss, workspace, st);
 }
 
 int swarp_neighbors(const swarp_world_t* w, const void* pos, int32_t* idx, int32_t* count,

@@ -9,8 +9,11 @@ namespace {
 template <int FL>
 int run_fwd_x2(const RolloutArgs<float>& R, cudaStream_t st) {
   const Layout<float> L(R.G, kX2Agents, R.N, R.S, false, false);
-  return launch_kernel(rollout_fwd_x2_kernel<FL>, (R.E + R.G - 1) / R.G, R.G * kX2Threads, L.total,
-                       st, &R);
+  const int grid = (R.E + R.G - 1) / R.G;
+  const int rc = launch_kernel(rollout_fwd_x2_kernel<FL>, grid, R.G * kX2Threads, L.total, st, &R);
+  if (rc != 0 || !R.goal) return rc;
+  sum_partials_kernel<float><<<1, 256, 0, st>>>(R.loss_partial, grid, R.loss_out);
+  return cudaGetLastError() == cudaSuccess ? 0 : kErrCuda;
 }
 template <int FL>
 int run_bwd_x2(const RolloutArgs<float>& R, cudaStream_t st) {

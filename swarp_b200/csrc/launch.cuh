@@ -87,8 +87,11 @@ template <typename T, int FL, int AS>
 int run_fwd(const RolloutArgs<T>& R, cudaStream_t st) {
   const Layout<T> L(R.G, R.A, R.N, R.S, false, (FL & F_BODIES) != 0,
                     (FL & F_BOXES) != 0 && (FL & F_COLL) != 0);
-  return launch_kernel(rollout_fwd_kernel<T, FL, AS>, (R.E + R.G - 1) / R.G, R.G * R.A, L.total,
-                       st, &R);
+  const int grid = (R.E + R.G - 1) / R.G;
+  const int rc = launch_kernel(rollout_fwd_kernel<T, FL, AS>, grid, R.G * R.A, L.total, st, &R);
+  if (rc != 0 || !R.goal) return rc;
+  sum_partials_kernel<T><<<1, 256, 0, st>>>(R.loss_partial, grid, R.loss_out);
+  return cudaGetLastError() == cudaSuccess ? 0 : kErrCuda;
 }
 template <typename T, int FL, int AS>
 int run_bwd(const RolloutArgs<T>& R, cudaStream_t st) {

@@ -65,9 +65,10 @@ extern "C" int swarp_rollout_noalloc(const swarp_world_t* w, int32_t horizon, sw
     if (rc != SWARP_OK) return rc;
   }
   const swarp_bodies_t none = {nullptr, nullptr, nullptr, nullptr};
+  const swarp_goal_loss_t no_goal = {nullptr, nullptr, nullptr};
   int rc = swarp_rollout_fwd(w, horizon, init, actions, traj, final_out, nullptr, none, none,
-                             scratch, need, stream);
+                             no_goal, scratch, need, stream);
   if (rc != SWARP_OK) return rc;
   return swarp_rollout_bwd(w, horizon, init, actions, traj, adj_traj, adj_final, none, none, none,
-                           adj_actions, adj_init, nullptr, scratch, need, stream);
+                           adj_actions, adj_init, nullptr, no_goal, scratch, need, stream);
 }

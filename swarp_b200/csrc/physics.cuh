@@ -52,6 +52,9 @@ template <typename T> __device__ __forceinline__ T wmax(T a, T b) { return a > b
 template <typename T> __device__ __forceinline__ T wmin(T a, T b) { return a < b ? a : b; }
 // Warp clamp: min(max(lo, x), hi)
 template <typename T> __device__ __forceinline__ T wclamp(T x, T lo, T hi) { return wmin(wmax(lo, x), hi); }
+// wmax(x, c) for a constant c >= +0 in one min/max instruction: the same value for every x
+// (a NaN x gives c in both forms; -0 against +0 gives +0 in both).
+template <typename T> __device__ __forceinline__ T wmax_c(T x, T c) { return fmax(x, c); }
 // gradient gate of Warp's clamp adjoint (closed interval)
 template <typename T> __device__ __forceinline__ bool clamp_pass(T x, T lo, T hi) { return !(x < lo) && !(x > hi); }
 template <typename T> __device__ __forceinline__ T dot2(T ax, T ay, T bx, T by) { return Num<T>::fma_(ax, bx, ay * by); }
@@ -139,7 +142,7 @@ __device__ __forceinline__ T normal_coeff(T ov, T vn, T inv_denom, const WorldC<
   T ovs = ov;
   if (W.max_overlap > T(0)) ovs = W.max_overlap * tanh_ratio(ov, W.max_overlap);
   T x = nc_num(ovs, vn, W) * inv_denom;
-  return wmax(x, T(0));
+  return wmax_c(x, T(0));
 }
 // VJP of normal_coeff: cotangent g on its value -> (d ov, d vn)
 template <typename T>
@@ -168,7 +171,7 @@ __device__ __forceinline__ void normal_coeff_vjp(T ov, T vn, T inv_denom, T g, c
 template <typename T>
 __device__ __forceinline__ bool pair_force_add(T dx, T dy, T d2, T rvx, T rvy, T min_dist,
                                                T inv_denom, const WorldC<T>& W, T& fx, T& fy) {
-  const T m = wmax(d2, Eps2<T>::v);
+  const T m = wmax_c(d2, Eps2<T>::v);
   const T inv = Num<T>::rsqrt_(m);
   const T ov = pair_overlap(min_dist, m, inv);
   if (ov > T(0)) {
@@ -196,7 +199,7 @@ __device__ __forceinline__ void pair_force_vjp(T dx, T dy, T rvx, T rvy, T min_d
                                                T gx, T gy, const WorldC<T>& W, T& gdx, T& gdy,
                                                T& grvx, T& grvy) {
   const T d2 = dot2(dx, dy, dx, dy);
-  const T m = wmax(d2, Eps2<T>::v);
+  const T m = wmax_c(d2, Eps2<T>::v);
   const T inv = Num<T>::rsqrt_(m);
   const T ov = pair_overlap(min_dist, m, inv);
   if (!(ov > T(0))) return;
@@ -239,7 +242,7 @@ __device__ __forceinline__ bool pair_vjp_terms(T dx, T dy, T rvx, T rvy, T min_d
                                                T gay, T idb, T gbx, T gby, const WorldC<T>& W,
                                                PairTerms<T>& r) {
   const T d2 = dot2(dx, dy, dx, dy);
-  const T m = wmax(d2, Eps2<T>::v);
+  const T m = wmax_c(d2, Eps2<T>::v);
   const T inv = Num<T>::rsqrt_(m);
   const T ov = pair_overlap(min_dist, m, inv);
   if (!(ov > T(0))) return false;
@@ -252,7 +255,7 @@ __device__ __forceinline__ bool pair_vjp_terms(T dx, T dy, T rvx, T rvy, T min_d
   }
   const T num = nc_num(ovs, vn, W);
   const T xa = num * ida, xb = num * idb;
-  const T cfa = wmax(xa, T(0)), cfb = wmax(xb, T(0));
+  const T cfa = wmax_c(xa, T(0)), cfb = wmax_c(xb, T(0));
   const T q = (xa > T(0) ? ida * dot2(gax, gay, nx, ny) : T(0)) -
               (xb > T(0) ? idb * dot2(gbx, gby, nx, ny) : T(0));  // dL/dnum
   const T gvn = -W.c * q;
@@ -284,6 +287,56 @@ __device__ __forceinline__ void pair_vjp_sym(T dx, T dy, T rvx, T rvy, T min_dis
   grvy += t.vy;
   gdx += t.px;
   gdy += t.py;
+}
+
+// Branch-free forms of the disc-disc contact without depth saturation (max_overlap == 0),
+// for loops that evaluate two agents' contacts side by side: every operation of
+// pair_force_add / pair_vjp_terms in the same order, the branches turned into selects, so
+// the results are bitwise theirs. `have` false (no pair this round) leaves everything as it
+// was; a pair out of contact adds nothing.
+template <typename T>
+__device__ __forceinline__ bool pair_force_add_nb(bool have, T dx, T dy, T rvx, T rvy, T min_dist,
+                                                  T inv_denom, const WorldC<T>& W, T& fx, T& fy) {
+  const T d2 = dot2(dx, dy, dx, dy);
+  const T m = wmax_c(d2, Eps2<T>::v);
+  const T inv = Num<T>::rsqrt_(m);
+  const T ov = pair_overlap(min_dist, m, inv);
+  const bool on = have && ov > T(0);
+  const T nx = dx * inv, ny = dy * inv;
+  const T vn = dot2(rvx, rvy, nx, ny);
+  const T cf = wmax_c(nc_num(ov, vn, W) * inv_denom, T(0));
+  fx = on ? Num<T>::fma_(cf, nx, fx) : fx;
+  fy = on ? Num<T>::fma_(cf, ny, fy) : fy;
+  return on;
+}
+template <typename T>
+__device__ __forceinline__ bool pair_vjp_terms_nb(bool have, T dx, T dy, T rvx, T rvy, T min_dist,
+                                                  T ida, T gax, T gay, T idb, T gbx, T gby,
+                                                  const WorldC<T>& W, PairTerms<T>& r) {
+  const T d2 = dot2(dx, dy, dx, dy);
+  const T m = wmax_c(d2, Eps2<T>::v);
+  const T inv = Num<T>::rsqrt_(m);
+  const T ov = pair_overlap(min_dist, m, inv);
+  const T nx = dx * inv, ny = dy * inv;
+  const T vn = dot2(rvx, rvy, nx, ny);
+  const T num = nc_num(ov, vn, W);
+  const T xa = num * ida, xb = num * idb;
+  const T cfa = wmax_c(xa, T(0)), cfb = wmax_c(xb, T(0));
+  const T q = (xa > T(0) ? ida * dot2(gax, gay, nx, ny) : T(0)) -
+              (xb > T(0) ? idb * dot2(gbx, gby, nx, ny) : T(0));
+  const T gvn = -W.c * q;
+  const T gov = W.k * q;
+  r.vx = gvn * nx;
+  r.vy = gvn * ny;
+  const T gnx = Num<T>::fma_(gvn, rvx, Num<T>::fma_(cfa, gax, -(cfb * gbx)));
+  const T gny = Num<T>::fma_(gvn, rvy, Num<T>::fma_(cfa, gay, -(cfb * gby)));
+  const T gdist = Num<T>::fma_(-dot2(gnx, gny, nx, ny), inv, -gov);
+  const T bx = gnx * inv, by = gny * inv;
+  const T gd2 = gdist * T(0.5) * inv;
+  const bool far = d2 > Eps2<T>::v;
+  r.px = far ? Num<T>::fma_(T(2) * dx, gd2, bx) : bx;
+  r.py = far ? Num<T>::fma_(T(2) * dy, gd2, by) : by;
+  return have && ov > T(0);
 }
 
 // ------------------------------------------------------------- static obstacles
@@ -504,6 +557,50 @@ __device__ __forceinline__ void wall_pens(T px, T py, T reach, const WorldC<T>& 
 // wall would be taken anyway: without depth saturation every wall's coefficient is
 // computed and masked by its penetration sign (no divergence). The accumulation order
 // matches the reference (left, right into fx; bottom, top into fy).
+// The four walls without depth saturation (max_overlap == 0), branch-free.
+template <typename T>
+__device__ __forceinline__ void wall_force_lin(T px, T py, T vx, T vy, T ra, T inv_denom,
+                                               const WorldC<T>& W, T& fx, T& fy) {
+  T pl, pr, pb, pt;
+  wall_pens(px, py, ra + W.margin, W, pl, pr, pb, pt);
+  const T cl = wmax_c(nc_num(pl, vx, W) * inv_denom, T(0));
+  const T cr = wmax_c(nc_num(pr, (-vx), W) * inv_denom, T(0));
+  const T cb = wmax_c(nc_num(pb, vy, W) * inv_denom, T(0));
+  const T ct = wmax_c(nc_num(pt, (-vy), W) * inv_denom, T(0));
+  fx = (pl > T(0) ? cl : T(0)) + (pr > T(0) ? -cr : T(0));
+  fy = (pb > T(0) ? cb : T(0)) + (pt > T(0) ? -ct : T(0));
+}
+// The VJP of wall_force_lin in two parts: the factors dx = dL/d(numerators) of the x
+// walls (right minus left) and dy, which need only the agent's own state and force
+// cotangent, and their application to the state gradient (wall_lin_vjp_apply).
+template <typename T>
+__device__ __forceinline__ void wall_lin_vjp_factors(T px, T py, T vx, T vy, T ra, T inv_denom,
+                                                     T gx, T gy, const WorldC<T>& W, T& dx,
+                                                     T& dy) {
+  T pl, pr, pb, pt;
+  wall_pens(px, py, ra + W.margin, W, pl, pr, pb, pt);
+  // d(coefficient)/d(numerator) = inv_denom on the active side of max(x, 0)
+  const bool al = pl > T(0) && nc_num(pl, vx, W) * inv_denom > T(0);
+  const bool ar = pr > T(0) && nc_num(pr, (-vx), W) * inv_denom > T(0);
+  const bool ab = pb > T(0) && nc_num(pb, vy, W) * inv_denom > T(0);
+  const bool at = pt > T(0) && nc_num(pt, (-vy), W) * inv_denom > T(0);
+  const T nl = al ? gx * inv_denom : T(0);   // left:   f_x += c_l
+  const T nr = ar ? -gx * inv_denom : T(0);  // right:  f_x -= c_r
+  const T nb = ab ? gy * inv_denom : T(0);
+  const T nt = at ? -gy * inv_denom : T(0);
+  dx = nr - nl;
+  dy = nt - nb;
+}
+// numerator k*pen - c*vn; pen_l = reach - px + x0 (d/dpx = -1), pen_r (+1); vn = +-v
+template <typename T>
+__device__ __forceinline__ void wall_lin_vjp_apply(T dx, T dy, const WorldC<T>& W, T& gpx, T& gpy,
+                                                   T& gvx, T& gvy) {
+  gpx = Num<T>::fma_(W.k, dx, gpx);
+  gvx = Num<T>::fma_(W.c, dx, gvx);
+  gpy = Num<T>::fma_(W.k, dy, gpy);
+  gvy = Num<T>::fma_(W.c, dy, gvy);
+}
+
 template <typename T>
 __device__ __forceinline__ void wall_force(T px, T py, T vx, T vy, T ra, T inv_denom,
                                            const WorldC<T>& W, T& fx, T& fy) {
@@ -518,12 +615,7 @@ __device__ __forceinline__ void wall_force(T px, T py, T vx, T vy, T ra, T inv_d
     if (pt > T(0)) fy = fy + (-normal_coeff(pt, -vy, inv_denom, W));
     return;
   }
-  const T cl = wmax(nc_num(pl, vx, W) * inv_denom, T(0));
-  const T cr = wmax(nc_num(pr, (-vx), W) * inv_denom, T(0));
-  const T cb = wmax(nc_num(pb, vy, W) * inv_denom, T(0));
-  const T ct = wmax(nc_num(pt, (-vy), W) * inv_denom, T(0));
-  fx = (pl > T(0) ? cl : T(0)) + (pr > T(0) ? -cr : T(0));
-  fy = (pb > T(0) ? cb : T(0)) + (pt > T(0) ? -ct : T(0));
+  wall_force_lin(px, py, vx, vy, ra, inv_denom, W, fx, fy);
 }
 
 template <typename T>
@@ -555,20 +647,9 @@ __device__ __forceinline__ void wall_force_vjp(T px, T py, T vx, T vy, T ra, T i
     }
     return;
   }
-  // d(coefficient)/d(numerator) = inv_denom on the active side of max(x, 0)
-  const bool al = pl > T(0) && nc_num(pl, vx, W) * inv_denom > T(0);
-  const bool ar = pr > T(0) && nc_num(pr, (-vx), W) * inv_denom > T(0);
-  const bool ab = pb > T(0) && nc_num(pb, vy, W) * inv_denom > T(0);
-  const bool at = pt > T(0) && nc_num(pt, (-vy), W) * inv_denom > T(0);
-  const T nl = al ? gx * inv_denom : T(0);   // left:   f_x += c_l
-  const T nr = ar ? -gx * inv_denom : T(0);  // right:  f_x -= c_r
-  const T nb = ab ? gy * inv_denom : T(0);
-  const T nt = at ? -gy * inv_denom : T(0);
-  // numerator k*pen - c*vn; pen_l = reach - px + x0 (d/dpx = -1), pen_r (+1); vn = +-v
-  gpx = Num<T>::fma_(W.k, nr - nl, gpx);
-  gvx = Num<T>::fma_(W.c, nr - nl, gvx);
-  gpy = Num<T>::fma_(W.k, nt - nb, gpy);
-  gvy = Num<T>::fma_(W.c, nt - nb, gvy);
+  T dx, dy;
+  wall_lin_vjp_factors(px, py, vx, vy, ra, inv_denom, gx, gy, W, dx, dy);
+  wall_lin_vjp_apply(dx, dy, W, gpx, gpy, gvx, gvy);
 }
 
 // ------------------------------------------------------------------- integrate

@@ -83,6 +83,12 @@ template <typename T> struct RolloutArgs {
   // the reduced total (one scalar); both null when the norm is not requested
   T* gsq_partial;
   T* gsq_out;
+  // optional fused goal loss: goal [E, A, 2]; forward: per-CTA partials (workspace) and the
+  // reduced scalar; adjoint: the scalar cotangent of the loss (all null without a goal)
+  const T* goal;
+  T* loss_partial;
+  T* loss_out;
+  const T* loss_grad;
   // movable bodies (F_BODIES): per-shape constants, state per shape slot [E, N] at t = 0
   // and after every step [H, E, N], cotangent of the final body state (nullable)
   const int *o_kind, *o_body;
@@ -734,6 +740,49 @@ __device__ __forceinline__ void init_pads(T* xy, int nbuf, int G, int A) {
   }
 }
 
+// Deterministic CTA sum (fixed shuffle tree, then warp sums in warp order) stored by
+// thread 0. Every thread of the block must call it. A partial warp (a CTA size that is
+// not a multiple of 32) may not shuffle over its missing lanes: it gathers its lanes' values
+// in lane order instead.
+template <typename T>
+__device__ __forceinline__ void block_sum_store(T v, T* out) {
+  __shared__ T warp_sums[32];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int in_warp = min(32, (int)blockDim.x - wid * 32);  // this warp's threads
+  if (in_warp < 32) {
+    const unsigned mask = (1u << in_warp) - 1u;
+    __syncwarp(mask);
+    T s = T(0);
+    for (int i = 0; i < in_warp; ++i) s += __shfl_sync(mask, v, i);
+    v = s;
+  } else {
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  }
+  if (lane == 0) warp_sums[wid] = v;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    T s = T(0);
+    const int nw = (blockDim.x + 31) >> 5;
+    for (int i = 0; i < nw; ++i) s += warp_sums[i];
+    *out = s;
+  }
+}
+
+// The fused goal loss (swarp_goal_loss_t): one agent's |pos_T - goal|^2, and the seed of
+// its cotangent, loss_grad * 2 (pos_T - goal), added to the final-position cotangent.
+template <typename T>
+__device__ __forceinline__ T goal_dist2(const T* goal, long long i, T px, T py) {
+  const T dx = px - goal[2 * i], dy = py - goal[2 * i + 1];
+  return Num<T>::fma_(dx, dx, dy * dy);
+}
+template <typename T>
+__device__ __forceinline__ void seed_goal_loss(const RolloutArgs<T>& R, long long i, T px, T py,
+                                               Agent<T>& g) {
+  const T s = T(2) * R.loss_grad[0];
+  g.px = Num<T>::fma_(s, px - R.goal[2 * i], g.px);
+  g.py = Num<T>::fma_(s, py - R.goal[2 * i + 1], g.py);
+}
+
 // ================================================================== forward
 template <typename T, int FL, int AS>
 __global__ void __launch_bounds__(1024) rollout_fwd_kernel(const RolloutArgs<T> R) {
@@ -865,6 +914,8 @@ __global__ void __launch_bounds__(1024) rollout_fwd_kernel(const RolloutArgs<T> 
     if (kDrone && R.f_d.z) store_drone(R.f_d, ia, xd);
     if (R.true_max) R.true_max[ia] = tmax;
   }
+  if (R.goal) block_sum_store(valid ? goal_dist2(R.goal, ia, x.px, x.py) : T(0),
+                              R.loss_partial + blockIdx.x);
 }
 
 // ================================================================== adjoint
@@ -1032,23 +1083,6 @@ __device__ __forceinline__ void bodies_step_vjp(const BodyS<T>* st, const BodyC<
   for (int o = 0; o < N; ++o) gbody[o] = gbnew[o];
 }
 
-// Deterministic CTA sum (fixed shuffle tree, then warp sums in warp order) stored by
-// thread 0. Every thread of the block must call it.
-template <typename T>
-__device__ __forceinline__ void block_sum_store(T v, T* out) {
-  __shared__ T warp_sums[32];
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  if (lane == 0) warp_sums[wid] = v;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    T s = T(0);
-    const int nw = (blockDim.x + 31) >> 5;
-    for (int i = 0; i < nw; ++i) s += warp_sums[i];
-    *out = s;
-  }
-}
-
 // Sum of the per-CTA partials in a fixed order (one block), accumulated in double.
 template <typename T>
 __global__ void __launch_bounds__(256) sum_partials_kernel(const T* partial, int n, T* out) {
@@ -1143,6 +1177,10 @@ __global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : 1024)
 
   Agent<T> g{};
   add_cotangent(R.gf_pos, R.gf_th, R.gf_vel, R.gf_s, R.gf_w, ia, g);
+  if (R.goal) {  // the fused goal loss's seed, from the final positions
+    const T2 pH = reinterpret_cast<const T2*>(R.t_pos)[(long long)(R.H - 1) * R.E * A + ia];
+    seed_goal_loss(R, ia, pH.x, pH.y, g);
+  }
   Drone<T> gd{};  // cotangent of the drone fields
   if (kDrone) add_drone_cotangent(R.gf_d, ia, gd);
   // One-substep holonomic velocity fleets without bodies: the step's adjoint reads only the

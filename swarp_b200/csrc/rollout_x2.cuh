@@ -79,6 +79,113 @@ __device__ __forceinline__ unsigned contacts_of(const float4* rec_env, const flo
   return cm;
 }
 
+// Both agents' contacts side by side (no depth saturation): each round takes the next
+// candidate of each agent's mask (ascending index, as contacts_of) and evaluates the two
+// pairs in one branch-free block, so the two independent chains interleave; the rounds
+// are as many as the larger of the two counts instead of their sum. Results are bitwise
+// contacts_of's.
+__device__ __forceinline__ void contacts_of_both(const float4* rec_env, const float* rad_env,
+                                                 unsigned m0, unsigned m1, const Agent<float>& x0,
+                                                 const Agent<float>& x1, const AgentP<float>& P0,
+                                                 const AgentP<float>& P1, const WorldC<float>& W,
+                                                 float& fx0, float& fy0, float& fx1, float& fy1,
+                                                 unsigned& c0, unsigned& c1, int& n0, int& n1) {
+  c0 = 0u;
+  c1 = 0u;
+  while (m0 | m1) {
+    const bool h0 = m0 != 0u, h1 = m1 != 0u;
+    const int b0 = h0 ? __ffs(m0) - 1 : 0, b1 = h1 ? __ffs(m1) - 1 : 0;
+    m0 &= m0 - 1u;
+    m1 &= m1 - 1u;
+    const float4 q0 = rec_env[b0], q1 = rec_env[b1];
+    const float r0 = rad_env[b0], r1 = rad_env[b1];
+    const float dx0 = x0.px - q0.x, dy0 = x0.py - q0.y;
+    const float dx1 = x1.px - q1.x, dy1 = x1.py - q1.y;
+    const bool in0 = h0 && in_radius(dx0, dy0, W.r2_thr);
+    const bool in1 = h1 && in_radius(dx1, dy1, W.r2_thr);
+    n0 += in0 ? 1 : 0;
+    n1 += in1 ? 1 : 0;
+    if (pair_force_add_nb(in0, dx0, dy0, x0.vx - q0.z, x0.vy - q0.w, P0.radius + r0 + W.margin,
+                          P0.inv_denom, W, fx0, fy0))
+      c0 |= 1u << b0;
+    if (pair_force_add_nb(in1, dx1, dy1, x1.vx - q1.z, x1.vy - q1.w, P1.radius + r1 + W.margin,
+                          P1.inv_denom, W, fx1, fy1))
+      c1 |= 1u << b1;
+  }
+}
+
+// The adjoint's counterpart over the two checkpointed contact masks (no depth
+// saturation): the terms of pair_vjp_sym for the next contact of each agent per round,
+// added to each agent's gradient in ascending partner order as force_vjp adds them.
+__device__ __forceinline__ void contact_vjp_both(const float4* rec_env, const float2* fb_env,
+                                                 const float* rad_env, const float* iden_env,
+                                                 unsigned m0, unsigned m1, const Agent<float>& x0,
+                                                 const Agent<float>& x1, const AgentP<float>& P0,
+                                                 const AgentP<float>& P1, const WorldC<float>& W,
+                                                 float gfx0, float gfy0, float gfx1, float gfy1,
+                                                 Agent<float>& g0, Agent<float>& g1) {
+  while (m0 | m1) {
+    const bool h0 = m0 != 0u, h1 = m1 != 0u;
+    const int b0 = h0 ? __ffs(m0) - 1 : 0, b1 = h1 ? __ffs(m1) - 1 : 0;
+    m0 &= m0 - 1u;
+    m1 &= m1 - 1u;
+    const float4 q0 = rec_env[b0], q1 = rec_env[b1];
+    const float2 f0 = fb_env[b0], f1 = fb_env[b1];
+    PairTerms<float> t0, t1;
+    const bool on0 = pair_vjp_terms_nb(h0, x0.px - q0.x, x0.py - q0.y, x0.vx - q0.z, x0.vy - q0.w,
+                                       P0.radius + rad_env[b0] + W.margin, P0.inv_denom, gfx0,
+                                       gfy0, iden_env[b0], f0.x, f0.y, W, t0);
+    const bool on1 = pair_vjp_terms_nb(h1, x1.px - q1.x, x1.py - q1.y, x1.vx - q1.z, x1.vy - q1.w,
+                                       P1.radius + rad_env[b1] + W.margin, P1.inv_denom, gfx1,
+                                       gfy1, iden_env[b1], f1.x, f1.y, W, t1);
+    g0.vx = on0 ? g0.vx + t0.vx : g0.vx;
+    g0.vy = on0 ? g0.vy + t0.vy : g0.vy;
+    g0.px = on0 ? g0.px + t0.px : g0.px;
+    g0.py = on0 ? g0.py + t0.py : g0.py;
+    g1.vx = on1 ? g1.vx + t1.vx : g1.vx;
+    g1.vy = on1 ? g1.vy + t1.vy : g1.vy;
+    g1.px = on1 ? g1.px + t1.px : g1.px;
+    g1.py = on1 ? g1.py + t1.py : g1.py;
+  }
+}
+
+// Static forces (obstacles, then walls) of both agents as static_force sums them, in one
+// block: they depend on the agents' own states only, so the kernels evaluate them where
+// their arithmetic can overlap the neighbor work.
+template <int FL>
+__device__ __forceinline__ void static_forces_both(const Obs<float>* obs, int N,
+                                                   const Agent<float>& x0, const Agent<float>& x1,
+                                                   const AgentP<float>& P0, const AgentP<float>& P1,
+                                                   const WorldC<float>& W, float& sx0, float& sy0,
+                                                   float& sx1, float& sy1) {
+  sx0 = sy0 = sx1 = sy1 = 0.f;
+  if (FL & F_OBS) {
+    for (int o = 0; o < N; ++o) {
+      float gx, gy;
+      obstacle_force(x0.px, x0.py, x0.vx, x0.vy, P0.radius, P0.inv_denom, obs[o], W, gx, gy);
+      sx0 = sx0 + gx;
+      sy0 = sy0 + gy;
+      obstacle_force(x1.px, x1.py, x1.vx, x1.vy, P1.radius, P1.inv_denom, obs[o], W, gx, gy);
+      sx1 = sx1 + gx;
+      sy1 = sy1 + gy;
+    }
+  }
+  if (W.bounds_mode == BOUNDS_SOFT) {
+    float wx0, wy0, wx1, wy1;
+    if (W.max_overlap > 0.f) {
+      wall_force(x0.px, x0.py, x0.vx, x0.vy, P0.radius, P0.inv_denom, W, wx0, wy0);
+      wall_force(x1.px, x1.py, x1.vx, x1.vy, P1.radius, P1.inv_denom, W, wx1, wy1);
+    } else {
+      wall_force_lin(x0.px, x0.py, x0.vx, x0.vy, P0.radius, P0.inv_denom, W, wx0, wy0);
+      wall_force_lin(x1.px, x1.py, x1.vx, x1.vy, P1.radius, P1.inv_denom, W, wx1, wy1);
+    }
+    sx0 = sx0 + wx0;
+    sy0 = sy0 + wy0;
+    sx1 = sx1 + wx1;
+    sy1 = sy1 + wy1;
+  }
+}
+
 __device__ __forceinline__ void load_pair(const float* pos, const float* th, const float* vel,
                                           const float* s, const float* w, long long i,
                                           Agent<float>& x0, Agent<float>& x1) {
@@ -165,6 +272,8 @@ __global__ void __launch_bounds__(64, SWARP_X2_FWD_MINB) rollout_fwd_x2_kernel(c
       reinterpret_cast<float4*>(xy_env)[j] = make_float4(x0.px, x1.px, x0.py, x1.py);
       rec_env[a0] = make_float4(x0.px, x0.py, x0.vx, x0.vy);
       rec_env[a0 + 1] = make_float4(x1.px, x1.py, x1.vx, x1.vy);
+      float sx0, sy0, sx1, sy1;
+      static_forces_both<FL>(obs_env, N, x0, x1, P0, P1, W, sx0, sy0, sx1, sy1);
       __syncthreads();
       unsigned m0, m1;
       scan_pair16(xy_env, x0, x1, W.r2_scan, m0, m1);
@@ -172,15 +281,23 @@ __global__ void __launch_bounds__(64, SWARP_X2_FWD_MINB) rollout_fwd_x2_kernel(c
       m1 &= ~(1u << (a0 + 1));
       float fx0 = 0.f, fy0 = 0.f, fx1 = 0.f, fy1 = 0.f;
       int n0 = 0, n1 = 0;
-      const unsigned c0 = contacts_of(rec_env, rad_env, m0, x0, P0, W, fx0, fy0, n0);
-      const unsigned c1 = contacts_of(rec_env, rad_env, m1, x1, P1, W, fx1, fy1, n1);
+      unsigned c0, c1;
+      if (W.max_overlap > 0.f) {
+        c0 = contacts_of(rec_env, rad_env, m0, x0, P0, W, fx0, fy0, n0);
+        c1 = contacts_of(rec_env, rad_env, m1, x1, P1, W, fx1, fy1, n1);
+      } else {
+        contacts_of_both(rec_env, rad_env, m0, m1, x0, x1, P0, P1, W, fx0, fy0, fx1, fy1, c0, c1,
+                         n0, n1);
+      }
       tmax0 = max(tmax0, n0);
       tmax1 = max(tmax1, n1);
       if (valid)
         reinterpret_cast<uint2*>(R.cmask)[(((long long)t * R.S + k) * EA + ia) >> 1] =
             make_uint2(c0, c1);
-      static_force<float, FL>(obs_env, N, x0, P0, W, fx0, fy0);
-      static_force<float, FL>(obs_env, N, x1, P1, W, fx1, fy1);
+      fx0 = fx0 + sx0;
+      fy0 = fy0 + sy0;
+      fx1 = fx1 + sx1;
+      fy1 = fy1 + sy1;
       buf ^= 1;
       Agent<float> y0, y1;
       integrate_sel<float, FL>(x0, act.x, act.y, fx0, fy0, P0, W, y0);
@@ -196,6 +313,11 @@ __global__ void __launch_bounds__(64, SWARP_X2_FWD_MINB) rollout_fwd_x2_kernel(c
     if (R.f_pos) store_pair(R.f_pos, R.f_th, R.f_vel, R.f_s, R.f_w, ia, x0, x1);
     if (R.true_max) reinterpret_cast<int2*>(R.true_max)[ia >> 1] = make_int2(tmax0, tmax1);
   }
+  if (R.goal)
+    block_sum_store(valid ? goal_dist2(R.goal, ia, x0.px, x0.py) +
+                                goal_dist2(R.goal, ia + 1, x1.px, x1.py)
+                          : 0.f,
+                    R.loss_partial + blockIdx.x);
 }
 
 // ------------------------------------------------------------------- adjoint
@@ -253,8 +375,14 @@ __global__ void __launch_bounds__(64, SWARP_X2_BWD_MINB) rollout_bwd_x2_kernel(c
 
   Agent<float> g0{}, g1{};
   add_cotangent_pair(R.gf_pos, R.gf_th, R.gf_vel, R.gf_s, R.gf_w, ia, g0, g1);
+  if (R.goal) {  // the fused goal loss's seed, from the final positions
+    const float4 pH = reinterpret_cast<const float4*>(R.t_pos)[((long long)(H - 1) * EA + ia) >> 1];
+    seed_goal_loss(R, ia, pH.x, pH.y, g0);
+    seed_goal_loss(R, ia + 1, pH.z, pH.w, g1);
+  }
   Agent<float> n0, n1, c0, c1;  // output and input states of step t
   load_traj((long long)(H - 1) * EA + ia, n0, n1);
+
   if (H > 1)
     load_traj((long long)(H - 2) * EA + ia, c0, c1);
   else
@@ -286,11 +414,37 @@ __global__ void __launch_bounds__(64, SWARP_X2_BWD_MINB) rollout_bwd_x2_kernel(c
     rec_env[a0] = make_float4(c0.px, c0.py, c0.vx, c0.vy);
     rec_env[a0 + 1] = make_float4(c1.px, c1.py, c1.vx, c1.vy);
     reinterpret_cast<float4*>(fb_env)[j] = make_float4(gfx0, gfy0, gfx1, gfy1);
+    // the walls' VJP factors need only the agents' own states and force cotangents
+    const bool lin_walls = W.bounds_mode == BOUNDS_SOFT && !(W.max_overlap > 0.f);
+    float wdx0 = 0.f, wdy0 = 0.f, wdx1 = 0.f, wdy1 = 0.f;
+    if (lin_walls) {
+      wall_lin_vjp_factors(c0.px, c0.py, c0.vx, c0.vy, P0.radius, P0.inv_denom, gfx0, gfy0, W,
+                           wdx0, wdy0);
+      wall_lin_vjp_factors(c1.px, c1.py, c1.vx, c1.vy, P1.radius, P1.inv_denom, gfx1, gfy1, W,
+                           wdx1, wdy1);
+    }
     __syncthreads();
-    force_vjp<float, FL, A>(nullptr, rec_env, fb_env, nullptr, rad_env, iden_env, obs_env, nullptr,
-                            nullptr, N, A, a0, cm.x, c0, P0, W, gfx0, gfy0, gi0);
-    force_vjp<float, FL, A>(nullptr, rec_env, fb_env, nullptr, rad_env, iden_env, obs_env, nullptr,
-                            nullptr, N, A, a0 + 1, cm.y, c1, P1, W, gfx1, gfy1, gi1);
+    if (W.max_overlap > 0.f) {
+      force_vjp<float, FL, A>(nullptr, rec_env, fb_env, nullptr, rad_env, iden_env, obs_env,
+                              nullptr, nullptr, N, A, a0, cm.x, c0, P0, W, gfx0, gfy0, gi0);
+      force_vjp<float, FL, A>(nullptr, rec_env, fb_env, nullptr, rad_env, iden_env, obs_env,
+                              nullptr, nullptr, N, A, a0 + 1, cm.y, c1, P1, W, gfx1, gfy1, gi1);
+    } else {
+      contact_vjp_both(rec_env, fb_env, rad_env, iden_env, cm.x, cm.y, c0, c1, P0, P1, W, gfx0,
+                       gfy0, gfx1, gfy1, gi0, gi1);
+      if (FL & F_OBS) {
+        for (int o = 0; o < N; ++o) {
+          obstacle_force_vjp(c0.px, c0.py, c0.vx, c0.vy, P0.radius, P0.inv_denom, obs_env[o],
+                             gfx0, gfy0, W, gi0.px, gi0.py, gi0.vx, gi0.vy);
+          obstacle_force_vjp(c1.px, c1.py, c1.vx, c1.vy, P1.radius, P1.inv_denom, obs_env[o],
+                             gfx1, gfy1, W, gi1.px, gi1.py, gi1.vx, gi1.vy);
+        }
+      }
+      if (lin_walls) {
+        wall_lin_vjp_apply(wdx0, wdy0, W, gi0.px, gi0.py, gi0.vx, gi0.vy);
+        wall_lin_vjp_apply(wdx1, wdy1, W, gi1.px, gi1.py, gi1.vx, gi1.vy);
+      }
+    }
     g0 = gi0;
     g1 = gi1;
     fbuf ^= 1;

@@ -194,6 +194,75 @@ def rollout_bodies(
     return fin, Trajectory(tuple(traj), extra), body
 
 
+class _GoalLossFn(torch.autograd.Function):
+    """``(goal, actions [T,E,A,D], n state tensors) -> loss`` (0-d): the goal loss
+    sum |pos_T - goal|^2 reduced in the forward kernel's epilogue, its cotangent seeded in
+    the adjoint kernel's prologue (no torch ops between the two kernels)."""
+
+    @staticmethod
+    def forward(ctx, stepper: Stepper, goal, actions, *state):
+        state5 = tuple(t.contiguous() for t in state)
+        acts = actions.contiguous()
+        loss = torch.empty((), dtype=stepper.dtype, device=stepper.device)
+        traj, _, _, rec = stepper.rollout_forward(state5, acts, final=False, moving_bodies=False,
+                                                  goal=goal, loss_out=loss)
+        ctx.stepper, ctx.rec, ctx.n = stepper, rec, len(state5)
+        ctx.save_for_backward(acts, goal, *state5, *traj)
+        return loss
+
+    @staticmethod
+    def backward(ctx, g_loss):
+        acts, goal, *rest = ctx.saved_tensors
+        n = ctx.n
+        state5, traj5 = tuple(rest[:n]), tuple(rest[n:2 * n])
+        g_act, g_init = ctx.stepper.rollout_backward(
+            state5, acts, traj5, (None,) * n, (None,) * n, ctx.rec, goal=goal,
+            loss_grad=g_loss.detach().to(ctx.stepper.dtype).contiguous())
+        return (None, None, g_act, *g_init)
+
+
+def rollout_goal_loss(stepper: Stepper, state: TorchState, actions_seq: torch.Tensor,
+                      goal: torch.Tensor) -> torch.Tensor:
+    """``sum over envs and agents of ||pos_T - goal||^2`` after a rollout of ``actions_seq``
+    ``[T, E, A, act_dim]`` from ``state``, differentiable w.r.t. the actions and the
+    initial state (``goal`` ``[E, A, 2]`` is a constant).
+
+    The same value and gradients as ``((rollout(...)[0].pos - goal) ** 2).sum()``, with the
+    loss reduced in the forward kernel (per-CTA partials, fixed order) and its gradient
+    seeded inside the adjoint kernel: a BPTT step is then two rollout kernels and one
+    small reduction, with no elementwise torch ops between them. A fused fast path of
+    this library; the reference's callers write such losses in torch. Fleets with
+    movable bodies are not accepted (use ``rollout_bodies``).
+    """
+    if stepper.any_movable:
+        raise NotImplementedError("rollout_goal_loss does not take movable bodies")
+    state = fill_state_defaults(state)
+    n = stepper.n_state
+    core = tuple(state[:n])
+    stepper._check_inputs(core, actions_seq, horizon_dim=True)
+    E, A = core[0].shape[0], core[0].shape[1]
+    if tuple(goal.shape) != (E, A, 2):
+        raise ValueError(f"goal must be [{E}, {A}, 2]; got {tuple(goal.shape)}")
+    goal = goal.detach().to(device=stepper.device, dtype=stepper.dtype).contiguous()
+    if torch.is_grad_enabled() and (actions_seq.requires_grad or
+                                    any(t.requires_grad for t in core)):
+        return _GoalLossFn.apply(stepper, goal, actions_seq, *core)
+    with torch.no_grad():
+        loss = torch.empty((), dtype=stepper.dtype, device=stepper.device)
+        stepper.rollout_forward(tuple(t.contiguous() for t in core), actions_seq.contiguous(),
+                                final=False, moving_bodies=False, goal=goal, loss_out=loss)
+    return loss
+
+
+class FusedGoalLoss:
+    """Marker for :class:`~swarp_b200.interop.graphs.GraphedRollout` (and
+    :class:`~swarp_b200.interop.streamed.StreamedRollout`): take the step's loss from
+    :func:`rollout_goal_loss` with this ``goal`` instead of a torch loss on the rollout."""
+
+    def __init__(self, goal: torch.Tensor) -> None:
+        self.goal = goal
+
+
 class _CheckpointedFn(torch.autograd.Function):
     """``(actions [T,E,A,D], n state tensors) -> final n``, keeping only the state at
     every ``every``-th step: the forward runs the fused rollout kernel one segment of

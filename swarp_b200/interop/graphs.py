@@ -21,12 +21,16 @@ from collections.abc import Callable
 import torch
 
 from swarp_b200.core.stepper import Stepper
-from swarp_b200.interop.autograd import TorchState, Trajectory, fill_state_defaults, rollout
+from swarp_b200.interop.autograd import (FusedGoalLoss, TorchState, Trajectory, fill_state_defaults,
+                                         rollout, rollout_goal_loss)
 
 
 class GraphedRollout:
     """``loss_fn(final, trajectory) -> scalar`` differentiated w.r.t. the actions (and,
     with ``wrt_state``, the five initial-state fields), captured as one CUDA graph.
+    ``loss_fn`` may also be a :class:`~swarp_b200.interop.autograd.FusedGoalLoss`: the
+    goal loss computed inside the rollout kernels (its goal tensor is read at every
+    replay, so it can be refilled in place between calls).
 
     ``state`` / ``actions`` give the shapes and the first inputs. Calling the object
     (optionally with new inputs, device or pinned host tensors of the same shapes) replays
@@ -81,8 +85,11 @@ class GraphedRollout:
         self.grad_state = TorchState(*self.grads[1:6]) if wrt_state else None
 
     def _body(self):
-        fin, traj = rollout(self.stepper, self.state, self.actions)
-        loss = self.loss_fn(fin, traj)
+        if isinstance(self.loss_fn, FusedGoalLoss):
+            loss = rollout_goal_loss(self.stepper, self.state, self.actions, self.loss_fn.goal)
+        else:
+            fin, traj = rollout(self.stepper, self.state, self.actions)
+            loss = self.loss_fn(fin, traj)
         wrt = [self.actions] + (list(self.state[:5]) if self.wrt_state else [])
         grads = torch.autograd.grad(loss, wrt)
         pair = None

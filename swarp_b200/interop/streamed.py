@@ -26,7 +26,7 @@ import torch
 
 from swarp_b200 import _lib
 from swarp_b200.core.stepper import Stepper
-from swarp_b200.interop.autograd import TorchState, Trajectory
+from swarp_b200.interop.autograd import FusedGoalLoss, TorchState, Trajectory
 from swarp_b200.interop.graphs import GraphedRollout
 
 
@@ -43,7 +43,8 @@ class StreamedRollout:
     for a batch held in pinned host memory, pipelined over env chunks.
 
     ``aux_like`` are example tensors ``[E, ...]`` of the extra per-env inputs ``loss_fn``
-    reads (goals, weights); they are chunked along the env axis like the state. Calling the
+    reads (goals, weights); they are chunked along the env axis like the state
+    (``loss_fn="goal"``: the fused goal loss, ``aux_like[0]`` the goals). Calling the
     object with host tensors enqueues one BPTT step of the whole batch and returns at once:
     the gradient lands in ``grad_out`` (host, ``[T, E, A, D]``) and the per-chunk losses in
     ``loss_out`` (host, ``[chunks]``, float64) when :meth:`synchronize` returns. Consecutive
@@ -73,8 +74,11 @@ class StreamedRollout:
                             torch.zeros(Ec, A, **opts))
             acts = torch.zeros(horizon, Ec, A, act_dim, **opts)
 
-            def fn(final, traj: Trajectory, _aux=aux):
-                return loss_fn(final, traj, *_aux)
+            if loss_fn == "goal":  # the fused goal loss on the first auxiliary input
+                fn = FusedGoalLoss(aux[0])
+            else:
+                def fn(final, traj: Trajectory, _aux=aux):
+                    return loss_fn(final, traj, *_aux)
 
             g = GraphedRollout(stepper, st, acts, fn, grad_norm=False)
             loss64 = torch.zeros(1, device=dev, dtype=torch.float64)

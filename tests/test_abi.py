@@ -42,7 +42,7 @@ def test_error_strings_and_version(lib):
     lib.swarp_error_string.restype = C.c_char_p
     assert lib.swarp_error_string(0) == b"ok"
     assert b"unsupported" in lib.swarp_error_string(-2)
-    assert lib.swarp_abi_version() == 6
+    assert lib.swarp_abi_version() == 7
 
 
 def test_invalid_world_is_rejected_without_a_gpu(lib):
@@ -56,22 +56,22 @@ def test_invalid_world_is_rejected_without_a_gpu(lib):
     fwd.restype = C.c_int
     fwd.argtypes = _lib.SIGNATURES["swarp_rollout_fwd"][1]
     rc = fwd(None, 4, _lib.State(), None, _lib.State(), _lib.State(), None, _lib.Bodies(),
-             _lib.Bodies(), None, 0, None)
+             _lib.Bodies(), _lib.GoalLoss(), None, 0, None)
     assert rc == -1
     w.dtype, w.n_envs, w.n_agents, w.act_dim, w.substeps, w.dt = 0, 2, 3, 2, 1, 0.1
     w.params, w.model_tag, w.ctrl_mode = 8, 8, 8  # non-null placeholders, never dereferenced
     w.fleet_models, w.fleet_modes = 1 << 4, 1  # an unknown model tag
     rc = fwd(C.byref(w), 4, _lib.State(), None, _lib.State(), _lib.State(), None, _lib.Bodies(),
-             _lib.Bodies(), None, 0, None)
+             _lib.Bodies(), _lib.GoalLoss(), None, 0, None)
     assert rc == -2
     w.fleet_models = 1 << 3  # a drone fleet without its drone state fields
     rc = fwd(C.byref(w), 4, _lib.State(), None, _lib.State(), _lib.State(), None, _lib.Bodies(),
-             _lib.Bodies(), None, 0, None)
+             _lib.Bodies(), _lib.GoalLoss(), None, 0, None)
     assert rc == -1
     w.fleet_models = 1
     w.n_agents = 5000
     rc = fwd(C.byref(w), 4, _lib.State(), None, _lib.State(), _lib.State(), None, _lib.Bodies(),
-             _lib.Bodies(), None, 0, None)
+             _lib.Bodies(), _lib.GoalLoss(), None, 0, None)
     assert rc == -3
 
 
