@@ -441,10 +441,12 @@ def config_block(wl: Workload, world: int) -> dict:
 
 
 # ------------------------------------------------------------------ GPU side
-def profile_traffic(cid: int):
-    """DRAM bytes per launch of the adjoint kernel from the committed ncu summary, if any."""
+def profile_traffic(cid: int, kernel: str):
+    """DRAM bytes per launch of the forward ("fwd") or adjoint ("bwd") kernel, from the ncu
+    capture summarised in profiles/ (dram__bytes_read.sum + dram__bytes_write.sum of a
+    half-size capture, doubled: traffic grows with the envs), if one exists for cid."""
     path = os.path.join(ROOT, "profiles", "rollout_kernels_config2.md")
-    key = f"traffic_bytes_per_launch_config{cid}:"
+    key = f"traffic_bytes_per_launch_config{cid}_{kernel}:"
     try:
         for line in open(path):
             if line.startswith(key):
@@ -724,7 +726,9 @@ def main() -> None:
             "achieved": bwd_gbs if dom == "bwd" else fwd_gbs, "peak": peak, "unit": "GB/s",
             "peak_source": peak_src}
     roof["frac"] = roof["achieved"] / peak
-    roof["traffic"] = profile_traffic(args.config) if dom == "bwd" else None
+    roof["traffic"] = profile_traffic(args.config, dom)
+    roof["traffic_source"] = ("ncu capture summarised in profiles/rollout_kernels_config2.md"
+                              if roof["traffic"] is not None else None)
     cfg = config_block(wl, world)
     line = {
         "metric": wl.metric, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,

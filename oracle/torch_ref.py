@@ -393,7 +393,15 @@ def obb_contact(cax, cay, tha, hax, hay, cbx, cby, thb, hbx, hby, reach):
 
 def obb_force(cax, cay, tha, hax, hay, vax, vay, wa, cbx, cby, thb, hbx, hby, vbx, vby, wb, reach,
               k, c, denom, max_overlap):
-    """``swarp/core/collisions.py:447-486``: force on box A from box B (and the point)."""
+    """``swarp/core/collisions.py:447-486``: force on box A from box B."""
+    fx, fy, _, _ = obb_force_at(cax, cay, tha, hax, hay, vax, vay, wa, cbx, cby, thb, hbx, hby,
+                                vbx, vby, wb, reach, k, c, denom, max_overlap)
+    return fx, fy
+
+
+def obb_force_at(cax, cay, tha, hax, hay, vax, vay, wa, cbx, cby, thb, hbx, hby, vbx, vby, wb,
+                 reach, k, c, denom, max_overlap):
+    """obb_force with the contact point it acts at (``collisions.py:447-486`` returns both)."""
     s, nx, ny, xx, xy = obb_contact(cax, cay, tha, hax, hay, cbx, cby, thb, hbx, hby, reach)
     ov = reach - s
     rax, ray = xx - cax, xy - cay
@@ -403,7 +411,7 @@ def obb_force(cax, cay, tha, hax, hay, vax, vay, wa, cbx, cby, thb, hbx, hby, vb
     cf = normal_coeff(ov, rvx * nx + rvy * ny, k, c, denom, max_overlap)
     z = torch.zeros_like(s)
     active = ov > 0
-    return torch.where(active, cf * nx, z), torch.where(active, cf * ny, z)
+    return torch.where(active, cf * nx, z), torch.where(active, cf * ny, z), xx, xy
 
 
 def agent_pair_force(a_lt_b, box_a, box_b, pax, pay, tha, vax, vay, wa, ra, hax, hay,
@@ -915,6 +923,27 @@ def _reaction(px, py, vx, vy, ra, am, cx, cy, ang, st, r_o, hx, hy, vox, voy, om
     return -fx, -fy, rx, ry
 
 
+def _reaction_box(px, py, th, vx, vy, wa, hax, hay, am, cx, cy, ang, st, r_o, hx, hy, vox, voy,
+                  om, w: RefWorld):
+    """``swarp/core/bodies.py:131-166``: force on the body from a box agent, and its lever
+    from the shape centre: the negated ``_box_obstacle_force`` (``collisions.py:544-582``)
+    and its contact point (a circle shape: its centre)."""
+    denom = 1.0 + w.c * (w.dt / w.substeps) / am
+    k, c, m, mo = w.k, w.c, w.margin, w.max_overlap
+    zc = torch.zeros_like(px)
+    if st == BOX:
+        fx, fy, xx, xy = obb_force_at(px, py, th, hax, hay, vx, vy, wa, cx, cy, ang, hx + zc,
+                                      hy + zc, vox, voy, om, m, k, c, denom, mo)
+    elif st == SEGMENT:
+        fx, fy, xx, xy = obb_force_at(px, py, th, hax, hay, vx, vy, wa, cx, cy, ang, hx + zc, zc,
+                                      vox, voy, om, r_o + m, k, c, denom, mo)
+    else:
+        gx, gy = box_force(cx, cy, vox, voy, px, py, th, hax, hay, r_o + m, k, c, denom, mo,
+                           vx, vy, wa)
+        fx, fy, xx, xy = -gx, -gy, cx + zc, cy + zc
+    return -fx, -fy, xx - cx, xy - cy
+
+
 def _closest_in_box(dx, dy, ang, hx, hy):
     ca, sa = torch.cos(ang), torch.sin(ang)
     lx = ca * dx + sa * dy
@@ -967,13 +996,16 @@ def body_pass(state, obs: RefObstacles, w: RefWorld):
     body, as in every configuration here, the two readings coincide).
     Returns a new :class:`RefObstacles`.
     """
-    pos, _, vel, _, _ = state[:5]
+    pos, theta, vel, _, ang_vel = state[:5]
     px, py = pos[..., 0], pos[..., 1]
     vx, vy = vel[..., 0], vel[..., 1]
     E, A = px.shape
     dt = w.dt / w.substeps
     ra_all = w.col(P_RADIUS).expand(E, A)
     am_all = w.col(P_MASS).expand(E, A)
+    box_all = (w.col(P_SHAPE) > 0.5).expand(E, A)
+    hx_all, hy_all = w.col(P_HALF_X).expand(E, A), w.col(P_HALF_Y).expand(E, A)
+    any_box = bool(box_all.any())
     N = obs.n
     new = {
         "pos": [obs.pos[:, s] for s in range(N)],
@@ -1021,9 +1053,20 @@ def body_pass(state, obs: RefObstacles, w: RefWorld):
             for a in range(A):
                 pax, pay = px[:, a], py[:, a]
                 ra = ra_all[:, a]
+                if any_box:  # a box agent's bounding disc: max(radius, half-diagonal)
+                    isb = box_all[:, a]
+                    hxa, hya = hx_all[:, a], hy_all[:, a]
+                    ra = torch.where(isb, wmax(ra, torch.sqrt(hxa * hxa + hya * hya)), ra)
                 apart = bounds_apart(pax - csx, pay - csy, ra + bound + w.margin)
-                rfx, rfy, rx, ry = _reaction(pax, pay, vx[:, a], vy[:, a], ra, am_all[:, a],
-                                             csx, csy, th, st, r_o, hx, hy, vsx, vsy, om, w)
+                rfx, rfy, rx, ry = _reaction(pax, pay, vx[:, a], vy[:, a], ra_all[:, a],
+                                             am_all[:, a], csx, csy, th, st, r_o, hx, hy, vsx,
+                                             vsy, om, w)
+                if any_box:
+                    bfx, bfy, brx, bry = _reaction_box(
+                        pax, pay, theta[:, a], vx[:, a], vy[:, a], ang_vel[:, a], hxa, hya,
+                        am_all[:, a], csx, csy, th, st, r_o, hx, hy, vsx, vsy, om, w)
+                    rfx, rfy = torch.where(isb, bfx, rfx), torch.where(isb, bfy, rfy)
+                    rx, ry = torch.where(isb, brx, rx), torch.where(isb, bry, ry)
                 lx, ly = owx + rx, owy + ry
                 z = torch.zeros_like(fx)
                 fx = fx + torch.where(apart, z, rfx)

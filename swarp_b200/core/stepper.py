@@ -194,9 +194,8 @@ class Stepper:
         self.n_obstacles = obs.n_obstacles
         moving = obs.kind[obs.body.long()] != 0  # shapes whose body root is movable
         self.any_movable = bool(moving.any().item())
-        if self.any_movable and (self.box_agents or self.has_drones):
-            raise NotImplementedError("box agents or drones against movable obstacles are not on "
-                                      "the CUDA path")
+        if self.any_movable and self.has_drones:
+            raise NotImplementedError("drones against movable obstacles are not on the CUDA path")
         self.movable_shapes = 0
         self._poses_from_bodies = False
         if self.any_movable:

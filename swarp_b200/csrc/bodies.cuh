@@ -16,6 +16,7 @@
 // shapes (agent reactions, lever arms through the body angle, contacts with any other
 // shape, drag, the clamp); bodies with box or segment shapes run forward only.
 #pragma once
+#include "boxes.cuh"
 #include "physics.cuh"
 
 namespace swarp {
@@ -142,13 +143,33 @@ template <typename T> struct BodyPassOut {
   bool clamp_x, clamp_y;
 };
 
+// Reaction of a box agent (heading th, turn rate w, half extents hx, hy; its record q and
+// inverse implicit denominator ida) on the body shape `sh`: the negated force the agent
+// feels from that shape (box_agent_shape_force, the function its own static pass sums)
+// and the lever from the shape centre to the contact point (bodies.py:131-166).
+template <typename T, typename T4>
+__device__ __forceinline__ void reaction_box(const T4& q, T th, T w, T hx, T hy, T ida,
+                                             const Obs<T>& sh, const WorldC<T>& W, T& fx, T& fy,
+                                             T& rx, T& ry) {
+  const Ob<T> oa{q.x, q.y, Num<T>::cos_(th), Num<T>::sin_(th), hx, hy, q.z, q.w, w};
+  T gx, gy, xx, xy;
+  box_agent_shape_force(oa, sh, ida, W, gx, gy, xx, xy);
+  fx = -gx;
+  fy = -gy;
+  rx = xx - sh.cx;
+  ry = xy - sh.cy;
+}
+
 // Forward body pass of root o of one env. `obs` holds the env's current shape poses;
 // agent records rec (x, y, vx, vy), radii and inverse denominators for the reactions.
+// Worlds with box agents also pass every agent's (heading, turn rate) pairs thw and
+// (box flag, hx, hy, -) rows shp (both null otherwise).
 template <typename T, typename T4>
 __device__ __forceinline__ void body_pass_root(int o, const BodyS<T>& b, const BodyC<T>* bc,
                                                const Obs<T>* obs, int N, const T4* rec,
                                                const T* rad, const T* iden, int A,
-                                               const WorldC<T>& W, bool clamp, BodyPassOut<T>& out) {
+                                               const WorldC<T>& W, bool clamp, BodyPassOut<T>& out,
+                                               const T* thw = nullptr, const T* shp = nullptr) {
   const T dt = W.dt;
   const T ca = Num<T>::cos_(b.th), sa = Num<T>::sin_(b.th);
   T fx = T(0), fy = T(0), tau = T(0), ext = T(0);
@@ -168,9 +189,19 @@ __device__ __forceinline__ void body_pass_root(int o, const BodyS<T>& b, const B
     ext = wmax(ext, bc[s].reach);
     for (int a = 0; a < A; ++a) {
       const T4 q = rec[a];
-      if (bounds_apart(q.x - sh.cx, q.y - sh.cy, rad[a] + sh.bound + W.margin)) continue;
+      const bool boxa = shp != nullptr && shp[4 * a] > T(0.5);
+      T hx = T(0), hy = T(0), rb = rad[a];
+      if (boxa) {  // the agent's bounding disc: max(radius, half-diagonal)
+        hx = shp[4 * a + 1];
+        hy = shp[4 * a + 2];
+        rb = wmax(rb, Num<T>::sqrt_(hx * hx + hy * hy));
+      }
+      if (bounds_apart(q.x - sh.cx, q.y - sh.cy, rb + sh.bound + W.margin)) continue;
       T gx, gy, rx, ry;
-      reaction(q.x, q.y, q.z, q.w, rad[a], iden[a], sh, W, gx, gy, rx, ry);
+      if (boxa)
+        reaction_box(q, thw[2 * a], thw[2 * a + 1], hx, hy, iden[a], sh, W, gx, gy, rx, ry);
+      else
+        reaction(q.x, q.y, q.z, q.w, rad[a], iden[a], sh, W, gx, gy, rx, ry);
       const T lx = owx + rx, ly = owy + ry;
       fx = fx + gx;
       fy = fy + gy;

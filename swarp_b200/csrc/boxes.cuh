@@ -141,11 +141,13 @@ __device__ __noinline__ ObbContact<T> obb_contact(const Ob<T>& A, const Ob<T>& B
 // Force on box A from box B (spring-damper along the contact normal, damped by the two
 // material points' closing velocity at the contact point). Returns whether in contact.
 template <typename T>
-__device__ __noinline__ bool obb_force(const Ob<T>& A, const Ob<T>& B, T reach, T inv_denom,
-                                          const WorldC<T>& W, T& fx, T& fy) {
+__device__ __noinline__ bool obb_force_at(const Ob<T>& A, const Ob<T>& B, T reach, T inv_denom,
+                                          const WorldC<T>& W, T& fx, T& fy, T& xx, T& xy) {
   const ObbContact<T> c = obb_contact(A, B, reach);
   fx = T(0);
   fy = T(0);
+  xx = c.px;  // the contact point (collisions.py:447-486 returns it with the force)
+  xy = c.py;
   const T ov = reach - c.s;
   if (!(ov > T(0))) return false;
   const T rax = c.px - A.cx, ray = c.py - A.cy, rbx = c.px - B.cx, rby = c.py - B.cy;
@@ -155,6 +157,12 @@ __device__ __noinline__ bool obb_force(const Ob<T>& A, const Ob<T>& B, T reach, 
   fx = cf * c.nx;
   fy = cf * c.ny;
   return true;
+}
+template <typename T>
+__device__ __forceinline__ bool obb_force(const Ob<T>& A, const Ob<T>& B, T reach, T inv_denom,
+                                          const WorldC<T>& W, T& fx, T& fy) {
+  T xx, xy;
+  return obb_force_at(A, B, reach, inv_denom, W, fx, fy, xx, xy);
 }
 
 // box_force for agent pairs, kept out of line: the box paths are the cold, large part of
@@ -258,6 +266,31 @@ __device__ __noinline__ void box_static_force(const Obs<T>* sobs, int N, bool wa
   }
   fx = fx + sx;
   fy = fy + sy;
+}
+
+// Force on a box agent (pose oa, inverse implicit denominator ida) from one obstacle
+// shape, and the point it acts at (collisions.py:544-582, _box_obstacle_force): a BOX is
+// the box-box contact with reach = margin, a SEGMENT the degenerate box (half length, 0)
+// with reach = radius + margin, a CIRCLE the negated SDF law of its centre, acting there.
+// box_static_force sums these forces on the agent; the body pass negates the same values
+// for the reaction on a movable shape (bodies.py:131-166), lever = point - shape centre.
+template <typename T>
+__device__ __noinline__ void box_agent_shape_force(const Ob<T>& oa, const Obs<T>& ob, T ida,
+                                                   const WorldC<T>& W, T& fx, T& fy, T& xx,
+                                                   T& xy) {
+  if (ob.type == SHAPE_BOX || ob.type == SHAPE_SEGMENT) {
+    const bool seg = ob.type == SHAPE_SEGMENT;
+    const Ob<T> B{ob.cx, ob.cy, ob.ca, ob.sa, ob.hx, seg ? T(0) : ob.hy, ob.vx, ob.vy, ob.om};
+    obb_force_at(oa, B, seg ? ob.r + W.margin : W.margin, ida, W, fx, fy, xx, xy);
+  } else {
+    Obs<T> me = obs_of(oa);
+    T gx, gy;
+    box_force(ob.cx, ob.cy, ob.vx, ob.vy, me, ob.r + W.margin, ida, W, gx, gy);
+    fx = -gx;
+    fy = -gy;
+    xx = ob.cx;
+    xy = ob.cy;
+  }
 }
 
 }  // namespace swarp

@@ -349,8 +349,6 @@ int swarp_rollout_fwd(const swarp_world_t* w, int32_t horizon, swarp_state_t ini
   if (!state_complete(init) || !state_complete(traj) || !actions) return SWARP_ERR_INVALID_ARG;
   if ((flags_of(w) & F_BODIES) && (!bodies_complete(bodies_init) || !bodies_complete(bodies_traj)))
     return SWARP_ERR_INVALID_ARG;
-  // box agents against moving bodies: not built
-  if ((flags_of(w) & F_BOXES) && (flags_of(w) & F_BODIES)) return SWARP_ERR_UNSUPPORTED;
   const bool any_fin = final_out.pos || final_out.theta || final_out.vel || final_out.speed || final_out.ang_vel;
   if (any_fin && !state_complete(final_out)) return SWARP_ERR_INVALID_ARG;
   if (flags_of(w) & F_DRONE) {

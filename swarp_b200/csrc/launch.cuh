@@ -86,7 +86,7 @@ inline int launch_kernel(K kernel, int grid, int block, size_t smem, cudaStream_
 template <typename T, int FL, int AS>
 int run_fwd(const RolloutArgs<T>& R, cudaStream_t st) {
   const Layout<T> L(R.G, R.A, R.N, R.S, false, (FL & F_BODIES) != 0,
-                    (FL & F_BOXES) != 0 && (FL & F_COLL) != 0);
+                    (FL & F_BOXES) != 0 && (FL & (F_COLL | F_BODIES)) != 0);
   const int grid = (R.E + R.G - 1) / R.G;
   const int rc = launch_kernel(rollout_fwd_kernel<T, FL, AS>, grid, R.G * R.A, L.total, st, &R);
   if (rc != 0 || !R.goal) return rc;
@@ -118,10 +118,13 @@ int run_bwd(const RolloutArgs<T>& R, cudaStream_t st) {
 #define SWARP_FLAG_CASES_DRONE(X, R) \
   X(R + 0) X(R + 4) X(R + 1) X(R + 5) X(R + 3) X(R + 7) X(R + 17) X(R + 21)
 
-// Box-agent worlds: the cases without moving bodies (R = F_BOXES, F_BOXES | F_RK4).
+// Box-agent worlds: the cases without moving bodies (R = F_BOXES, F_BOXES | F_RK4); the
+// forward also runs box agents pushing movable bodies (their adjoint is not built).
 #define SWARP_FLAG_CASES_BOXES(X, R)                                                           \
   X(R + 0) X(R + 4) X(R + 8) X(R + 12) X(R + 1) X(R + 5) X(R + 9) X(R + 13) X(R + 3) X(R + 7) \
   X(R + 11) X(R + 15) X(R + 17) X(R + 21) X(R + 25) X(R + 29)
+#define SWARP_FLAG_CASES_BOXES_BODIES(X, R) \
+  X(R + 36) X(R + 37) X(R + 39) X(R + 53) X(R + 44) X(R + 45) X(R + 47) X(R + 61)
 
 template <typename T, int RB> int launch_fwd_part(const RolloutArgs<T>& R, int fl, cudaStream_t st) {
   const bool a16 = std::is_same<T, float>::value && R.A == 16;
@@ -133,7 +136,7 @@ template <typename T, int RB> int launch_fwd_part(const RolloutArgs<T>& R, int f
   if constexpr ((RB & F_DRONE) != 0) {
     switch (fl) { SWARP_FLAG_CASES_DRONE(SWARP_X, RB) }
   } else if constexpr ((RB & F_BOXES) != 0) {
-    switch (fl) { SWARP_FLAG_CASES_BOXES(SWARP_X, RB) }
+    switch (fl) { SWARP_FLAG_CASES_BOXES(SWARP_X, RB) SWARP_FLAG_CASES_BOXES_BODIES(SWARP_X, RB) }
   } else {
     switch (fl) { SWARP_FLAG_CASES_EULER(SWARP_X, RB) }
   }

@@ -392,14 +392,15 @@ __device__ __forceinline__ void store_bodies(T* pos, T* ang, T* vel, T* om, long
 template <typename T, typename T4>
 __device__ __forceinline__ void bodies_step(const BodyS<T>* in, BodyS<T>* out, const BodyC<T>* bc,
                                             Obs<T>* obs, int N, const T4* rec, const T* rad,
-                                            const T* iden, int A, const WorldC<T>& W, bool clamp) {
+                                            const T* iden, int A, const WorldC<T>& W, bool clamp,
+                                            const T* thw = nullptr, const T* shp = nullptr) {
   for (int o = 0; o < N; ++o) {
     if (!moving_root(bc, o)) {
       if (out != in) out[o] = in[o];
       continue;
     }
     BodyPassOut<T> P;
-    body_pass_root(o, in[o], bc, obs, N, rec, rad, iden, A, W, clamp, P);
+    body_pass_root(o, in[o], bc, obs, N, rec, rad, iden, A, W, clamp, P, thw, shp);
     out[o] = P.next;
   }
   for (int s = 0; s < N; ++s)
@@ -790,6 +791,9 @@ __global__ void __launch_bounds__(1024) rollout_fwd_kernel(const RolloutArgs<T> 
   constexpr bool kBodies = (FL & F_BODIES) != 0;
   constexpr bool kShare = (FL & (F_COLL | F_BODIES)) != 0;  // agent records in smem each substep
   constexpr bool kBoxes = (FL & F_BOXES) != 0 && (FL & F_COLL) != 0;  // shapes meet in pairs
+  // box agents' (heading, turn rate) and (box, hx, hy) tables: for agent pairs, and for the
+  // reactions of box agents on movable bodies
+  constexpr bool kBoxTab = (FL & F_BOXES) != 0 && (FL & (F_COLL | F_BODIES)) != 0;
   using T2 = typename V2<T>::t;
   extern __shared__ __align__(16) unsigned char smem[];
   const int A = AS > 0 ? AS : R.A;
@@ -800,7 +804,7 @@ __global__ void __launch_bounds__(1024) rollout_fwd_kernel(const RolloutArgs<T> 
   const int e = e0 + le;
   const bool valid = e < R.E;
   const int ec = valid ? e : R.E - 1;
-  const Layout<T> L(G, A, N, R.S, false, kBodies, kBoxes);
+  const Layout<T> L(G, A, N, R.S, false, kBodies, kBoxTab);
   const int NP4 = L.NP * 4;
   T2* sthw = reinterpret_cast<T2*>(smem + L.thw);  // [2][G*A] (th, w), box worlds
   T4* sshp = reinterpret_cast<T4*>(smem + L.shp);  // [G*A] (box, hx, hy, -)
@@ -817,7 +821,7 @@ __global__ void __launch_bounds__(1024) rollout_fwd_kernel(const RolloutArgs<T> 
   const WorldC<T> W = R.W;
   srad[tid] = P.radius;
   siden[tid] = P.inv_denom;
-  if (kBoxes) sshp[tid] = T4{P.box ? T(1) : T(0), P.hx, P.hy, T(0)};
+  if (kBoxTab) sshp[tid] = T4{P.box ? T(1) : T(0), P.hx, P.hy, T(0)};
   if (FL & F_OBS) load_obstacles(R, sobs, e0);
   if (FL & F_COLL) init_pads(sxy, 2, G, A);
   if (kBodies) {
@@ -863,7 +867,7 @@ __global__ void __launch_bounds__(1024) rollout_fwd_kernel(const RolloutArgs<T> 
       if (kShare) {
         if (FL & F_COLL) put_xy(xy_env, a, x.px, x.py);
         rec_env[a] = T4{x.px, x.py, x.vx, x.vy};
-        if (kBoxes) sthw[buf * GA + le * A + a] = T2{x.th, x.w};
+        if (kBoxTab) sthw[buf * GA + le * A + a] = T2{x.th, x.w};
         __syncthreads();
       }
       if (FL & F_COLL) {
@@ -886,7 +890,9 @@ __global__ void __launch_bounds__(1024) rollout_fwd_kernel(const RolloutArgs<T> 
         __syncthreads();  // every agent has read this substep's shape poses
         if (a == 0)
           bodies_step(sbst + le * N, sbst + le * N, sbc, obs_env, N, rec_env, rad_env, iden_env, A,
-                      W, R.body_clamp != 0);
+                      W, R.body_clamp != 0,
+                      kBoxTab ? reinterpret_cast<const T*>(sthw + buf * GA + le * A) : nullptr,
+                      kBoxTab ? reinterpret_cast<const T*>(shp_env) : nullptr);
       }
       if (kShare) buf ^= 1;
       Agent<T> y;

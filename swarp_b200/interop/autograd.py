@@ -136,6 +136,11 @@ def _run(stepper: Stepper, state: TorchState, actions_seq: torch.Tensor):
     # Reference rule: movable bodies advance on untaped steps; on taped ones only when
     # the stepper opts in (bodies_in_grad), which also makes them differentiable.
     moving = stepper.any_movable and (not grad_mode or stepper.bodies_in_grad)
+    if moving and grad_mode and stepper.box_agents:
+        raise NotImplementedError(
+            "gradients through movable bodies pushed by box agents are not built (the forward "
+            "is: step without grad, or keep bodies_in_grad False to freeze bodies on taped "
+            "steps as the reference does)")
     if grad_mode:
         out = _RolloutFn.apply(stepper, moving, actions_seq, *core)
         fin, traj, body = out[:n], out[n:2 * n], out[2 * n:2 * n + 4]

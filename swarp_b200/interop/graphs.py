@@ -72,6 +72,9 @@ class GraphedRollout:
         if wrt_state:
             for t in self.state[:5]:
                 t.requires_grad_(True)
+        # the unit cotangent of the loss, allocated once: autograd would otherwise fill a
+        # fresh one inside the graph at every replay
+        self._one = torch.ones((), device=dev, dtype=stepper.dtype)
         side = torch.cuda.Stream(device=dev)
         side.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(side):
@@ -91,7 +94,8 @@ class GraphedRollout:
             fin, traj = rollout(self.stepper, self.state, self.actions)
             loss = self.loss_fn(fin, traj)
         wrt = [self.actions] + (list(self.state[:5]) if self.wrt_state else [])
-        grads = torch.autograd.grad(loss, wrt)
+        one = self._one if loss.dtype == self._one.dtype else torch.ones_like(loss)
+        grads = torch.autograd.grad(loss, wrt, grad_outputs=one)
         pair = None
         if self.grad_norm == "fused":
             pair = torch.stack([loss.detach(), self.stepper.last_grad_sqnorm])

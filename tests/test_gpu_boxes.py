@@ -369,3 +369,76 @@ def test_grad_sixteen_agent_fleet_f32():
     st = stepper(cfgs, dtype=torch.float32, c=1.0, bounds=(-0.6, 0.6, -0.6, 0.6), dt=0.05)
     check(st, rand_scene(24, 16, 86, spread=0.6), rand_actions(3, 24, 16, 87), seed=88,
           dtype=torch.float32, rtol_f=1e-5, rtol_g=1e-4)
+
+
+@pytest.mark.parametrize("shape", [0, 1, 2], ids=["circle-body", "box-body", "segment-body"])
+def test_box_agents_push_movable_body_f64(shape):
+    """Box and disc agents pushing one movable body (reference swarp/core/bodies.py:131-166,
+    _reaction_box): the body takes the negated box-obstacle force each box agent feels, at
+    the contact point, so off-centre pushes spin it. Forward against the oracle in float64."""
+    from oracle import torch_ref as R
+    from swarp_b200.interop.autograd import rollout_bodies
+
+    from ref_bridge import ref_obstacles, ref_world
+
+    E, A, T = 4, 6, 20
+    cfgs = mixed_fleet(A, 31)
+    st = stepper(cfgs, c=2.0, bounds=(-0.8, 0.8, -0.8, 0.8))
+    g = torch.Generator().manual_seed(32)
+    half = {0: [0.0, 0.0], 1: [0.14, 0.07], 2: [0.16, 0.0]}[shape]
+    obs = Obstacles(
+        pos=(torch.rand(E, 1, 2, generator=g, dtype=D) - 0.5) * 0.1,
+        radius=torch.tensor([{0: 0.1, 1: 0.0, 2: 0.04}[shape]], dtype=D),
+        shape=torch.tensor([shape], dtype=torch.int32),
+        angle=torch.rand(E, 1, generator=g, dtype=D),
+        half_extents=torch.tensor([half], dtype=D),
+        kind=torch.ones(1, dtype=torch.int32), mass=torch.tensor([1.2], dtype=D),
+        inertia=torch.tensor([0.015], dtype=D))
+    st.set_obstacles(obs)
+    ang = torch.rand(E, A, generator=g, dtype=D) * 2 * math.pi
+    rad = 0.2 + 0.06 * torch.rand(E, A, generator=g, dtype=D)
+    pos = obs.pos + torch.stack([torch.cos(ang), torch.sin(ang)], -1) * rad[..., None]
+    s5 = state(pos, theta=(torch.rand(E, A, generator=g, dtype=D) * 2 - 1) * 3.0)
+    push = -(pos - obs.pos)  # toward the body
+    push = push / push.norm(dim=-1, keepdim=True)
+    acts = (push.unsqueeze(0).expand(T, E, A, 2)
+            + 0.3 * torch.randn(T, E, A, 2, generator=g, dtype=D)).contiguous()
+    w = ref_world(st)
+    ob = ref_obstacles(st)
+    with torch.no_grad():
+        fin_r, traj_r, body_r = R.rollout(tuple(s5), acts, w, ob)
+        fin, traj, body = rollout_bodies(st, TorchState(*(x.to(DEV) for x in s5)), acts.to(DEV))
+    for f, name in enumerate(["pos", "theta", "vel", "speed", "ang_vel"]):
+        ref = torch.stack([t[f] for t in traj_r])
+        scale = max(float(ref.abs().max()), 1e-30)
+        torch.testing.assert_close(traj.stacked[f].cpu(), ref, rtol=1e-10, atol=1e-10 * scale,
+                                   msg=lambda m: f"traj {name}: {m}")
+    for got, ref, name in [(body.pos[:, 0], body_r[-1].body_pos[:, 0], "pos"),
+                           (body.angle[:, 0], body_r[-1].body_angle[:, 0], "angle"),
+                           (body.vel[:, 0], body_r[-1].body_vel[:, 0], "vel"),
+                           (body.ang_vel[:, 0], body_r[-1].body_ang_vel[:, 0], "ang_vel")]:
+        torch.testing.assert_close(got.cpu(), ref, rtol=1e-10, atol=1e-12,
+                                   msg=lambda m: f"body {name}: {m}")
+    moved = (body.pos[:, 0].cpu() - obs.pos[:, 0]).norm(dim=-1)
+    assert float(moved.max()) > 1e-3, "the agents pushed the body"
+    if shape != 0:
+        assert float((body.angle[:, 0].cpu() - obs.angle[:, 0]).abs().max()) > 1e-4  # it spun
+
+
+def test_box_agents_with_bodies_in_grad_are_rejected():
+    """The body adjoint covers disc agents only: a grad rollout that would move bodies
+    pushed by box agents raises, while the reference rule (bodies frozen on taped steps)
+    differentiates."""
+    from swarp_b200.interop.autograd import rollout_bodies
+
+    E, A, T = 2, 3, 4
+    st = stepper(mixed_fleet(A, 3))
+    st.set_obstacles(Obstacles(pos=torch.zeros(E, 1, 2, dtype=D), radius=torch.tensor([0.1], dtype=D),
+                               kind=torch.ones(1, dtype=torch.int32)))
+    s5 = [x.to(DEV) for x in rand_scene(E, A, 4)]
+    acts = torch.zeros(T, E, A, 2, dtype=D, device=DEV, requires_grad=True)
+    _, _, body = rollout_bodies(st, TorchState(*s5), acts)  # frozen: no body state returned
+    assert body is None
+    st.bodies_in_grad = True
+    with pytest.raises(NotImplementedError):
+        rollout_bodies(st, TorchState(*s5), acts)
