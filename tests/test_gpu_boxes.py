@@ -381,9 +381,11 @@ def test_box_agents_push_movable_body_f64(shape):
 
     from ref_bridge import ref_obstacles, ref_world
 
-    E, A, T = 4, 6, 20
+    E, A, T = 4, 6, 30
     cfgs = mixed_fleet(A, 31)
-    st = stepper(cfgs, c=2.0, bounds=(-0.8, 0.8, -0.8, 0.8))
+    # dt 0.05: the default body damping 10 / s leaves 1 - 10 dt = 0.5 of the body velocity
+    # per step (at dt 0.1 it would leave none and the body could not move)
+    st = stepper(cfgs, c=2.0, bounds=(-0.8, 0.8, -0.8, 0.8), dt=0.05)
     g = torch.Generator().manual_seed(32)
     half = {0: [0.0, 0.0], 1: [0.14, 0.07], 2: [0.16, 0.0]}[shape]
     obs = Obstacles(
