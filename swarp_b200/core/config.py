@@ -78,6 +78,18 @@ class Obstacles:
     def n_obstacles(self) -> int:
         return self.pos.shape[1]
 
+    def env_slice(self, start: int, stop: int) -> Obstacles:
+        """The set of envs ``[start, stop)``: per-env fields sliced (views), per-shape
+        constants shared."""
+        def cut(t):
+            return t if t is None or t.dim() < 2 else t[start:stop]
+
+        angle = self.angle if self.angle is None or self.angle.dim() == 1 else self.angle[start:stop]
+        return Obstacles(pos=self.pos[start:stop], radius=self.radius, shape=self.shape,
+                         angle=angle, half_extents=self.half_extents, vel=cut(self.vel),
+                         ang_vel=cut(self.ang_vel), kind=self.kind, mass=self.mass,
+                         inertia=self.inertia, body=self.body, body_offset=self.body_offset)
+
     def resolve(self, device, dtype: torch.dtype) -> Obstacles:
         """Every field materialised, contiguous, on ``device`` in ``dtype`` (int32 tags)."""
         key = (str(device), dtype)

@@ -240,6 +240,22 @@ class Stepper:
         self._wc_cache.clear()
         self.params_per_env = t.detach().to(device=self.device, dtype=self.dtype).contiguous()
 
+    def env_slice(self, start: int, stop: int) -> Stepper:
+        """A stepper for envs ``[start, stop)`` of this one's batch: the same agents and
+        world, the obstacle poses and per-env parameters of those envs (views). Stepping
+        it on the slice of a batch gives that slice of the batch's results bit for bit
+        (envs are independent). Movable bodies are not sliced (their state is per call)."""
+        if self.any_movable:
+            raise NotImplementedError("env_slice does not carry movable-body state")
+        st = Stepper(self.configs, dt=self.dt, substeps=self.substeps, device=self.device,
+                     dtype=self.dtype, world=self.world)
+        if self.obstacles is not None:
+            st.set_obstacles(self.obstacles.env_slice(start, stop))
+        if self.params_per_env is not None:
+            st.set_agent_params_per_env(self.params_per_env[start:stop])
+        st.track_neighbor_overflow = self.track_neighbor_overflow
+        return st
+
     # ------------------------------------------------------------- C world
     def world_c(self, n_envs: int, act_dim: int) -> _lib.WorldC:
         key = (n_envs, act_dim)

@@ -65,8 +65,14 @@ class StreamedRollout:
         self.lib = _lib.load()
         opts = {"device": dev, "dtype": stepper.dtype}
         Ec, A = self.Ec, self.A
+        # Per-env world data (obstacle poses, per-env parameters): every chunk has its own
+        # stepper over its envs' slice, and so its own captured step (one slot per chunk).
+        # Otherwise the chunks share `slots` captured steps round-robin.
+        self.per_chunk = stepper.n_obstacles > 0 or stepper.params_per_env is not None
+        n_slots = self.n_chunks if self.per_chunk else max(2, slots)
         self.slots = []
-        for _ in range(max(2, slots)):
+        for i in range(n_slots):
+            st_i = stepper.env_slice(i * Ec, (i + 1) * Ec) if self.per_chunk else stepper
             aux = tuple(torch.zeros((Ec, *t.shape[1:]), device=dev, dtype=t.dtype)
                         for t in aux_like)
             st = TorchState(torch.zeros(Ec, A, 2, **opts), torch.zeros(Ec, A, **opts),
@@ -80,7 +86,7 @@ class StreamedRollout:
                 def fn(final, traj: Trajectory, _aux=aux):
                     return loss_fn(final, traj, *_aux)
 
-            g = GraphedRollout(stepper, st, acts, fn, grad_norm=False)
+            g = GraphedRollout(st_i, st, acts, fn, grad_norm=False)
             loss64 = torch.zeros(1, device=dev, dtype=torch.float64)
             self.slots.append({"graph": g, "aux": aux, "loss64": loss64,
                                "ev_in": torch.cuda.Event(), "ev_done": torch.cuda.Event(),
@@ -117,7 +123,7 @@ class StreamedRollout:
         esz = actions.element_size()
         row_full, row_chunk = E * A * D * esz, Ec * A * D * esz
         for c in range(self.n_chunks):
-            s = self.slots[self._next % len(self.slots)]
+            s = self.slots[c if self.per_chunk else self._next % len(self.slots)]
             self._next += 1
             g: GraphedRollout = s["graph"]
             e0 = c * Ec
