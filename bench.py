@@ -553,20 +553,16 @@ def main() -> None:
     if not wl.body:
         # the same loss fused into the rollout kernels (rollout_goal_loss): the step is the
         # forward kernel, one small reduction and the adjoint kernel
+        # with ranks, the (loss, ||g||^2) all-reduce is captured in the same graph, in stream
+        # order after the adjoint (measured at 2 GPUs: an asynchronous all-reduce that
+        # overlapped the next step's one-wave forward kernel cost 0.060 ms per step, one
+        # in stream order 0.017 ms)
         graphed = GraphedRollout(st, state, acts, FusedGoalLoss(goal),
-                                 grad_norm="fused" if dist is not None else False, warmup=3)
-
-        # a ring of 8 pending reductions: on some 4-GPU boxes the 2-element all-reduce took
-        # about 1 ms (measured: 1.43 ms per step when each step waits for its own), which a
-        # 3-deep ring hid only partly (0.75 ms); where it is fast (0.42 ms per step at 4 GPUs)
-        # the depth costs nothing
-        reducer = (PairReducer(graphed.loss_and_grad_norm, depth=8) if dist is not None
-                   else None)
+                                 grad_norm="fused" if dist is not None else False, warmup=3,
+                                 all_reduce=dist is not None)
 
         def step():
             graphed()
-            if reducer is not None:  # overlaps the next step's rollout
-                reducer(graphed.loss_and_grad_norm)
     else:
         def step():
             eager_step(state, acts)
@@ -594,8 +590,7 @@ def main() -> None:
             dist.barrier()
         return e0.elapsed_time(e1), clk
 
-    ms, clocks = timed_loop(step, args.steps, True,
-                            finish=reducer.drain if reducer is not None else None)
+    ms, clocks = timed_loop(step, args.steps, True)
     n_eager = max(20, min(args.steps, 200))
     for _ in range(3):
         eager_step(state, acts)
@@ -613,8 +608,9 @@ def main() -> None:
         overflow = {"agents_over_K": int(ov.sum()), "max_true_count":
                     int(st.last_true_count_max.max()), "K": st.world.max_neighbors}
 
-    # ---- collective: device time of the (loss, ||g||^2) all-reduce, back to back and
-    # when every step waits for its own (the pattern a ring of pending reductions avoids)
+    # ---- collective: device time of the (loss, ||g||^2) all-reduce alone, back to back,
+    # and of the step when the same all-reduce runs asynchronously on NCCL's stream,
+    # overlapping the next step (the pattern the timed step avoids)
     allreduce = None
     if dist is not None:
         buf = torch.zeros(2, device=dev, dtype=torch.float32)
@@ -622,19 +618,24 @@ def main() -> None:
             dist.all_reduce(buf)
         n_ar = 100
         ar_ms, _ = timed_loop(lambda: dist.all_reduce(buf), n_ar, False)
+        plain = GraphedRollout(st, state, acts, FusedGoalLoss(goal), grad_norm="fused",
+                               warmup=3)
+        reducer = PairReducer(plain.loss_and_grad_norm, depth=8)
 
-        def step_wait():
-            graphed()
-            dist.all_reduce(graphed.loss_and_grad_norm)
+        def step_async():
+            plain()
+            reducer(plain.loss_and_grad_norm)
 
         for _ in range(3):
-            step_wait()
+            step_async()
         n_sw = max(20, min(args.steps, 200))
-        sw_ms, _ = timed_loop(step_wait, n_sw, False)
+        sw_ms, _ = timed_loop(step_async, n_sw, False, finish=reducer.drain)
+        plain.release()
         ar_t = torch.tensor([ar_ms / n_ar * 1e3, sw_ms / n_sw], device=dev, dtype=torch.float64)
         dist.all_reduce(ar_t, op=dist.ReduceOp.MAX)
         allreduce = {"us_per_allreduce_back_to_back": float(ar_t[0]),
-                     "ms_per_step_waiting_for_each_allreduce": float(ar_t[1]),
+                     "ms_per_step_with_async_allreduce_overlapping": float(ar_t[1]),
+                     "timed_step": "all-reduce captured in the step's graph, in stream order",
                      "bytes": 8, "backend": "nccl"}
 
     # ---- end to end through the public API with host buffers: every step copies its
@@ -752,7 +753,7 @@ def main() -> None:
                 "grad_matches_device_step": e2e_grad_ok},
         # forward + loss reduction + adjoint per step, plus the fused-norm reduction when
         # ranks all-reduce it
-        "gpu_launches": (4 if reducer is not None else 3) * args.steps,
+        "gpu_launches": (4 if dist is not None else 3) * args.steps,
         "timed_path": ("one CUDA-graph replay of the whole BPTT step per step "
                        "(swarp_b200.interop.graphs.GraphedRollout with the goal loss fused into "
                        "the rollout kernels, rollout_goal_loss)" if graphed is not None else

@@ -40,12 +40,17 @@ class GraphedRollout:
     all-reduce across ranks (``None`` otherwise). ``grad_norm="fused"`` takes the norm
     from the adjoint kernel's epilogue instead of a second pass over the gradient; it
     equals the exact norm when the loss depends on the actions only through the rollout.
+    With ``all_reduce`` (and an initialised process group), the pair is summed across ranks
+    by one NCCL all-reduce captured in the same graph, in stream order after the adjoint:
+    a collective that overlapped the next step's forward kernel would take SM resources
+    from it (one wave of it fills every SM's register file) and slow the step more than
+    the all-reduce's own ~20 us. Release such a graph before destroying the process group.
     """
 
     def __init__(self, stepper: Stepper, state: TorchState, actions: torch.Tensor,
                  loss_fn: Callable[[TorchState, Trajectory], torch.Tensor], *,
                  wrt_state: bool = False, grad_norm: bool | str = True,
-                 warmup: int = 3) -> None:
+                 warmup: int = 3, all_reduce: bool = False, group=None) -> None:
         if stepper.any_movable:
             raise NotImplementedError(
                 "GraphedRollout does not capture movable bodies: their state advances on the "
@@ -60,6 +65,8 @@ class GraphedRollout:
         if grad_norm not in (True, False, "fused"):
             raise ValueError(f"grad_norm must be True, False or 'fused'; got {grad_norm!r}")
         self.grad_norm = grad_norm
+        self.all_reduce = bool(all_reduce) and grad_norm is not False
+        self.group = group
         if grad_norm == "fused":
             stepper.track_grad_norm = True
         # Static leaves, detached from any history the given inputs carry: a backward that
@@ -102,6 +109,9 @@ class GraphedRollout:
         elif self.grad_norm:
             g = grads[0].reshape(-1)
             pair = torch.stack([loss.detach(), torch.dot(g, g)])
+        dist = torch.distributed
+        if self.all_reduce and dist.is_available() and dist.is_initialized():
+            dist.all_reduce(pair, group=self.group)
         return loss.detach(), grads, pair
 
     def __call__(self, state: TorchState | None = None, actions: torch.Tensor | None = None):
