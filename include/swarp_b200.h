@@ -40,7 +40,12 @@ extern "C" {
 #define SWARP_ERR_SCRATCH_LIMIT (-6) /* swarp_rollout_noalloc: rollout needs more workspace
                                         than SWARP_NOALLOC_SCRATCH_BYTES                 */
 
-#define SWARP_MAX_AGENTS 1024
+/* Agents per env. Envs of up to SWARP_MAX_CTA_AGENTS agents run in one CTA; larger envs
+ * run one env per thread-block cluster of up to 8 CTAs (2-D disc fleets: no movable
+ * bodies, box agents or drones, which return SWARP_ERR_UNSUPPORTED there). The reference
+ * has no per-env agent limit (swarp/core/neighbors.py:135-254 grids any count). */
+#define SWARP_MAX_AGENTS 4096
+#define SWARP_MAX_CTA_AGENTS 1024
 #define SWARP_NUM_PARAMS 22
 
 typedef enum { SWARP_F32 = 0, SWARP_F64 = 1 } swarp_dtype_t;

@@ -23,7 +23,8 @@ ERRORS = {
     -5: "workspace missing or too small",
     -6: "rollout needs more workspace than the allocation-free entry point's static scratch",
 }
-MAX_AGENTS = 1024
+MAX_AGENTS = 4096
+MAX_CTA_AGENTS = 1024  # larger envs run one env per thread-block cluster
 
 
 class State(C.Structure):

@@ -20,9 +20,15 @@ SOURCES = ["capi.cu", "noalloc.cu", "k_fwd_f32.cu", "k_fwd_f64.cu", "k_bwd_f32.c
            "k_bwd_f64.cu", "k_fwd_f32_rk4.cu", "k_fwd_f64_rk4.cu", "k_bwd_f32_rk4.cu",
            "k_bwd_f64_rk4.cu", "k_x2_f32.cu", "k_fwd_f32_box.cu", "k_fwd_f64_box.cu",
            "k_bwd_f32_box.cu", "k_bwd_f64_box.cu", "k_fwd_f32_drone.cu", "k_fwd_f64_drone.cu",
-           "k_bwd_f32_drone.cu", "k_bwd_f64_drone.cu"]
-DEPS = [*SOURCES, "launch.cuh", "rollout.cuh", "rollout_x2.cuh", "physics.cuh", "bodies.cuh",
-        "boxes.cuh", "boxes_vjp.cuh", "drone.cuh"]
+           "k_bwd_f32_drone.cu", "k_bwd_f64_drone.cu", "k_cl_fwd_f32.cu", "k_cl_fwd_f64.cu",
+           "k_cl_bwd_f32.cu", "k_cl_bwd_f64.cu"]
+# headers every translation unit includes, and those only some include
+COMMON_HEADERS = ["launch.cuh", "rollout.cuh", "physics.cuh", "bodies.cuh", "boxes.cuh",
+                  "boxes_vjp.cuh", "drone.cuh"]
+EXTRA_HEADERS = {"k_x2_f32.cu": ["rollout_x2.cuh"], "capi.cu": ["rollout_cluster.cuh"],
+                 **{f"k_cl_{d}_{t}.cu": ["k_cl.cuh", "rollout_cluster.cuh"]
+                    for d in ("fwd", "bwd") for t in ("f32", "f64")}}
+DEPS = [*SOURCES, *COMMON_HEADERS, "rollout_x2.cuh", "k_cl.cuh", "rollout_cluster.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--extended-lambda", "-fmad=false",
          "-Xcompiler", "-fPIC", "-Xcompiler", "-O2"]
@@ -51,17 +57,18 @@ def build(force: bool = False, verbose: bool = False, extra: list[str] | None = 
     objdir = os.path.join(HERE, "_build")
     os.makedirs(objdir, exist_ok=True)
     objs, procs = [], []
-    # every translation unit includes every header: a header change rebuilds all of them,
-    # a change to one .cu file only that one (unless forced or given extra flags)
-    headers = [os.path.join(CSRC, d) for d in DEPS if not d.endswith(".cu")]
+    # a translation unit is rebuilt when it, a common header or one of its own headers
+    # changed (or when forced or given extra flags)
+    headers = [os.path.join(CSRC, d) for d in COMMON_HEADERS]
     headers.append(os.path.join(ROOT, "include", "swarp_b200.h"))
     newest_hdr = max(os.path.getmtime(h) for h in headers)
     for src in SOURCES:
         obj = os.path.join(objdir, src.replace(".cu", ".o"))
         objs.append(obj)
         path = os.path.join(CSRC, src)
+        own = [os.path.getmtime(os.path.join(CSRC, h)) for h in EXTRA_HEADERS.get(src, [])]
         if (not force and not extra and os.path.exists(obj)
-                and os.path.getmtime(obj) > max(newest_hdr, os.path.getmtime(path))):
+                and os.path.getmtime(obj) > max(newest_hdr, os.path.getmtime(path), *own)):
             continue
         cmd = [nvcc(), *ARCH, *FLAGS, *(extra or []), "-c", "-o", obj, path]
         if verbose:

@@ -117,7 +117,7 @@ class Stepper:
         _REGISTRY[self.handle] = self
         if self.n_agents > _lib.MAX_AGENTS:
             raise ValueError(f"{self.n_agents} agents per env exceed the {_lib.MAX_AGENTS} this "
-                             "build runs in one CTA")
+                             "build runs (one env per cluster of 8 CTAs)")
         # 6-DOF drones carry four more state fields (z, vz, attitude, body rates)
         self.has_drones = any(c.model == DynamicsModel.DRONE for c in self.configs)
         self.n_state = 9 if self.has_drones else 5
@@ -131,6 +131,9 @@ class Stepper:
         self.box_agents = any(c.shape == AgentShape.BOX for c in self.configs)
         if self.has_drones and self.box_agents:
             raise NotImplementedError("box agents and drones in one fleet are not on the CUDA path")
+        if self.n_agents > _lib.MAX_CTA_AGENTS and (self.has_drones or self.box_agents):
+            raise NotImplementedError(f"box agents and drones run in envs of at most "
+                                      f"{_lib.MAX_CTA_AGENTS} agents")
         self.params = torch.tensor(param_rows(self.configs), dtype=self.dtype, device=self.device)
         self.params_per_env: torch.Tensor | None = None
         self.model_tag = torch.tensor([int(c.model) for c in self.configs], dtype=torch.int32,
@@ -196,6 +199,9 @@ class Stepper:
         self.any_movable = bool(moving.any().item())
         if self.any_movable and self.has_drones:
             raise NotImplementedError("drones against movable obstacles are not on the CUDA path")
+        if self.any_movable and self.n_agents > _lib.MAX_CTA_AGENTS:
+            raise NotImplementedError(f"movable obstacles run in envs of at most "
+                                      f"{_lib.MAX_CTA_AGENTS} agents")
         self.movable_shapes = 0
         self._poses_from_bodies = False
         if self.any_movable:

@@ -10,6 +10,7 @@
 
 #include "../../include/swarp_b200.h"
 #include "launch.cuh"
+#include "rollout_cluster.cuh"
 
 using namespace swarp;
 
@@ -61,6 +62,50 @@ int envs_per_cta(int A, int E) {
   int G = A >= target ? 1 : target / A;
   if (G > E) G = E;
   return G < 1 ? 1 : G;
+}
+
+// Envs of more than one CTA's agents run one env per thread-block cluster
+// (rollout_cluster.cuh). SWARP_CLUSTER_MIN_AGENTS (default 1025) and
+// SWARP_CLUSTER_CTA_THREADS (default 512, at most kClusterMaxThreads) are read on every call,
+// so a test can run small envs through the cluster kernels as well.
+int env_int(const char* name, int dflt) {
+  const char* s = std::getenv(name);
+  return (s && *s) ? std::atoi(s) : dflt;
+}
+int cluster_min_agents() {
+  const int v = env_int("SWARP_CLUSTER_MIN_AGENTS", SWARP_MAX_CTA_AGENTS + 1);
+  return v < 2 ? 2 : v;
+}
+bool use_cluster(int A, int fl) {
+  return A >= cluster_min_agents() && !(fl & F_MASK);
+}
+// CTAs per env (CS <= kClusterMaxCTAs) and threads per CTA (a multiple of 32): the fewest
+// CTAs of at most SWARP_CLUSTER_CTA_THREADS threads that hold the env. False if none does.
+bool cluster_shape(int A, int& CS, int& BT) {
+  int bt_max = env_int("SWARP_CLUSTER_CTA_THREADS", kClusterMaxThreads);
+  bt_max = std::max(32, std::min(kClusterMaxThreads, bt_max / 32 * 32));
+  CS = (A + bt_max - 1) / bt_max;
+  if (CS < 1) CS = 1;
+  BT = ((A + CS - 1) / CS + 31) / 32 * 32;
+  return CS <= kClusterMaxCTAs;
+}
+int max_smem_optin() {
+  int dev = 0, v = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+    return 0;
+  return v;
+}
+// Checks and sets up a cluster launch of R (fl its flags): 0, or the error code.
+template <typename T> int cluster_setup(RolloutArgs<T>& R, int fl, bool bwd, int& BT) {
+  if (fl & (F_BODIES | F_BOXES | F_DRONE | F_MASK)) return SWARP_ERR_UNSUPPORTED;
+  int CS = 0;
+  if (!cluster_shape(R.A, CS, BT)) return SWARP_ERR_TOO_MANY_AGENTS;
+  const ClusterLayout<T> L(R.A, BT, R.N, R.S, bwd);
+  if (L.total > (size_t)max_smem_optin()) return SWARP_ERR_TOO_MANY_AGENTS;
+  R.CS = CS;
+  R.G = 1;
+  return SWARP_OK;
 }
 
 // Largest value x of type T with sqrt(x) <= R (both rounded in T): the exact set test
@@ -234,9 +279,13 @@ size_t partials_offset(const swarp_world_t* w, int horizon) {
   return (b + 255) & ~size_t(255);
 }
 size_t partials_bytes(const swarp_world_t* w) {
-  // the CTA count of the generic or the two-agents-per-thread kernels, whichever is larger
+  // the CTA count of the generic or the two-agents-per-thread kernels, whichever is larger,
+  // or of the cluster kernels (CS CTAs per env)
   const int G = std::min(envs_per_cta(w->n_agents, w->n_envs), x2_envs_per_cta(w->n_envs));
-  const size_t n = (size_t)(w->n_envs + G - 1) / G;
+  size_t n = (size_t)(w->n_envs + G - 1) / G;
+  int CS = 1, BT = 0;
+  if (use_cluster(w->n_agents, flags_of(w)) && cluster_shape(w->n_agents, CS, BT))
+    n = std::max(n, (size_t)w->n_envs * CS);
   return n * (w->dtype == SWARP_F32 ? sizeof(float) : sizeof(double));
 }
 
@@ -267,6 +316,11 @@ int fwd_typed(const swarp_world_t* w, int horizon, swarp_state_t init, const voi
   const int fl = flags_of(w);
   R.cutoff = (fl & F_TRUNC) ? static_cast<int16_t*>(ws) : nullptr;
   R.cmask = (fl & F_MASK) ? static_cast<uint32_t*>(ws) : nullptr;
+  if (use_cluster(R.A, fl)) {
+    int BT = 0;
+    const int rc = cluster_setup(R, fl, false, BT);
+    return rc != SWARP_OK ? rc : launch_fwd_cl<T>(R, fl, BT, st);
+  }
   if constexpr (std::is_same<T, float>::value) {
     if (x2_ok(R, fl, false)) {
       R.G = x2_envs_per_cta(R.E);
@@ -310,6 +364,11 @@ int bwd_typed(const swarp_world_t* w, int horizon, swarp_state_t init, const voi
   R.gsq_partial = gsq ? reinterpret_cast<T*>(static_cast<unsigned char*>(ws) +
                                              partials_offset(w, horizon))
                       : nullptr;
+  if (use_cluster(R.A, fl)) {
+    int BT = 0;
+    const int rc = cluster_setup(R, fl, true, BT);
+    return rc != SWARP_OK ? rc : launch_bwd_cl<T>(R, fl, BT, st);
+  }
   if constexpr (std::is_same<T, float>::value) {
     if (x2_ok(R, fl, true)) {
       R.G = x2_envs_per_cta(R.E);  // fewer CTAs than the partials buffer is sized for
@@ -323,8 +382,17 @@ template <typename T>
 int nbr_typed(const swarp_world_t* w, const void* pos, int32_t* idx, int32_t* count,
               int32_t* true_count, cudaStream_t st) {
   const int E = w->n_envs, A = w->n_agents;
-  const int G = envs_per_cta(A, E);
   const T thr = radius_sq_threshold<T>(w->neighbor_radius);
+  if (A >= cluster_min_agents()) {  // several CTAs per env, each stages the whole env
+    const int slices = (A + SWARP_MAX_CTA_AGENTS - 1) / SWARP_MAX_CTA_AGENTS;
+    const int block = ((A + slices - 1) / slices + 31) / 32 * 32;
+    if (size_t((A + 1) / 2) * 4 * sizeof(T) > (size_t)max_smem_optin())
+      return SWARP_ERR_TOO_MANY_AGENTS;
+    return launch_neighbors_wide<T>(E, A, slices, block, w->max_neighbors,
+                                    radius_sq_scan_threshold(thr), thr,
+                                    static_cast<const T*>(pos), idx, count, true_count, st);
+  }
+  const int G = envs_per_cta(A, E);
   return launch_neighbors<T>(E, A, G, w->max_neighbors, radius_sq_scan_threshold(thr), thr,
                              static_cast<const T*>(pos), idx, count, true_count, st);
 }

@@ -47,6 +47,13 @@ template <typename T> inline int launch_bwd(const RolloutArgs<T>& R, int fl, cud
 template <typename T>
 int launch_neighbors(int E, int A, int G, int K, T r2_scan, T r2, const T* pos, int* idx, int* cnt,
                      int* tru, cudaStream_t st);
+// Envs wider than one CTA (rollout_cluster.cuh): one env per cluster of R.CS CTAs of
+// `block` threads each; lists of such envs from `slices` CTAs per env.
+template <typename T> int launch_fwd_cl(const RolloutArgs<T>& R, int fl, int block, cudaStream_t st);
+template <typename T> int launch_bwd_cl(const RolloutArgs<T>& R, int fl, int block, cudaStream_t st);
+template <typename T>
+int launch_neighbors_wide(int E, int A, int slices, int block, int K, T r2_scan, T r2, const T* pos,
+                          int* idx, int* cnt, int* tru, cudaStream_t st);
 
 #ifdef SWARP_DEFINE_LAUNCHERS
 

@@ -58,6 +58,7 @@ template <typename P> struct DroneF {
 
 template <typename T> struct RolloutArgs {
   int E, A, G, H, S, act_dim, N;
+  int CS;  // CTAs per env (cluster kernels, rollout_cluster.cuh); 0 or 1 otherwise
   WorldC<T> W;
   const T* params;
   long long params_env_stride;
