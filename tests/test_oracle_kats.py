@@ -385,3 +385,91 @@ def test_gradcheck_oracle_rk4_step(model, mode):
         return R.step((p, th, v, s, om), act, w)[0]
 
     assert torch.autograd.gradcheck(fn, (*st, a), eps=1e-6, atol=1e-5)
+
+
+# ------------------------------------------------- contact laws: finite differences
+# The reference pins its contact gradients only where no contact is active
+# (tests/unit/test_gradients.py:174-221); the oracle's autograd through the contact laws is
+# pinned here by central finite differences (torch.autograd.gradcheck) on contact-active
+# inputs held away from the laws' kinks (contact onset, the clamp of the coefficient at
+# zero, the box's face switch and corner region, the wall's onset).
+
+
+def _gc(fn, *xs):
+    inputs = tuple(torch.as_tensor(x, dtype=D).clone().requires_grad_(True) for x in xs)
+    assert torch.autograd.gradcheck(fn, inputs, eps=1e-7, atol=1e-6, rtol=1e-6)
+
+
+@pytest.mark.parametrize("max_overlap", [0.0, 0.03])
+def test_pair_force_finite_differences(max_overlap):
+    # overlap 0.12 - |d| > 0 in every row; k * ov - c * vn > 0 (repulsive, unclamped)
+    dx = [0.05, -0.07, 0.01, 0.09]
+    dy = [0.03, 0.02, -0.08, -0.01]
+    rvx = [0.2, -0.1, 0.05, -0.3]
+    rvy = [-0.1, 0.3, 0.1, 0.05]
+
+    def fn(dx, dy, rvx, rvy):
+        return R.pair_force(dx, dy, rvx, rvy, 0.12, 40.0, 0.5, 1.3, max_overlap)
+
+    _gc(fn, dx, dy, rvx, rvy)
+
+
+@pytest.mark.parametrize("inside", [False, True])
+def test_box_force_finite_differences(inside):
+    # outside: the point's closest box point on a face or a corner, within reach; inside:
+    # the point past a face (the face with the larger q chosen, away from the tie)
+    if inside:
+        px, py = [0.05, -0.02, 0.01], [0.01, 0.06, -0.075]
+    else:
+        px, py = [0.17, -0.03, 0.16], [0.02, -0.13, 0.11]
+    vx, vy = [0.1, -0.2, 0.05], [0.0, 0.1, -0.1]
+
+    def fn(px, py, vx, vy, cx, cy, ang, vox, voy, om):
+        return R.box_force(px, py, vx, vy, cx, cy, ang, 0.12, 0.08, 0.06, 40.0, 0.5, 1.2, 0.0,
+                           vox, voy, om)
+
+    _gc(fn, px, py, vx, vy, [0.01] * 3, [-0.01] * 3, [0.2] * 3, [0.05] * 3, [-0.02] * 3,
+        [0.3] * 3)
+
+
+def test_wall_law_finite_differences():
+    # agents pressed into each of the four walls (and one into a corner), closing speeds
+    # below k * penetration / c so the coefficient stays positive
+    w = world(holo(5), 0.05, collisions=False, k=40.0, c=0.5, margin=0.02,
+              bounds=(-1.0, 1.0, -1.0, 1.0), soft_walls=True)
+    px = [-0.95, 0.96, 0.1, -0.2, 0.97]
+    py = [0.1, -0.3, -0.94, 0.955, 0.96]
+    vx = [-0.1, 0.2, 0.0, 0.05, 0.1]
+    vy = [0.0, 0.05, -0.2, 0.1, 0.1]
+
+    def fn(px, py, vx, vy):
+        ra = torch.full_like(px, 0.07)
+        return R.wall_forces(px, py, vx, vy, ra, w, torch.full_like(px, 1.2))
+
+    _gc(fn, px, py, vx, vy)
+
+
+def test_obstacle_step_gradcheck():
+    # a full step with circle, box and segment obstacles in contact, through autograd
+    cfgs = holo(3, mode=ControlMode.ACCELERATION)
+    w = world(cfgs, 0.05, collisions=True, k=40.0, c=0.5, margin=0.02, neighbor_radius=0.3,
+              bounds=(-1.0, 1.0, -1.0, 1.0), soft_walls=True)
+    ob = R.RefObstacles(pos=torch.tensor([[[0.0, 0.0], [0.5, 0.5], [-0.5, 0.4]]], dtype=D),
+                        angle=torch.tensor([[0.0, 0.3, -0.4]], dtype=D),
+                        vel=torch.zeros(1, 3, 2, dtype=D), ang_vel=torch.zeros(1, 3, dtype=D),
+                        radius=torch.tensor([0.1, 0.0, 0.02], dtype=D),
+                        half=torch.tensor([[0.0, 0.0], [0.1, 0.06], [0.2, 0.0]], dtype=D),
+                        shape=[0, 1, 2], kind=[0, 0, 0])
+    st = state_of([[0.15, 0.03], [0.5, 0.63], [-0.48, 0.45]],
+                  vel=[[-0.1, 0.0], [0.0, -0.1], [0.05, -0.05]])
+    acts = 0.1 * torch.randn(1, 3, 2, dtype=D, generator=torch.Generator().manual_seed(1))
+
+    def fn(pos, vel, act):
+        out, _, _ = R.step((pos, st[1], vel, st[3], st[4]), act, w, ob)
+        return out[0], out[2]
+
+    fx, fy = R.obstacle_forces(st[0][..., 0], st[0][..., 1], st[2][..., 0], st[2][..., 1],
+                               torch.full((1, 3), 0.08, dtype=D), ob, w,
+                               torch.ones(1, 3, dtype=D))
+    assert bool((fx.abs() + fy.abs() > 0).all()), "every agent touches its obstacle"
+    _gc(fn, st[0], st[2], acts)
