@@ -561,11 +561,19 @@ def main() -> None:
                                  grad_norm="fused" if dist is not None else False, warmup=3,
                                  all_reduce=dist is not None)
 
-        def step():
-            graphed()
     else:
-        def step():
-            eager_step(state, acts)
+        # movable bodies: the same step (rollout_bodies, the body loss, autograd.grad) captured
+        # in one graph; every replay pushes the bodies from the same initial pose
+        def body_loss(_final, _traj, body):
+            return (body.pos[:, 0] - goal).norm(dim=-1).sum()
+
+        st.restore_bodies(snap)
+        graphed = GraphedRollout(st, state, acts, body_loss,
+                                 grad_norm=True if dist is not None else False, warmup=3,
+                                 all_reduce=dist is not None)
+
+    def step():
+        graphed()
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -612,7 +620,7 @@ def main() -> None:
     # and of the step when the same all-reduce runs asynchronously on NCCL's stream,
     # overlapping the next step (the pattern the timed step avoids)
     allreduce = None
-    if dist is not None:
+    if dist is not None and not wl.body:
         buf = torch.zeros(2, device=dev, dtype=torch.float32)
         for _ in range(20):
             dist.all_reduce(buf)
@@ -645,7 +653,7 @@ def main() -> None:
     h2d = sum(p.numel() * p.element_size() for p in pin)
     grad_h = torch.empty(wl.acts.shape, dtype=torch.float32).pin_memory()
     streamed = None
-    if graphed is not None:
+    if not wl.body:
         from swarp_b200.interop.streamed import StreamedRollout
 
         streamed = StreamedRollout(st, E, H, 2, "goal", aux_like=[goal], chunks=args.e2e_chunks)
@@ -662,21 +670,15 @@ def main() -> None:
         def e2e_end():
             streamed.end()
     else:
+        # the captured body step: inputs copied into its static buffers, gradient and loss out
         loss_h = torch.zeros(1, dtype=torch.float64).pin_memory()
         d2h = grad_h.numel() * grad_h.element_size() + 8
-        d_acts = torch.empty_like(acts)
 
         def e2e_step():
-            d_acts.copy_(pin[0], non_blocking=True)
-            p, th, gl = (x.to(dev, non_blocking=True) for x in pin[1:])
-            goal.copy_(gl)
-            a = d_acts.detach().requires_grad_(True)
-            st.restore_bodies(snap)
-            _, _, body = rollout_bodies(st, TorchState(p, th, torch.zeros_like(p), zero, zero), a)
-            loss = (body.pos[:, 0] - goal).norm(dim=-1).sum()
-            (g,) = torch.autograd.grad(loss, [a])
-            grad_h.copy_(g, non_blocking=True)
-            loss_h.copy_(loss.detach().double().reshape(1), non_blocking=True)
+            goal.copy_(pin[3], non_blocking=True)
+            graphed(TorchState(pin[1], pin[2], None, None, None), pin[0])
+            grad_h.copy_(graphed.grad_actions, non_blocking=True)
+            loss_h.copy_(graphed.loss.double().reshape(1), non_blocking=True)
 
         e2e_begin = e2e_end = None
 
@@ -693,15 +695,13 @@ def main() -> None:
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
     e2e_value = world * E * H / (float(e2e_ms.item()) / 1e3)
     # the gradient that came back equals the device-timed step's (same envs, same inputs)
-    e2e_grad_ok = None
-    if graphed is not None:
-        graphed(TorchState(pin[1].to(dev), pin[2].to(dev), None, None, None), pin[0].to(dev))
-        e2e_grad_ok = bool(torch.equal(graphed.grad_actions.cpu(), grad_h))
+    goal.copy_(pin[3])
+    graphed(TorchState(pin[1].to(dev), pin[2].to(dev), None, None, None), pin[0].to(dev))
+    e2e_grad_ok = bool(torch.equal(graphed.grad_actions.cpu(), grad_h))
     if streamed is not None:
         streamed.release()
 
-    if graphed is not None:
-        graphed.release()  # before the process group goes: the graph follows NCCL work
+    graphed.release()  # before the process group goes: the graph follows NCCL work
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -748,16 +748,20 @@ def main() -> None:
                 "path": (f"StreamedRollout: {streamed.n_chunks if streamed else 1} env chunks, "
                          "host-to-device copies, captured BPTT step and device-to-host copies "
                          "of the action gradient and loss on three streams"
-                         if graphed is not None else
-                         "eager rollout_bodies + autograd.grad; gradient copied back"),
+                         if streamed is not None else
+                         "inputs copied into the captured body step (GraphedRollout), action "
+                         "gradient and loss copied back"),
                 "grad_matches_device_step": e2e_grad_ok},
         # forward + loss reduction + adjoint per step, plus the fused-norm reduction when
         # ranks all-reduce it
-        "gpu_launches": (4 if dist is not None else 3) * args.steps,
+        # (body worlds: the two rollout kernels; the body loss and the body-state hand-over
+        # are torch ops in the same graph)
+        "gpu_launches": (2 if wl.body else (4 if dist is not None else 3)) * args.steps,
         "timed_path": ("one CUDA-graph replay of the whole BPTT step per step "
                        "(swarp_b200.interop.graphs.GraphedRollout with the goal loss fused into "
-                       "the rollout kernels, rollout_goal_loss)" if graphed is not None else
-                       "eager rollout_bodies + autograd.grad"),
+                       "the rollout kernels, rollout_goal_loss)" if not wl.body else
+                       "one CUDA-graph replay per step of rollout_bodies + the body loss + "
+                       "autograd.grad (swarp_b200.interop.graphs.GraphedRollout)"),
         "value_eager": value_eager,
     }
     if overflow is not None:

@@ -90,22 +90,22 @@ inline int launch_kernel(K kernel, int grid, int block, size_t smem, cudaStream_
              : kErrCuda;
 }
 
-template <typename T, int FL, int AS>
+template <typename T, int FL, int AS, int LB = 1024>
 int run_fwd(const RolloutArgs<T>& R, cudaStream_t st) {
   const Layout<T> L(R.G, R.A, R.N, R.S, false, (FL & F_BODIES) != 0,
                     (FL & F_BOXES) != 0 && (FL & (F_COLL | F_BODIES)) != 0);
   const int grid = (R.E + R.G - 1) / R.G;
-  const int rc = launch_kernel(rollout_fwd_kernel<T, FL, AS>, grid, R.G * R.A, L.total, st, &R);
+  const int rc = launch_kernel(rollout_fwd_kernel<T, FL, AS, LB>, grid, R.G * R.A, L.total, st, &R);
   if (rc != 0 || !R.goal) return rc;
   sum_partials_kernel<T><<<1, 256, 0, st>>>(R.loss_partial, grid, R.loss_out);
   return cudaGetLastError() == cudaSuccess ? 0 : kErrCuda;
 }
-template <typename T, int FL, int AS>
+template <typename T, int FL, int AS, int LB = 1024>
 int run_bwd(const RolloutArgs<T>& R, cudaStream_t st) {
   const Layout<T> L(R.G, R.A, R.N, R.S, true, (FL & F_BODIES) != 0,
                     (FL & F_BOXES) != 0 && (FL & F_COLL) != 0, (FL & F_DRONE) != 0);
   const int grid = (R.E + R.G - 1) / R.G;
-  const int rc = launch_kernel(rollout_bwd_kernel<T, FL, AS>, grid, R.G * R.A, L.total, st, &R);
+  const int rc = launch_kernel(rollout_bwd_kernel<T, FL, AS, LB>, grid, R.G * R.A, L.total, st, &R);
   if (rc != 0 || !R.gsq_partial) return rc;
   sum_partials_kernel<T><<<1, 256, 0, st>>>(R.gsq_partial, grid, R.gsq_out);
   return cudaGetLastError() == cudaSuccess ? 0 : kErrCuda;
@@ -139,6 +139,8 @@ template <typename T, int RB> int launch_fwd_part(const RolloutArgs<T>& R, int f
   case F:                                                                   \
     if constexpr (std::is_same<T, float>::value && ((F) & F_COLL))          \
       if (a16) return run_fwd<T, F, 16>(R, st);                             \
+    if constexpr (((F) & F_BODIES) != 0)                                    \
+      if (R.G * R.A <= kSmallCTA) return run_fwd<T, F, 0, kSmallCTA>(R, st); \
     return run_fwd<T, F, 0>(R, st);
   if constexpr ((RB & F_DRONE) != 0) {
     switch (fl) { SWARP_FLAG_CASES_DRONE(SWARP_X, RB) }
@@ -157,6 +159,8 @@ template <typename T, int RB> int launch_bwd_part(const RolloutArgs<T>& R, int f
   case F:                                                                   \
     if constexpr (std::is_same<T, float>::value && ((F) & F_COLL))          \
       if (a16) return run_bwd<T, F, 16>(R, st);                             \
+    if constexpr (((F) & F_BODIES) != 0)                                    \
+      if (R.G * R.A <= kSmallCTA) return run_bwd<T, F, 0, kSmallCTA>(R, st); \
     return run_bwd<T, F, 0>(R, st);
   if constexpr ((RB & F_DRONE) != 0) {
     switch (fl) { SWARP_FLAG_CASES_DRONE(SWARP_X, RB) }

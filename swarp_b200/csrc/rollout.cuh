@@ -50,6 +50,12 @@ enum : int {
 
 // Largest CTA the 16-agent specializations are launched with (host: envs_per_cta).
 constexpr int kMaxThreadsAS16 = 256;
+// Launch bound of the small-CTA instances of movable-body worlds (CTAs of at most this many
+// threads): their kernels then keep their state in up to 255 registers instead of 64.
+// Body worlds are latency-bound (one body thread per env, a few agents), where spilled
+// registers cost more than the occupancy the 1024-thread bound buys (measured at
+// 4096 envs x 4 agents + one 3-circle body: 2.09 -> 1.84 ms per BPTT step).
+constexpr int kSmallCTA = 256;
 
 // The four drone field arrays of one state (null when the world has no drones).
 template <typename P> struct DroneF {
@@ -786,8 +792,8 @@ __device__ __forceinline__ void seed_goal_loss(const RolloutArgs<T>& R, long lon
 }
 
 // ================================================================== forward
-template <typename T, int FL, int AS>
-__global__ void __launch_bounds__(1024) rollout_fwd_kernel(const RolloutArgs<T> R) {
+template <typename T, int FL, int AS, int LB = 1024>
+__global__ void __launch_bounds__(LB) rollout_fwd_kernel(const RolloutArgs<T> R) {
   using T4 = typename V4<T>::t;
   constexpr bool kBodies = (FL & F_BODIES) != 0;
   constexpr bool kShare = (FL & (F_COLL | F_BODIES)) != 0;  // agent records in smem each substep
@@ -1107,8 +1113,8 @@ __global__ void __launch_bounds__(256) sum_partials_kernel(const T* partial, int
 
 // The compile-time 16-agent instances run in CTAs of at most kMaxThreadsAS16 threads:
 // their adjoint then has up to 255 registers instead of 64 (measured 230 -> 224 us).
-template <typename T, int FL, int AS>
-__global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : 1024)
+template <typename T, int FL, int AS, int LB = 1024>
+__global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : LB)
     rollout_bwd_kernel(const RolloutArgs<T> R) {
   using T2 = typename V2<T>::t;
   using T4 = typename V4<T>::t;

@@ -21,8 +21,9 @@ from collections.abc import Callable
 import torch
 
 from swarp_b200.core.stepper import Stepper
-from swarp_b200.interop.autograd import (FusedGoalLoss, TorchState, Trajectory, fill_state_defaults,
-                                         rollout, rollout_goal_loss)
+from swarp_b200.interop.autograd import (BodyState, FusedGoalLoss, TorchState, Trajectory,
+                                         fill_state_defaults, rollout, rollout_bodies,
+                                         rollout_goal_loss)
 
 
 class GraphedRollout:
@@ -45,16 +46,35 @@ class GraphedRollout:
     a collective that overlapped the next step's forward kernel would take SM resources
     from it (one wave of it fills every SM's register file) and slow the step more than
     the all-reduce's own ~20 us. Release such a graph before destroying the process group.
+
+    Movable bodies: with ``stepper.bodies_in_grad`` the captured step pushes the bodies
+    (``rollout_bodies``) and ``loss_fn`` is called as ``loss_fn(final, trajectory,
+    bodies)`` with the final :class:`~swarp_b200.interop.autograd.BodyState`. Every replay
+    starts the bodies from the static state ``self.bodies`` (a copy of the stepper's body
+    state and obstacle poses at construction; ``bodies=`` of a call refills it) and leaves
+    the final body state in ``self.final_bodies``; replays do not advance the stepper's own
+    body state. Without ``bodies_in_grad`` a taped step freezes the bodies (the reference's
+    rule) and the world captures like one with static obstacles.
     """
 
     def __init__(self, stepper: Stepper, state: TorchState, actions: torch.Tensor,
                  loss_fn: Callable[[TorchState, Trajectory], torch.Tensor], *,
                  wrt_state: bool = False, grad_norm: bool | str = True,
                  warmup: int = 3, all_reduce: bool = False, group=None) -> None:
-        if stepper.any_movable:
-            raise NotImplementedError(
-                "GraphedRollout does not capture movable bodies: their state advances on the "
-                "host side between rollouts; use rollout_bodies eagerly")
+        self.bodies: BodyState | None = None
+        self.final_bodies: BodyState | None = None
+        self._moving = stepper.any_movable and stepper.bodies_in_grad
+        if self._moving:
+            if isinstance(loss_fn, FusedGoalLoss):
+                raise NotImplementedError("the fused goal loss does not take movable bodies")
+            if stepper.box_agents:
+                raise NotImplementedError("gradients through movable bodies pushed by box agents "
+                                          "are not built")
+            # the static body state every replay starts from, and the obstacle set (with its
+            # placed shape poses) the captured world description points at
+            self.bodies = BodyState(*(t.detach().clone() for t in stepper.body_state))
+            self._obstacles0 = stepper.obstacles
+            self._from_bodies0 = stepper._poses_from_bodies
         if stepper.has_drones:
             raise NotImplementedError("GraphedRollout captures 2-D fleets; run a fleet with "
                                       "drones through rollout eagerly")
@@ -86,17 +106,35 @@ class GraphedRollout:
         side.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(side):
             for _ in range(max(1, warmup)):
+                self._install_bodies()
                 self._body()
         torch.cuda.current_stream(dev).wait_stream(side)
         self.graph = torch.cuda.CUDAGraph()
+        self._install_bodies()
         with torch.cuda.graph(self.graph):
             self.loss, self.grads, self.loss_and_grad_norm = self._body()
+        self._install_bodies()
         self.grad_actions = self.grads[0]
         self.grad_state = TorchState(*self.grads[1:6]) if wrt_state else None
+
+    def _install_bodies(self) -> None:
+        """Point the stepper at the static body state and the obstacle set of construction
+        (a body rollout replaces both attributes with its outputs)."""
+        if not self._moving:
+            return
+        st = self.stepper
+        st.obstacles = self._obstacles0
+        st.body_state = tuple(self.bodies)
+        st._poses_from_bodies = self._from_bodies0
+        st._wc_cache.clear()
 
     def _body(self):
         if isinstance(self.loss_fn, FusedGoalLoss):
             loss = rollout_goal_loss(self.stepper, self.state, self.actions, self.loss_fn.goal)
+        elif self._moving:
+            fin, traj, body = rollout_bodies(self.stepper, self.state, self.actions)
+            self.final_bodies = body
+            loss = self.loss_fn(fin, traj, body)
         else:
             fin, traj = rollout(self.stepper, self.state, self.actions)
             loss = self.loss_fn(fin, traj)
@@ -114,8 +152,14 @@ class GraphedRollout:
             dist.all_reduce(pair, group=self.group)
         return loss.detach(), grads, pair
 
-    def __call__(self, state: TorchState | None = None, actions: torch.Tensor | None = None):
+    def __call__(self, state: TorchState | None = None, actions: torch.Tensor | None = None,
+                 bodies: BodyState | None = None):
         with torch.no_grad():
+            if bodies is not None:
+                if self.bodies is None:
+                    raise ValueError("this graph pushes no movable bodies")
+                for dst, src in zip(self.bodies, tuple(bodies), strict=True):
+                    dst.copy_(src, non_blocking=True)
             if actions is not None:
                 self.actions.copy_(actions, non_blocking=True)
             if state is not None:
