@@ -552,11 +552,12 @@ def main() -> None:
     graphed = reducer = None
     if not wl.body:
         # the same loss fused into the rollout kernels (rollout_goal_loss): the step is the
-        # forward kernel, one small reduction and the adjoint kernel
-        # with ranks, the (loss, ||g||^2) all-reduce is captured in the same graph, in stream
-        # order after the adjoint (measured at 2 GPUs: an asynchronous all-reduce that
-        # overlapped the next step's one-wave forward kernel cost 0.060 ms per step, one
-        # in stream order 0.017 ms)
+        # forward kernel, one small reduction and the adjoint kernel. With ranks, the
+        # (loss, ||g||^2) all-reduce is either captured in the same graph, in stream order
+        # after the adjoint, or started asynchronously on NCCL's stream so that it overlaps
+        # the next step (PairReducer); which costs less depends on the box (measured at
+        # 2 GPUs: 0.017 vs 0.060 ms per step on one box, 0.019 vs 0.009 ms on another), so
+        # the bench times both before the timed region and all ranks take the faster.
         graphed = GraphedRollout(st, state, acts, FusedGoalLoss(goal),
                                  grad_norm="fused" if dist is not None else False, warmup=3,
                                  all_reduce=dist is not None)
@@ -574,9 +575,6 @@ def main() -> None:
 
     def step():
         graphed()
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
 
     def timed_loop(fn, n, sample_clocks, finish=None, start=None):
         if dist is not None:
@@ -598,7 +596,36 @@ def main() -> None:
             dist.barrier()
         return e0.elapsed_time(e1), clk
 
-    ms, clocks = timed_loop(step, args.steps, True)
+    schedule, finish, plain, cal = "in-graph", None, None, None
+    if dist is not None and not wl.body:
+        plain = GraphedRollout(st, state, acts, FusedGoalLoss(goal), grad_norm="fused",
+                               warmup=3)
+        reducer = PairReducer(plain.loss_and_grad_norm, depth=8)
+
+        def step_async():
+            plain()
+            reducer(plain.loss_and_grad_norm)
+
+        n_cal = max(20, min(args.steps, 200))
+        for fn in (step, step_async):
+            for _ in range(3):
+                fn()
+        t_sync, _ = timed_loop(step, n_cal, False)
+        t_async, _ = timed_loop(step_async, n_cal, False, finish=reducer.drain)
+        cal_t = torch.tensor([t_sync / n_cal, t_async / n_cal], device=dev, dtype=torch.float64)
+        dist.all_reduce(cal_t, op=dist.ReduceOp.MAX)  # every rank takes the same schedule
+        cal = {"ms_per_step_in_graph": float(cal_t[0]), "ms_per_step_async": float(cal_t[1]),
+               "steps": n_cal}
+        if float(cal_t[1]) < float(cal_t[0]):
+            schedule, finish = "async", reducer.drain
+            step = step_async  # noqa: F811
+    for _ in range(args.warmup):
+        step()
+    if finish is not None:
+        finish()
+    torch.cuda.synchronize()
+
+    ms, clocks = timed_loop(step, args.steps, True, finish=finish)
     n_eager = max(20, min(args.steps, 200))
     for _ in range(3):
         eager_step(state, acts)
@@ -617,8 +644,7 @@ def main() -> None:
                     int(st.last_true_count_max.max()), "K": st.world.max_neighbors}
 
     # ---- collective: device time of the (loss, ||g||^2) all-reduce alone, back to back,
-    # and of the step when the same all-reduce runs asynchronously on NCCL's stream,
-    # overlapping the next step (the pattern the timed step avoids)
+    # and the two schedules' step times that chose the timed one
     allreduce = None
     if dist is not None and not wl.body:
         buf = torch.zeros(2, device=dev, dtype=torch.float32)
@@ -626,24 +652,14 @@ def main() -> None:
             dist.all_reduce(buf)
         n_ar = 100
         ar_ms, _ = timed_loop(lambda: dist.all_reduce(buf), n_ar, False)
-        plain = GraphedRollout(st, state, acts, FusedGoalLoss(goal), grad_norm="fused",
-                               warmup=3)
-        reducer = PairReducer(plain.loss_and_grad_norm, depth=8)
-
-        def step_async():
-            plain()
-            reducer(plain.loss_and_grad_norm)
-
-        for _ in range(3):
-            step_async()
-        n_sw = max(20, min(args.steps, 200))
-        sw_ms, _ = timed_loop(step_async, n_sw, False, finish=reducer.drain)
         plain.release()
-        ar_t = torch.tensor([ar_ms / n_ar * 1e3, sw_ms / n_sw], device=dev, dtype=torch.float64)
+        ar_t = torch.tensor([ar_ms / n_ar * 1e3], device=dev, dtype=torch.float64)
         dist.all_reduce(ar_t, op=dist.ReduceOp.MAX)
-        allreduce = {"us_per_allreduce_back_to_back": float(ar_t[0]),
-                     "ms_per_step_with_async_allreduce_overlapping": float(ar_t[1]),
-                     "timed_step": "all-reduce captured in the step's graph, in stream order",
+        allreduce = {"us_per_allreduce_back_to_back": float(ar_t[0]), "calibration": cal,
+                     "timed_step": ("all-reduce captured in the step's graph, in stream order"
+                                    if schedule == "in-graph" else
+                                    "all-reduce started asynchronously on NCCL's stream after "
+                                    "each replay, overlapping the next step (8 in flight)"),
                      "bytes": 8, "backend": "nccl"}
 
     # ---- end to end through the public API with host buffers: every step copies its
