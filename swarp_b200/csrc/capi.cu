@@ -167,13 +167,27 @@ bool state_complete(const swarp_state_t& s) {
 }
 bool drone_complete(const swarp_state_t& s) { return s.z && s.vz && s.attitude && s.body_rates; }
 
+// Contact masks checkpointed by the forward (F_MASK) so that the adjoint gathers its pairs
+// without rescanning the env: for envs of up to 32 agents without list truncation (every
+// world kind), and for 2-D disc fleets of up to kMaskMaxAgents agents with or without
+// truncation (ceil(A / 32) words per agent and substep). SWARP_CONTACT_MASKS=0 (read on
+// every call) keeps the larger worlds on the rescan path, for comparisons.
+constexpr int kMaskMaxAgents = 256;
+bool wide_masks_enabled() {
+  const char* s = std::getenv("SWARP_CONTACT_MASKS");
+  return !(s && s[0] == '0');
+}
+
 int flags_of(const swarp_world_t* w) {
   int fl = 0;
   if (w->collisions) {
     fl |= F_COLL;
-    if (w->n_agents - 1 > w->max_neighbors)
-      fl |= F_TRUNC;
-    else if (w->n_agents <= 32)
+    const bool trunc = w->n_agents - 1 > w->max_neighbors;
+    if (trunc) fl |= F_TRUNC;
+    if (!trunc && w->n_agents <= 32)
+      fl |= F_MASK;
+    else if (w->n_agents <= kMaskMaxAgents && !w->box_agents && !(w->fleet_models & 0x8) &&
+             wide_masks_enabled())
       fl |= F_MASK;
   }
   if (w->obstacles.n_obstacles > 0) {
@@ -268,15 +282,19 @@ template <typename Q> DroneF<Q> drone_of(const swarp_state_t& s) {
                    static_cast<Q*>(s.body_rates)};
 }
 
-// Workspace: [contact checkpoint cells (F_TRUNC cutoffs / F_MASK masks)] then, 256-byte
-// aligned, one partial sum per adjoint CTA for the fused ||grad_actions||^2 epilogue.
+// Workspace: [contact masks (F_MASK): cells x ceil(A/32) words] then, 256-byte aligned,
+// [list cutoffs (F_TRUNC): cells int16] then, 256-byte aligned, one partial sum per CTA
+// for the fused goal-loss and ||grad_actions||^2 epilogues.
+size_t align256(size_t b) { return (b + 255) & ~size_t(255); }
+size_t cutoff_offset(const swarp_world_t* w, int horizon) {
+  const size_t cells = (size_t)horizon * w->substeps * (size_t)w->n_envs * w->n_agents;
+  const size_t nw = (size_t)(w->n_agents + 31) / 32;
+  return (flags_of(w) & F_MASK) ? align256(cells * nw * sizeof(uint32_t)) : 0;
+}
 size_t partials_offset(const swarp_world_t* w, int horizon) {
   const size_t cells = (size_t)horizon * w->substeps * (size_t)w->n_envs * w->n_agents;
-  const int fl = flags_of(w);
-  size_t b = 0;
-  if (fl & F_TRUNC) b = cells * sizeof(int16_t);  // list cutoffs
-  if (fl & F_MASK) b = cells * sizeof(uint32_t);  // contact masks
-  return (b + 255) & ~size_t(255);
+  const size_t b = (flags_of(w) & F_TRUNC) ? cells * sizeof(int16_t) : 0;
+  return align256(cutoff_offset(w, horizon) + b);
 }
 size_t partials_bytes(const swarp_world_t* w) {
   // the CTA count of the generic or the two-agents-per-thread kernels, whichever is larger,
@@ -314,7 +332,9 @@ int fwd_typed(const swarp_world_t* w, int horizon, swarp_state_t init, const voi
   R.f_d = drone_of<T>(fin);
   R.true_max = true_max;
   const int fl = flags_of(w);
-  R.cutoff = (fl & F_TRUNC) ? static_cast<int16_t*>(ws) : nullptr;
+  R.cutoff = (fl & F_TRUNC) ? reinterpret_cast<int16_t*>(static_cast<unsigned char*>(ws) +
+                                                         cutoff_offset(w, horizon))
+                            : nullptr;
   R.cmask = (fl & F_MASK) ? static_cast<uint32_t*>(ws) : nullptr;
   if (use_cluster(R.A, fl)) {
     int BT = 0;
@@ -358,7 +378,9 @@ int bwd_typed(const swarp_world_t* w, int horizon, swarp_state_t init, const voi
   R.gf_d = drone_of<const T>(gfin);
   R.gi_d = drone_of<T>(ginit);
   const int fl = flags_of(w);
-  R.cutoff = (fl & F_TRUNC) ? static_cast<int16_t*>(ws) : nullptr;
+  R.cutoff = (fl & F_TRUNC) ? reinterpret_cast<int16_t*>(static_cast<unsigned char*>(ws) +
+                                                         cutoff_offset(w, horizon))
+                            : nullptr;
   R.cmask = (fl & F_MASK) ? static_cast<uint32_t*>(ws) : nullptr;
   R.gsq_out = static_cast<T*>(gsq);
   R.gsq_partial = gsq ? reinterpret_cast<T*>(static_cast<unsigned char*>(ws) +

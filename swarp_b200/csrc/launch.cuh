@@ -112,12 +112,14 @@ int run_bwd(const RolloutArgs<T>& R, cudaStream_t st) {
 }
 
 // Every valid flag combination: no contacts, contacts, truncating contacts, checkpointed
-// contacts; each with/without obstacles and with/without the holonomic-velocity fleet;
-// moving bodies (always with obstacles) with each contact mode and fleet kind.
+// contacts, truncating checkpointed contacts; each with/without obstacles and with/without
+// the holonomic-velocity fleet; moving bodies (always with obstacles) with each contact
+// mode and fleet kind.
 #define SWARP_FLAG_CASES_EULER(X, R)                                                           \
   X(R + 0) X(R + 4) X(R + 8) X(R + 12) X(R + 1) X(R + 5) X(R + 9) X(R + 13) X(R + 3) X(R + 7) \
   X(R + 11) X(R + 15) X(R + 17) X(R + 21) X(R + 25) X(R + 29) X(R + 36) X(R + 37) X(R + 39)   \
-  X(R + 53) X(R + 44) X(R + 45) X(R + 47) X(R + 61)
+  X(R + 53) X(R + 44) X(R + 45) X(R + 47) X(R + 61) X(R + 19) X(R + 23) X(R + 27) X(R + 31)   \
+  X(R + 55) X(R + 63)
 // (each instantiated once with R = 0 and once with R = F_RK4)
 
 // Drone worlds: the contact and obstacle cases without moving bodies (R = F_DRONE,

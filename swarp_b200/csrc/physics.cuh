@@ -184,6 +184,15 @@ __device__ __forceinline__ bool pair_force_add(T dx, T dy, T d2, T rvx, T rvy, T
   }
   return false;
 }
+// Whether two discs at d = p_self - p_other with min_dist are in contact, the decision of
+// pair_force_add and pair_vjp_terms (the same arithmetic).
+template <typename T>
+__device__ __forceinline__ bool pair_in_contact(T dx, T dy, T min_dist) {
+  const T m = wmax_c(dot2(dx, dy, dx, dy), Eps2<T>::v);
+  const T inv = Num<T>::rsqrt_(m);
+  return pair_overlap(min_dist, m, inv) > T(0);
+}
+
 // Force value (no accumulation), used where the result is negated/levered.
 template <typename T>
 __device__ __forceinline__ void pair_force(T dx, T dy, T rvx, T rvy, T min_dist, T inv_denom,

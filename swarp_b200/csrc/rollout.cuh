@@ -14,11 +14,14 @@
 // (FFMA2/FMUL2, sm_100) distance test of two neighbors. The test builds a 32-bit
 // membership mask per chunk of 32 agents; only set bits run the contact law.
 //
-// Contact checkpoint (F_MASK, A <= 32 and no list truncation): the forward stores per
-// agent and substep the 32-bit mask of neighbors it was in contact with. Contact is
-// symmetric, so the adjoint runs the pair VJPs over exactly those bits and never
-// repeats the neighbor scan. Otherwise (A > 32 or a truncating cap) the adjoint
-// rescans, and with truncation the forward stores each list's cutoff index instead.
+// Contact checkpoint (F_MASK: envs of up to 32 agents, and 2-D disc fleets of up to 256
+// agents with or without list truncation): the forward stores per agent and substep the
+// mask of the in-radius agents it is in contact with, listed or not, one 32-bit word per
+// 32 agents (word-major, [H*S][words][E*A]). Contact is symmetric, so the adjoint runs the
+// pair VJPs over exactly those bits, in the rescan's ascending order, and never repeats
+// the neighbor scan; with a truncating cap the forward also stores each list's cutoff
+// index, which gates each pair's own and cross terms. Otherwise (larger envs, box agents
+// or drones beyond one word or with truncation) the adjoint rescans with the cutoffs.
 #pragma once
 #include "bodies.cuh"
 #include "boxes.cuh"
@@ -80,7 +83,7 @@ template <typename T> struct RolloutArgs {
   T *f_pos, *f_th, *f_vel, *f_s, *f_w;
   int* true_max;
   int16_t* cutoff;   // workspace [H*S, E, A] (F_TRUNC)
-  uint32_t* cmask;   // workspace [H*S, E, A] (F_MASK)
+  uint32_t* cmask;   // workspace [H*S, NW, E*A], NW = ceil(A / 32) (F_MASK)
   // adjoint
   const T *gt_pos, *gt_th, *gt_vel, *gt_s, *gt_w;  // cotangent of trajectory (nullable)
   const T *gf_pos, *gf_th, *gf_vel, *gf_s, *gf_w;  // cotangent of final (nullable)
@@ -494,10 +497,13 @@ __device__ __forceinline__ unsigned scan_chunk(const double* xy_env, int c, int 
 // Calls fn(b, q) for every agent b != a of the env within the neighbor radius, ascending
 // b, with q = b's (x, y, vx, vy) record. Returns the count of such agents. thr_scan is
 // the scan's widened threshold, thr the exact one (in_radius).
-template <typename T, int AS, typename Fn>
+struct NoChunkEnd {
+  __device__ __forceinline__ void operator()(int) const {}
+};
+template <typename T, int AS, typename Fn, typename EndFn = NoChunkEnd>
 __device__ __forceinline__ int for_each_in_radius(const T* xy_env, const typename V4<T>::t* rec_env,
                                                   int A, int a, T px, T py, T thr_scan, T thr,
-                                                  Fn&& fn) {
+                                                  Fn&& fn, EndFn&& chunk_end = EndFn{}) {
   const int NP = (A + 1) / 2;
   int total = 0;
   const int nchunk = AS > 0 ? (AS + 31) / 32 : (A + 31) / 32;
@@ -515,33 +521,52 @@ __device__ __forceinline__ int for_each_in_radius(const T* xy_env, const typenam
       ++total;
       fn(b, q);
     }
+    chunk_end(c);  // after the chunk's members (every thread of the env reaches it)
   }
   return total;
 }
 
 // Contact force on agent a from its capped neighbor list (the first K within R by index).
 // Returns the uncapped count; cutoff = index of the K-th listed neighbor if truncated,
-// else A; cmask = contacts among agents 0..31.
+// else A. With contact masks (F_MASK; mout non-null) it also writes the env's contact mask
+// of agent a, one 32-bit word per 32 agents (word c at mout[c * mstride]): bit b for every
+// agent b within the radius that a is in contact with, listed or not (pair contact is
+// symmetric, so the adjoint can gather each pair from either side without a rescan).
 template <typename T, int FL, int AS>
 __device__ __forceinline__ int neighbor_force(const T* xy_env, const typename V4<T>::t* rec_env,
                                               const T* rad_env, int A, int a, const Agent<T>& x,
                                               const AgentP<T>& P, const WorldC<T>& W, T& fx, T& fy,
-                                              int& cutoff, unsigned& cmask) {
+                                              int& cutoff, uint32_t* mout = nullptr,
+                                              long long mstride = 0) {
   int listed = 0;
   cutoff = A;
-  cmask = 0u;
-  const int total = for_each_in_radius<T, AS>(xy_env, rec_env, A, a, x.px, x.py, W.r2_scan, W.r2_thr,
-                                              [&](int b, const typename V4<T>::t& q) {
-    if (FL & F_TRUNC) {
-      if (listed >= W.K) return;
-      ++listed;
-      if (listed == W.K) cutoff = b;
-    }
-    const T dx = x.px - q.x, dy = x.py - q.y;
-    if (pair_force_add(dx, dy, dot2(dx, dy, dx, dy), x.vx - q.z, x.vy - q.w,
-                       P.radius + rad_env[b] + W.margin, P.inv_denom, W, fx, fy))
-      cmask |= 1u << (b & 31);
-  });
+  unsigned word = 0u;  // contacts of the current chunk of 32 agents
+  const int total = for_each_in_radius<T, AS>(
+      xy_env, rec_env, A, a, x.px, x.py, W.r2_scan, W.r2_thr,
+      [&](int b, const typename V4<T>::t& q) {
+        bool listed_b = true;
+        if (FL & F_TRUNC) {
+          if (listed >= W.K) {
+            listed_b = false;
+          } else {
+            ++listed;
+            if (listed == W.K) cutoff = b;
+          }
+        }
+        if (!(FL & F_MASK) && !listed_b) return;
+        const T dx = x.px - q.x, dy = x.py - q.y;
+        const T md = P.radius + rad_env[b] + W.margin;
+        const bool contact = listed_b ? pair_force_add(dx, dy, dot2(dx, dy, dx, dy), x.vx - q.z,
+                                                       x.vy - q.w, md, P.inv_denom, W, fx, fy)
+                                      : pair_in_contact(dx, dy, md);
+        if ((FL & F_MASK) && contact) word |= 1u << (b & 31);
+      },
+      [&](int c) {
+        if (FL & F_MASK) {
+          if (mout) mout[c * mstride] = word;
+          word = 0u;
+        }
+      });
   if ((FL & F_TRUNC) && total <= W.K) cutoff = A;
   return total;
 }
@@ -583,6 +608,31 @@ __device__ __forceinline__ int neighbor_force_box(const T* xy_env, const typenam
   });
   if ((FL & F_TRUNC) && total <= W.K) cutoff = A;
   return total;
+}
+
+// Contact force from the checkpointed contact mask words mw[c * mstride] (c < NW), the
+// forward's sum: ascending b, only neighbors on the agent's list (b <= cut_a with list
+// truncation).
+template <typename T, int FL>
+__device__ __forceinline__ void mask_force_w(const typename V4<T>::t* rec_env, const T* rad_env,
+                                             const uint32_t* mw, long long mstride, int NW,
+                                             int cut_a, const Agent<T>& x, const AgentP<T>& P,
+                                             const WorldC<T>& W, T& fx, T& fy) {
+  for (int c = 0; c < NW; ++c) {
+    unsigned m = mw[c * mstride];
+    while (m) {
+      const int b = 32 * c + __ffs(m) - 1;
+      m &= m - 1u;
+      if ((FL & F_TRUNC) && b > cut_a) {  // ascending: the rest are past the list
+        c = NW;
+        break;
+      }
+      const auto q = rec_env[b];
+      const T dx = x.px - q.x, dy = x.py - q.y;
+      pair_force_add(dx, dy, dot2(dx, dy, dx, dy), x.vx - q.z, x.vy - q.w,
+                     P.radius + rad_env[b] + W.margin, P.inv_denom, W, fx, fy);
+    }
+  }
 }
 
 // Contact force from a checkpointed contact mask (ascending b, the forward's order).
@@ -844,6 +894,7 @@ __global__ void __launch_bounds__(LB) rollout_fwd_kernel(const RolloutArgs<T> R)
   const T4* shp_env = sshp + le * A;
   const long long ia = (long long)ec * A + a;
   const long long EA = (long long)R.E * A;
+  const int NW = (A + 31) >> 5;  // contact-mask words per agent and substep
   Agent<T> x;
   load_state(R.i_pos, R.i_th, R.i_vel, R.i_s, R.i_w, ia, x);
   constexpr bool kDrone = (FL & F_DRONE) != 0;
@@ -879,18 +930,23 @@ __global__ void __launch_bounds__(LB) rollout_fwd_kernel(const RolloutArgs<T> R)
       }
       if (FL & F_COLL) {
         int cutoff;
-        unsigned cm;
         int tc;
-        if (kBoxes)
+        const long long ws = ((long long)t * R.S + k) * EA + ia;
+        if (kBoxes) {
+          unsigned cm;
           tc = neighbor_force_box<T, FL, AS>(xy_env, rec_env, thw_env0 + buf * GA, shp_env, rad_env,
                                              A, a, x, P, W, fx, fy, cutoff, cm);
-        else
+          if ((FL & F_MASK) && valid) R.cmask[ws] = cm;  // box worlds: one word (A <= 32)
+        } else {
+          // contact-mask words of this substep: word-major [H*S][NW][E*A]
+          uint32_t* mout = ((FL & F_MASK) && valid)
+                               ? R.cmask + ((long long)t * R.S + k) * NW * EA + ia
+                               : nullptr;
           tc = neighbor_force<T, FL, AS>(xy_env, rec_env, rad_env, A, a, x, P, W, fx, fy, cutoff,
-                                         cm);
+                                         mout, EA);
+        }
         tmax = max(tmax, tc);
-        const long long ws = ((long long)t * R.S + k) * EA + ia;
         if ((FL & F_TRUNC) && valid) R.cutoff[ws] = (int16_t)cutoff;
-        if ((FL & F_MASK) && valid) R.cmask[ws] = cm;
       }
       static_force<T, FL>(obs_env, N, x, P, W, fx, fy);
       if (kBodies) {
@@ -950,18 +1006,48 @@ __device__ __forceinline__ void force_vjp(const T* xy_env, const typename V4<T>:
                                           const BodyC<T>* sbc, typename V4<T>::t* gpose, int N,
                                           int A, int a, unsigned cmask, const Agent<T>& x,
                                           const AgentP<T>& P, const WorldC<T>& W, T gfx, T gfy,
-                                          Agent<T>& gin) {
+                                          Agent<T>& gin, const uint32_t* mw = nullptr,
+                                          long long mstride = 0) {
   using T4 = typename V4<T>::t;
   if (FL & F_MASK) {
-    unsigned m = cmask;
-    while (m) {
-      const int b = __ffs(m) - 1;
-      m &= m - 1u;
+    // the checkpointed contacts (word 0 in cmask, words c >= 1 at mw[c * mstride]): every
+    // in-radius contact of agent a in ascending order, the pairs the rescan below finds in
+    // contact; with list truncation the own and cross terms are gated by the cutoffs
+    const int cut_a = (FL & F_TRUNC) ? cut_env[a] : A;
+    auto visit = [&](int b) {
       const auto q = rec_env[b];
       const auto gb = fb_env[b];
-      pair_vjp_sym(x.px - q.x, x.py - q.y, x.vx - q.z, x.vy - q.w, P.radius + rad_env[b] + W.margin,
-                   P.inv_denom, gfx, gfy, iden_env[b], gb.x, gb.y, W, gin.px, gin.py, gin.vx,
-                   gin.vy);
+      if (FL & F_TRUNC) {
+        const bool own = b <= cut_a;
+        const bool cross = a <= cut_env[b];
+        pair_vjp_sym(x.px - q.x, x.py - q.y, x.vx - q.z, x.vy - q.w,
+                     P.radius + rad_env[b] + W.margin, P.inv_denom, own ? gfx : T(0),
+                     own ? gfy : T(0), iden_env[b], cross ? gb.x : T(0), cross ? gb.y : T(0), W,
+                     gin.px, gin.py, gin.vx, gin.vy);
+      } else {
+        pair_vjp_sym(x.px - q.x, x.py - q.y, x.vx - q.z, x.vy - q.w,
+                     P.radius + rad_env[b] + W.margin, P.inv_denom, gfx, gfy, iden_env[b], gb.x,
+                     gb.y, W, gin.px, gin.py, gin.vx, gin.vy);
+      }
+    };
+    unsigned m = cmask;
+    if (A <= 32) {
+      while (m) {
+        const int b = __ffs(m) - 1;
+        m &= m - 1u;
+        visit(b);
+      }
+    } else {
+      const int NW = (A + 31) >> 5;
+      for (int c = 0; c < NW; ++c) {
+        const unsigned next = (c + 1 < NW) ? mw[(c + 1) * mstride] : 0u;  // load ahead
+        while (m) {
+          const int b = 32 * c + __ffs(m) - 1;
+          m &= m - 1u;
+          visit(b);
+        }
+        m = next;
+      }
     }
   } else if (FL & F_COLL) {
     const int cut_a = (FL & F_TRUNC) ? cut_env[a] : A;
@@ -1232,7 +1318,9 @@ __global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : LB)
       load_drone(R.i_d, ia, curd);
     load_action23(R, (long long)(H - 1) * EA + ia, a2, a3);
   }
-  if ((FL & F_MASK) && S == 1) cm0 = R.cmask[(long long)(H - 1) * EA + ia];
+  // contact-mask words, word-major [H*S][NW][E*A]; word 0 of each step is loaded ahead
+  const int NW = (A + 31) >> 5;
+  if ((FL & F_MASK) && S == 1) cm0 = R.cmask[(long long)(H - 1) * NW * EA + ia];
   int fbuf = 0;
   T gsq = T(0);  // this agent's sum over the horizon of ||d loss / d action||^2
   for (int t = H - 1; t >= 0; --t) {
@@ -1255,7 +1343,7 @@ __global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : LB)
           load_drone(R.i_d, ia, pcurd);
         load_action23(R, (long long)(t - 1) * EA + ia, pa2, pa3);
       }
-      if ((FL & F_MASK) && S == 1) pcm = R.cmask[(long long)(t - 1) * EA + ia];
+      if ((FL & F_MASK) && S == 1) pcm = R.cmask[(long long)(t - 1) * NW * EA + ia];
     }
     T ga0 = T(0), ga1 = T(0), ga2 = T(0), ga3 = T(0);
 
@@ -1288,7 +1376,8 @@ __global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : LB)
                                  gfy, gin);
       else
         force_vjp<T, FL, AS>(xy_env, rec_env, fb_env, cut_env, rad_env, iden_env, obs_env, sbc,
-                             nullptr, N, A, a, cm0, cur, P, W, gfx, gfy, gin);
+                             nullptr, N, A, a, cm0, cur, P, W, gfx, gfy, gin,
+                             (FL & F_MASK) ? R.cmask + (long long)t * NW * EA + ia : nullptr, EA);
       g = gin;
       fbuf ^= 1;
     } else {
@@ -1321,11 +1410,14 @@ __global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : LB)
         if (FL & F_COLL) {
           const T2* thw_env = sthw + k * GA + le * A;
           if (FL & F_MASK) {
-            const unsigned cmk = R.cmask[((long long)t * S + k) * EA + ia];
-            if (kBoxes)
-              mask_force_box(rec_env, thw_env, shp_env, rad_env, cmk, a, x, P, W, fx, fy);
-            else
-              mask_force(rec_env, rad_env, cmk, x, P, W, fx, fy);
+            const uint32_t* mw = R.cmask + ((long long)t * S + k) * NW * EA + ia;
+            if (kBoxes) {
+              mask_force_box(rec_env, thw_env, shp_env, rad_env, mw[0], a, x, P, W, fx, fy);
+            } else {
+              const int cut_a =
+                  (FL & F_TRUNC) ? R.cutoff[((long long)t * S + k) * EA + ia] : A;
+              mask_force_w<T, FL>(rec_env, rad_env, mw, EA, NW, cut_a, x, P, W, fx, fy);
+            }
           } else {
             int cutoff;
             unsigned cm;
@@ -1333,8 +1425,7 @@ __global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : LB)
               neighbor_force_box<T, FL, AS>(xy_env, rec_env, thw_env, shp_env, rad_env, A, a, x, P,
                                             W, fx, fy, cutoff, cm);
             else
-              neighbor_force<T, FL, AS>(xy_env, rec_env, rad_env, A, a, x, P, W, fx, fy, cutoff,
-                                        cm);
+              neighbor_force<T, FL, AS>(xy_env, rec_env, rad_env, A, a, x, P, W, fx, fy, cutoff);
           }
         }
         static_force<T, FL>(obs_env, N, x, P, W, fx, fy);
@@ -1379,7 +1470,9 @@ __global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : LB)
         fb_env[a] = T2{gfx, gfy};
         const long long ws = ((long long)t * S + k) * EA + ia;
         if (FL & F_TRUNC) cut_env[a] = R.cutoff[ws];
-        const unsigned cm = (FL & F_MASK) ? R.cmask[ws] : 0u;
+        const uint32_t* mw =
+            (FL & F_MASK) ? R.cmask + ((long long)t * S + k) * NW * EA + ia : nullptr;
+        const unsigned cm = (FL & F_MASK) ? mw[0] : 0u;
         __syncthreads();
         if (FL & F_BOXES)
           force_vjp_box<T, FL, AS>(xy_env, rec_env, sthw + k * GA + le * A, shp_env, fb_env,
@@ -1387,7 +1480,8 @@ __global__ void __launch_bounds__(AS == 16 ? kMaxThreadsAS16 : LB)
                                    gfy, gin);
         else
           force_vjp<T, FL, AS>(xy_env, rec_env, fb_env, cut_env, rad_env, iden_env, obs_env, sbc,
-                               sgpose + size_t(tid) * N, N, A, a, cm, in, P, W, gfx, gfy, gin);
+                               sgpose + size_t(tid) * N, N, A, a, cm, in, P, W, gfx, gfy, gin,
+                               mw, EA);
         if (kBodies) {
           __syncthreads();  // shape-pose cotangents of every agent are in
           if (a == 0)
