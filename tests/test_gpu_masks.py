@@ -75,7 +75,7 @@ def _obstacles(E, seed):
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
 @pytest.mark.parametrize("A,K,substeps,obs", [(40, 64, 1, False), (40, 3, 1, True),
-                                              (96, 8, 2, False), (256, 32, 1, False),
+                                              (96, 8, 2, False), (256, 10, 1, False),
                                               (256, 12, 2, True)])
 def test_masks_bitwise_rescan(dtype, A, K, substeps, obs):
     models = [DynamicsModel.HOLONOMIC, DynamicsModel.DIFF_DRIVE, DynamicsModel.KINEMATIC_BICYCLE]
