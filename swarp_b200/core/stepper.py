@@ -197,8 +197,6 @@ class Stepper:
         self.n_obstacles = obs.n_obstacles
         moving = obs.kind[obs.body.long()] != 0  # shapes whose body root is movable
         self.any_movable = bool(moving.any().item())
-        if self.any_movable and self.has_drones:
-            raise NotImplementedError("drones against movable obstacles are not on the CUDA path")
         if self.any_movable and self.n_agents > _lib.MAX_CTA_AGENTS:
             raise NotImplementedError(f"movable obstacles run in envs of at most "
                                       f"{_lib.MAX_CTA_AGENTS} agents")

@@ -142,7 +142,7 @@ int validate_world(const swarp_world_t* w, int horizon) {
   if (!w->params || !w->model_tag || !w->ctrl_mode) return SWARP_ERR_INVALID_ARG;
   if (w->fleet_models & ~0xF) return SWARP_ERR_UNSUPPORTED;  // unknown tags
   if (w->fleet_models == 0 || w->fleet_modes == 0 || (w->fleet_modes & ~0x7)) return SWARP_ERR_INVALID_ARG;
-  // drones together with box agents (exclusive in the reference) or moving bodies: not built
+  // drones together with box agents (exclusive in the reference): not built
   if ((w->fleet_models & 0x8) && w->box_agents) return SWARP_ERR_UNSUPPORTED;
   if (w->bounds_mode < 0 || w->bounds_mode > 2) return SWARP_ERR_INVALID_ARG;
   if (w->integrator < 0 || w->integrator > 1) return SWARP_ERR_INVALID_ARG;
@@ -442,7 +442,6 @@ int swarp_rollout_fwd(const swarp_world_t* w, int32_t horizon, swarp_state_t ini
   const bool any_fin = final_out.pos || final_out.theta || final_out.vel || final_out.speed || final_out.ang_vel;
   if (any_fin && !state_complete(final_out)) return SWARP_ERR_INVALID_ARG;
   if (flags_of(w) & F_DRONE) {
-    if ((flags_of(w) & F_BODIES)) return SWARP_ERR_UNSUPPORTED;
     if (!drone_complete(init) || !drone_complete(traj)) return SWARP_ERR_INVALID_ARG;
     if (any_fin && !drone_complete(final_out)) return SWARP_ERR_INVALID_ARG;
   }
@@ -468,7 +467,6 @@ int swarp_rollout_bwd(const swarp_world_t* w, int32_t horizon, swarp_state_t ini
   if (goal_loss.goal && !goal_loss.loss_grad) return SWARP_ERR_INVALID_ARG;
   if ((flags_of(w) & F_BOXES) && (flags_of(w) & F_BODIES)) return SWARP_ERR_UNSUPPORTED;
   if (flags_of(w) & F_DRONE) {
-    if (flags_of(w) & F_BODIES) return SWARP_ERR_UNSUPPORTED;
     if (!drone_complete(init) || !drone_complete(traj) || !drone_complete(adj_init))
       return SWARP_ERR_INVALID_ARG;
   }

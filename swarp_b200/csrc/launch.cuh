@@ -122,10 +122,12 @@ int run_bwd(const RolloutArgs<T>& R, cudaStream_t st) {
   X(R + 55) X(R + 63)
 // (each instantiated once with R = 0 and once with R = F_RK4)
 
-// Drone worlds: the contact and obstacle cases without moving bodies (R = F_DRONE,
-// F_DRONE | F_RK4); a drone fleet is never a holonomic-velocity fleet.
-#define SWARP_FLAG_CASES_DRONE(X, R) \
-  X(R + 0) X(R + 4) X(R + 1) X(R + 5) X(R + 3) X(R + 7) X(R + 17) X(R + 21)
+// Drone worlds: the contact and obstacle cases, and movable bodies (always with obstacles)
+// with each contact mode (R = F_DRONE, F_DRONE | F_RK4); a drone fleet is never a
+// holonomic-velocity fleet.
+#define SWARP_FLAG_CASES_DRONE(X, R)                                                       \
+  X(R + 0) X(R + 4) X(R + 1) X(R + 5) X(R + 3) X(R + 7) X(R + 17) X(R + 21) X(R + 36) X(R + 37) \
+  X(R + 39) X(R + 53)
 
 // Box-agent worlds: the cases without moving bodies (R = F_BOXES, F_BOXES | F_RK4); the
 // forward also runs box agents pushing movable bodies (their adjoint is not built).

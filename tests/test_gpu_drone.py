@@ -190,3 +190,50 @@ def test_warp_step_and_default_drone_fields():
                  acts.cpu(), ref_world(st))[0]
     for f in range(9):
         close(out[f].cpu(), ref[f], 1e-10, NAMES[f])
+
+
+@pytest.mark.parametrize("substeps", [1, 2])
+def test_drones_push_movable_body_f64(substeps):
+    """A mixed fleet with drones around a movable three-circle body: the drones push it as
+    discs (their 2-D position, velocity and radius), the body moves on grad rollouts
+    (bodies_in_grad), and trajectories (all nine fields), the final body state and the
+    gradients of a loss on both match the oracle at the float64 bars."""
+    from swarp_b200.interop.autograd import rollout_bodies
+
+    from test_gpu_bodies import compound_body, transport_world
+
+    E, A, T = 4, 6, 12
+    st = Stepper(fleet(A), dt=0.02, substeps=substeps, device=DEV, dtype=D,
+                 world=transport_world())
+    obs = compound_body(E, 31)
+    st.set_obstacles(obs)
+    st.bodies_in_grad = True
+    s9 = list(state9(E, A, 32, spread=0.25))
+    s9[0] = obs.pos[:, 1:2, :] + (s9[0] - s9[0].mean(1, keepdim=True)) * 0.9
+    acts = thrusts(T, E, A, 33, spread=1.0)
+    goal = torch.tensor([0.3, -0.1], dtype=D)
+
+    w = ref_world(st)
+    ob = ref_obstacles(st)
+    ro = [t.clone().requires_grad_(True) for t in s9]
+    ra = acts.clone().requires_grad_(True)
+    fin_r, traj_r, body_r = R.rollout(tuple(ro), ra, w, ob)
+    loss_r = ((body_r[-1].body_pos[:, 0] - goal) ** 2).sum() + (fin_r[0] ** 2).sum() \
+        + 0.1 * fin_r[5].sum()
+    gref = torch.autograd.grad(loss_r, [ra, *ro])
+
+    co = [t.to(DEV).clone().requires_grad_(True) for t in s9]
+    ca = acts.to(DEV).clone().requires_grad_(True)
+    fin, traj, body = rollout_bodies(st, TorchState(*co), ca)
+    loss = ((body.pos[:, 0] - goal.to(DEV)) ** 2).sum() + (fin.pos ** 2).sum() + 0.1 * fin.z.sum()
+    gcuda = torch.autograd.grad(loss, [ca, *co])
+    for f in range(9):
+        close(traj.stacked[f].detach().cpu(), torch.stack([t[f] for t in traj_r]).detach(), 1e-10,
+              f"traj {NAMES[f]}")
+    close(body.pos[:, 0].detach().cpu(), body_r[-1].body_pos[:, 0].detach(), 1e-10, "body pos")
+    close(body.angle[:, 0].detach().cpu(), body_r[-1].body_angle[:, 0].detach(), 1e-10,
+          "body angle")
+    moved = (body.pos[:, 0].detach().cpu() - ob.body_pos[:, 0]).norm(dim=-1).max()
+    assert float(moved) > 1e-3, "the body was pushed"
+    for i, n in enumerate(["actions", *NAMES]):
+        close(gcuda[i].cpu(), gref[i], 1e-9, f"grad {n}")
