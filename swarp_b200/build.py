@@ -30,7 +30,11 @@ EXTRA_HEADERS = {"k_x2_f32.cu": ["rollout_x2.cuh"], "capi.cu": ["rollout_cluster
                     for d in ("fwd", "bwd") for t in ("f32", "f64")}}
 DEPS = [*SOURCES, *COMMON_HEADERS, "rollout_x2.cuh", "k_cl.cuh", "rollout_cluster.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--extended-lambda", "-fmad=false",
+# -ftz=true: float32 arithmetic flushes subnormal inputs and results to zero (float64 is
+# unaffected); every float kernel is built the same way, so the kernels that must agree bit
+# for bit (forward and adjoint recomputation, paired and one-agent, cluster and one-CTA)
+# still do
+FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--extended-lambda", "-fmad=false", "-ftz=true",
          "-Xcompiler", "-fPIC", "-Xcompiler", "-O2"]
 LINK = ["--shared", "-cudart", "shared"]
 
@@ -47,7 +51,8 @@ def _stale(lib: str, deps: list[str]) -> bool:
         return True
     t = os.path.getmtime(lib)
     hdr = os.path.join(ROOT, "include", "swarp_b200.h")
-    return any(os.path.getmtime(p) > t for p in [*deps, hdr])
+    # this file holds the compiler flags: a change to it rebuilds everything
+    return any(os.path.getmtime(p) > t for p in [*deps, hdr, os.path.abspath(__file__)])
 
 
 def build(force: bool = False, verbose: bool = False, extra: list[str] | None = None) -> str:
@@ -61,6 +66,7 @@ def build(force: bool = False, verbose: bool = False, extra: list[str] | None = 
     # changed (or when forced or given extra flags)
     headers = [os.path.join(CSRC, d) for d in COMMON_HEADERS]
     headers.append(os.path.join(ROOT, "include", "swarp_b200.h"))
+    headers.append(os.path.abspath(__file__))
     newest_hdr = max(os.path.getmtime(h) for h in headers)
     for src in SOURCES:
         obj = os.path.join(objdir, src.replace(".cu", ".o"))
