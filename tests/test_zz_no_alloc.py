@@ -4,7 +4,7 @@
 running under another runtime's memory manager (an XLA/JAX custom call, another
 framework's operator) must not allocate behind that manager's back, and a real-time
 control loop cannot wait on cudaMalloc, which may synchronize the device. It keeps the
-forward/adjoint workspace (per-substep contact masks, or list cutoffs when the neighbor
+forward/adjoint workspace (per-substep contact masks, plus list cutoffs when the neighbor
 cap truncates) in a static device array owned by the library.
 
 Here it is called through the C ABI twice in a row per case, on different inputs, so the
@@ -39,7 +39,7 @@ def _inputs(seed, dtype):
 
 
 # (dtype, max_neighbors): K=16 checkpoints contact masks, K=8 truncates the lists and
-# checkpoints their cutoffs instead
+# checkpoints their cutoffs beside the masks
 CASES = [(torch.float32, 16), (torch.float32, 8), (torch.float64, 16)]
 
 
