@@ -38,10 +38,10 @@ bool x2_enabled() {
 bool aligned(const void* p, unsigned n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; }
 
 // Whether a float world can take the two-agents-per-thread kernels (their preconditions:
-// 16 or 32 agents, 2 action slots, checkpointed contact masks, no moving bodies,
-// vector-aligned fields; the adjoint also one substep per step).
+// 16 agents, 2 action slots, checkpointed contact masks, no moving bodies, vector-aligned
+// fields; the adjoint also one substep per step).
 bool x2_ok(const RolloutArgs<float>& R, int fl, bool bwd) {
-  if (!x2_enabled() || (R.A != 16 && R.A != 32) || R.act_dim != 2) return false;
+  if (!x2_enabled() || R.A != 16 || R.act_dim != 2) return false;
   if (!(fl & F_MASK) || (fl & (F_BODIES | F_TRUNC | F_BOXES | F_DRONE))) return false;
   if (bwd && R.S != 1) return false;
   const void* v16[] = {R.t_pos, R.t_vel, R.i_pos, R.i_vel, R.act, R.f_pos, R.f_vel, R.g_act};
@@ -53,11 +53,7 @@ bool x2_ok(const RolloutArgs<float>& R, int fl, bool bwd) {
     if (p && !aligned(p, 8)) return false;
   return true;
 }
-// 64 threads (the kernels' launch bound), A / 2 threads per env
-int x2_envs_per_cta(int E, int A) {
-  const int g = 128 / A;
-  return E < g ? E : g;
-}
+int x2_envs_per_cta(int E) { return E < 8 ? E : 8; }  // 64 threads: the kernels' launch bound
 
 // Envs per CTA: whole envs, about threads_target() threads.
 int envs_per_cta(int A, int E) {
@@ -303,8 +299,7 @@ size_t partials_offset(const swarp_world_t* w, int horizon) {
 size_t partials_bytes(const swarp_world_t* w) {
   // the CTA count of the generic or the two-agents-per-thread kernels, whichever is larger,
   // or of the cluster kernels (CS CTAs per env)
-  const int G = std::min(envs_per_cta(w->n_agents, w->n_envs),
-                         x2_envs_per_cta(w->n_envs, w->n_agents));
+  const int G = std::min(envs_per_cta(w->n_agents, w->n_envs), x2_envs_per_cta(w->n_envs));
   size_t n = (size_t)(w->n_envs + G - 1) / G;
   int CS = 1, BT = 0;
   if (use_cluster(w->n_agents, flags_of(w)) && cluster_shape(w->n_agents, CS, BT))
@@ -348,7 +343,7 @@ int fwd_typed(const swarp_world_t* w, int horizon, swarp_state_t init, const voi
   }
   if constexpr (std::is_same<T, float>::value) {
     if (x2_ok(R, fl, false)) {
-      R.G = x2_envs_per_cta(R.E, R.A);
+      R.G = x2_envs_per_cta(R.E);
       return launch_fwd_x2(R, fl, st);
     }
   }
@@ -398,7 +393,7 @@ int bwd_typed(const swarp_world_t* w, int horizon, swarp_state_t init, const voi
   }
   if constexpr (std::is_same<T, float>::value) {
     if (x2_ok(R, fl, true)) {
-      R.G = x2_envs_per_cta(R.E, R.A);  // no more CTAs than the partials buffer is sized for
+      R.G = x2_envs_per_cta(R.E);  // fewer CTAs than the partials buffer is sized for
       return launch_bwd_x2(R, fl, st);
     }
   }

@@ -21,8 +21,7 @@ constexpr int kErrCuda = -4;
 // each part compiles in a translation unit of its own (k_*.cu).
 template <typename T, int RB> int launch_fwd_part(const RolloutArgs<T>& R, int fl, cudaStream_t st);
 template <typename T, int RB> int launch_bwd_part(const RolloutArgs<T>& R, int fl, cudaStream_t st);
-// Two agents per thread (float, A == 16 or 32, contact masks, no moving bodies;
-// rollout_x2.cuh).
+// Two agents per thread (float, A == 16, contact masks, no moving bodies; rollout_x2.cuh).
 // R.G counts envs per CTA of 8 threads each.
 int launch_fwd_x2(const RolloutArgs<float>& R, int fl, cudaStream_t st);
 int launch_bwd_x2(const RolloutArgs<float>& R, int fl, cudaStream_t st);

@@ -1,4 +1,4 @@
-// Two agents per thread for float envs of exactly 16 or 32 agents (the benchmark shapes).
+// Two agents per thread for float envs of exactly 16 agents (the benchmark shape).
 //
 // Thread j of an env owns agents 2j and 2j+1. Everything that is per agent (scan
 // arithmetic, contact law, walls, integrator and their adjoints) is the same device code
@@ -10,7 +10,7 @@
 // adjacent agents, and loop, barrier and address overhead is paid once per two agents.
 // The two agents' independent chains also double the instruction-level parallelism.
 //
-// Preconditions (checked by the host): A == 16 or 32, act_dim == 2, contact masks checkpointed
+// Preconditions (checked by the host): A == 16, act_dim == 2, contact masks checkpointed
 // (no list truncation), no moving bodies, every pointer 16-byte aligned; the adjoint
 // additionally one substep per step. Other worlds take the one-agent kernels.
 #pragma once
@@ -18,9 +18,8 @@
 
 namespace swarp {
 
-// Agents per env of the instances (template argument AS); AS / 2 threads per env.
-constexpr int kX2Agents = 16;
-constexpr int kX2AgentsWide = 32;
+constexpr int kX2Agents = 16;     // agents per env
+constexpr int kX2Threads = 8;     // threads per env
 
 // Register budgets, as resident 64-thread CTAs per SM. A 16,000-env batch is 4,000 warps:
 // 14 CTAs (28 warps) per SM hold it in one wave on 148 SMs.
@@ -34,8 +33,7 @@ constexpr int kX2AgentsWide = 32;
 // Both agents' candidate masks over the env (self bits included; a superset of the
 // in-radius sets at thr = W.r2_scan): one 16-byte table load per pair of candidates,
 // shared by the two agents.
-template <int AS>
-__device__ __forceinline__ void scan_pair(const float* xy_env, const Agent<float>& x0,
+__device__ __forceinline__ void scan_pair16(const float* xy_env, const Agent<float>& x0,
                                             const Agent<float>& x1, float thr, unsigned& m0,
                                             unsigned& m1) {
   const float4* P = reinterpret_cast<const float4*>(xy_env);
@@ -45,7 +43,7 @@ __device__ __forceinline__ void scan_pair(const float* xy_env, const Agent<float
   m0 = 0u;
   m1 = 0u;
 #pragma unroll
-  for (int p = AS / 2 - 1; p >= 0; --p) {
+  for (int p = kX2Agents / 2 - 1; p >= 0; --p) {
     const float4 q = P[p];
     const float2 qx = make_float2(q.x, q.y), qy = make_float2(q.z, q.w);
     const float2 dx0 = __ffma2_rn(qx, M1, PX0), dy0 = __ffma2_rn(qy, M1, PY0);
@@ -224,14 +222,13 @@ __device__ __forceinline__ void add_cotangent_pair(const float* pos, const float
 }
 
 // ------------------------------------------------------------------- forward
-template <int FL, int AS>
+template <int FL>
 __global__ void __launch_bounds__(64, SWARP_X2_FWD_MINB) rollout_fwd_x2_kernel(const RolloutArgs<float> R) {
-  constexpr int A = AS;
-  constexpr int TPE = AS / 2;  // threads per env
+  constexpr int A = kX2Agents;
   extern __shared__ __align__(16) unsigned char smem[];
   const int G = R.G, GA = G * A, N = R.N;
   const int tid = threadIdx.x;
-  const int le = tid / TPE, j = tid - le * TPE;
+  const int le = tid / kX2Threads, j = tid - le * kX2Threads;
   const int a0 = 2 * j;
   const int e0 = blockIdx.x * G;
   const int e = e0 + le;
@@ -279,7 +276,7 @@ __global__ void __launch_bounds__(64, SWARP_X2_FWD_MINB) rollout_fwd_x2_kernel(c
       static_forces_both<FL>(obs_env, N, x0, x1, P0, P1, W, sx0, sy0, sx1, sy1);
       __syncthreads();
       unsigned m0, m1;
-      scan_pair<AS>(xy_env, x0, x1, W.r2_scan, m0, m1);
+      scan_pair16(xy_env, x0, x1, W.r2_scan, m0, m1);
       m0 &= ~(1u << a0);
       m1 &= ~(1u << (a0 + 1));
       float fx0 = 0.f, fy0 = 0.f, fx1 = 0.f, fy1 = 0.f;
@@ -325,14 +322,13 @@ __global__ void __launch_bounds__(64, SWARP_X2_FWD_MINB) rollout_fwd_x2_kernel(c
 
 // ------------------------------------------------------------------- adjoint
 // One substep per step, contacts from the checkpointed masks.
-template <int FL, int AS>
+template <int FL>
 __global__ void __launch_bounds__(64, SWARP_X2_BWD_MINB) rollout_bwd_x2_kernel(const RolloutArgs<float> R) {
-  constexpr int A = AS;
-  constexpr int TPE = AS / 2;  // threads per env
+  constexpr int A = kX2Agents;
   extern __shared__ __align__(16) unsigned char smem[];
   const int G = R.G, GA = G * A, N = R.N;
   const int tid = threadIdx.x;
-  const int le = tid / TPE, j = tid - le * TPE;
+  const int le = tid / kX2Threads, j = tid - le * kX2Threads;
   const int a0 = 2 * j;
   const int e0 = blockIdx.x * G;
   const int e = e0 + le;
