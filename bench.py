@@ -464,7 +464,7 @@ def main() -> None:
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5])
     ap.add_argument("--impl", default="swarp_b200", choices=["swarp_b200", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=30)
-    ap.add_argument("--e2e-chunks", type=int, default=8,
+    ap.add_argument("--e2e-chunks", type=int, default=2,
                     help="env chunks the end-to-end leg pipelines host copies over")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--envs", type=int, default=None,
