@@ -115,3 +115,41 @@ def test_ctypes_layout_matches_c(tmp_path):
         struct, field = key.split(".")
         cls = {"swarp_world_t": _lib.WorldC, "swarp_state_t": _lib.State}.get(struct, _lib.ObstaclesC)
         assert getattr(cls, field).offset == int(val), key
+
+
+def _world(A, K, box=False):
+    w = _lib.WorldC()
+    w.dtype, w.n_envs, w.n_agents, w.act_dim, w.substeps, w.dt = 0, 100, A, 2, 2, 0.05
+    w.params, w.model_tag, w.ctrl_mode = 8, 8, 8  # non-null placeholders, never dereferenced
+    w.fleet_models, w.fleet_modes = 1, 1
+    w.collisions, w.max_neighbors, w.neighbor_radius = 1, K, 0.2
+    w.box_agents = int(box)
+    return w
+
+
+@pytest.mark.parametrize("A,K,box,masks_off,nw,trunc", [
+    (16, 16, False, False, 1, False),   # contact masks, one word
+    (16, 8, False, False, 1, True),     # truncating lists: masks and cutoffs
+    (40, 64, False, False, 2, False),   # two mask words
+    (40, 64, False, True, 0, False),    # SWARP_CONTACT_MASKS=0: the rescan path
+    (256, 32, False, False, 8, True),   # the config-5 shape
+    (300, 8, False, False, 0, True),    # above 256 agents: cutoffs only
+    (40, 64, True, False, 0, False),    # box agents beyond 32: no masks
+])
+def test_workspace_holds_the_contact_checkpoint(lib, monkeypatch, A, K, box, masks_off, nw,
+                                                trunc):
+    """The workspace the forward fills for its adjoint: ceil(A/32) mask words per agent and
+    substep where masks are checkpointed, int16 list cutoffs where lists can truncate, then
+    one partial sum per CTA (host logic only, no GPU)."""
+    if masks_off:
+        monkeypatch.setenv("SWARP_CONTACT_MASKS", "0")
+    fn = lib.swarp_rollout_workspace_bytes
+    fn.restype = C.c_size_t
+    fn.argtypes = [C.POINTER(_lib.WorldC), C.c_int32]
+    H = 6
+    w = _world(A, K, box)
+    cells = H * 2 * 100 * A
+    align = lambda b: (b + 255) // 256 * 256  # noqa: E731
+    head = align(align(cells * nw * 4) + (cells * 2 if trunc else 0))
+    got = fn(C.byref(w), H)
+    assert head < got <= head + 100 * 4, (got, head)
