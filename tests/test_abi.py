@@ -153,3 +153,15 @@ def test_workspace_holds_the_contact_checkpoint(lib, monkeypatch, A, K, box, mas
     head = align(align(cells * nw * 4) + (cells * 2 if trunc else 0))
     got = fn(C.byref(w), H)
     assert head < got <= head + 100 * 4, (got, head)
+
+
+def test_workspace_partials_cover_cluster_ctas(lib):
+    """Envs above 1024 agents run one env per cluster of several CTAs, each of which writes
+    one partial sum: the workspace holds one per CTA (E x 4 for 2048 agents)."""
+    fn = lib.swarp_rollout_workspace_bytes
+    fn.restype = C.c_size_t
+    fn.argtypes = [C.POINTER(_lib.WorldC), C.c_int32]
+    w = _world(2048, 8)
+    cells = 6 * 2 * 100 * 2048
+    head = (cells * 2 + 255) // 256 * 256  # cutoffs only (no masks above 256 agents)
+    assert fn(C.byref(w), 6) >= head + 100 * 4 * 4
