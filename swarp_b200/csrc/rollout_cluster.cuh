@@ -6,9 +6,10 @@
 //  - the env's pair-packed scan table (x, y of every agent, the layout of rollout.cuh) is
 //    REPLICATED: each agent stores its position into every CTA's copy (CS remote stores),
 //    so the O(A) candidate scan of every agent reads only its own CTA's shared memory;
-//  - each agent's record (x, y, vx, vy), radius, damping denominator and, in the adjoint,
-//    force cotangent and list cutoff stay in its OWN CTA; a thread reads them from the
-//    owning CTA (mapa + ld.shared::cluster) only for the neighbors it actually lists.
+//  - each agent's record (vx, vy, radius, damping denominator) and, in the adjoint, its
+//    (force cotangent, list cutoff) record stay in its OWN CTA; a thread reads them from
+//    the owning CTA (mapa + ld.shared::cluster, one 16-byte load each) only for the
+//    neighbors it actually lists, and takes their positions from its local scan table.
 // A cluster barrier (barrier.cluster arrive.release / wait.acquire) replaces the CTA
 // barrier of the single-CTA kernels wherever an env's agents exchange data, and a last one
 // keeps every CTA resident until no peer can still read its shared memory.
@@ -36,19 +37,16 @@ constexpr int kClusterMaxCTAs = 8;       // portable cluster size
 // Shared-memory carve-up of one cluster CTA (host: sizes; device: offsets).
 template <typename T> struct ClusterLayout {
   int NP, nbuf;
-  size_t xy, rec, own, fb, cut, rad, iden, obs, total;
+  size_t xy, rec, own, fbc, obs, total;
   __host__ __device__ ClusterLayout(int A, int BT, int N, int S, bool bwd) {
     NP = (A + 1) / 2;
     nbuf = bwd ? (S > 2 ? S : 2) : 2;
     size_t off = 0;
     auto take = [&](size_t bytes) { size_t o = off; off = (off + bytes + 15) & ~size_t(15); return o; };
     xy = take(size_t(nbuf) * NP * 4 * sizeof(T));        // whole env, replicated
-    rec = take(size_t(nbuf) * BT * 4 * sizeof(T));       // own agents' (x, y, vx, vy)
-    own = bwd ? take(size_t(S) * BT * 4 * sizeof(T)) : 0;  // own (th, s, w) per substep
-    fb = bwd ? take(size_t(2) * BT * 2 * sizeof(T)) : 0;   // own force cotangents
-    cut = bwd ? take(size_t(2) * BT * sizeof(int)) : 0;    // own list cutoffs
-    rad = take(size_t(BT) * sizeof(T));
-    iden = take(size_t(BT) * sizeof(T));
+    rec = take(size_t(nbuf) * BT * 4 * sizeof(T));  // own agents' (vx, vy, radius, 1/denom)
+    own = bwd ? take(size_t(S) * BT * 5 * sizeof(T)) : 0;  // own (th, s, w, x, y) per substep
+    fbc = bwd ? take(size_t(2) * BT * 4 * sizeof(T)) : 0;  // own (force cot. x, y, cutoff, -)
     obs = take(size_t(N > 0 ? N : 0) * sizeof(Obs<T>));
     total = off;
   }
@@ -74,8 +72,8 @@ __device__ __forceinline__ void put_xy_all(const cg::cluster_group& cl, T* xy_en
   for (int r = 0; r < CS; ++r) put_xy(cl.map_shared_rank(xy_env, r), a, x, y);
 }
 
-// for_each_in_radius with the exact test on the scan table's coordinates (the values the
-// records hold): calls fn(b) for every member b != a in ascending order; returns the count.
+// for_each_in_radius with the exact test on the scan table's coordinates: calls
+// fn(b, x_b, y_b) for every member b != a in ascending order; returns the count.
 template <typename T, typename Fn>
 __device__ __forceinline__ int for_each_in_radius_xy(const T* xy_env, int A, int a, T px, T py,
                                                      T thr_scan, T thr, Fn&& fn) {
@@ -95,58 +93,56 @@ __device__ __forceinline__ int for_each_in_radius_xy(const T* xy_env, int A, int
       get_xy(xy_env, b, qx, qy);
       if (!in_radius(px - qx, py - qy, thr)) continue;
       ++total;
-      fn(b);
+      fn(b, qx, qy);
     }
   }
   return total;
 }
 
-// neighbor_force of the single-CTA kernels, the listed neighbors' records read from the
-// CTA that owns them.
+// neighbor_force of the single-CTA kernels, the listed neighbors' records (vx, vy,
+// radius, 1/denom) read from the CTA that owns them.
 template <typename T, int FL>
 __device__ __forceinline__ int neighbor_force_cl(const cg::cluster_group& cl, const Owner& own,
                                                  const T* xy_env, const typename V4<T>::t* rec,
-                                                 const T* rad, int A, int a, const Agent<T>& x,
+                                                 int A, int a, const Agent<T>& x,
                                                  const AgentP<T>& P, const WorldC<T>& W, T& fx,
                                                  T& fy, int& cutoff) {
   int listed = 0;
   cutoff = A;
   const int total = for_each_in_radius_xy<T>(xy_env, A, a, x.px, x.py, W.r2_scan, W.r2_thr,
-                                             [&](int b) {
+                                             [&](int b, T qx, T qy) {
     if (FL & F_TRUNC) {
       if (listed >= W.K) return;
       ++listed;
       if (listed == W.K) cutoff = b;
     }
     const auto q = peer_load(cl, rec, own, b);
-    const T rb = peer_load(cl, rad, own, b);
-    const T dx = x.px - q.x, dy = x.py - q.y;
-    pair_force_add(dx, dy, dot2(dx, dy, dx, dy), x.vx - q.z, x.vy - q.w, P.radius + rb + W.margin,
+    const T dx = x.px - qx, dy = x.py - qy;
+    pair_force_add(dx, dy, dot2(dx, dy, dx, dy), x.vx - q.x, x.vy - q.y, P.radius + q.z + W.margin,
                    P.inv_denom, W, fx, fy);
   });
   if ((FL & F_TRUNC) && total <= W.K) cutoff = A;
   return total;
 }
 
-// force_vjp of the single-CTA kernels (rescan path), remote reads for the listed neighbors.
+// force_vjp of the single-CTA kernels (rescan path), remote reads of the members' records
+// and (force cotangent, cutoff) records.
 template <typename T, int FL>
 __device__ __forceinline__ void force_vjp_cl(const cg::cluster_group& cl, const Owner& own,
                                              const T* xy_env, const typename V4<T>::t* rec,
-                                             const typename V2<T>::t* fb, const int* cut,
-                                             const T* rad, const T* iden, const Obs<T>* sobs,
+                                             const typename V4<T>::t* fbc, const Obs<T>* sobs,
                                              int N, int A, int a, int cut_a, const Agent<T>& x,
                                              const AgentP<T>& P, const WorldC<T>& W, T gfx, T gfy,
                                              Agent<T>& gin) {
   if (FL & F_COLL) {
-    for_each_in_radius_xy<T>(xy_env, A, a, x.px, x.py, W.r2_scan, W.r2_thr, [&](int b) {
+    for_each_in_radius_xy<T>(xy_env, A, a, x.px, x.py, W.r2_scan, W.r2_thr,
+                             [&](int b, T qx, T qy) {
       const auto q = peer_load(cl, rec, own, b);
-      const auto gb = peer_load(cl, fb, own, b);
-      const T rb = peer_load(cl, rad, own, b);
-      const T ib = peer_load(cl, iden, own, b);
+      const auto gb = peer_load(cl, fbc, own, b);
       const bool mine = !(FL & F_TRUNC) || b <= cut_a;
-      const bool cross = !(FL & F_TRUNC) || a <= peer_load(cl, cut, own, b);
-      pair_vjp_sym(x.px - q.x, x.py - q.y, x.vx - q.z, x.vy - q.w, P.radius + rb + W.margin,
-                   P.inv_denom, mine ? gfx : T(0), mine ? gfy : T(0), ib, cross ? gb.x : T(0),
+      const bool cross = !(FL & F_TRUNC) || T(a) <= gb.z;
+      pair_vjp_sym(x.px - qx, x.py - qy, x.vx - q.x, x.vy - q.y, P.radius + q.z + W.margin,
+                   P.inv_denom, mine ? gfx : T(0), mine ? gfy : T(0), q.w, cross ? gb.x : T(0),
                    cross ? gb.y : T(0), W, gin.px, gin.py, gin.vx, gin.vy);
     });
   }
@@ -155,7 +151,7 @@ __device__ __forceinline__ void force_vjp_cl(const cg::cluster_group& cl, const 
 
 // ================================================================== forward
 template <typename T, int FL>
-__global__ void __launch_bounds__(kClusterMaxThreads) rollout_fwd_cl_kernel(const RolloutArgs<T> R) {
+__global__ void __launch_bounds__(kClusterMaxThreads, 1) rollout_fwd_cl_kernel(const RolloutArgs<T> R) {
   using T4 = typename V4<T>::t;
   constexpr bool kColl = (FL & F_COLL) != 0;
   extern __shared__ __align__(16) unsigned char smem[];
@@ -172,15 +168,11 @@ __global__ void __launch_bounds__(kClusterMaxThreads) rollout_fwd_cl_kernel(cons
   const int NP4 = L.NP * 4;
   T* sxy = reinterpret_cast<T*>(smem + L.xy);
   T4* srec = reinterpret_cast<T4*>(smem + L.rec);
-  T* srad = reinterpret_cast<T*>(smem + L.rad);
-  T* siden = reinterpret_cast<T*>(smem + L.iden);
   Obs<T>* sobs = reinterpret_cast<Obs<T>*>(smem + L.obs);
 
   AgentP<T> P;
   load_params(R, e, ac, P);
   const WorldC<T> W = R.W;
-  srad[tid] = P.radius;
-  siden[tid] = P.inv_denom;
   if (FL & F_OBS) load_obstacles(R, sobs, e);
   if (kColl) init_pads(sxy, 2, 1, A);
   cl.sync();  // every CTA of the cluster has started and set up its shared memory
@@ -201,11 +193,11 @@ __global__ void __launch_bounds__(kClusterMaxThreads) rollout_fwd_cl_kernel(cons
         T* xy_env = sxy + buf * NP4;
         T4* rec = srec + buf * BT;
         if (live) put_xy_all(cl, xy_env, CS, a, x.px, x.py);
-        rec[tid] = T4{x.px, x.py, x.vx, x.vy};
+        rec[tid] = T4{x.vx, x.vy, P.radius, P.inv_denom};
         cl.sync();
         if (live) {
           int cutoff;
-          const int tc = neighbor_force_cl<T, FL>(cl, own, xy_env, rec, srad, A, a, x, P, W, fx, fy,
+          const int tc = neighbor_force_cl<T, FL>(cl, own, xy_env, rec, A, a, x, P, W, fx, fy,
                                                   cutoff);
           tmax = max(tmax, tc);
           if (FL & F_TRUNC) R.cutoff[((long long)t * R.S + k) * EA + ia] = (int16_t)cutoff;
@@ -232,7 +224,7 @@ __global__ void __launch_bounds__(kClusterMaxThreads) rollout_fwd_cl_kernel(cons
 
 // ================================================================== adjoint
 template <typename T, int FL>
-__global__ void __launch_bounds__(kClusterMaxThreads) rollout_bwd_cl_kernel(const RolloutArgs<T> R) {
+__global__ void __launch_bounds__(kClusterMaxThreads, 1) rollout_bwd_cl_kernel(const RolloutArgs<T> R) {
   using T2 = typename V2<T>::t;
   using T4 = typename V4<T>::t;
   constexpr bool kColl = (FL & F_COLL) != 0;
@@ -250,18 +242,13 @@ __global__ void __launch_bounds__(kClusterMaxThreads) rollout_bwd_cl_kernel(cons
   const int NP4 = L.NP * 4;
   T* sxy = reinterpret_cast<T*>(smem + L.xy);      // [nbuf][NP*4] whole env
   T4* srec = reinterpret_cast<T4*>(smem + L.rec);  // [nbuf][BT]
-  T* sown = reinterpret_cast<T*>(smem + L.own);    // [S][BT][4] th, s, w
-  T2* sfb = reinterpret_cast<T2*>(smem + L.fb);    // [2][BT]
-  int* scut = reinterpret_cast<int*>(smem + L.cut);  // [2][BT]
-  T* srad = reinterpret_cast<T*>(smem + L.rad);
-  T* siden = reinterpret_cast<T*>(smem + L.iden);
+  T* sown = reinterpret_cast<T*>(smem + L.own);    // [S][BT][5] th, s, w, x, y
+  T4* sfbc = reinterpret_cast<T4*>(smem + L.fbc);  // [2][BT] force cotangent, cutoff
   Obs<T>* sobs = reinterpret_cast<Obs<T>*>(smem + L.obs);
 
   AgentP<T> P;
   load_params(R, e, ac, P);
   const WorldC<T> W = R.W;
-  srad[tid] = P.radius;
-  siden[tid] = P.inv_denom;
   if (FL & F_OBS) load_obstacles(R, sobs, e);
   if (kColl) init_pads(sxy, L.nbuf, 1, A);
   cl.sync();
@@ -318,20 +305,18 @@ __global__ void __launch_bounds__(kClusterMaxThreads) rollout_bwd_cl_kernel(cons
       integrate_vjp_sel<T, FL>(cur, a0, a1, nxt, g, P, W, gin, gfx, gfy, ga0, ga1);
       T* xy_env = sxy + fbuf * NP4;
       T4* rec = srec + fbuf * BT;
-      T2* fb = sfb + fbuf * BT;
-      int* cut = scut + fbuf * BT;
+      T4* fbc = sfbc + fbuf * BT;
       int cut_a = A;
       if (kColl) {
         if (live) put_xy_all(cl, xy_env, CS, a, cur.px, cur.py);
-        rec[tid] = T4{cur.px, cur.py, cur.vx, cur.vy};
-        fb[tid] = T2{gfx, gfy};
+        rec[tid] = T4{cur.vx, cur.vy, P.radius, P.inv_denom};
         if (FL & F_TRUNC) cut_a = R.cutoff[(long long)t * EA + ia];
-        cut[tid] = cut_a;
+        fbc[tid] = T4{gfx, gfy, T(cut_a), T(0)};
         cl.sync();
       }
       if (live)
-        force_vjp_cl<T, FL>(cl, own, xy_env, rec, fb, cut, srad, siden, sobs, N, A, a, cut_a, cur,
-                            P, W, gfx, gfy, gin);
+        force_vjp_cl<T, FL>(cl, own, xy_env, rec, fbc, sobs, N, A, a, cut_a, cur, P, W, gfx, gfy,
+                            gin);
       g = gin;
       fbuf ^= 1;
     } else {
@@ -342,18 +327,20 @@ __global__ void __launch_bounds__(kClusterMaxThreads) rollout_bwd_cl_kernel(cons
         T* xy_env = sxy + k * NP4;
         T4* rec = srec + k * BT;
         if (kColl && live) put_xy_all(cl, xy_env, CS, a, x.px, x.py);
-        rec[tid] = T4{x.px, x.py, x.vx, x.vy};
-        T* ow = sown + (size_t(k) * BT + tid) * 4;
+        rec[tid] = T4{x.vx, x.vy, P.radius, P.inv_denom};
+        T* ow = sown + (size_t(k) * BT + tid) * 5;
         ow[0] = x.th;
         ow[1] = x.s;
         ow[2] = x.w;
+        ow[3] = x.px;
+        ow[4] = x.py;
         if (k == S - 1) break;
         T fx = T(0), fy = T(0);
         if (kColl) {
           cl.sync();
           if (live) {
             int cutoff;
-            neighbor_force_cl<T, FL>(cl, own, xy_env, rec, srad, A, a, x, P, W, fx, fy, cutoff);
+            neighbor_force_cl<T, FL>(cl, own, xy_env, rec, A, a, x, P, W, fx, fy, cutoff);
           }
         }
         static_force<T, FL>(sobs, N, x, P, W, fx, fy);
@@ -365,24 +352,22 @@ __global__ void __launch_bounds__(kClusterMaxThreads) rollout_bwd_cl_kernel(cons
       for (int k = S - 1; k >= 0; --k) {
         T* xy_env = sxy + k * NP4;
         T4* rec = srec + k * BT;
-        const T* ow = sown + (size_t(k) * BT + tid) * 4;
+        const T* ow = sown + (size_t(k) * BT + tid) * 5;
         const T4 rr = rec[tid];
-        const Agent<T> in{rr.x, rr.y, ow[0], rr.z, rr.w, ow[1], ow[2]};
+        const Agent<T> in{ow[3], ow[4], ow[0], rr.x, rr.y, ow[1], ow[2]};
         Agent<T> gin;
         T gfx, gfy;
         integrate_vjp_sel<T, FL>(in, a0, a1, out, g, P, W, gin, gfx, gfy, ga0, ga1);
-        T2* fb = sfb + fbuf * BT;
-        int* cut = scut + fbuf * BT;
+        T4* fbc = sfbc + fbuf * BT;
         int cut_a = A;
         if (kColl) {
-          fb[tid] = T2{gfx, gfy};
           if (FL & F_TRUNC) cut_a = R.cutoff[((long long)t * S + k) * EA + ia];
-          cut[tid] = cut_a;
+          fbc[tid] = T4{gfx, gfy, T(cut_a), T(0)};
           cl.sync();
         }
         if (live)
-          force_vjp_cl<T, FL>(cl, own, xy_env, rec, fb, cut, srad, siden, sobs, N, A, a, cut_a, in,
-                              P, W, gfx, gfy, gin);
+          force_vjp_cl<T, FL>(cl, own, xy_env, rec, fbc, sobs, N, A, a, cut_a, in, P, W, gfx, gfy,
+                              gin);
         g = gin;
         out = in;
         fbuf ^= 1;
@@ -435,7 +420,8 @@ __global__ void __launch_bounds__(1024) neighbors_wide_kernel(int E, int A, int 
   T px, py;
   get_xy(xy_env, a, px, py);
   int listed = 0;
-  const int total = for_each_in_radius_xy<T>(xy_env, A, a, px, py, r2_scan, r2_thr, [&](int b) {
+  const int total = for_each_in_radius_xy<T>(xy_env, A, a, px, py, r2_scan, r2_thr,
+                                             [&](int b, T, T) {
     if (listed < K) idx[ia * K + listed++] = b;
   });
   count[ia] = listed;
