@@ -59,10 +59,14 @@ int launch_neighbors_wide(int E, int A, int slices, int block, int K, T r2_scan,
 
 // Raise a kernel's dynamic shared-memory limit once per size (per device): the attribute
 // call is not stream-ordered, so keeping it off the common launch path also keeps launches
-// inside CUDA-graph capture free of it after the first (uncaptured) call of a shape.
+// inside CUDA-graph capture free of it after the first (uncaptured) call of a shape. The
+// default limit (48 KB) covers static and dynamic shared memory together, and these kernels
+// also hold a little static shared memory (the block reductions' warp sums), so sizes from
+// kSmemNoRaise up are raised explicitly.
+constexpr size_t kSmemNoRaise = 40 * 1024;
 template <typename K>
 inline bool ensure_smem_limit(K kernel, size_t smem) {
-  if (smem <= 48 * 1024) return true;
+  if (smem <= kSmemNoRaise) return true;
   static std::mutex mu;
   static std::unordered_map<long long, size_t> raised;  // (device, kernel) -> limit set
   int dev = 0;
@@ -183,9 +187,7 @@ int launch_neighbors(int E, int A, int G, int K, T r2_scan, T r2, const T* pos, 
   const size_t smem = ((size_t(G) * ((A + 1) / 2) * 4 * sizeof(T) + 15) & ~size_t(15)) +
                       size_t(G) * A * 4 * sizeof(T);
   auto k = neighbors_kernel<T>;
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-    return kErrCuda;
+  if (!ensure_smem_limit(k, smem)) return kErrCuda;
   k<<<(E + G - 1) / G, G * A, smem, st>>>(E, A, G, K, r2_scan, r2, pos, idx, cnt, tru);
   return cudaGetLastError() == cudaSuccess ? 0 : kErrCuda;
 }

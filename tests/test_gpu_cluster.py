@@ -242,3 +242,47 @@ def test_oversized_and_unsupported_wide_envs():
         Stepper([AgentConfig(shape=AgentShape.BOX, half_extents=(0.01, 0.01))] * 1100,
                 dt=0.05, device=DEV, dtype=torch.float32,
                 world=WorldConfig(neighbor_radius=0.05, max_neighbors=8))
+
+
+def test_2048_agents_f32_goal_loss_against_cpu_restatement():
+    """Float32, 2048 agents (4 CTAs of 512 threads; the forward's dynamic shared memory is
+    exactly 48 KB here, so the launch must raise the kernel's shared-memory limit),
+    holonomic velocity fleet, truncating lists and the fused goal loss, against the float64
+    C restatement: states within 1e-5 and action gradients within 1e-4 of the field's
+    largest magnitude (the float32 bars)."""
+    E, A, T, K = 4, 2048, 3, 32
+    cfgs = [AgentConfig(radius=0.01, max_speed=1.0, max_accel=2.0) for _ in range(A)]
+    bounds = (-1.0, 1.0, -1.0, 1.0)
+    world = WorldConfig(collision_k=100.0, collision_c=1.0, collision_margin=0.025,
+                        bounds=bounds, neighbor_radius=0.06, max_neighbors=K)
+    st = Stepper(cfgs, dt=0.05, device=DEV, dtype=torch.float32, world=world)
+    st.track_neighbor_overflow = True
+    g = torch.Generator().manual_seed(21)
+    pos = (torch.randn(E, A, 2, generator=g, dtype=D) * 0.3).clamp(-0.95, 0.95)
+    z = torch.zeros(E, A, dtype=D)
+    state = [pos, z, torch.zeros(E, A, 2, dtype=D), z, z]
+    acts = torch.rand(T, E, A, 2, generator=g, dtype=D) * 2 - 1
+    goal = torch.rand(E, A, 2, generator=g, dtype=D) * 2 - 1
+    f32 = lambda x: x.to(DEV, torch.float32)  # noqa: E731
+    a_gpu = f32(acts).requires_grad_(True)
+    loss = rollout_goal_loss(st, TorchState(*map(f32, state)), a_gpu, f32(goal))
+    (ga,) = torch.autograd.grad(loss, [a_gpu])
+    assert int(st.last_true_count_max.max()) > K, "the case truncates"
+    _, traj = rollout(st, TorchState(*map(f32, state)), f32(acts))
+
+    common = dict(params=param_rows(cfgs), model_tag=[int(c.model) for c in cfgs],
+                  ctrl_mode=[int(c.ctrl_mode) for c in cfgs], dt=0.05, substeps=1,
+                  collisions=True, k=100.0, c=1.0, margin=0.025, max_overlap=0.0,
+                  neighbor_radius=0.06, max_neighbors=K, bounds_mode=1, bounds=bounds,
+                  init=[x.numpy() for x in state], actions=acts.numpy(), obstacles=None,
+                  threads=0, dtype=np.float64)
+    traj_c, _, _ = cpu_port.rollout(**common)
+    fin_c = traj_c[0][-1]
+    _, ga_c, _ = cpu_port.rollout(**common, grad_final_pos=2.0 * (fin_c - goal.numpy()))
+    for f in range(5):
+        ref = traj_c[f]
+        np.testing.assert_allclose(traj.stacked[f].cpu().numpy(), ref, rtol=1e-5,
+                                   atol=1e-5 * max(np.abs(ref).max(), 1e-30), err_msg=f"field {f}")
+    assert float(loss) == pytest.approx(float(((fin_c - goal.numpy()) ** 2).sum()), rel=1e-4)
+    sc = np.abs(ga_c).max()
+    np.testing.assert_allclose(ga.cpu().numpy(), ga_c, rtol=1e-4, atol=1e-4 * sc)
