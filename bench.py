@@ -87,8 +87,10 @@ def nav_world(A: int, radius: float = 0.05, neighbor_radius: float | None = None
 
 
 def build_workload(cid: int, rank: int = 0, dev="cuda:0", n_envs: int | None = None,
-                   make_stepper: bool = True) -> Workload:
-    """The seeded synthetic inputs of config ``cid`` (rank-dependent seeds)."""
+                   make_stepper: bool = True, n_agents: int | None = None) -> Workload:
+    """The seeded synthetic inputs of config ``cid`` (rank-dependent seeds). ``n_agents``
+    widens config 5's dense swarm (same start distribution, radius and list length) to more
+    agents per env: a profiling case for the thread-block-cluster kernels, not a bench line."""
     from swarp_b200.core.config import ObstacleKind, Obstacles, WorldConfig
     from swarp_b200.core.stepper import Stepper
     from swarp_b200.dynamics.base import AgentConfig, DynamicsModel
@@ -100,11 +102,15 @@ def build_workload(cid: int, rank: int = 0, dev="cuda:0", n_envs: int | None = N
     if cid in (1, 2, 5):
         E, A, H = {1: (1024, 8, 32), 2: (16000, 16, 64), 5: (2048, 256, 32)}[cid]
         E = n_envs or E
+        if n_agents is not None:
+            if cid != 5:
+                raise ValueError("n_agents overrides config 5 only")
+            A = n_agents
         cfgs = [AgentConfig(radius=0.05, max_speed=1.0, max_accel=2.0) for _ in range(A)]
         if cid == 5:
             world = nav_world(A, neighbor_radius=0.15, max_neighbors=32)
             pos = np.clip(rng.normal(0.0, 0.6, (E, A, 2)), -1.0, 1.0).astype(f32)
-            name = ("config5: dense swarm, holonomic VELOCITY, 2048 envs x 256 agents, "
+            name = (f"config5: dense swarm, holonomic VELOCITY, {E} envs x {A} agents, "
                     "N(0, 0.6^2) starts, R=0.15, K=32, H=32")
         else:
             world = nav_world(A)
@@ -469,7 +475,12 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--envs", type=int, default=None,
                     help="override the config's envs per GPU (smaller cases for profiling)")
+    ap.add_argument("--agents", type=int, default=None,
+                    help="config 5 with this many agents per env (a profiling case for envs "
+                         "wider than one CTA; no CPU baseline, no reference arm)")
     args = ap.parse_args()
+    if args.agents is not None and (args.config != 5 or args.impl == "reference"):
+        ap.error("--agents applies to config 5 of this implementation only")
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -494,7 +505,8 @@ def main() -> None:
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    wl = build_workload(args.config, rank=rank, dev=dev, n_envs=args.envs)
+    wl = build_workload(args.config, rank=rank, dev=dev, n_envs=args.envs,
+                        n_agents=args.agents)
     st, E, A, H = wl.stepper, wl.E, wl.A, wl.H
     pos = torch.from_numpy(wl.pos).to(dev)
     theta = torch.from_numpy(wl.theta).to(dev)
@@ -739,7 +751,8 @@ def main() -> None:
     dom = "bwd" if t_bwd >= t_fwd else "fwd"
     # 16-agent float worlds without moving bodies take the two-agents-per-thread instances
     x2 = A == 16 and not wl.body and (dom == "fwd" or st.substeps == 1)
-    roof = {"bound": "hbm", "kernel": f"rollout_{dom}_{'x2_' if x2 else ''}kernel<...>",
+    variant = "x2_" if x2 else "cl_" if A > 1024 else ""  # envs above 1024 agents: clusters
+    roof = {"bound": "hbm", "kernel": f"rollout_{dom}_{variant}kernel<...>",
             "achieved": bwd_gbs if dom == "bwd" else fwd_gbs, "peak": peak, "unit": "GB/s",
             "peak_source": peak_src}
     roof["frac"] = roof["achieved"] / peak
@@ -784,7 +797,7 @@ def main() -> None:
         line["neighbor_overflow"] = overflow
     if allreduce is not None:
         line["allreduce"] = allreduce
-    if world == 1 and not args.no_cpu_baseline:
+    if world == 1 and not args.no_cpu_baseline and args.agents is None:
         line["cpu_baseline"] = cpu_baseline_block(wl)
     print(json.dumps(line), flush=True)
 
