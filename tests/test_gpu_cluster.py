@@ -10,6 +10,8 @@ plus force and integrate kernels, swarp/core/stepper.py:784-1011). Here envs of 
   hand-written adjoint): trajectories within 1e-12 and gradients within 1e-10;
 - lists, counts and uncapped counts of 2048- and 1501-agent envs bit for bit against the
   reference's membership rule restated in numpy, and the rollout's uncapped counts;
+- a float32 2048-agent goal-loss case: bitwise across 4- and 8-CTA clusters, and against
+  the float32 and float64 restatements within the float32 problem's own sensitivity;
 - small envs forced through the cluster kernels (SWARP_CLUSTER_MIN_AGENTS /
   SWARP_CLUSTER_CTA_THREADS): bitwise the single-CTA kernels' trajectories and gradients
   (same device arithmetic in the same order), over models, RK4, substeps, truncation,
