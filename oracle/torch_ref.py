@@ -17,6 +17,8 @@ What it restates (reference = ddebenedittis/swarp, paths relative to that projec
 * ``swarp/core/collisions.py:690-815`` obstacle, wall and static forces
 * ``swarp/core/collisions.py:818-881`` ``collision_forces_kernel`` (list-order gather)
 * ``swarp/core/neighbors.py:76-97``    ``_brute_force`` (ascending index, cap, true count)
+* ``swarp/core/neighbors.py:135-254, 388-394, 591-620`` the radix-sort uniform grid that
+  ``"auto"`` picks above 512 agents per env (its frame, cells and list order)
 * ``swarp/core/bodies.py:79-127,167-255,367-569`` movable compound-body pass
 * ``swarp/core/stepper.py:549-648``    substep order: neighbors, forces, bodies, integrate
 * ``swarp/dynamics/kernels.py:102-163,349-369,494-508,758-768`` the 6-DOF drone (Euler, RK4)
@@ -35,6 +37,7 @@ gradient oracle for bodies (pinned by finite differences in the tests).
 
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass, field
 
 import torch
@@ -537,6 +540,87 @@ def brute_neighbors(pos, radius: float, max_neighbors: int):
     ar = torch.arange(A, device=pos.device).expand(E, A, A)
     sel = order < K
     idx[sel.nonzero(as_tuple=True)[0], sel.nonzero(as_tuple=True)[1], order[sel]] = ar[sel]
+    return in_list, idx, count, true_count
+
+
+def default_uniform_bins(n_agents: int) -> int:
+    """``swarp/core/neighbors.py:394``: cells per axis, about sqrt(n_agents), in [4, 128]."""
+    return max(4, min(128, int(math.ceil(math.sqrt(n_agents)))))
+
+
+def auto_neighbor_method(n_agents: int) -> str:
+    """``swarp/core/neighbors.py:388-389``: ``"auto"`` picks the uniform grid above 512
+    agents per env, brute force otherwise."""
+    return "uniform_grid" if n_agents > 512 else "brute"
+
+
+def uniform_grid_frame(pos, radius: float, bins: int, bounds=None):
+    """Grid origin and cell size, in the dtype of ``pos``.
+
+    With a pinned world rectangle (``swarp/core/neighbors.py:591-620``) the origin is its
+    lower corner and the cell size ``max(radius, extent / bins)``, both computed in Python
+    floats and stored in the position dtype. Without one (``_bounds_reduce`` /
+    ``_finalize_grid``, ``neighbors.py:149-178``) they come from the minimum and maximum
+    coordinates over the WHOLE batch, all envs together, in the position dtype.
+    """
+    dt = pos.dtype
+    if bounds is not None:
+        x_min, x_max, y_min, y_max = bounds
+        extent = max(x_max - x_min, y_max - y_min)
+        origin = torch.tensor([x_min, y_min], dtype=dt)
+        cell = torch.tensor(max(radius, extent / bins), dtype=dt)
+        return origin, cell
+    lo = pos.reshape(-1, 2).min(0).values
+    hi = pos.reshape(-1, 2).max(0).values
+    ext = torch.maximum(hi[0] - lo[0], hi[1] - lo[1])
+    cell = torch.maximum(torch.tensor(radius, dtype=dt), ext / torch.tensor(bins, dtype=dt))
+    return lo.clone(), cell
+
+
+def uniform_grid_neighbors(pos, radius: float, max_neighbors: int, bins: int | None = None,
+                           bounds=None):
+    """``swarp/core/neighbors.py:182-254`` (``_compute_keys``, radix sort, ``_build_offsets``,
+    ``_query_uniform``): the uniform-grid lists, in the reference's list order.
+
+    Each agent falls in cell ``clamp(int((p - origin) / cell), 0, bins - 1)`` per axis (the
+    division in the position dtype, truncation toward zero). A query visits the 3 x 3
+    block of cells around its own, rows ``dy = -1, 0, 1`` and in each row ``dx = -1, 0, 1``,
+    and each cell's agents in ascending index (the radix sort is stable and its values
+    start in index order); it keeps ``b != a`` with ``length(p_b - p_a) <= radius`` and
+    lists the first ``max_neighbors`` of them. So the list order is (block cell, index)
+    rather than the brute force's index order: both give the same sets when no list
+    truncates, different ones when a list truncates.
+
+    Returns ``(in_list [E,A,A] bool, idx [E,A,K] int64 padded with -1, count [E,A],
+    true_count [E,A])`` like :func:`brute_neighbors`, ``idx`` in the grid's list order.
+    """
+    E, A, _ = pos.shape
+    bins = bins or default_uniform_bins(A)
+    origin, cell = uniform_grid_frame(pos, radius, bins, bounds)
+    c = ((pos - origin) / cell).to(torch.int32).clamp(0, bins - 1).to(torch.int64)  # [E,A,2]
+    dcx = c[..., 0].unsqueeze(1) - c[..., 0].unsqueeze(2)  # [E, a, b] = cx_b - cx_a
+    dcy = c[..., 1].unsqueeze(1) - c[..., 1].unsqueeze(2)
+    in_block = (dcx.abs() <= 1) & (dcy.abs() <= 1)
+    dxy = pos.unsqueeze(1) - pos.unsqueeze(2)  # p_b - p_a
+    dist = wlength(dxy[..., 0], dxy[..., 1])
+    eye = torch.eye(A, dtype=torch.bool).unsqueeze(0)
+    member = in_block & (dist <= radius) & ~eye
+    ar = torch.arange(A).expand(E, A, A)
+    key = ((dcy + 1) * 3 + (dcx + 1)) * A + ar  # visit order of the candidates
+    key = torch.where(member, key, torch.full_like(key, 9 * A))
+    order = torch.argsort(key, dim=-1, stable=True)  # [E, a, rank] -> b
+    ranked = torch.gather(member, -1, order)
+    true_count = member.sum(-1)
+    K = max_neighbors
+    count = torch.clamp(true_count, max=K)
+    idx = torch.full((E, A, K), -1, dtype=torch.int64)
+    take = min(K, A)
+    first = order[..., :take]
+    idx[..., :take] = torch.where(ranked[..., :take], first, torch.full_like(first, -1))
+    in_list = torch.zeros((E, A, A), dtype=torch.bool)
+    rank = torch.arange(A).expand(E, A, A)
+    listed_rank = ranked & (rank < K)
+    in_list.scatter_(-1, order, listed_rank)
     return in_list, idx, count, true_count
 
 
