@@ -18,6 +18,9 @@
  *   obstacle / wall forces      swarp/core/collisions.py:690-780
  *   collision_forces_kernel     swarp/core/collisions.py:818-881 (list-order gather)
  *   _brute_force          swarp/core/neighbors.py:76-97
+ *   _compute_keys / _query_uniform, static frame
+ *                         swarp/core/neighbors.py:182-254, 591-620 (list_order 1: the
+ *                         uniform grid's (3 x 3 block cell, index) list order)
  *   substep order         swarp/core/stepper.py:549-648 (neighbors, forces, integrate)
  * The adjoint differentiates these with Warp's branch conventions at kinks (max sends
  * the gradient to the second argument on a tie, clamp passes it on the closed
@@ -57,6 +60,10 @@ typedef struct {
   const double *obs_pos, *obs_angle, *obs_vel, *obs_ang_vel, *obs_radius, *obs_half;
   const int* obs_shape;
   int threads;
+  /* 0: ascending index (brute force); 1: the radix-sort uniform grid's order with a
+     static frame: cells clamp((p - origin) / cell, 0, bins - 1) per axis */
+  int list_order, grid_bins;
+  double grid_origin[2], grid_cell;
 } cpu_world_t;
 
 typedef struct {
@@ -72,6 +79,8 @@ typedef struct {
   real bx0, bx1, by0, by1;
   real R;
   int K, bounds_mode;
+  int order, bins; /* list order (cpu_world_t.list_order) and grid cells per axis */
+  real ox, oy, cs;
 } wc_t;
 
 static inline real wmax(real a, real b) { return a > b ? a : b; }
@@ -521,13 +530,61 @@ static void integ_vjp(const st_t* in, real a0, real a1, const st_t* out, const s
 /* ------------------------------------------------------------- one env */
 typedef struct {
   int A, K;
-  int* list;   /* [A*A] neighbor indices per agent (ascending, capped) */
+  int* list;   /* [A*A] neighbor indices per agent (capped, in list order) */
   int* nlist;  /* [A] */
+  int *cell, *cstart, *cfill, *csorted; /* grid order: [A] cells, [bins^2+1] starts,
+                                          [bins^2] cursors, [A] agents by cell */
   real *fx, *fy, *gfx, *gfy;
   st_t *sub;   /* [S+1][A] substep states of the current step */
 } scratch_t;
 
+static inline int grid_cell(real p, real o, const wc_t* W) {
+  int c = (int)((p - o) / W->cs); /* truncation toward zero, as wp.int32() */
+  return c < 0 ? 0 : (c > W->bins - 1 ? W->bins - 1 : c);
+}
+
+/* The uniform grid's lists: agents bucketed by cell in ascending index (the stable radix
+   sort), then per agent the 3 x 3 block, rows dy = -1..1, columns dx = -1..1. */
+static void grid_lists(const st_t* x, int A, const wc_t* W, scratch_t* sc) {
+  const int B = W->bins, NC = B * B;
+  for (int c = 0; c <= NC; ++c) sc->cstart[c] = 0;
+  for (int a = 0; a < A; ++a) {
+    sc->cell[a] = grid_cell(x[a].py, W->oy, W) * B + grid_cell(x[a].px, W->ox, W);
+    ++sc->cstart[sc->cell[a] + 1];
+  }
+  for (int c = 0; c < NC; ++c) sc->cstart[c + 1] += sc->cstart[c];
+  for (int c = 0; c < NC; ++c) sc->cfill[c] = sc->cstart[c];
+  for (int a = 0; a < A; ++a) sc->csorted[sc->cfill[sc->cell[a]]++] = a;  /* stable */
+  for (int a = 0; a < A; ++a) {
+    const int cy = sc->cell[a] / B, cx = sc->cell[a] - cy * B;
+    int n = 0;
+    for (int dy = -1; dy <= 1; ++dy) {
+      const int ny = cy + dy;
+      if (ny < 0 || ny >= B) continue;
+      for (int dx = -1; dx <= 1; ++dx) {
+        const int nx = cx + dx;
+        if (nx < 0 || nx >= B) continue;
+        const int c = ny * B + nx;
+        for (int i = sc->cstart[c]; i < sc->cstart[c + 1]; ++i) {
+          const int b = sc->csorted[i];
+          if (b == a) continue;
+          real ddx = x[b].px - x[a].px, ddy = x[b].py - x[a].py;
+          if (sqrt(ddx * ddx + ddy * ddy) <= W->R) {
+            if (n < W->K) sc->list[a * A + n] = b;
+            ++n;
+          }
+        }
+      }
+    }
+    sc->nlist[a] = n < W->K ? n : W->K;
+  }
+}
+
 static void neighbor_lists(const st_t* x, int A, const wc_t* W, scratch_t* sc) {
+  if (W->order == 1) {
+    grid_lists(x, A, W, sc);
+    return;
+  }
   for (int a = 0; a < A; ++a) {
     int n = 0;
     for (int b = 0; b < A; ++b) {
@@ -651,6 +708,12 @@ int SFX(swarp_cpu_rollout)(const cpu_world_t* w, const real* i_pos, const real* 
   W.R = (real)w->neighbor_radius;
   W.K = w->max_neighbors;
   W.bounds_mode = w->bounds_mode;
+  W.order = w->list_order;
+  W.bins = w->grid_bins > 0 ? w->grid_bins : 1;
+  W.ox = (real)w->grid_origin[0];
+  W.oy = (real)w->grid_origin[1];
+  W.cs = (real)w->grid_cell;
+  if (W.order == 1 && !(W.cs > 0)) return -1;
 #ifdef _OPENMP
   if (w->threads > 0) omp_set_num_threads(w->threads);
 #pragma omp parallel
@@ -666,6 +729,11 @@ int SFX(swarp_cpu_rollout)(const cpu_world_t* w, const real* i_pos, const real* 
     sc.gfx = sc.fx + 2 * A;
     sc.gfy = sc.fx + 3 * A;
     sc.sub = (st_t*)malloc(sizeof(st_t) * A * (S + 1));
+    const int NC = W.order == 1 ? W.bins * W.bins : 0;
+    sc.cell = (int*)malloc(sizeof(int) * (2 * A + 2 * NC + 1));
+    sc.csorted = sc.cell + A;
+    sc.cstart = sc.cell + 2 * A;
+    sc.cfill = sc.cstart + NC + 1;
     prm_t* P = (prm_t*)malloc(sizeof(prm_t) * A);
     ob_t* obs = (ob_t*)malloc(sizeof(ob_t) * (w->n_obstacles > 0 ? w->n_obstacles : 1));
     st_t* g = (st_t*)malloc(sizeof(st_t) * A * 2);
@@ -766,6 +834,7 @@ int SFX(swarp_cpu_rollout)(const cpu_world_t* w, const real* i_pos, const real* 
     free(sc.nlist);
     free(sc.fx);
     free(sc.sub);
+    free(sc.cell);
     free(P);
     free(obs);
     free(g);

@@ -22,6 +22,8 @@ class CpuWorld(C.Structure):
         ("obs_pos", C.c_void_p), ("obs_angle", C.c_void_p), ("obs_vel", C.c_void_p),
         ("obs_ang_vel", C.c_void_p), ("obs_radius", C.c_void_p), ("obs_half", C.c_void_p),
         ("obs_shape", C.c_void_p), ("threads", C.c_int),
+        ("list_order", C.c_int), ("grid_bins", C.c_int), ("grid_origin", C.c_double * 2),
+        ("grid_cell", C.c_double),
     ]
 
 
@@ -46,11 +48,14 @@ def _p(a):
 
 def rollout(*, params, model_tag, ctrl_mode, dt, substeps, collisions, k, c, margin, max_overlap,
             neighbor_radius, max_neighbors, bounds_mode, bounds, init, actions, grad_final_pos=None,
-            obstacles=None, threads=0, dtype=np.float32):
+            obstacles=None, threads=0, dtype=np.float32, grid=None):
     """Forward rollout (+ adjoint of <grad_final_pos, final pos> when given).
 
     ``init``: five arrays (pos [E,A,2], theta, vel [E,A,2], speed, ang_vel);
     ``actions`` [T,E,A,D]. Returns ``(traj5, grad_actions | None, grad_init5 | None)``.
+    ``grid=(bins, (x_min, x_max, y_min, y_max))`` lists neighbors in the order of the
+    reference's uniform grid with that static frame (origin at the rectangle's lower
+    corner, cell ``max(neighbor_radius, extent / bins)``); ``None`` in ascending index.
     """
     T, E, A, D = actions.shape
     keep = []
@@ -71,6 +76,11 @@ def rollout(*, params, model_tag, ctrl_mode, dt, substeps, collisions, k, c, mar
     w.params_env_stride = A * 22 if pr.ndim == 3 else 0
     w.model_tag = _p(arr(model_tag, np.int32))
     w.ctrl_mode = _p(arr(ctrl_mode, np.int32))
+    if grid is not None:
+        bins, (x0, x1, y0, y1) = grid
+        w.list_order, w.grid_bins = 1, int(bins)
+        w.grid_origin = (C.c_double * 2)(x0, y0)
+        w.grid_cell = max(neighbor_radius, max(x1 - x0, y1 - y0) / bins)
     if obstacles is not None:
         w.n_obstacles = obstacles["pos"].shape[1]
         for name in ("pos", "angle", "vel", "ang_vel", "radius", "half"):

@@ -149,6 +149,10 @@ class RefWorld:
     ang_damping: float = 10.0
     bodies_move: bool = True
     rk4: bool = False  # Integrator.RK4 instead of semi-implicit Euler
+    # "brute" (ascending index), "uniform_grid" (the radix-sort grid's order; frame from
+    # ``bounds`` when given, else from the batch) or "auto" (the grid above 512 agents)
+    neighbor_method: str = "brute"
+    uniform_bins: int | None = None
 
     def col(self, j):
         """Parameter column ``j`` broadcastable to ``[E, A]``."""
@@ -640,8 +644,18 @@ def collision_forces(state, w: RefWorld, obs: RefObstacles | None):
     th, om = state[1], state[4]
     hax, hay = w.col(P_HALF_X).expand(E, A), w.col(P_HALF_Y).expand(E, A)
     if w.collisions:
-        in_list, _, _, true_count = brute_neighbors(pos.detach(), w.neighbor_radius,
-                                                    w.max_neighbors)
+        method = w.neighbor_method
+        if method == "auto":
+            method = auto_neighbor_method(A)
+        if method == "uniform_grid":
+            in_list, _, _, true_count = uniform_grid_neighbors(
+                pos.detach(), w.neighbor_radius, w.max_neighbors, bins=w.uniform_bins,
+                bounds=w.bounds)
+        elif method == "brute":
+            in_list, _, _, true_count = brute_neighbors(pos.detach(), w.neighbor_radius,
+                                                        w.max_neighbors)
+        else:
+            raise ValueError(f"neighbor_method {method!r} is not restated")
         ar = torch.arange(A, device=px.device).unsqueeze(0)
         for b in range(A):
             sel = in_list[:, :, b]

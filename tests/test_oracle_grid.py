@@ -8,7 +8,9 @@ with the frame from the batch or pinned to a world rectangle, and for points out
 rectangle. Then the list order: the grid lists in (3 x 3 block cell, index) order, so a
 truncating list keeps a different set than brute force's ascending-index one; that
 difference is the one the CUDA path (ascending index for every method) has against the
-reference for truncating lists in envs above 512 agents.
+reference for truncating lists in envs above 512 agents. The C restatement
+(oracle/cpu_port.c, ``grid=``) lists in the same grid order with a static frame, and the
+two restatements agree through a truncating rollout and its adjoint.
 """
 
 from __future__ import annotations
@@ -86,3 +88,53 @@ def test_grid_list_order_and_truncation():
     differ = sum(s != t for su, sb in zip(sets(u_idx, u_cnt), sets(b_idx, b_cnt))
                  for s, t in zip(su, sb))
     assert differ > 0, "truncated lists keep different sets in grid and index order"
+
+
+def _grid_rollouts(E, A, T, K, seed, bins, bounds=(-1.0, 1.0, -1.0, 1.0), R_=0.12):
+    """One truncating case through both restatements with grid-ordered lists, float64."""
+    from oracle import cpu_port
+    from swarp_b200.dynamics.base import AgentConfig, param_rows
+
+    cfgs = [AgentConfig(radius=0.03, max_speed=1.0, max_accel=2.0) for _ in range(A)]
+    D = torch.float64
+    g = torch.Generator().manual_seed(seed)
+    pos = (torch.rand(E, A, 2, generator=g, dtype=D) * 2 - 1) * 0.9
+    z = torch.zeros(E, A, dtype=D)
+    vel = torch.randn(E, A, 2, generator=g, dtype=D) * 0.3
+    acts = (torch.rand(T, E, A, 2, generator=g, dtype=D) * 2 - 1)
+    gf = torch.randn(E, A, 2, generator=g, dtype=D)
+    params = param_rows(cfgs)
+    tags = [int(c.model) for c in cfgs]
+    modes = [int(c.ctrl_mode) for c in cfgs]
+    out = {}
+    for method in ("uniform_grid", "brute"):
+        w = R.RefWorld(params=torch.tensor(params), model_tag=tags, ctrl_mode=modes, dt=0.05,
+                       k=60.0, c=1.0, margin=0.02, neighbor_radius=R_, max_neighbors=K,
+                       bounds=bounds, soft_walls=True, neighbor_method=method,
+                       uniform_bins=bins)
+        st = [x.clone().requires_grad_(True) for x in (pos, z, vel, z, z)]
+        a = acts.clone().requires_grad_(True)
+        fin, traj, _ = R.rollout(tuple(st), a, w, None)
+        (fin[0] * gf).sum().backward()
+        ref = [torch.stack([traj[t][f] for t in range(T)]).detach().numpy() for f in range(5)]
+        out[method] = (ref, a.grad.numpy())
+    traj_c, ga_c, _ = cpu_port.rollout(
+        params=params, model_tag=tags, ctrl_mode=modes, dt=0.05, substeps=1, collisions=True,
+        k=60.0, c=1.0, margin=0.02, max_overlap=0.0, neighbor_radius=R_, max_neighbors=K,
+        bounds_mode=1, bounds=bounds, init=[x.numpy() for x in (pos, z, vel, z, z)],
+        actions=acts.numpy(), grad_final_pos=gf.numpy(), threads=2, dtype=np.float64,
+        grid=(bins, bounds))
+    return out, traj_c, ga_c
+
+
+def test_cpu_port_grid_order_matches_torch_oracle():
+    """The C restatement's grid-ordered lists (static frame) against the torch oracle's,
+    through a truncating rollout and its adjoint; and the grid order changes the result
+    against ascending-index lists (the lists truncate)."""
+    out, traj_c, ga_c = _grid_rollouts(E=2, A=300, T=3, K=4, seed=9, bins=17)
+    ref, ga = out["uniform_grid"]
+    for f in range(5):
+        np.testing.assert_allclose(traj_c[f], ref[f], rtol=1e-10, atol=1e-12)
+    np.testing.assert_allclose(ga_c, ga, rtol=1e-9, atol=1e-9 * np.abs(ga).max())
+    idx_ref, _ = out["brute"]
+    assert np.abs(idx_ref[2] - ref[2]).max() > 1e-3, "grid and index order keep other members"
