@@ -51,6 +51,17 @@ def test_world_config_validation_and_override():
     assert over.collision_k == 50.0 and over.bounds == (-1, 1, -1, 1)
 
 
+def test_neighbor_method_validation_matches_reference():
+    """swarp/core/neighbors.py:378-379, 391-392: unknown methods and bins below 1 raise
+    (checked before anything touches the device)."""
+    with pytest.raises(ValueError, match="method must be"):
+        swarp.Stepper([AgentConfig()], device="cuda:0",
+                      world=WorldConfig(neighbor_method="octree"))
+    with pytest.raises(ValueError, match="uniform_bins"):
+        swarp.Stepper([AgentConfig()], device="cuda:0",
+                      world=WorldConfig(neighbor_method="uniform_grid", uniform_bins=0))
+
+
 def test_action_bounds_table():
     lo, hi = swarp.action_bounds(AgentConfig(model=DynamicsModel.DIFF_DRIVE, max_speed=2.0,
                                              max_ang_vel=3.0))
