@@ -129,12 +129,17 @@ class Stepper:
             raise NotImplementedError("floor friction of movable bodies (obstacle_friction) is "
                                       "not on the CUDA path")
         # Every method is served by the brute-force (ascending-index) lists of the fused
-        # kernels; the names and bins are checked as the reference's NeighborGrid checks them
-        # (swarp/core/neighbors.py:378-379, 391-392).
-        if world.neighbor_method not in ("auto", "grid", "brute", "uniform_grid"):
-            raise ValueError('method must be "auto", "grid", "brute", or "uniform_grid"')
-        if world.uniform_bins is not None and world.uniform_bins < 1:
-            raise ValueError("uniform_bins must be >= 1")
+        # kernels. With collisions on (the reference then builds a NeighborGrid), the radius,
+        # method and bins are checked as NeighborGrid checks them
+        # (swarp/core/neighbors.py:376-379, 391-394).
+        if world.collisions:
+            reach = 2.0 * max(c.radius for c in self.configs) + world.collision_margin
+            if not (world.neighbor_radius or reach) > 0.0:
+                raise ValueError("radius must be positive")
+            if world.neighbor_method not in ("auto", "grid", "brute", "uniform_grid"):
+                raise ValueError('method must be "auto", "grid", "brute", or "uniform_grid"')
+            if world.uniform_bins is not None and world.uniform_bins < 1:
+                raise ValueError("uniform_bins must be >= 1")
         self.box_agents = any(c.shape == AgentShape.BOX for c in self.configs)
         if self.has_drones and self.box_agents:
             raise NotImplementedError("box agents and drones in one fleet are not on the CUDA path")

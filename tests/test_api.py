@@ -52,14 +52,17 @@ def test_world_config_validation_and_override():
 
 
 def test_neighbor_method_validation_matches_reference():
-    """swarp/core/neighbors.py:378-379, 391-392: unknown methods and bins below 1 raise
-    (checked before anything touches the device)."""
+    """swarp/core/neighbors.py:376-379, 391-394: with collisions on, a zero list radius,
+    unknown methods and bins below 1 raise (checked before anything touches the device)."""
     with pytest.raises(ValueError, match="method must be"):
         swarp.Stepper([AgentConfig()], device="cuda:0",
                       world=WorldConfig(neighbor_method="octree"))
     with pytest.raises(ValueError, match="uniform_bins"):
         swarp.Stepper([AgentConfig()], device="cuda:0",
                       world=WorldConfig(neighbor_method="uniform_grid", uniform_bins=0))
+    with pytest.raises(ValueError, match="radius must be positive"):
+        swarp.Stepper([AgentConfig(radius=0.0)], device="cuda:0",
+                      world=WorldConfig(collision_margin=0.0))
 
 
 def test_action_bounds_table():
