@@ -69,3 +69,12 @@ def test_action_bounds_table():
     lo, hi = swarp.action_bounds(AgentConfig(model=DynamicsModel.DIFF_DRIVE, max_speed=2.0,
                                              max_ang_vel=3.0))
     assert lo == [-2.0, -3.0] and hi == [2.0, 3.0]
+
+
+def test_streamed_chunk_count():
+    """StreamedRollout splits the batch into the most equal env chunks up to the asked
+    count (equal chunks replay one captured step)."""
+    from swarp_b200.interop.streamed import _chunks
+
+    assert _chunks(16000, 2) == 2 and _chunks(16000, 3) == 2 and _chunks(12, 5) == 4
+    assert _chunks(7, 4) == 1 and _chunks(3, 8) == 3 and _chunks(1, 1) == 1
